@@ -1,0 +1,51 @@
+// Host-side planning / launching of the tcgen05 GEMM (dense linear and implicit-GEMM conv).
+#pragma once
+
+#include <cuda_fp16.h>
+
+#include "common.h"
+#include "gemm_tc.cuh"
+
+namespace dlm {
+
+// A fully-encoded GEMM launch: tensor maps + kernel parameters.  Built once, launched many
+// times (the UNet builds all of its ops at plan time and replays them in a CUDA graph).
+struct GemmOp {
+  CUtensorMap tmA[3];
+  CUtensorMap tmB;
+  GemmParams p;
+  int bn = 0;
+  int grid = 0;
+};
+
+struct GemmEpilogue {
+  unsigned flags = 0;
+  float alpha = 1.0f;
+  float resid_scale = 1.0f;
+  const __half* bias = nullptr;
+  const __half* bias2d = nullptr;
+  int rows_per_img = 1;
+  const __half* resid = nullptr;
+  int ldr = 0;
+};
+
+// One source of an implicit-GEMM conv K segment.
+struct ConvSource {
+  int kind = 0;               // 0: 3x3 s1, 1: 1x1, 2: 3x3 s2 from parity planes
+  const __half* ptr = nullptr; // NHWC [Nb, oH, oW, C] (kinds 0/1) or planes [4, Nb, oH, oW, C]
+  int C = 0;                  // channels, multiple of 64
+};
+
+// Dense: C[M, ldc] = epi(A[M, K] (row stride lda) * W[N, K]^T).
+int gemm_plan_dense(GemmOp* op, const __half* A, int lda, const __half* W, int M, int N, int K,
+                    __half* C, int ldc, const GemmEpilogue& epi, int force_bn = 0);
+
+// Implicit-GEMM conv producing NHWC out[Nb, oH, oW, Cout] (row stride ldc) from up to three
+// K segments; W is [Cout, sum(taps_s * C_s)] with the K index ordered (segment, tap, channel).
+int gemm_plan_conv(GemmOp* op, int Nb, int oH, int oW, const ConvSource* srcs, int nsrc,
+                   const __half* W, int Cout, __half* C, int ldc, const GemmEpilogue& epi,
+                   int force_bn = 0);
+
+int gemm_launch(const GemmOp& op, cudaStream_t stream);
+
+}  // namespace dlm

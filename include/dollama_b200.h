@@ -1,0 +1,106 @@
+/*
+ * dollama_b200 — C ABI of the B200-native (sm_100a) dense-contraction hot path of dollama:
+ * the SDXL UNet / VAE matmuls (implicit-GEMM conv2d, transformer linears, flash attention)
+ * and the BitNet tag-LM ternary x int8 GEMM/GEMV.
+ *
+ * Conventions for every entry point:
+ *   - pointers are DEVICE pointers unless the name says `host`; sizes are element counts;
+ *   - work is enqueued on `stream` (0 = legacy default stream) and returns without a sync;
+ *   - the return value is a dlm_status: 0 on success, negative on failure; the message of
+ *     the last failure on the calling thread is available from dlm_last_error();
+ *   - empty problems (any size 0) return DLM_OK without launching, as the reference's
+ *     launchers silently return on empty dims (src/kernels/conv2d.cu:762-770,
+ *     src/kernels/attention_fast.cu:295-298);
+ *   - fp16 is IEEE binary16 passed as `void*` / `const void*` (no CUDA types in signatures);
+ *     cudaStream_t is passed as `void*`.
+ *
+ * Activations of the UNet / VAE entry points are NHWC (token-major) inside this library;
+ * the model-level entry points take and return the reference's NCHW tensors.
+ */
+#ifndef DOLLAMA_B200_H_
+#define DOLLAMA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum dlm_status {
+  DLM_OK = 0,
+  DLM_ERR_INVALID = -1,      /* bad argument (null pointer, unsupported shape/alignment)     */
+  DLM_ERR_CUDA = -2,         /* a CUDA runtime/driver call failed                            */
+  DLM_ERR_TIMEOUT = -3,      /* a kernel gave up a bounded wait (see dlm_get_device_status)  */
+  DLM_ERR_UNSUPPORTED = -4,  /* valid in the reference but not provided by this library      */
+  DLM_ERR_NOMEM = -5,        /* device memory / arena exhausted                              */
+  DLM_ERR_NOT_FOUND = -6     /* a named weight tensor is missing                             */
+} dlm_status;
+
+/* ------------------------------------------------------------------ library */
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* dlm_last_error(void);
+
+/* Library version string. */
+const char* dlm_version(void);
+
+/* Reads (and clears when `clear` != 0) the device status word of the current device:
+ * 0 = no kernel gave up a wait; otherwise the code of the first kernel role that timed out.
+ * Synchronizes `stream`. */
+int dlm_get_device_status(int* out_code, int clear, void* stream);
+
+/* ------------------------------------------------------------------ GEMM (tcgen05)
+ *
+ * Replaces launch_gemm_fp16 (reference src/kernels/gemm.cuh:44-53, gemm.cu:518):
+ *   C[M,N] = alpha * op(A)[M,K] * op(B)[K,N] + beta * C, row-major fp16, fp32 accumulate.
+ * Supported: transA = 0 and transB = 1 (B is [N,K], PyTorch Linear layout) — the only form
+ * the reference's UNet / VAE / LM paths use.  K % 8 == 0 and N % 32 == 0.
+ * transB = 0 and transA = 1 return DLM_ERR_UNSUPPORTED.
+ */
+int dlm_launch_gemm_fp16(const void* A, const void* B, void* C, int M, int N, int K, float alpha,
+                         float beta, int transA, int transB, void* stream);
+
+/* Epilogue flags of dlm_gemm_fp16_ex. */
+#define DLM_EPI_BIAS 1u     /* + bias[n]                                                */
+#define DLM_EPI_RESID 2u    /* + residual[m, n] (residual may alias C, in place)        */
+#define DLM_EPI_GEGLU 4u    /* columns interleaved (x1_j, x2_j): C[m, j] = x1 * gelu(x2) */
+#define DLM_EPI_SILU 8u     /* SiLU after bias                                          */
+#define DLM_EPI_BIAS2D 16u  /* + bias2d[m / rows_per_img, n] (per-image channel bias)   */
+
+/* Fused linear: C[M, ldc] = epi(A[M,K] (row stride lda) * W[N,K]^T).  With DLM_EPI_GEGLU the
+ * output has N/2 columns.  Fuses the reference's GEMM + launch_bias_add_rowvec +
+ * launch_add + launch_geglu sequence (src/infer/unet.cu:517-526, 759-770). */
+int dlm_gemm_fp16_ex(const void* A, int lda, const void* W, void* C, int ldc, int M, int N, int K,
+                     unsigned flags, const void* bias, const void* bias2d, int rows_per_img,
+                     const void* residual, int ldr, void* stream);
+
+/* ------------------------------------------------------------------ conv2d (implicit GEMM)
+ *
+ * Replaces launch_conv2d (reference src/kernels/conv2d.cuh:38-40, conv2d.cu:757) for the
+ * shapes of the UNet / VAE hot path, on NHWC activations and without an im2col buffer
+ * (conv2d.cu:219 im2col + gemm.cu:425 GEMM + conv2d.cu:171 bias pass become one kernel):
+ *   out[N, oH, oW, Cout] = conv(in[N, H, W, Cin], w) + bias
+ * Kernels: 3x3 pad 1 stride 1, 3x3 pad 1 stride 2 (Downsample2D, unet.cu:864-868), 1x1 stride 1
+ * (conv_shortcut).  Cin % 64 == 0, Cout % 32 == 0, oW divides or is a multiple of 128 pixels.
+ * w_krsc is [Cout, KH, KW, Cin] (see dlm_pack_conv_weight); bias may be NULL.
+ * Stride 2 needs `scratch` of dlm_conv2d_nhwc_scratch_bytes() bytes (parity planes).
+ */
+size_t dlm_conv2d_nhwc_scratch_bytes(int N, int H, int W, int Cin, int ksize, int stride);
+int dlm_conv2d_nhwc(const void* in, int N, int H, int W, int Cin, const void* w_krsc,
+                    const void* bias, void* out, int Cout, int ksize, int stride, void* scratch,
+                    size_t scratch_bytes, void* stream);
+
+/* PyTorch conv weight [Cout, Cin, KH, KW] -> [Cout, KH, KW, Cin] (the GEMM K order). */
+int dlm_pack_conv_weight(const void* w_oihw, void* w_krsc, int Cout, int Cin, int KH, int KW,
+                         void* stream);
+
+/* Layout conversions between the reference's NCHW tensors and this library's NHWC. */
+int dlm_nchw_to_nhwc(const void* in, void* out, int N, int C, int HW, void* stream);
+int dlm_nhwc_to_nchw(const void* in, void* out, int N, int C, int HW, void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif /* DOLLAMA_B200_H_ */
