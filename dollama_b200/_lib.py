@@ -38,6 +38,16 @@ _SIGS = {
     "dlm_pack_conv_weight": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p]),
     "dlm_nchw_to_nhwc": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
     "dlm_nhwc_to_nchw": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
+    "dlm_launch_attention": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
+                                     c_int, c_int, c_float, c_void_p]),
+    "dlm_attention_tokens": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p,
+                                     c_int, c_int, c_int, c_int, c_int, c_int, c_float, c_void_p]),
+    "dlm_group_norm_nhwc_scratch_bytes": (c_size_t, [c_int, c_int]),
+    "dlm_group_norm_nhwc": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_void_p,
+                                    c_void_p, c_float, c_int, c_int, c_void_p, c_void_p, c_size_t,
+                                    c_void_p]),
+    "dlm_launch_layer_norm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_float,
+                                      c_void_p]),
 }
 
 EPI_BIAS = 1

@@ -1,0 +1,322 @@
+// GroupNorm and LayerNorm on NHWC / token-major fp16 activations (HBM-bound).
+//
+// GroupNorm (replaces launch_group_norm / _mb / _silu, reference src/kernels/groupnorm.cuh:51-108,
+// groupnorm.cu:246-467) is two launches:
+//   gn_stats   grid (chunks, N): each block reduces a chunk of pixels to per-group partial
+//              (sum, sum of squares) in fp32, in a fixed order (deterministic, like the
+//              reference's multi-block GN, groupnorm.cu:246-327);
+//   gn_apply   each block first folds its image's partials (fixed order, fp64) into mean / rstd
+//              per group, then writes y = (x - mean) * rstd * gamma + beta (optional SiLU) as fp16.
+// The input may be the channel concatenation of two NHWC sources (the UNet up-path skip concat,
+// unet.cu:250 k_concat_chw): gn_apply writes the normalised concat in one pass, so the concat
+// copy never exists.
+// LayerNorm (launch_layer_norm, layernorm.cuh:51-57): one warp per token row, two-pass mean /
+// variance in registers.
+#include <cuda_fp16.h>
+
+#include "norm.h"
+#include "ptx.cuh"
+
+namespace dlm {
+
+namespace {
+
+constexpr int kGroups = 32;
+constexpr int kStatThreads = 256;
+
+__device__ __forceinline__ void load8(const __half* p, float* f) {
+  const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+  const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __half22float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+// partials[(n * chunks + chunk) * 32 + g] = (sum, sumsq)
+__global__ void __launch_bounds__(kStatThreads)
+    gn_stats_kernel(const __half* __restrict__ x1, int C1, const __half* __restrict__ x2, int C2,
+                    int HW, int pix_per_chunk, float2* __restrict__ partials) {
+  extern __shared__ float sh[];  // [PL][C] sums then [PL][C] sumsq
+  const int C = C1 + C2;
+  const int nvec = C >> 3;
+  const int chunk = blockIdx.x, n = blockIdx.y, chunks = gridDim.x;
+  const int PL = nvec >= kStatThreads ? 1 : kStatThreads / nvec;
+  float* s_sum = sh;
+  float* s_sq = sh + PL * C;
+  const int p0 = chunk * pix_per_chunk;
+  const int p1 = min(HW, p0 + pix_per_chunk);
+  for (int t = threadIdx.x; t < PL * nvec; t += blockDim.x) {
+    const int cv = t % nvec, pl = t / nvec;
+    const int c = cv * 8;
+    float a[8], q[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) a[i] = q[i] = 0.0f;
+    for (int pix = p0 + pl; pix < p1; pix += PL) {
+      float f[8];
+      const size_t row = static_cast<size_t>(n) * HW + pix;
+      if (c < C1)
+        load8(x1 + row * C1 + c, f);
+      else
+        load8(x2 + row * C2 + (c - C1), f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        a[i] += f[i];
+        q[i] = fmaf(f[i], f[i], q[i]);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      s_sum[pl * C + c + i] = a[i];
+      s_sq[pl * C + c + i] = q[i];
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < kGroups) {
+    const int g = threadIdx.x;
+    const int cpg = C / kGroups;
+    float a = 0.0f, q = 0.0f;
+    for (int pl = 0; pl < PL; ++pl)
+      for (int c = g * cpg; c < (g + 1) * cpg; ++c) {
+        a += s_sum[pl * C + c];
+        q += s_sq[pl * C + c];
+      }
+    partials[(static_cast<size_t>(n) * chunks + chunk) * kGroups + g] = make_float2(a, q);
+  }
+}
+
+// Each block handles `pix_per_block` pixels of image n = blockIdx.y.
+__global__ void __launch_bounds__(256)
+    gn_apply_kernel(const __half* __restrict__ x1, int C1, const __half* __restrict__ x2, int C2,
+                    int HW, const float2* __restrict__ partials, int chunks,
+                    const __half* __restrict__ gamma, const __half* __restrict__ beta, float eps,
+                    int silu, int pix_per_block, __half* __restrict__ out) {
+  __shared__ float s_mean[kGroups], s_rstd[kGroups];
+  const int C = C1 + C2;
+  const int n = blockIdx.y;
+  if (threadIdx.x < kGroups) {
+    const int g = threadIdx.x;
+    double a = 0.0, q = 0.0;
+    const float2* pp = partials + static_cast<size_t>(n) * chunks * kGroups + g;
+    for (int k = 0; k < chunks; ++k) {
+      const float2 v = pp[static_cast<size_t>(k) * kGroups];
+      a += v.x;
+      q += v.y;
+    }
+    const double cnt = static_cast<double>(HW) * (C / kGroups);
+    const double mean = a / cnt;
+    double var = q / cnt - mean * mean;
+    if (var < 0.0) var = 0.0;
+    s_mean[g] = static_cast<float>(mean);
+    s_rstd[g] = static_cast<float>(1.0 / sqrt(var + static_cast<double>(eps)));
+  }
+  __syncthreads();
+  const int nvec = C >> 3;
+  const int cpg = C / kGroups;
+  const int p0 = blockIdx.x * pix_per_block;
+  const int p1 = min(HW, p0 + pix_per_block);
+  const size_t total = static_cast<size_t>(p1 - p0) * nvec;
+  for (size_t t = threadIdx.x; t < total; t += blockDim.x) {
+    const int cv = static_cast<int>(t % nvec);
+    const int pix = p0 + static_cast<int>(t / nvec);
+    const int c = cv * 8;
+    const size_t row = static_cast<size_t>(n) * HW + pix;
+    float f[8], gm[8], bt[8];
+    if (c < C1)
+      load8(x1 + row * C1 + c, f);
+    else
+      load8(x2 + row * C2 + (c - C1), f);
+    load8(gamma + c, gm);
+    load8(beta + c, bt);
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) {
+      const int g0 = (c + i) / cpg, g1 = (c + i + 1) / cpg;
+      float y0 = (f[i] - s_mean[g0]) * s_rstd[g0] * gm[i] + bt[i];
+      float y1 = (f[i + 1] - s_mean[g1]) * s_rstd[g1] * gm[i + 1] + bt[i + 1];
+      if (silu) {
+        y0 = silu_f(y0);
+        y1 = silu_f(y1);
+      }
+      o[i >> 1] = pack_half2(y0, y1);
+    }
+    *reinterpret_cast<uint4*>(out + row * C + c) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// One warp per row; C % 256 == 0 is not required, C % 8 == 0 and C <= 8 * 32 * kLnVec.
+constexpr int kLnVec = 8;  // up to 2048 channels
+__global__ void __launch_bounds__(256)
+    layer_norm_kernel(const __half* __restrict__ x, const __half* __restrict__ gamma,
+                      const __half* __restrict__ beta, __half* __restrict__ out, int rows, int C,
+                      float eps) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const int nvec = C >> 3;
+  const __half* xr = x + static_cast<size_t>(warp) * C;
+  float v[kLnVec][8];
+  float s = 0.0f;
+#pragma unroll
+  for (int k = 0; k < kLnVec; ++k) {
+    const int cv = lane + 32 * k;
+    if (cv < nvec) {
+      load8(xr + cv * 8, v[k]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) s += v[k][i];
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float mean = s / C;
+  float q = 0.0f;
+#pragma unroll
+  for (int k = 0; k < kLnVec; ++k) {
+    const int cv = lane + 32 * k;
+    if (cv < nvec) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float d = v[k][i] - mean;
+        q = fmaf(d, d, q);
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+  const float rstd = rsqrtf(q / C + eps);
+  __half* orow = out + static_cast<size_t>(warp) * C;
+#pragma unroll
+  for (int k = 0; k < kLnVec; ++k) {
+    const int cv = lane + 32 * k;
+    if (cv < nvec) {
+      float gm[8], bt[8];
+      if (gamma) load8(gamma + cv * 8, gm);
+      if (beta) load8(beta + cv * 8, bt);
+      uint32_t o[4];
+#pragma unroll
+      for (int i = 0; i < 8; i += 2) {
+        float y0 = (v[k][i] - mean) * rstd, y1 = (v[k][i + 1] - mean) * rstd;
+        if (gamma) {
+          y0 *= gm[i];
+          y1 *= gm[i + 1];
+        }
+        if (beta) {
+          y0 += bt[i];
+          y1 += bt[i + 1];
+        }
+        o[i >> 1] = pack_half2(y0, y1);
+      }
+      *reinterpret_cast<uint4*>(orow + cv * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
+}  // namespace
+
+int gn_plan(GnOp* op, const __half* x1, int C1, const __half* x2, int C2, int N, int HW,
+            const __half* gamma, const __half* beta, float eps, bool silu, __half* out,
+            float2* partials, size_t partial_cap) {
+  const int C = C1 + C2;
+  DLM_REQUIRE(op && x1 && gamma && beta && out && partials, DLM_ERR_INVALID, "gn: null pointer");
+  DLM_REQUIRE(C % kGroups == 0 && C1 % 8 == 0 && C2 % 8 == 0 && (C2 == 0 || x2 != nullptr),
+              DLM_ERR_INVALID, "gn: channels %d+%d must be multiples of 8 and of 32 in total", C1, C2);
+  DLM_REQUIRE(C <= 4096, DLM_ERR_INVALID, "gn: at most 4096 channels");
+  const int sms = num_sms();
+  int chunks = (4 * sms + N - 1) / N;
+  int ppc = (HW + chunks - 1) / chunks;
+  if (ppc < 8) ppc = 8;
+  chunks = (HW + ppc - 1) / ppc;
+  DLM_REQUIRE(static_cast<size_t>(N) * chunks * kGroups <= partial_cap, DLM_ERR_NOMEM,
+              "gn: partial buffer too small (%zu < %zu)", partial_cap,
+              static_cast<size_t>(N) * chunks * kGroups);
+  op->x1 = x1;
+  op->x2 = x2;
+  op->C1 = C1;
+  op->C2 = C2;
+  op->N = N;
+  op->HW = HW;
+  op->gamma = gamma;
+  op->beta = beta;
+  op->eps = eps;
+  op->silu = silu;
+  op->out = out;
+  op->partials = partials;
+  op->chunks = chunks;
+  op->pix_per_chunk = ppc;
+  const int nvec = C / 8;
+  const int PL = nvec >= kStatThreads ? 1 : kStatThreads / nvec;
+  op->stat_smem = 2 * PL * C * static_cast<int>(sizeof(float));
+  int ppb = (HW + (2 * sms + N - 1) / N - 1) / ((2 * sms + N - 1) / N);
+  if (ppb < 4) ppb = 4;
+  op->pix_per_block = ppb;
+  return DLM_OK;
+}
+
+size_t gn_partial_elems(int N, int HW) {
+  const int sms = 148 * 2;  // generous bound for any SM count up to 296
+  (void)HW;
+  return static_cast<size_t>(N) * ((4 * sms + N - 1) / N + 1) * kGroups;
+}
+
+int gn_launch(const GnOp& op, cudaStream_t s) {
+  if (op.stat_smem > 48 * 1024) {
+    DLM_CHECK_CUDA(cudaFuncSetAttribute(gn_stats_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        op.stat_smem));
+  }
+  gn_stats_kernel<<<dim3(op.chunks, op.N), kStatThreads, op.stat_smem, s>>>(
+      op.x1, op.C1, op.x2, op.C2, op.HW, op.pix_per_chunk, op.partials);
+  DLM_CHECK_CUDA(cudaGetLastError());
+  const int blocks = (op.HW + op.pix_per_block - 1) / op.pix_per_block;
+  gn_apply_kernel<<<dim3(blocks, op.N), 256, 0, s>>>(op.x1, op.C1, op.x2, op.C2, op.HW, op.partials,
+                                                     op.chunks, op.gamma, op.beta, op.eps,
+                                                     op.silu ? 1 : 0, op.pix_per_block, op.out);
+  DLM_CHECK_CUDA(cudaGetLastError());
+  return DLM_OK;
+}
+
+int layer_norm(const __half* x, const __half* gamma, const __half* beta, __half* out, int rows, int C,
+               float eps, cudaStream_t s) {
+  DLM_REQUIRE(x && out, DLM_ERR_INVALID, "layer_norm: null pointer");
+  DLM_REQUIRE(C % 8 == 0 && C <= 8 * 32 * kLnVec, DLM_ERR_INVALID,
+              "layer_norm: C=%d must be a multiple of 8 and <= %d", C, 8 * 32 * kLnVec);
+  const int warps_per_block = 8;
+  const int blocks = (rows + warps_per_block - 1) / warps_per_block;
+  layer_norm_kernel<<<blocks, warps_per_block * 32, 0, s>>>(x, gamma, beta, out, rows, C, eps);
+  DLM_CHECK_CUDA(cudaGetLastError());
+  return DLM_OK;
+}
+
+}  // namespace dlm
+
+extern "C" {
+
+size_t dlm_group_norm_nhwc_scratch_bytes(int N, int HW) {
+  return dlm::gn_partial_elems(N, HW) * sizeof(float2);
+}
+
+int dlm_group_norm_nhwc(const void* x1, int C1, const void* x2, int C2, int N, int HW,
+                        const void* gamma, const void* beta, float eps, int groups, int silu,
+                        void* out, void* scratch, size_t scratch_bytes, void* stream) {
+  if (N == 0 || HW == 0 || C1 + C2 == 0) return DLM_OK;
+  DLM_REQUIRE(groups == 32, DLM_ERR_UNSUPPORTED, "group_norm_nhwc: groups must be 32");
+  DLM_REQUIRE(scratch != nullptr, DLM_ERR_INVALID, "group_norm_nhwc: null scratch");
+  dlm::GnOp op;
+  int rc = dlm::gn_plan(&op, static_cast<const __half*>(x1), C1, static_cast<const __half*>(x2), C2,
+                        N, HW, static_cast<const __half*>(gamma), static_cast<const __half*>(beta),
+                        eps, silu != 0, static_cast<__half*>(out), static_cast<float2*>(scratch),
+                        scratch_bytes / sizeof(float2));
+  if (rc != DLM_OK) return rc;
+  return dlm::gn_launch(op, static_cast<cudaStream_t>(stream));
+}
+
+int dlm_launch_layer_norm(const void* in, const void* gamma, const void* beta, void* out, int rows,
+                          int C, float eps, void* stream) {
+  if (rows == 0 || C == 0) return DLM_OK;
+  return dlm::layer_norm(static_cast<const __half*>(in), static_cast<const __half*>(gamma),
+                         static_cast<const __half*>(beta), static_cast<__half*>(out), rows, C, eps,
+                         static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,34 @@
+// GroupNorm (NHWC, optional two-source concat + SiLU) and LayerNorm launchers (norm.cu).
+#pragma once
+
+#include <cuda_fp16.h>
+
+#include "common.h"
+
+namespace dlm {
+
+struct GnOp {
+  const __half* x1 = nullptr;
+  const __half* x2 = nullptr;
+  int C1 = 0, C2 = 0, N = 0, HW = 0;
+  const __half* gamma = nullptr;
+  const __half* beta = nullptr;
+  float eps = 1e-5f;
+  bool silu = false;
+  __half* out = nullptr;
+  float2* partials = nullptr;
+  int chunks = 0, pix_per_chunk = 0, pix_per_block = 0, stat_smem = 0;
+};
+
+// out[N, HW, C1 + C2] = GN32(concat(x1[N, HW, C1], x2[N, HW, C2])) (+ SiLU); `partials` is a
+// scratch buffer of at least gn_partial_elems(N, HW) float2.
+int gn_plan(GnOp* op, const __half* x1, int C1, const __half* x2, int C2, int N, int HW,
+            const __half* gamma, const __half* beta, float eps, bool silu, __half* out,
+            float2* partials, size_t partial_cap);
+size_t gn_partial_elems(int N, int HW);
+int gn_launch(const GnOp& op, cudaStream_t s);
+
+int layer_norm(const __half* x, const __half* gamma, const __half* beta, __half* out, int rows, int C,
+               float eps, cudaStream_t s);
+
+}  // namespace dlm

@@ -255,6 +255,13 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N, bool b_mn_maj
 }
 
 // ---------------------------------------------------------------- small math
+// 2^x with the hardware approximation (ex2.approx.ftz.f32, max relative error ~2^-22).
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
 
 __device__ __forceinline__ float gelu_erf_f(float x) {

@@ -99,6 +99,41 @@ int dlm_pack_conv_weight(const void* w_oihw, void* w_krsc, int Cout, int Cin, in
 int dlm_nchw_to_nhwc(const void* in, void* out, int N, int C, int HW, void* stream);
 int dlm_nhwc_to_nchw(const void* in, void* out, int N, int C, int HW, void* stream);
 
+/* ------------------------------------------------------------------ attention (tcgen05 flash)
+ *
+ * Replaces launch_attention / launch_attention_fast (reference src/kernels/attention.cuh:53-73):
+ * out = softmax(q k^T * scale) v, q/k/v/out [B, H, S, Dh] contiguous fp16, fp32 online softmax.
+ * Dh must be 64 (the UNet's head_dim, src/infer/unet.cu:683-684).
+ */
+int dlm_launch_attention(const void* q, const void* k, const void* v, void* out, int B, int H,
+                         int Sq, int Sk, int Dh, float scale, void* stream);
+
+/* Same op on token-major projections: q is [B*Sq, ldq] with head h in columns [h*64, h*64+64),
+ * k / v are [B*Sk, ldk / ldv], out is [B*Sq, ldo].  Removes the reference's split/merge-heads
+ * copies (src/infer/unet.cu:198,213). */
+int dlm_attention_tokens(const void* q, int ldq, const void* k, int ldk, const void* v, int ldv,
+                         void* out, int ldo, int B, int H, int Sq, int Sk, int Dh, float scale,
+                         void* stream);
+
+/* ------------------------------------------------------------------ normalisation
+ *
+ * GroupNorm(32) over NHWC activations, optionally of the channel concatenation of two sources
+ * (x2 may be NULL with C2 = 0), optionally followed by SiLU; out is [N, HW, C1 + C2].
+ * Replaces launch_group_norm / launch_group_norm_mb / launch_group_norm_silu (reference
+ * src/kernels/groupnorm.cuh:51-108) and the up-path concat (src/infer/unet.cu:250).
+ * Deterministic (fixed-order reductions).  `scratch` holds the per-chunk partial sums:
+ * dlm_group_norm_nhwc_scratch_bytes(N, HW) bytes.
+ */
+size_t dlm_group_norm_nhwc_scratch_bytes(int N, int HW);
+int dlm_group_norm_nhwc(const void* x1, int C1, const void* x2, int C2, int N, int HW,
+                        const void* gamma, const void* beta, float eps, int groups, int silu,
+                        void* out, void* scratch, size_t scratch_bytes, void* stream);
+
+/* LayerNorm over the last dim of [rows, C] (reference src/kernels/layernorm.cuh:51-57);
+ * gamma / beta may be NULL.  C % 8 == 0, C <= 2048. */
+int dlm_launch_layer_norm(const void* in, const void* gamma, const void* beta, void* out, int rows,
+                          int C, float eps, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -1,0 +1,79 @@
+"""tcgen05 flash attention parity against a PyTorch fp32 softmax(QK^T/8)V (GPU).
+
+Shapes are the UNet's (src/infer/unet.cu:677-797): self-attention at 32^2 / 64^2 tokens,
+cross-attention to 77 context tokens (keys masked beyond Sk), both in the reference's
+[B, H, S, 64] layout and in the token-major layout the UNet uses.  Tolerance: the per-layer
+bar max|err|/max|ref| <= 2e-3 plus the reference's attention tolerance
+(src/tests/test_attention_fast.cu:56-63).
+"""
+import ctypes
+import math
+
+import pytest
+import torch
+
+from dollama_b200 import _lib as L
+from tests.helpers import max_rel_err, allclose_k
+
+pytestmark = pytest.mark.gpu
+
+
+def _p(t):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _s():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def ref_attn(q, k, v):
+    s = (q.float() @ k.float().transpose(-1, -2)) / 8.0
+    return torch.softmax(s, dim=-1) @ v.float()
+
+
+@pytest.mark.parametrize("B,H,Sq,Sk", [(1, 1, 128, 128), (2, 10, 1024, 1024), (2, 10, 4096, 4096),
+                                       (2, 20, 1024, 77), (1, 2, 256, 300), (2, 3, 200, 130)])
+def test_attention_bhsd(B, H, Sq, Sk):
+    g = torch.Generator().manual_seed(B * 100 + Sq + Sk)
+    q = torch.randn(B, H, Sq, 64, generator=g).half().cuda()
+    k = torch.randn(B, H, Sk, 64, generator=g).half().cuda()
+    v = torch.randn(B, H, Sk, 64, generator=g).half().cuda()
+    o = torch.empty_like(q)
+    L.call("dlm_launch_attention", _p(q), _p(k), _p(v), _p(o), B, H, Sq, Sk, 64, 1.0 / 8.0, _s())
+    torch.cuda.synchronize()
+    ref = ref_attn(q, k, v)
+    assert max_rel_err(o, ref) < 2e-3
+    assert allclose_k(o, ref, Sk)
+
+
+def test_attention_tokens_cross():
+    B, H, Sq, Sk = 2, 10, 4096, 77
+    C = H * 64
+    g = torch.Generator().manual_seed(5)
+    qkv = torch.randn(B * Sq, C, generator=g).half().cuda()
+    kv = torch.randn(B * Sk, 2 * C, generator=g).half().cuda()
+    out = torch.empty(B * Sq, C, dtype=torch.float16, device="cuda")
+    L.call("dlm_attention_tokens", _p(qkv), C, _p(kv), 2 * C, ctypes.c_void_p(kv.data_ptr() + 2 * C),
+           2 * C, _p(out), C, B, H, Sq, Sk, 64, 0.125, _s())
+    torch.cuda.synchronize()
+    q = qkv.view(B, Sq, H, 64).transpose(1, 2)
+    k = kv[:, :C].reshape(B, Sk, H, 64).transpose(1, 2)
+    v = kv[:, C:].reshape(B, Sk, H, 64).transpose(1, 2)
+    ref = ref_attn(q, k, v).transpose(1, 2).reshape(B * Sq, C)
+    assert max_rel_err(out, ref) < 2e-3
+
+
+def test_attention_tokens_self_fused_qkv():
+    B, H, S = 2, 20, 1024
+    C = H * 64
+    g = torch.Generator().manual_seed(6)
+    qkv = torch.randn(B * S, 3 * C, generator=g).half().cuda()
+    out = torch.empty(B * S, C, dtype=torch.float16, device="cuda")
+    base = qkv.data_ptr()
+    L.call("dlm_attention_tokens", ctypes.c_void_p(base), 3 * C, ctypes.c_void_p(base + 2 * C), 3 * C,
+           ctypes.c_void_p(base + 4 * C), 3 * C, _p(out), C, B, H, S, S, 64, 0.125, _s())
+    torch.cuda.synchronize()
+    t = qkv.view(B, S, 3, H, 64)
+    q, k, v = (t[:, :, i].transpose(1, 2) for i in range(3))
+    ref = ref_attn(q, k, v).transpose(1, 2).reshape(B * S, C)
+    assert max_rel_err(out, ref) < 2e-3
