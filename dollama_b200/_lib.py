@@ -28,6 +28,7 @@ _SIGS = {
     "dlm_last_error": (c_char_p, []),
     "dlm_version": (c_char_p, []),
     "dlm_get_device_status": (c_int, [ctypes.POINTER(c_int), c_int, c_void_p]),
+    "dlm_memcpy": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p]),
     "dlm_launch_gemm_fp16": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_float,
                                      c_float, c_int, c_int, c_void_p]),
     "dlm_gemm_fp16_ex": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
@@ -48,6 +49,17 @@ _SIGS = {
                                     c_void_p]),
     "dlm_launch_layer_norm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_float,
                                       c_void_p]),
+    "dlm_unet_create": (c_int, [ctypes.POINTER(c_int), c_int, c_int, ctypes.POINTER(c_char_p),
+                                ctypes.POINTER(c_void_p), ctypes.POINTER(ctypes.c_int64),
+                                ctypes.POINTER(c_void_p), c_void_p]),
+    "dlm_unet_destroy": (c_int, [c_void_p]),
+    "dlm_unet_forward": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_float, c_void_p,
+                                 c_void_p, c_void_p, c_void_p, c_void_p]),
+    "dlm_unet_set_graph": (c_int, [c_void_p, c_int]),
+    "dlm_unet_stage": (c_int, [c_void_p, c_char_p, ctypes.POINTER(c_void_p), ctypes.POINTER(c_int),
+                               ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
+    "dlm_unet_info": (c_int, [c_void_p, ctypes.POINTER(ctypes.c_int64),
+                              ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(c_int)]),
 }
 
 EPI_BIAS = 1

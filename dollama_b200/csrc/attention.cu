@@ -344,6 +344,12 @@ int attn_plan(AttnOp* op, int B, int H, int Sq, int Sk, int Dh, float scale, con
   return DLM_OK;
 }
 
+int attn_prepare_kernels() {
+  DLM_CHECK_CUDA(cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      kAttnSmem));
+  return DLM_OK;
+}
+
 int attn_launch(const AttnOp& op, cudaStream_t s) {
   static bool attr_set[64] = {false};
   int dev = 0;

@@ -31,5 +31,6 @@ struct AttnOp {
 int attn_plan(AttnOp* op, int B, int H, int Sq, int Sk, int Dh, float scale, const AttnTensor& q,
               const AttnTensor& k, const AttnTensor& v, const AttnTensor& o);
 int attn_launch(const AttnOp& op, cudaStream_t s);
+int attn_prepare_kernels();
 
 }  // namespace dlm

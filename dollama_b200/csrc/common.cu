@@ -108,6 +108,13 @@ const char* dlm_last_error(void) { return g_last_error; }
 
 const char* dlm_version(void) { return "dollama_b200 0.1 (sm_100a)"; }
 
+int dlm_memcpy(void* dst, const void* src, size_t bytes, void* stream) {
+  if (bytes == 0) return DLM_OK;
+  DLM_REQUIRE(dst != nullptr && src != nullptr, DLM_ERR_INVALID, "dlm_memcpy: null pointer");
+  DLM_CHECK_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, static_cast<cudaStream_t>(stream)));
+  return DLM_OK;
+}
+
 int dlm_get_device_status(int* out_code, int clear, void* stream) {
   DLM_REQUIRE(out_code != nullptr, DLM_ERR_INVALID, "dlm_get_device_status: null out_code");
   int* p = dlm::device_status_ptr();

@@ -54,13 +54,14 @@ int pick_bn(int M, int N) {
 
 bool bn_supported(int bn) { return bn == 256 || bn == 192 || bn == 160 || bn == 128 || bn == 64; }
 
-void fill_epilogue(GemmParams& p, const GemmEpilogue& e) {
+void fill_epilogue(GemmParams& p, const GemmEpilogue& e, int N) {
   p.flags = e.flags;
   p.alpha = e.alpha;
   p.resid_scale = e.resid_scale;
   p.bias = e.bias;
   p.bias2d = e.bias2d;
   p.rows_per_img = e.rows_per_img > 0 ? e.rows_per_img : 1;
+  p.ldb2 = e.ldb2 > 0 ? e.ldb2 : N;
   p.resid = e.resid;
   p.ldr = e.ldr;
 }
@@ -120,7 +121,7 @@ int gemm_plan_dense(GemmOp* op, const __half* A, int lda, const __half* W, int M
   p.amode = 0;
   p.out = C;
   p.ldo = ldc;
-  fill_epilogue(p, epi);
+  fill_epilogue(p, epi, p.N);
   p.status = device_status_ptr();
   op->bn = bn;
   const int tiles = p.m_tiles * p.n_tiles;
@@ -191,11 +192,25 @@ int gemm_plan_conv(GemmOp* op, int Nb, int oH, int oW, const ConvSource* srcs, i
   p.nseg = nsrc;
   p.out = C;
   p.ldo = ldc;
-  fill_epilogue(p, epi);
+  fill_epilogue(p, epi, p.N);
   p.status = device_status_ptr();
   op->bn = bn;
   const int tiles = p.m_tiles * p.n_tiles;
   op->grid = tiles < num_sms() ? tiles : num_sms();
+  return DLM_OK;
+}
+
+int gemm_prepare_kernels() {
+  // Sets the dynamic shared-memory limit of every tile variant up front, so that no attribute
+  // call happens inside a CUDA-graph capture.
+  GemmOp dummy;
+  std::memset(&dummy, 0, sizeof(dummy));
+  (void)dummy;
+  DLM_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm_smem_bytes(256)));
+  DLM_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<192>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm_smem_bytes(192)));
+  DLM_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<160>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm_smem_bytes(160)));
+  DLM_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm_smem_bytes(128)));
+  DLM_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm_smem_bytes(64)));
   return DLM_OK;
 }
 

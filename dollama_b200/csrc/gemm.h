@@ -25,6 +25,7 @@ struct GemmEpilogue {
   const __half* bias = nullptr;
   const __half* bias2d = nullptr;
   int rows_per_img = 1;
+  int ldb2 = 0;  // row stride of bias2d (0 = N)
   const __half* resid = nullptr;
   int ldr = 0;
 };
@@ -47,5 +48,8 @@ int gemm_plan_conv(GemmOp* op, int Nb, int oH, int oW, const ConvSource* srcs, i
                    int force_bn = 0);
 
 int gemm_launch(const GemmOp& op, cudaStream_t stream);
+
+// Sets kernel attributes of every variant on the current device (call before graph capture).
+int gemm_prepare_kernels();
 
 }  // namespace dlm

@@ -48,6 +48,7 @@ struct GemmParams {
   const __half* bias;
   const __half* bias2d;
   int rows_per_img;
+  int ldb2;  // row stride of bias2d
   const __half* resid;
   int ldr;
   int* status;
@@ -291,7 +292,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
         if (p.flags & DLM_EPI_BIAS2D) {
-          const __half* b2 = p.bias2d + static_cast<size_t>(row / p.rows_per_img) * p.N + n;
+          const __half* b2 = p.bias2d + static_cast<size_t>(row / p.rows_per_img) * p.ldb2 + n;
 #pragma unroll
           for (int j = 0; j < 32; j += 8) {
             float b[8];

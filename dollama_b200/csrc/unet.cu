@@ -1,0 +1,1132 @@
+// SDXL UNet2DConditionModel forward on the B200 kernels (host orchestration, C++).
+//
+// Replaces the reference's UNet graph (src/infer/unet.cu: launch_unet_impl :902, resnet_block :537,
+// transformer_block :677, transformer2d :810, downsample/upsample :861-881) and its weight handle
+// (unet_weights_create :1336, launch_unet_batched :1475), behind dlm_unet_* in the C ABI.
+//
+// Design (B200-first, not a translation):
+//   * activations are NHWC / token-major end to end, so Transformer2D needs no CHW<->SC
+//     transposes and attention reads heads by stride (no split/merge copies);
+//   * every conv is an implicit GEMM (no im2col); conv2 of a resnet and its 1x1 conv_shortcut
+//     are ONE GEMM (the shortcut is two more K segments over the raw input), with the bias,
+//     conv_shortcut bias and the identity residual in the epilogue;
+//   * conv1's bias and the resnet's time_emb_proj are folded into one per-image channel bias,
+//     computed for all 23 resnets by a single GEMM per step;
+//   * the up-path skip concat exists only inside GroupNorm's output (two-source GN apply) and
+//     as separate K segments of the shortcut;
+//   * q/k/v is one GEMM, cross-attention k/v one GEMM, GEGLU is the proj GEMM's epilogue
+//     (weights interleaved at load), bias + residual adds are GEMM epilogues;
+//   * all tensor maps / launch parameters are built once per (B, H, W) plan over a static
+//     activation arena; the step replays as one CUDA graph (no allocation, no host sync).
+#include <cmath>
+#include <cstring>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "attention.h"
+#include "gemm.h"
+#include "norm.h"
+#include "ops.h"
+#include "unet.h"
+
+namespace dlm {
+
+namespace {
+
+// ---------------------------------------------------------------- small kernels
+
+// sin_out[b, 0:320] = [cos(t f_i) | sin(t f_i)], f_i = 10000^(-i/160)  (flip_sin_to_cos, shift 0)
+// add_in[b] = [text_embeds[b] (1280) | 6 x sinusoidal(time_ids[k], 256)]
+__global__ void time_inputs_kernel(const float* __restrict__ t, const __half* __restrict__ tid,
+                                   const __half* __restrict__ te, int te_dim, int tproj,
+                                   int add_dim, __half* __restrict__ sin_out,
+                                   __half* __restrict__ add_in) {
+  const int b = blockIdx.x;
+  const float ts = *t;
+  const float lnp = logf(10000.0f);
+  const int half = tproj / 2;
+  for (int i = threadIdx.x; i < half; i += blockDim.x) {
+    const float f = expf(-lnp * static_cast<float>(i) / static_cast<float>(half));
+    const float a = ts * f;
+    sin_out[b * tproj + i] = __float2half_rn(cosf(a));
+    sin_out[b * tproj + half + i] = __float2half_rn(sinf(a));
+  }
+  const int row = te_dim + 6 * add_dim;
+  for (int i = threadIdx.x; i < te_dim; i += blockDim.x) add_in[b * row + i] = te[b * te_dim + i];
+  const int ah = add_dim / 2;
+  for (int i = threadIdx.x; i < 6 * ah; i += blockDim.x) {
+    const int k = i / ah, j = i - k * ah;
+    const float f = expf(-lnp * static_cast<float>(j) / static_cast<float>(ah));
+    const float a = __half2float(tid[k]) * f;
+    add_in[b * row + te_dim + k * add_dim + j] = __float2half_rn(cosf(a));
+    add_in[b * row + te_dim + k * add_dim + ah + j] = __float2half_rn(sinf(a));
+  }
+}
+
+__global__ void silu_kernel(const __half* __restrict__ x, __half* __restrict__ y, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = __float2half_rn(silu_f(__half2float(x[i])));
+}
+
+__global__ void set_scalar_kernel(float* p, float v) { *p = v; }
+
+// NCHW [B, Cin, H, W] -> NHWC [B, H, W, Cpad] with zero channels beyond Cin.
+__global__ void nchw_to_nhwc_pad_kernel(const __half* __restrict__ in, __half* __restrict__ out,
+                                        int B, int Cin, int HW, int Cpad) {
+  const size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x;
+  const size_t total = static_cast<size_t>(B) * HW;
+  if (i >= total) return;
+  const int b = static_cast<int>(i / HW), p = static_cast<int>(i % HW);
+  __half* o = out + i * Cpad;
+  for (int c = 0; c < Cpad; ++c)
+    o[c] = c < Cin ? in[(static_cast<size_t>(b) * Cin + c) * HW + p] : __float2half_rn(0.0f);
+}
+
+// NHWC [B, HW, ld] (first Cout channels) -> NCHW [B, Cout, HW]
+__global__ void nhwc_to_nchw_narrow_kernel(const __half* __restrict__ in, int ld,
+                                           __half* __restrict__ out, int B, int Cout, int HW) {
+  const size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x;
+  const size_t total = static_cast<size_t>(B) * HW;
+  if (i >= total) return;
+  const int b = static_cast<int>(i / HW), p = static_cast<int>(i % HW);
+  for (int c = 0; c < Cout; ++c) out[(static_cast<size_t>(b) * Cout + c) * HW + p] = in[i * ld + c];
+}
+
+// p[o, kh, kw, i] (row stride ldp) = w[o, i, kh, kw] for o < Cout, i < Cin; zero for the padding
+// rows o in [Cout, Cout_pad) and channels i in [Cin, Cin_pad).
+__global__ void pack_conv_pad_kernel(const __half* __restrict__ w, __half* __restrict__ p, int Cout,
+                                     int Cout_pad, int Cin, int Cin_pad, int KK, int ldp) {
+  const size_t total = static_cast<size_t>(Cout_pad) * KK * Cin_pad;
+  for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int i = static_cast<int>(idx % Cin_pad);
+    const int tap = static_cast<int>((idx / Cin_pad) % KK);
+    const int o = static_cast<int>(idx / (static_cast<size_t>(Cin_pad) * KK));
+    __half v = __float2half_rn(0.0f);
+    if (o < Cout && i < Cin) v = w[(static_cast<size_t>(o) * Cin + i) * KK + tap];
+    p[static_cast<size_t>(o) * ldp + static_cast<size_t>(tap) * Cin_pad + i] = v;
+  }
+}
+
+__global__ void add_half_kernel(const __half* __restrict__ a, const __half* __restrict__ b,
+                                __half* __restrict__ y, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = __float2half_rn(__half2float(a[i]) + __half2float(b[i]));
+}
+
+int blocks_for(size_t n, int t) { return static_cast<int>((n + t - 1) / t); }
+
+constexpr int kCtxTokens = 77;
+constexpr int kCtxDim = 2048;
+constexpr int kTembDim = 1280;
+constexpr int kTimeProj = 320;
+constexpr int kAddTime = 256;
+constexpr int kTextDim = 1280;
+constexpr int kAddIn = kTextDim + 6 * kAddTime;  // 2816
+constexpr int kC[3] = {320, 640, 1280};
+
+}  // namespace
+
+// ================================================================== weights
+
+struct WeightSpec {
+  std::string name;
+  std::vector<int64_t> shape;
+};
+
+static std::vector<WeightSpec> unet_weight_specs(const UNetCfg& cfg) {
+  std::vector<WeightSpec> S;
+  auto lin = [&](const std::string& n, int o, int i, bool bias = true) {
+    S.push_back({n + ".weight", {o, i}});
+    if (bias) S.push_back({n + ".bias", {o}});
+  };
+  auto cv = [&](const std::string& n, int o, int i, int k = 3) {
+    S.push_back({n + ".weight", {o, i, k, k}});
+    S.push_back({n + ".bias", {o}});
+  };
+  auto norm = [&](const std::string& n, int c) {
+    S.push_back({n + ".weight", {c}});
+    S.push_back({n + ".bias", {c}});
+  };
+  auto resnet = [&](const std::string& p, int cin, int cout) {
+    norm(p + "norm1", cin);
+    cv(p + "conv1", cout, cin);
+    lin(p + "time_emb_proj", cout, kTembDim);
+    norm(p + "norm2", cout);
+    cv(p + "conv2", cout, cout);
+    if (cin != cout) cv(p + "conv_shortcut", cout, cin, 1);
+  };
+  auto t2d = [&](const std::string& p, int c, int layers) {
+    norm(p + "norm", c);
+    lin(p + "proj_in", c, c);
+    for (int l = 0; l < layers; ++l) {
+      const std::string b = p + "transformer_blocks." + std::to_string(l) + ".";
+      norm(b + "norm1", c);
+      norm(b + "norm2", c);
+      norm(b + "norm3", c);
+      lin(b + "attn1.to_q", c, c, false);
+      lin(b + "attn1.to_k", c, c, false);
+      lin(b + "attn1.to_v", c, c, false);
+      lin(b + "attn1.to_out.0", c, c);
+      lin(b + "attn2.to_q", c, c, false);
+      lin(b + "attn2.to_k", c, kCtxDim, false);
+      lin(b + "attn2.to_v", c, kCtxDim, false);
+      lin(b + "attn2.to_out.0", c, c);
+      lin(b + "ff.net.0.proj", 8 * c, c);
+      lin(b + "ff.net.2", c, 4 * c);
+    }
+    lin(p + "proj_out", c, c);
+  };
+  lin("time_embedding.linear_1", kTembDim, kTimeProj);
+  lin("time_embedding.linear_2", kTembDim, kTembDim);
+  lin("add_embedding.linear_1", kTembDim, kAddIn);
+  lin("add_embedding.linear_2", kTembDim, kTembDim);
+  cv("conv_in", kC[0], 4);
+  int cin = kC[0];
+  for (int lvl = 0; lvl < 3; ++lvl) {
+    const int c = kC[lvl];
+    for (int r = 0; r < 2; ++r) {
+      resnet("down_blocks." + std::to_string(lvl) + ".resnets." + std::to_string(r) + ".",
+             r == 0 ? cin : c, c);
+      if (cfg.depth[lvl] > 0)
+        t2d("down_blocks." + std::to_string(lvl) + ".attentions." + std::to_string(r) + ".", c,
+            cfg.depth[lvl]);
+    }
+    if (lvl < 2) cv("down_blocks." + std::to_string(lvl) + ".downsamplers.0.conv", c, c);
+    cin = c;
+  }
+  resnet("mid_block.resnets.0.", kC[2], kC[2]);
+  t2d("mid_block.attentions.0.", kC[2], cfg.mid_depth);
+  resnet("mid_block.resnets.1.", kC[2], kC[2]);
+  std::vector<int> skip_ch = {kC[0], kC[0], kC[0], kC[0], kC[1], kC[1], kC[1], kC[2], kC[2]};
+  int cur = kC[2];
+  for (int u = 0; u < 3; ++u) {
+    const int lvl = 2 - u, c = kC[lvl];
+    for (int r = 0; r < 3; ++r) {
+      const int sk = skip_ch.back();
+      skip_ch.pop_back();
+      resnet("up_blocks." + std::to_string(u) + ".resnets." + std::to_string(r) + ".", cur + sk, c);
+      cur = c;
+      if (cfg.depth[lvl] > 0)
+        t2d("up_blocks." + std::to_string(u) + ".attentions." + std::to_string(r) + ".", c,
+            cfg.depth[lvl]);
+    }
+    if (u < 2) cv("up_blocks." + std::to_string(u) + ".upsamplers.0.conv", c, c);
+  }
+  norm("conv_norm_out", kC[0]);
+  cv("conv_out", 4, kC[0]);
+  return S;
+}
+
+static int64_t numel(const std::vector<int64_t>& s) {
+  int64_t n = 1;
+  for (auto d : s) n *= d;
+  return n;
+}
+
+UNetModel::~UNetModel() {
+  release_plan();
+  if (wbuf_) cudaFree(wbuf_);
+}
+
+void UNetModel::release_plan() {
+  if (gexec_) cudaGraphExecDestroy(gexec_);
+  gexec_ = nullptr;
+  if (cap_stream_) cudaStreamDestroy(cap_stream_);
+  cap_stream_ = nullptr;
+  if (abuf_) cudaFree(abuf_);
+  abuf_ = nullptr;
+  B_ = H_ = W_ = 0;
+  seq_.clear();
+  gemm_ops_.clear();
+  attn_ops_.clear();
+  gn_ops_.clear();
+  ln_ops_.clear();
+  custom_.clear();
+  stages_.clear();
+}
+
+__half* UNetModel::wtake(size_t elems) {
+  const size_t bytes = ((elems * 2 + 255) / 256) * 256;
+  if (woff_ + bytes > wcap_) return nullptr;
+  __half* p = reinterpret_cast<__half*>(static_cast<char*>(wbuf_) + woff_);
+  woff_ += bytes;
+  return p;
+}
+
+const __half* UNetModel::src(const std::string& n) const {
+  auto it = src_.find(n);
+  return it == src_.end() ? nullptr : it->second;
+}
+
+int UNetModel::create(const UNetCfg& cfg, int n, const char* const* names, const void* const* ptrs,
+                      const int64_t* numels, cudaStream_t s) {
+  cfg_ = cfg;
+  const auto specs = unet_weight_specs(cfg);
+  std::unordered_map<std::string, std::pair<const __half*, int64_t>> given;
+  for (int i = 0; i < n; ++i) {
+    DLM_REQUIRE(names[i] != nullptr && ptrs[i] != nullptr, DLM_ERR_INVALID,
+                "unet_create: null name or pointer at %d", i);
+    given[names[i]] = {static_cast<const __half*>(ptrs[i]), numels ? numels[i] : -1};
+  }
+  size_t total = 0;
+  for (const auto& sp : specs) {
+    auto it = given.find(sp.name);
+    DLM_REQUIRE(it != given.end(), DLM_ERR_NOT_FOUND, "unet_create: missing weight %s",
+                sp.name.c_str());
+    DLM_REQUIRE(it->second.second < 0 || it->second.second == numel(sp.shape), DLM_ERR_INVALID,
+                "unet_create: %s has %lld elements, expected %lld", sp.name.c_str(),
+                static_cast<long long>(it->second.second), static_cast<long long>(numel(sp.shape)));
+    src_[sp.name] = it->second.first;
+    total += static_cast<size_t>(numel(sp.shape)) * 2 + 512;
+  }
+  // prepared layouts are at most the raw size plus padded conv_in / conv_out and the temb concat
+  total += (1u << 24) + 64 * 1024 * sizeof(__half) * 64;
+  wcap_ = total;
+  DLM_CHECK_CUDA(cudaMalloc(&wbuf_, wcap_));
+  woff_ = 0;
+  int rc = prepare_weights(s);
+  if (rc != DLM_OK) return rc;
+  DLM_CHECK_CUDA(cudaStreamSynchronize(s));
+  src_.clear();  // the caller's buffers are no longer referenced
+  return DLM_OK;
+}
+
+// Copies / repacks every weight into the layouts the kernels read.
+int UNetModel::prepare_weights(cudaStream_t s) {
+  auto copy = [&](const std::string& name, size_t elems) -> __half* {
+    __half* d = wtake(elems);
+    if (!d) return nullptr;
+    if (cudaMemcpyAsync(d, src(name), elems * 2, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+      return nullptr;
+    w_[name] = d;
+    return d;
+  };
+  auto pack = [&](const std::string& name, __half* dst, int cout, int cout_pad, int cin, int cin_pad,
+                  int kk, int ldp) -> bool {
+    const size_t total = static_cast<size_t>(cout_pad) * kk * cin_pad;
+    pack_conv_pad_kernel<<<std::min<size_t>((total + 255) / 256, 4096), 256, 0, s>>>(
+        src(name), dst, cout, cout_pad, cin, cin_pad, kk, ldp);
+    return cudaGetLastError() == cudaSuccess;
+  };
+  auto fail = [&](const char* what) {
+    set_error("unet prepare: %s", what);
+    return DLM_ERR_NOMEM;
+  };
+
+  // time / add embedding MLPs
+  for (const char* nm : {"time_embedding.linear_1", "time_embedding.linear_2",
+                         "add_embedding.linear_1", "add_embedding.linear_2"}) {
+    const std::string b(nm);
+    const int in = b == "time_embedding.linear_1" ? kTimeProj
+                   : b == "add_embedding.linear_1" ? kAddIn
+                                                   : kTembDim;
+    if (!copy(b + ".weight", static_cast<size_t>(kTembDim) * in)) return fail(nm);
+    if (!copy(b + ".bias", kTembDim)) return fail(nm);
+  }
+  // conv_in: Cin 4 -> padded 64
+  {
+    __half* d = wtake(static_cast<size_t>(kC[0]) * 9 * 64);
+    if (!d || !pack("conv_in.weight", d, kC[0], kC[0], 4, 64, 9, 9 * 64)) return fail("conv_in");
+    w_["conv_in.packed"] = d;
+    if (!copy("conv_in.bias", kC[0])) return fail("conv_in.bias");
+  }
+  // conv_out: Cout 4 -> padded 32 rows
+  {
+    __half* d = wtake(static_cast<size_t>(32) * 9 * kC[0]);
+    if (!d || !pack("conv_out.weight", d, 4, 32, kC[0], kC[0], 9, 9 * kC[0])) return fail("conv_out");
+    w_["conv_out.packed"] = d;
+    __half* b = wtake(32);
+    if (!b) return fail("conv_out.bias");
+    DLM_CHECK_CUDA(cudaMemsetAsync(b, 0, 32 * 2, s));
+    DLM_CHECK_CUDA(cudaMemcpyAsync(b, src("conv_out.bias"), 4 * 2, cudaMemcpyDeviceToDevice, s));
+    w_["conv_out.bias_pad"] = b;
+    if (!copy("conv_norm_out.weight", kC[0]) || !copy("conv_norm_out.bias", kC[0]))
+      return fail("conv_norm_out");
+  }
+  // resnets: collect in forward order to build the temb-projection concat
+  resnets_.clear();
+  {
+    int cin = kC[0];
+    for (int lvl = 0; lvl < 3; ++lvl) {
+      for (int r = 0; r < 2; ++r)
+        resnets_.push_back({"down_blocks." + std::to_string(lvl) + ".resnets." + std::to_string(r) + ".",
+                            r == 0 ? cin : kC[lvl], kC[lvl], 0});
+      cin = kC[lvl];
+    }
+    resnets_.push_back({"mid_block.resnets.0.", kC[2], kC[2], 0});
+    resnets_.push_back({"mid_block.resnets.1.", kC[2], kC[2], 0});
+    std::vector<int> skip_ch = {kC[0], kC[0], kC[0], kC[0], kC[1], kC[1], kC[1], kC[2], kC[2]};
+    int cur = kC[2];
+    for (int u = 0; u < 3; ++u) {
+      const int c = kC[2 - u];
+      for (int r = 0; r < 3; ++r) {
+        const int sk = skip_ch.back();
+        skip_ch.pop_back();
+        resnets_.push_back({"up_blocks." + std::to_string(u) + ".resnets." + std::to_string(r) + ".",
+                            cur + sk, c, 0});
+        cur = c;
+      }
+    }
+  }
+  temb_total_ = 0;
+  for (auto& rs : resnets_) {
+    rs.temb_off = temb_total_;
+    temb_total_ += rs.cout;
+  }
+  __half* tw = wtake(static_cast<size_t>(temb_total_) * kTembDim);
+  __half* tb = wtake(static_cast<size_t>(temb_total_));
+  if (!tw || !tb) return fail("temb concat");
+  w_["temb_proj.weight"] = tw;
+  w_["temb_proj.bias"] = tb;
+  for (auto& rs : resnets_) {
+    const std::string& p = rs.prefix;
+    const int ci = rs.cin, co = rs.cout;
+    DLM_CHECK_CUDA(cudaMemcpyAsync(tw + static_cast<size_t>(rs.temb_off) * kTembDim,
+                                   src(p + "time_emb_proj.weight"),
+                                   static_cast<size_t>(co) * kTembDim * 2, cudaMemcpyDeviceToDevice, s));
+    // time_emb_proj.bias + conv1.bias: both are added to every pixel of conv1's output
+    add_half_kernel<<<blocks_for(co, 256), 256, 0, s>>>(src(p + "time_emb_proj.bias"),
+                                                       src(p + "conv1.bias"), tb + rs.temb_off, co);
+    DLM_CHECK_CUDA(cudaGetLastError());
+    for (const char* nn : {"norm1.weight", "norm1.bias"})
+      if (!copy(p + nn, ci)) return fail("resnet norm1");
+    for (const char* nn : {"norm2.weight", "norm2.bias"})
+      if (!copy(p + nn, co)) return fail("resnet norm2");
+    __half* w1 = wtake(static_cast<size_t>(co) * 9 * ci);
+    if (!w1 || !pack(p + "conv1.weight", w1, co, co, ci, ci, 9, 9 * ci)) return fail("conv1");
+    w_[p + "conv1.packed"] = w1;
+    const bool sc = ci != co;
+    const int k2 = 9 * co + (sc ? ci : 0);
+    __half* w2 = wtake(static_cast<size_t>(co) * k2);
+    if (!w2 || !pack(p + "conv2.weight", w2, co, co, co, co, 9, k2)) return fail("conv2");
+    w_[p + "conv2.packed"] = w2;
+    __half* b2 = wtake(co);
+    if (!b2) return fail("conv2 bias");
+    if (sc) {
+      DLM_CHECK_CUDA(cudaMemcpy2DAsync(w2 + 9 * co, static_cast<size_t>(k2) * 2,
+                                       src(p + "conv_shortcut.weight"), static_cast<size_t>(ci) * 2,
+                                       static_cast<size_t>(ci) * 2, co, cudaMemcpyDeviceToDevice, s));
+      add_half_kernel<<<blocks_for(co, 256), 256, 0, s>>>(src(p + "conv2.bias"),
+                                                         src(p + "conv_shortcut.bias"), b2, co);
+      DLM_CHECK_CUDA(cudaGetLastError());
+    } else {
+      DLM_CHECK_CUDA(cudaMemcpyAsync(b2, src(p + "conv2.bias"), co * 2, cudaMemcpyDeviceToDevice, s));
+    }
+    w_[p + "conv2.bias_f"] = b2;
+  }
+  // down / up samplers
+  for (int lvl = 0; lvl < 2; ++lvl) {
+    const std::string p = "down_blocks." + std::to_string(lvl) + ".downsamplers.0.conv";
+    const int c = kC[lvl];
+    __half* d = wtake(static_cast<size_t>(c) * 9 * c);
+    if (!d || !pack(p + ".weight", d, c, c, c, c, 9, 9 * c)) return fail("downsampler");
+    w_[p + ".packed"] = d;
+    if (!copy(p + ".bias", c)) return fail("downsampler bias");
+  }
+  for (int u = 0; u < 2; ++u) {
+    const std::string p = "up_blocks." + std::to_string(u) + ".upsamplers.0.conv";
+    const int c = kC[2 - u];
+    __half* d = wtake(static_cast<size_t>(c) * 9 * c);
+    if (!d || !pack(p + ".weight", d, c, c, c, c, 9, 9 * c)) return fail("upsampler");
+    w_[p + ".packed"] = d;
+    if (!copy(p + ".bias", c)) return fail("upsampler bias");
+  }
+  // transformers
+  auto prep_t2d = [&](const std::string& p, int c, int layers) -> int {
+    for (const char* nn : {"norm.weight", "norm.bias", "proj_in.bias", "proj_out.bias"})
+      if (!copy(p + nn, c)) return fail("t2d vec");
+    if (!copy(p + "proj_in.weight", static_cast<size_t>(c) * c)) return fail("proj_in");
+    if (!copy(p + "proj_out.weight", static_cast<size_t>(c) * c)) return fail("proj_out");
+    for (int l = 0; l < layers; ++l) {
+      const std::string b = p + "transformer_blocks." + std::to_string(l) + ".";
+      for (const char* nn : {"norm1.weight", "norm1.bias", "norm2.weight", "norm2.bias",
+                             "norm3.weight", "norm3.bias", "attn1.to_out.0.bias",
+                             "attn2.to_out.0.bias", "ff.net.2.bias"})
+        if (!copy(b + nn, c)) return fail("block vec");
+      const size_t cc = static_cast<size_t>(c) * c;
+      __half* qkv = wtake(3 * cc);
+      if (!qkv) return fail("qkv");
+      DLM_CHECK_CUDA(cudaMemcpyAsync(qkv, src(b + "attn1.to_q.weight"), cc * 2, cudaMemcpyDeviceToDevice, s));
+      DLM_CHECK_CUDA(cudaMemcpyAsync(qkv + cc, src(b + "attn1.to_k.weight"), cc * 2, cudaMemcpyDeviceToDevice, s));
+      DLM_CHECK_CUDA(cudaMemcpyAsync(qkv + 2 * cc, src(b + "attn1.to_v.weight"), cc * 2, cudaMemcpyDeviceToDevice, s));
+      w_[b + "attn1.qkv"] = qkv;
+      if (!copy(b + "attn1.to_out.0.weight", cc) || !copy(b + "attn2.to_q.weight", cc) ||
+          !copy(b + "attn2.to_out.0.weight", cc))
+        return fail("attn weights");
+      const size_t kv1 = static_cast<size_t>(c) * kCtxDim;
+      __half* kv = wtake(2 * kv1);
+      if (!kv) return fail("kv");
+      DLM_CHECK_CUDA(cudaMemcpyAsync(kv, src(b + "attn2.to_k.weight"), kv1 * 2, cudaMemcpyDeviceToDevice, s));
+      DLM_CHECK_CUDA(cudaMemcpyAsync(kv + kv1, src(b + "attn2.to_v.weight"), kv1 * 2, cudaMemcpyDeviceToDevice, s));
+      w_[b + "attn2.kv"] = kv;
+      // GEGLU proj: interleave rows (hidden_j, gate_j) so one output tile holds both halves
+      const int ff = 4 * c;
+      __half* gw = wtake(static_cast<size_t>(2 * ff) * c);
+      __half* gb = wtake(2 * ff);
+      if (!gw || !gb) return fail("geglu");
+      const __half* sw = src(b + "ff.net.0.proj.weight");
+      const __half* sb = src(b + "ff.net.0.proj.bias");
+      DLM_CHECK_CUDA(cudaMemcpy2DAsync(gw, 4 * static_cast<size_t>(c), sw, 2 * static_cast<size_t>(c),
+                                       2 * static_cast<size_t>(c), ff, cudaMemcpyDeviceToDevice, s));
+      DLM_CHECK_CUDA(cudaMemcpy2DAsync(gw + c, 4 * static_cast<size_t>(c), sw + static_cast<size_t>(ff) * c,
+                                       2 * static_cast<size_t>(c), 2 * static_cast<size_t>(c), ff,
+                                       cudaMemcpyDeviceToDevice, s));
+      DLM_CHECK_CUDA(cudaMemcpy2DAsync(gb, 4, sb, 2, 2, ff, cudaMemcpyDeviceToDevice, s));
+      DLM_CHECK_CUDA(cudaMemcpy2DAsync(gb + 1, 4, sb + ff, 2, 2, ff, cudaMemcpyDeviceToDevice, s));
+      w_[b + "ff.geglu.weight"] = gw;
+      w_[b + "ff.geglu.bias"] = gb;
+      if (!copy(b + "ff.net.2.weight", static_cast<size_t>(c) * ff)) return fail("ff2");
+    }
+    return DLM_OK;
+  };
+  for (int lvl = 1; lvl < 3; ++lvl)
+    for (int r = 0; r < 2; ++r)
+      if (cfg_.depth[lvl] > 0) {
+        int rc = prep_t2d("down_blocks." + std::to_string(lvl) + ".attentions." + std::to_string(r) + ".",
+                          kC[lvl], cfg_.depth[lvl]);
+        if (rc != DLM_OK) return rc;
+      }
+  {
+    int rc = prep_t2d("mid_block.attentions.0.", kC[2], cfg_.mid_depth);
+    if (rc != DLM_OK) return rc;
+  }
+  for (int u = 0; u < 2; ++u)
+    for (int r = 0; r < 3; ++r)
+      if (cfg_.depth[2 - u] > 0) {
+        int rc = prep_t2d("up_blocks." + std::to_string(u) + ".attentions." + std::to_string(r) + ".",
+                          kC[2 - u], cfg_.depth[2 - u]);
+        if (rc != DLM_OK) return rc;
+      }
+  DLM_CHECK_CUDA(cudaGetLastError());
+  return DLM_OK;
+}
+
+const __half* UNetModel::W(const std::string& n) const {
+  auto it = w_.find(n);
+  return it == w_.end() ? nullptr : it->second;
+}
+
+// ================================================================== plan
+
+__half* UNetModel::act(size_t elems) {
+  const size_t bytes = ((elems * 2 + 255) / 256) * 256;
+  const size_t off = aoff_;
+  aoff_ += bytes;
+  if (dry_) return reinterpret_cast<__half*>(static_cast<uintptr_t>(0x100000000ull + off));
+  return reinterpret_cast<__half*>(static_cast<char*>(abuf_) + off);
+}
+
+void UNetModel::push_gemm(const GemmOp& g) {
+  gemm_ops_.push_back(g);
+  seq_.push_back({OpKind::Gemm, static_cast<int>(gemm_ops_.size() - 1)});
+}
+void UNetModel::push_attn(const AttnOp& a) {
+  attn_ops_.push_back(a);
+  seq_.push_back({OpKind::Attn, static_cast<int>(attn_ops_.size() - 1)});
+}
+void UNetModel::push_gn(const GnOp& g) {
+  gn_ops_.push_back(g);
+  seq_.push_back({OpKind::Gn, static_cast<int>(gn_ops_.size() - 1)});
+}
+void UNetModel::push_ln(const LnArgs& l) {
+  ln_ops_.push_back(l);
+  seq_.push_back({OpKind::Ln, static_cast<int>(ln_ops_.size() - 1)});
+}
+void UNetModel::push_custom(std::function<int(cudaStream_t)> f) {
+  custom_.push_back(std::move(f));
+  seq_.push_back({OpKind::Custom, static_cast<int>(custom_.size() - 1)});
+}
+
+#define PLAN_CHECK(expr)            \
+  do {                              \
+    if (!dry_) {                    \
+      int _rc = (expr);             \
+      if (_rc != DLM_OK) return _rc; \
+    }                               \
+  } while (0)
+
+// GroupNorm(+SiLU) of concat(x1, x2) [B*HW, C1+C2] into a fresh scratch buffer.
+int UNetModel::plan_gn(const __half* x1, int C1, const __half* x2, int C2, int HW,
+                       const std::string& wprefix, float eps, bool silu, __half* out) {
+  if (dry_) return DLM_OK;
+  GnOp g;
+  int rc = gn_plan(&g, x1, C1, x2, C2, B_, HW, W(wprefix + ".weight"), W(wprefix + ".bias"), eps,
+                   silu, out, gn_partials_, gn_partial_cap_);
+  if (rc != DLM_OK) return rc;
+  push_gn(g);
+  return DLM_OK;
+}
+
+int UNetModel::plan_resnet(const ResnetInfo& rs, const __half* x1, int C1, const __half* x2, int C2,
+                           int H, int Wd, __half* out) {
+  const int HW = H * Wd, M = B_ * HW;
+  const int co = rs.cout;
+  const std::string& p = rs.prefix;
+  __half* h1 = scratch_a_;  // GN1 output (up to 2560 channels)
+  __half* h2 = scratch_b_;  // conv1 output
+  __half* h3 = scratch_c_;  // GN2 output
+  int rc = plan_gn(x1, C1, x2, C2, HW, p + "norm1", 1e-5f, true, h1);
+  if (rc != DLM_OK) return rc;
+  if (!dry_) {
+    GemmOp g;
+    ConvSource s0;
+    s0.kind = 0;
+    s0.ptr = h1;
+    s0.C = C1 + C2;
+    GemmEpilogue e;
+    e.flags = DLM_EPI_BIAS2D;
+    e.bias2d = tproj_ + rs.temb_off;
+    e.ldb2 = temb_total_;
+    e.rows_per_img = HW;
+    rc = gemm_plan_conv(&g, B_, H, Wd, &s0, 1, W(p + "conv1.packed"), co, h2, co, e);
+    if (rc != DLM_OK) return rc;
+    push_gemm(g);
+  }
+  rc = plan_gn(h2, co, nullptr, 0, HW, p + "norm2", 1e-5f, true, h3);
+  if (rc != DLM_OK) return rc;
+  if (!dry_) {
+    GemmOp g;
+    ConvSource srcs[3];
+    int ns = 0;
+    srcs[ns++] = ConvSource{0, h3, co};
+    GemmEpilogue e;
+    e.flags = DLM_EPI_BIAS;
+    e.bias = W(p + "conv2.bias_f");
+    if (C1 + C2 != co) {
+      srcs[ns++] = ConvSource{1, x1, C1};
+      if (C2 > 0) srcs[ns++] = ConvSource{1, x2, C2};
+    } else {
+      e.flags |= DLM_EPI_RESID;
+      e.resid = x1;
+      e.ldr = co;
+    }
+    rc = gemm_plan_conv(&g, B_, H, Wd, srcs, ns, W(p + "conv2.packed"), co, out, co, e);
+    if (rc != DLM_OK) return rc;
+    push_gemm(g);
+  }
+  (void)M;
+  return DLM_OK;
+}
+
+int UNetModel::plan_linear(const __half* A, int lda, const __half* Wt, int M, int N, int K, __half* C,
+                           int ldc, const GemmEpilogue& e) {
+  if (dry_) return DLM_OK;
+  GemmOp g;
+  int rc = gemm_plan_dense(&g, A, lda, Wt, M, N, K, C, ldc, e);
+  if (rc != DLM_OK) return rc;
+  push_gemm(g);
+  return DLM_OK;
+}
+
+int UNetModel::plan_attn(const __half* q, int ldq, const __half* k, int ldk, const __half* v, int ldv,
+                         __half* o, int ldo, int heads, int Sq, int Sk) {
+  if (dry_) return DLM_OK;
+  auto tok = [&](const __half* ptr, int ld, int S) {
+    AttnTensor t;
+    t.ptr = ptr;
+    t.ss = ld;
+    t.sh = 64;
+    t.sb = static_cast<long long>(S) * ld;
+    return t;
+  };
+  AttnOp a;
+  int rc = attn_plan(&a, B_, heads, Sq, Sk, 64, 0.125f, tok(q, ldq, Sq), tok(k, ldk, Sk),
+                     tok(v, ldv, Sk), tok(o, ldo, Sq));
+  if (rc != DLM_OK) return rc;
+  push_attn(a);
+  return DLM_OK;
+}
+
+// Transformer2D, in place on x [B*HW, C] (token-major == NHWC).
+int UNetModel::plan_t2d(const std::string& p, __half* x, int C, int H, int Wd, int layers) {
+  const int S = H * Wd, M = B_ * S, heads = C / 64;
+  __half* g = t_gn_;     // [M, C]
+  __half* h = t_h_;      // [M, C] running hidden state
+  __half* n = t_n_;      // [M, C] LN output
+  __half* qkv = t_qkv_;  // [M, 3C]
+  __half* ao = t_ao_;    // [M, C] attention output
+  __half* kv = t_kv_;    // [B*77, 2C]
+  __half* ff = t_ff_;    // [M, 4C]
+  int rc = plan_gn(x, C, nullptr, 0, S, p + "norm", 1e-6f, false, g);
+  if (rc != DLM_OK) return rc;
+  GemmEpilogue eb;
+  eb.flags = DLM_EPI_BIAS;
+  if (!dry_) eb.bias = W(p + "proj_in.bias");
+  rc = plan_linear(g, C, W(p + "proj_in.weight"), M, C, C, h, C, eb);
+  if (rc != DLM_OK) return rc;
+  for (int l = 0; l < layers; ++l) {
+    const std::string b = p + "transformer_blocks." + std::to_string(l) + ".";
+    // self attention
+    if (!dry_) push_ln({h, W(b + "norm1.weight"), W(b + "norm1.bias"), n, M, C, 1e-5f});
+    rc = plan_linear(n, C, W(b + "attn1.qkv"), M, 3 * C, C, qkv, 3 * C, GemmEpilogue{});
+    if (rc != DLM_OK) return rc;
+    rc = plan_attn(qkv, 3 * C, qkv + C, 3 * C, qkv + 2 * C, 3 * C, ao, C, heads, S, S);
+    if (rc != DLM_OK) return rc;
+    GemmEpilogue er;
+    er.flags = DLM_EPI_BIAS | DLM_EPI_RESID;
+    er.resid = h;
+    er.ldr = C;
+    if (!dry_) er.bias = W(b + "attn1.to_out.0.bias");
+    rc = plan_linear(ao, C, W(b + "attn1.to_out.0.weight"), M, C, C, h, C, er);
+    if (rc != DLM_OK) return rc;
+    // cross attention
+    if (!dry_) push_ln({h, W(b + "norm2.weight"), W(b + "norm2.bias"), n, M, C, 1e-5f});
+    rc = plan_linear(n, C, W(b + "attn2.to_q.weight"), M, C, C, qkv, C, GemmEpilogue{});
+    if (rc != DLM_OK) return rc;
+    rc = plan_linear(ehs_, kCtxDim, W(b + "attn2.kv"), B_ * kCtxTokens, 2 * C, kCtxDim, kv, 2 * C,
+                     GemmEpilogue{});
+    if (rc != DLM_OK) return rc;
+    rc = plan_attn(qkv, C, kv, 2 * C, kv + C, 2 * C, ao, C, heads, S, kCtxTokens);
+    if (rc != DLM_OK) return rc;
+    if (!dry_) er.bias = W(b + "attn2.to_out.0.bias");
+    rc = plan_linear(ao, C, W(b + "attn2.to_out.0.weight"), M, C, C, h, C, er);
+    if (rc != DLM_OK) return rc;
+    // GEGLU feed-forward
+    if (!dry_) push_ln({h, W(b + "norm3.weight"), W(b + "norm3.bias"), n, M, C, 1e-5f});
+    GemmEpilogue eg;
+    eg.flags = DLM_EPI_BIAS | DLM_EPI_GEGLU;
+    if (!dry_) eg.bias = W(b + "ff.geglu.bias");
+    rc = plan_linear(n, C, W(b + "ff.geglu.weight"), M, 8 * C, C, ff, 4 * C, eg);
+    if (rc != DLM_OK) return rc;
+    if (!dry_) er.bias = W(b + "ff.net.2.bias");
+    rc = plan_linear(ff, 4 * C, W(b + "ff.net.2.weight"), M, C, 4 * C, h, C, er);
+    if (rc != DLM_OK) return rc;
+  }
+  GemmEpilogue eo;
+  eo.flags = DLM_EPI_BIAS | DLM_EPI_RESID;
+  eo.resid = x;
+  eo.ldr = C;
+  if (!dry_) eo.bias = W(p + "proj_out.bias");
+  return plan_linear(h, C, W(p + "proj_out.weight"), M, C, C, x, C, eo);
+}
+
+int UNetModel::build(bool dry) {
+  dry_ = dry;
+  aoff_ = 0;
+  seq_.clear();
+  gemm_ops_.clear();
+  attn_ops_.clear();
+  gn_ops_.clear();
+  ln_ops_.clear();
+  custom_.clear();
+  stages_.clear();
+  const int B = B_, H0 = H_, W0 = W_;
+  const int C0 = kC[0], C1 = kC[1], C2 = kC[2];
+  const int H1 = H0 / 2, W1 = W0 / 2, H2 = H0 / 4, W2 = W0 / 4;
+  const size_t P0 = static_cast<size_t>(B) * H0 * W0, P1 = static_cast<size_t>(B) * H1 * W1,
+               P2 = static_cast<size_t>(B) * H2 * W2;
+  // ---- io and embedding buffers
+  d_t_ = reinterpret_cast<float*>(act(2));
+  tid_ = act(8);
+  te_ = act(static_cast<size_t>(B) * kTextDim);
+  ehs_ = act(static_cast<size_t>(B) * kCtxTokens * kCtxDim);
+  lat_in_ = act(static_cast<size_t>(B) * 4 * H0 * W0);
+  noise_out_ = act(static_cast<size_t>(B) * 4 * H0 * W0);
+  lat64_ = act(P0 * 64);
+  __half* sin = act(static_cast<size_t>(B) * kTimeProj);
+  __half* addin = act(static_cast<size_t>(B) * kAddIn);
+  __half* t1 = act(static_cast<size_t>(B) * kTembDim);
+  __half* temb = act(static_cast<size_t>(B) * kTembDim);
+  __half* a1 = act(static_cast<size_t>(B) * kTembDim);
+  __half* temb_silu = act(static_cast<size_t>(B) * kTembDim);
+  tproj_ = act(static_cast<size_t>(B) * temb_total_);
+  // ---- scratch shared by consecutive ops
+  const size_t maxPC = std::max({P0 * (C1 + C0), P1 * (C2 + C1), P2 * (2 * C2)});
+  scratch_a_ = act(maxPC);
+  scratch_b_ = act(std::max({P0 * C0, P1 * C1, P2 * C2}));
+  scratch_c_ = act(std::max({P0 * C0, P1 * C1, P2 * C2}));
+  const size_t tM = std::max(cfg_.depth[1] > 0 ? P1 : 0, P2);
+  const int tC = C2;
+  const size_t tMC = std::max(cfg_.depth[1] > 0 ? P1 * C1 : 0, P2 * C2);
+  (void)tM;
+  (void)tC;
+  t_gn_ = act(tMC);
+  t_h_ = act(tMC);
+  t_n_ = act(tMC);
+  t_qkv_ = act(3 * tMC);
+  t_ao_ = act(tMC);
+  t_kv_ = act(static_cast<size_t>(B) * kCtxTokens * 2 * C2);
+  t_ff_ = act(4 * tMC);
+  planes_ = act(std::max(P0 * C0, P1 * C1));
+  upbuf_ = act(std::max(P1 * C2, P0 * C1));
+  out32_ = act(P0 * 32);
+  gn_partial_cap_ = gn_partial_elems(B, H0 * W0);
+  gn_partials_ = reinterpret_cast<float2*>(act(gn_partial_cap_ * 4));
+
+  // ---- embeddings
+  if (!dry_) {
+    float* tp = d_t_;
+    const __half *tidp = tid_, *tep = te_;
+    push_custom([=](cudaStream_t s) {
+      time_inputs_kernel<<<B, 256, 0, s>>>(tp, tidp, tep, kTextDim, kTimeProj, kAddTime, sin, addin);
+      return cudaGetLastError() == cudaSuccess ? DLM_OK : DLM_ERR_CUDA;
+    });
+  }
+  {
+    GemmEpilogue e1;
+    e1.flags = DLM_EPI_BIAS | DLM_EPI_SILU;
+    GemmEpilogue e2;
+    e2.flags = DLM_EPI_BIAS;
+    if (!dry_) {
+      e1.bias = W("time_embedding.linear_1.bias");
+      e2.bias = W("time_embedding.linear_2.bias");
+    }
+    int rc = plan_linear(sin, kTimeProj, W("time_embedding.linear_1.weight"), B, kTembDim, kTimeProj,
+                         t1, kTembDim, e1);
+    if (rc != DLM_OK) return rc;
+    rc = plan_linear(t1, kTembDim, W("time_embedding.linear_2.weight"), B, kTembDim, kTembDim, temb,
+                     kTembDim, e2);
+    if (rc != DLM_OK) return rc;
+    if (!dry_) e1.bias = W("add_embedding.linear_1.bias");
+    rc = plan_linear(addin, kAddIn, W("add_embedding.linear_1.weight"), B, kTembDim, kAddIn, a1,
+                     kTembDim, e1);
+    if (rc != DLM_OK) return rc;
+    GemmEpilogue e3;
+    e3.flags = DLM_EPI_BIAS | DLM_EPI_RESID;
+    e3.resid = temb;
+    e3.ldr = kTembDim;
+    if (!dry_) e3.bias = W("add_embedding.linear_2.bias");
+    rc = plan_linear(a1, kTembDim, W("add_embedding.linear_2.weight"), B, kTembDim, kTembDim, temb,
+                     kTembDim, e3);
+    if (rc != DLM_OK) return rc;
+    stages_["temb_final"] = {temb, kTembDim, 1, 1};
+    if (!dry_) {
+      push_custom([=](cudaStream_t s) {
+        silu_kernel<<<blocks_for(static_cast<size_t>(B) * kTembDim, 256), 256, 0, s>>>(
+            temb, temb_silu, B * kTembDim);
+        return cudaGetLastError() == cudaSuccess ? DLM_OK : DLM_ERR_CUDA;
+      });
+    }
+    GemmEpilogue et;
+    et.flags = DLM_EPI_BIAS;
+    if (!dry_) et.bias = W("temb_proj.bias");
+    rc = plan_linear(temb_silu, kTembDim, W("temb_proj.weight"), B, temb_total_, kTembDim, tproj_,
+                     temb_total_, et);
+    if (rc != DLM_OK) return rc;
+  }
+  // ---- conv_in (latent NCHW -> NHWC padded to 64 channels)
+  __half* x0 = act(P0 * C0);
+  if (!dry_) {
+    const __half* li = lat_in_;
+    __half* l64 = lat64_;
+    push_custom([=](cudaStream_t s) {
+      nchw_to_nhwc_pad_kernel<<<blocks_for(P0, 256), 256, 0, s>>>(li, l64, B, 4, H0 * W0, 64);
+      return cudaGetLastError() == cudaSuccess ? DLM_OK : DLM_ERR_CUDA;
+    });
+    GemmOp g;
+    ConvSource s0{0, lat64_, 64};
+    GemmEpilogue e;
+    e.flags = DLM_EPI_BIAS;
+    e.bias = W("conv_in.bias");
+    int rc = gemm_plan_conv(&g, B, H0, W0, &s0, 1, W("conv_in.packed"), C0, x0, C0, e);
+    if (rc != DLM_OK) return rc;
+    push_gemm(g);
+  }
+  stages_["conv_in_out"] = {x0, C0, H0, W0};
+  struct Skip {
+    __half* p;
+    int C;
+  };
+  std::vector<Skip> skips;
+  skips.push_back({x0, C0});
+  int ri = 0;  // resnet index (forward order)
+  // ---- down blocks
+  __half* cur = x0;
+  int curC = C0;
+  const int Hs[3] = {H0, H1, H2}, Ws[3] = {W0, W1, W2};
+  const size_t Ps[3] = {P0, P1, P2};
+  for (int lvl = 0; lvl < 3; ++lvl) {
+    const int c = kC[lvl], H = Hs[lvl], Wd = Ws[lvl];
+    for (int r = 0; r < 2; ++r) {
+      __half* o = act(Ps[lvl] * c);
+      int rc = plan_resnet(resnets_[ri++], cur, curC, nullptr, 0, H, Wd, o);
+      if (rc != DLM_OK) return rc;
+      if (cfg_.depth[lvl] > 0) {
+        rc = plan_t2d("down_blocks." + std::to_string(lvl) + ".attentions." + std::to_string(r) + ".",
+                      o, c, H, Wd, cfg_.depth[lvl]);
+        if (rc != DLM_OK) return rc;
+      }
+      skips.push_back({o, c});
+      cur = o;
+      curC = c;
+    }
+    if (lvl < 2) {
+      __half* o = act(Ps[lvl + 1] * c);
+      if (!dry_) {
+        const __half* in = cur;
+        __half* pl = planes_;
+        const int Nb = B, Hh = H, Ww = Wd, Cc = c;
+        push_custom([=](cudaStream_t s) { return parity_planes(in, pl, Nb, Hh, Ww, Cc, s); });
+        GemmOp g;
+        ConvSource s0{2, planes_, c};
+        GemmEpilogue e;
+        e.flags = DLM_EPI_BIAS;
+        const std::string p = "down_blocks." + std::to_string(lvl) + ".downsamplers.0.conv";
+        e.bias = W(p + ".bias");
+        int rc = gemm_plan_conv(&g, B, Hs[lvl + 1], Ws[lvl + 1], &s0, 1, W(p + ".packed"), c, o, c, e);
+        if (rc != DLM_OK) return rc;
+        push_gemm(g);
+      }
+      skips.push_back({o, c});
+      cur = o;
+    }
+    stages_["down_block_" + std::to_string(lvl) + "_out"] = {cur, curC, lvl < 2 ? Hs[lvl + 1] : H2,
+                                                            lvl < 2 ? Ws[lvl + 1] : W2};
+  }
+  // ---- mid
+  {
+    __half* o = act(P2 * C2);
+    int rc = plan_resnet(resnets_[ri++], cur, C2, nullptr, 0, H2, W2, o);
+    if (rc != DLM_OK) return rc;
+    rc = plan_t2d("mid_block.attentions.0.", o, C2, H2, W2, cfg_.mid_depth);
+    if (rc != DLM_OK) return rc;
+    __half* o2 = act(P2 * C2);
+    rc = plan_resnet(resnets_[ri++], o, C2, nullptr, 0, H2, W2, o2);
+    if (rc != DLM_OK) return rc;
+    cur = o2;
+    curC = C2;
+    stages_["mid_block_out"] = {cur, C2, H2, W2};
+  }
+  // ---- up blocks
+  for (int u = 0; u < 3; ++u) {
+    const int lvl = 2 - u, c = kC[lvl], H = Hs[lvl], Wd = Ws[lvl];
+    for (int r = 0; r < 3; ++r) {
+      const Skip sk = skips.back();
+      skips.pop_back();
+      __half* o = act(Ps[lvl] * c);
+      int rc = plan_resnet(resnets_[ri++], cur, curC, sk.p, sk.C, H, Wd, o);
+      if (rc != DLM_OK) return rc;
+      if (cfg_.depth[lvl] > 0) {
+        rc = plan_t2d("up_blocks." + std::to_string(u) + ".attentions." + std::to_string(r) + ".", o,
+                      c, H, Wd, cfg_.depth[lvl]);
+        if (rc != DLM_OK) return rc;
+      }
+      cur = o;
+      curC = c;
+    }
+    if (u < 2) {
+      const int Hn = Hs[lvl - 1], Wn = Ws[lvl - 1];
+      __half* o = act(Ps[lvl - 1] * c);
+      if (!dry_) {
+        const __half* in = cur;
+        __half* ub = upbuf_;
+        const int Nb = B, Hh = H, Ww = Wd, Cc = c;
+        push_custom([=](cudaStream_t s) { return upsample2x_nhwc(in, ub, Nb, Hh, Ww, Cc, s); });
+        GemmOp g;
+        ConvSource s0{0, upbuf_, c};
+        GemmEpilogue e;
+        e.flags = DLM_EPI_BIAS;
+        const std::string p = "up_blocks." + std::to_string(u) + ".upsamplers.0.conv";
+        e.bias = W(p + ".bias");
+        int rc = gemm_plan_conv(&g, B, Hn, Wn, &s0, 1, W(p + ".packed"), c, o, c, e);
+        if (rc != DLM_OK) return rc;
+        push_gemm(g);
+      }
+      cur = o;
+      stages_["up_block_" + std::to_string(u) + "_out"] = {cur, c, Hn, Wn};
+    } else {
+      stages_["up_block_" + std::to_string(u) + "_out"] = {cur, c, H, Wd};
+    }
+  }
+  // ---- conv_norm_out -> SiLU -> conv_out (Cout padded to 32) -> NCHW
+  {
+    int rc = plan_gn(cur, C0, nullptr, 0, H0 * W0, "conv_norm_out", 1e-5f, true, scratch_c_);
+    if (rc != DLM_OK) return rc;
+    if (!dry_) {
+      GemmOp g;
+      ConvSource s0{0, scratch_c_, C0};
+      GemmEpilogue e;
+      e.flags = DLM_EPI_BIAS;
+      e.bias = W("conv_out.bias_pad");
+      rc = gemm_plan_conv(&g, B, H0, W0, &s0, 1, W("conv_out.packed"), 32, out32_, 32, e);
+      if (rc != DLM_OK) return rc;
+      push_gemm(g);
+      const __half* o32 = out32_;
+      __half* no = noise_out_;
+      push_custom([=](cudaStream_t s) {
+        nhwc_to_nchw_narrow_kernel<<<blocks_for(P0, 256), 256, 0, s>>>(o32, 32, no, B, 4, H0 * W0);
+        return cudaGetLastError() == cudaSuccess ? DLM_OK : DLM_ERR_CUDA;
+      });
+    }
+  }
+  return DLM_OK;
+}
+
+int UNetModel::plan(int B, int H, int Wd) {
+  if (B == B_ && H == H_ && Wd == W_ && abuf_ != nullptr) return DLM_OK;
+  release_plan();
+  DLM_REQUIRE(B > 0 && H > 0 && Wd > 0, DLM_ERR_INVALID, "unet: empty shape");
+  DLM_REQUIRE(H % 4 == 0 && Wd % 4 == 0, DLM_ERR_INVALID, "unet: latent %dx%d must be divisible by 4",
+              H, Wd);
+  const int w2 = Wd / 4, h2 = H / 4;
+  DLM_REQUIRE((w2 >= 128 || 128 % w2 == 0) && (h2 * w2) % 128 == 0 && (w2 >= 128 ? w2 % 128 == 0 : h2 % (128 / w2) == 0),
+              DLM_ERR_INVALID, "unet: latent %dx%d: the 1/4-resolution level must tile by 128 pixels", H, Wd);
+  B_ = B;
+  H_ = H;
+  W_ = Wd;
+  int rc = gemm_prepare_kernels();
+  if (rc == DLM_OK) rc = attn_prepare_kernels();
+  if (rc != DLM_OK) return rc;
+  rc = build(true);
+  if (rc != DLM_OK) {
+    release_plan();
+    return rc;
+  }
+  const size_t bytes = aoff_ + 4096;
+  if (cudaMalloc(&abuf_, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    release_plan();
+    set_error("unet: cannot allocate %zu bytes of activations", bytes);
+    return DLM_ERR_NOMEM;
+  }
+  arena_bytes_ = bytes;
+  B_ = B;
+  H_ = H;
+  W_ = Wd;
+  rc = build(false);
+  if (rc != DLM_OK) {
+    release_plan();
+    return rc;
+  }
+  return DLM_OK;
+}
+
+int UNetModel::run_ops(cudaStream_t s) {
+  for (const OpRef& o : seq_) {
+    int rc = DLM_OK;
+    switch (o.kind) {
+      case OpKind::Gemm: rc = gemm_launch(gemm_ops_[o.idx], s); break;
+      case OpKind::Attn: rc = attn_launch(attn_ops_[o.idx], s); break;
+      case OpKind::Gn: rc = gn_launch(gn_ops_[o.idx], s); break;
+      case OpKind::Ln: {
+        const LnArgs& l = ln_ops_[o.idx];
+        rc = layer_norm(l.x, l.g, l.b, l.out, l.rows, l.C, l.eps, s);
+        break;
+      }
+      case OpKind::Custom: rc = custom_[o.idx](s); break;
+    }
+    if (rc != DLM_OK) return rc;
+  }
+  return DLM_OK;
+}
+
+int UNetModel::forward(int B, int H, int Wd, const __half* latent, float timestep, const __half* ehs,
+                       const __half* te, const __half* tid, __half* noise_out, cudaStream_t s) {
+  DLM_REQUIRE(latent && ehs && te && tid && noise_out, DLM_ERR_INVALID, "unet_forward: null input");
+  int rc = plan(B, H, Wd);
+  if (rc != DLM_OK) return rc;
+  const size_t lat = static_cast<size_t>(B) * 4 * H * Wd;
+  DLM_CHECK_CUDA(cudaMemcpyAsync(lat_in_, latent, lat * 2, cudaMemcpyDeviceToDevice, s));
+  DLM_CHECK_CUDA(cudaMemcpyAsync(ehs_, ehs, static_cast<size_t>(B) * kCtxTokens * kCtxDim * 2,
+                                 cudaMemcpyDeviceToDevice, s));
+  DLM_CHECK_CUDA(cudaMemcpyAsync(te_, te, static_cast<size_t>(B) * kTextDim * 2,
+                                 cudaMemcpyDeviceToDevice, s));
+  DLM_CHECK_CUDA(cudaMemcpyAsync(tid_, tid, 6 * 2, cudaMemcpyDeviceToDevice, s));
+  set_scalar_kernel<<<1, 1, 0, s>>>(d_t_, timestep);
+  DLM_CHECK_CUDA(cudaGetLastError());
+  if (use_graph_) {
+    if (!gexec_) {
+      if (!cap_stream_) DLM_CHECK_CUDA(cudaStreamCreateWithFlags(&cap_stream_, cudaStreamNonBlocking));
+      cudaGraph_t graph = nullptr;
+      DLM_CHECK_CUDA(cudaStreamBeginCapture(cap_stream_, cudaStreamCaptureModeThreadLocal));
+      rc = run_ops(cap_stream_);
+      cudaError_t ce = cudaStreamEndCapture(cap_stream_, &graph);
+      if (rc != DLM_OK) {
+        if (graph) cudaGraphDestroy(graph);
+        return rc;
+      }
+      DLM_CHECK_CUDA(ce);
+      ce = cudaGraphInstantiate(&gexec_, graph, 0);
+      cudaGraphDestroy(graph);
+      DLM_CHECK_CUDA(ce);
+    }
+    DLM_CHECK_CUDA(cudaGraphLaunch(gexec_, s));
+  } else {
+    rc = run_ops(s);
+    if (rc != DLM_OK) return rc;
+  }
+  DLM_CHECK_CUDA(cudaMemcpyAsync(noise_out, noise_out_, lat * 2, cudaMemcpyDeviceToDevice, s));
+  return DLM_OK;
+}
+
+int UNetModel::stage(const std::string& name, const __half** ptr, int* C, int* H, int* Wd) const {
+  auto it = stages_.find(name);
+  DLM_REQUIRE(it != stages_.end(), DLM_ERR_NOT_FOUND, "unet: no stage %s", name.c_str());
+  *ptr = it->second.ptr;
+  *C = it->second.C;
+  *H = it->second.H;
+  *Wd = it->second.W;
+  return DLM_OK;
+}
+
+}  // namespace dlm
+
+// ================================================================== C ABI
+
+extern "C" {
+
+int dlm_unet_create(const int* depths, int mid_depth, int n, const char* const* names,
+                    const void* const* dev_ptrs, const int64_t* numels, void** handle, void* stream) {
+  DLM_REQUIRE(handle != nullptr && names != nullptr && dev_ptrs != nullptr && n > 0, DLM_ERR_INVALID,
+              "unet_create: null argument");
+  *handle = nullptr;
+  dlm::UNetCfg cfg;
+  if (depths) {
+    for (int i = 0; i < 3; ++i) cfg.depth[i] = depths[i];
+    cfg.mid_depth = mid_depth;
+  }
+  DLM_REQUIRE(cfg.depth[0] == 0 && cfg.depth[1] >= 0 && cfg.depth[2] >= 1 && cfg.mid_depth >= 1,
+              DLM_ERR_INVALID, "unet_create: depths must be (0, >=0, >=1), mid >= 1");
+  auto* m = new (std::nothrow) dlm::UNetModel();
+  DLM_REQUIRE(m != nullptr, DLM_ERR_NOMEM, "unet_create: out of host memory");
+  int rc = m->create(cfg, n, names, dev_ptrs, numels, static_cast<cudaStream_t>(stream));
+  if (rc != DLM_OK) {
+    delete m;
+    return rc;
+  }
+  *handle = m;
+  return DLM_OK;
+}
+
+int dlm_unet_destroy(void* handle) {
+  delete static_cast<dlm::UNetModel*>(handle);
+  return DLM_OK;
+}
+
+int dlm_unet_forward(void* handle, int B, int H, int W, const void* latent, float timestep,
+                     const void* ehs, const void* text_embeds, const void* time_ids, void* noise_out,
+                     void* stream) {
+  DLM_REQUIRE(handle != nullptr, DLM_ERR_INVALID, "unet_forward: null handle");
+  if (B == 0 || H == 0 || W == 0) return DLM_OK;
+  return static_cast<dlm::UNetModel*>(handle)->forward(
+      B, H, W, static_cast<const __half*>(latent), timestep, static_cast<const __half*>(ehs),
+      static_cast<const __half*>(text_embeds), static_cast<const __half*>(time_ids),
+      static_cast<__half*>(noise_out), static_cast<cudaStream_t>(stream));
+}
+
+int dlm_unet_set_graph(void* handle, int enable) {
+  DLM_REQUIRE(handle != nullptr, DLM_ERR_INVALID, "unet_set_graph: null handle");
+  static_cast<dlm::UNetModel*>(handle)->set_graph(enable != 0);
+  return DLM_OK;
+}
+
+int dlm_unet_stage(void* handle, const char* name, const void** ptr, int* C, int* H, int* W) {
+  DLM_REQUIRE(handle && name && ptr && C && H && W, DLM_ERR_INVALID, "unet_stage: null argument");
+  const __half* p = nullptr;
+  int rc = static_cast<dlm::UNetModel*>(handle)->stage(name, &p, C, H, W);
+  *ptr = p;
+  return rc;
+}
+
+int dlm_unet_info(void* handle, int64_t* arena_bytes, int64_t* weight_bytes, int* num_launches) {
+  DLM_REQUIRE(handle != nullptr, DLM_ERR_INVALID, "unet_info: null handle");
+  auto* m = static_cast<dlm::UNetModel*>(handle);
+  if (arena_bytes) *arena_bytes = static_cast<int64_t>(m->arena_bytes());
+  if (weight_bytes) *weight_bytes = static_cast<int64_t>(m->weight_bytes());
+  if (num_launches) *num_launches = m->num_launches();
+  return DLM_OK;
+}
+
+}  // extern "C"

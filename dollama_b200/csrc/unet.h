@@ -1,0 +1,131 @@
+// SDXL UNet model object: prepared weights, static activation arena, op plan, CUDA graph.
+#pragma once
+
+#include <functional>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include <cuda_fp16.h>
+
+#include "attention.h"
+#include "common.h"
+#include "gemm.h"
+#include "norm.h"
+
+namespace dlm {
+
+struct UNetCfg {
+  int depth[3] = {0, 2, 10};  // transformer layers per Transformer2D at 1x, 1/2x, 1/4x
+  int mid_depth = 10;
+};
+
+struct ResnetInfo {
+  std::string prefix;
+  int cin, cout;
+  int temb_off;  // column offset of this resnet in the concatenated time-embedding projection
+};
+
+struct LnArgs {
+  const __half* x;
+  const __half* g;
+  const __half* b;
+  __half* out;
+  int rows, C;
+  float eps;
+};
+
+class UNetModel {
+ public:
+  ~UNetModel();
+  int create(const UNetCfg& cfg, int n, const char* const* names, const void* const* ptrs,
+             const int64_t* numels, cudaStream_t s);
+  int forward(int B, int H, int W, const __half* latent, float timestep, const __half* ehs,
+              const __half* te, const __half* tid, __half* noise_out, cudaStream_t s);
+  void set_graph(bool on) {
+    if (on != use_graph_ && gexec_) {
+      cudaGraphExecDestroy(gexec_);
+      gexec_ = nullptr;
+    }
+    use_graph_ = on;
+  }
+  int stage(const std::string& name, const __half** ptr, int* C, int* H, int* W) const;
+  size_t arena_bytes() const { return arena_bytes_; }
+  size_t weight_bytes() const { return woff_; }
+  int num_launches() const {
+    int n = 0;
+    for (const auto& o : seq_) n += o.kind == OpKind::Gn ? 2 : 1;
+    return n;
+  }
+
+ private:
+  enum class OpKind { Gemm, Attn, Gn, Ln, Custom };
+  struct OpRef {
+    OpKind kind;
+    int idx;
+  };
+  struct StageInfo {
+    const __half* ptr;
+    int C, H, W;
+  };
+
+  int prepare_weights(cudaStream_t s);
+  const __half* src(const std::string& n) const;
+  const __half* W(const std::string& n) const;
+  __half* wtake(size_t elems);
+  __half* act(size_t elems);
+  int plan(int B, int H, int W);
+  int build(bool dry);
+  void release_plan();
+  int run_ops(cudaStream_t s);
+  int plan_gn(const __half* x1, int C1, const __half* x2, int C2, int HW, const std::string& wprefix,
+              float eps, bool silu, __half* out);
+  int plan_resnet(const ResnetInfo& rs, const __half* x1, int C1, const __half* x2, int C2, int H,
+                  int W, __half* out);
+  int plan_t2d(const std::string& p, __half* x, int C, int H, int W, int layers);
+  int plan_linear(const __half* A, int lda, const __half* Wt, int M, int N, int K, __half* C, int ldc,
+                  const GemmEpilogue& e);
+  int plan_attn(const __half* q, int ldq, const __half* k, int ldk, const __half* v, int ldv,
+                __half* o, int ldo, int heads, int Sq, int Sk);
+  void push_gemm(const GemmOp& g);
+  void push_attn(const AttnOp& a);
+  void push_gn(const GnOp& g);
+  void push_ln(const LnArgs& l);
+  void push_custom(std::function<int(cudaStream_t)> f);
+
+  UNetCfg cfg_;
+  // weights
+  std::unordered_map<std::string, const __half*> src_;  // caller's tensors (create only)
+  std::unordered_map<std::string, __half*> w_;          // prepared tensors
+  void* wbuf_ = nullptr;
+  size_t wcap_ = 0, woff_ = 0;
+  std::vector<ResnetInfo> resnets_;
+  int temb_total_ = 0;
+  // plan
+  int B_ = 0, H_ = 0, W_ = 0;
+  bool dry_ = false;
+  void* abuf_ = nullptr;
+  size_t aoff_ = 0, arena_bytes_ = 0;
+  std::vector<OpRef> seq_;
+  std::vector<GemmOp> gemm_ops_;
+  std::vector<AttnOp> attn_ops_;
+  std::vector<GnOp> gn_ops_;
+  std::vector<LnArgs> ln_ops_;
+  std::vector<std::function<int(cudaStream_t)>> custom_;
+  std::unordered_map<std::string, StageInfo> stages_;
+  bool use_graph_ = true;
+  cudaGraphExec_t gexec_ = nullptr;
+  cudaStream_t cap_stream_ = nullptr;
+  // buffers inside the arena
+  float* d_t_ = nullptr;
+  __half *tid_ = nullptr, *te_ = nullptr, *ehs_ = nullptr, *lat_in_ = nullptr, *noise_out_ = nullptr;
+  __half *lat64_ = nullptr, *tproj_ = nullptr;
+  __half *scratch_a_ = nullptr, *scratch_b_ = nullptr, *scratch_c_ = nullptr;
+  __half *t_gn_ = nullptr, *t_h_ = nullptr, *t_n_ = nullptr, *t_qkv_ = nullptr, *t_ao_ = nullptr,
+         *t_kv_ = nullptr, *t_ff_ = nullptr;
+  __half *planes_ = nullptr, *upbuf_ = nullptr, *out32_ = nullptr;
+  float2* gn_partials_ = nullptr;
+  size_t gn_partial_cap_ = 0;
+};
+
+}  // namespace dlm

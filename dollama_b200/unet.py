@@ -1,0 +1,97 @@
+"""Python host mirror of the reference's UNet handle API over the C ABI.
+
+Mirrors `unet_weights_create` / `launch_unet_batched` / `unet_weights_destroy`
+(reference src/infer/unet.cuh:90-146): the weights become device-resident once, and each
+call runs one UNet step for a CFG batch.  All compute runs in `libdollama_b200.so`; this
+module only marshals torch CUDA tensors' pointers.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib as L
+
+
+def _stream_ptr(stream=None):
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+class SDXLUNet:
+    """SDXL UNet2DConditionModel on the B200 kernels.
+
+    `state_dict` maps diffusers key names to fp16 CUDA tensors (the reference's
+    `w.get(...)` names).  `depths` / `mid_depth` default to SDXL (0, 2, 10) / 10.
+    """
+
+    def __init__(self, state_dict: dict, depths=(0, 2, 10), mid_depth: int = 10, stream=None):
+        names = list(state_dict.keys())
+        tens = [state_dict[n] for n in names]
+        for n, t in zip(names, tens):
+            if not (t.is_cuda and t.dtype == torch.float16 and t.is_contiguous()):
+                raise ValueError(f"{n}: expected a contiguous fp16 CUDA tensor")
+        n = len(names)
+        c_names = (ctypes.c_char_p * n)(*[x.encode() for x in names])
+        c_ptrs = (ctypes.c_void_p * n)(*[t.data_ptr() for t in tens])
+        c_numel = (ctypes.c_int64 * n)(*[t.numel() for t in tens])
+        c_depths = (ctypes.c_int * 3)(*depths)
+        h = ctypes.c_void_p()
+        L.call("dlm_unet_create", c_depths, int(mid_depth), n, c_names, c_ptrs, c_numel,
+               ctypes.byref(h), _stream_ptr(stream))
+        self._h = h
+        self.depths = tuple(depths)
+        self.mid_depth = mid_depth
+
+    def forward(self, latent, timestep: float, ehs, text_embeds, time_ids, out=None, stream=None):
+        """latent [B,4,H,W], ehs [B,77,2048], text_embeds [B,1280], time_ids [6] -> noise [B,4,H,W]."""
+        B, _, H, W = latent.shape
+        self._last_b = B
+        if out is None:
+            out = torch.empty_like(latent)
+        for t in (latent, ehs, text_embeds, time_ids, out):
+            if not (t.is_cuda and t.dtype == torch.float16 and t.is_contiguous()):
+                raise ValueError("inputs must be contiguous fp16 CUDA tensors")
+        L.call("dlm_unet_forward", self._h, B, H, W, ctypes.c_void_p(latent.data_ptr()),
+               float(timestep), ctypes.c_void_p(ehs.data_ptr()),
+               ctypes.c_void_p(text_embeds.data_ptr()), ctypes.c_void_p(time_ids.data_ptr()),
+               ctypes.c_void_p(out.data_ptr()), _stream_ptr(stream))
+        return out
+
+    __call__ = forward
+
+    def set_graph(self, enable: bool) -> None:
+        L.call("dlm_unet_set_graph", self._h, 1 if enable else 0)
+
+    def stage(self, name: str) -> torch.Tensor:
+        """Copy of a stage output of the last forward, NCHW fp16 (the reference's stage hook)."""
+        ptr = ctypes.c_void_p()
+        C, H, W = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+        L.call("dlm_unet_stage", self._h, name.encode(), ctypes.byref(ptr), ctypes.byref(C),
+               ctypes.byref(H), ctypes.byref(W))
+        B = getattr(self, "_last_b", None)
+        if B is None:
+            raise RuntimeError("stage(): no forward has run yet")
+        torch.cuda.synchronize()
+        total = B * H.value * W.value * C.value  # B images of [H, W, C]
+        out = torch.empty(total, dtype=torch.float16, device="cuda")
+        L.call("dlm_memcpy", ctypes.c_void_p(out.data_ptr()), ptr, total * 2, _stream_ptr())
+        torch.cuda.synchronize()
+        return out.view(B, H.value, W.value, C.value).permute(0, 3, 1, 2)
+
+    def info(self):
+        a, w, n = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int()
+        L.call("dlm_unet_info", self._h, ctypes.byref(a), ctypes.byref(w), ctypes.byref(n))
+        return {"arena_bytes": a.value, "weight_bytes": w.value, "launches_per_step": n.value}
+
+    def close(self):
+        if getattr(self, "_h", None):
+            L.lib().dlm_unet_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -50,6 +50,9 @@ const char* dlm_version(void);
  * Synchronizes `stream`. */
 int dlm_get_device_status(int* out_code, int clear, void* stream);
 
+/* Asynchronous copy between any two (device or host) buffers on `stream`. */
+int dlm_memcpy(void* dst, const void* src, size_t bytes, void* stream);
+
 /* ------------------------------------------------------------------ GEMM (tcgen05)
  *
  * Replaces launch_gemm_fp16 (reference src/kernels/gemm.cuh:44-53, gemm.cu:518):
@@ -133,6 +136,42 @@ int dlm_group_norm_nhwc(const void* x1, int C1, const void* x2, int C2, int N, i
  * gamma / beta may be NULL.  C % 8 == 0, C <= 2048. */
 int dlm_launch_layer_norm(const void* in, const void* gamma, const void* beta, void* out, int rows,
                           int C, float eps, void* stream);
+
+/* ------------------------------------------------------------------ SDXL UNet (model level)
+ *
+ * Replaces unet_weights_create / launch_unet_batched / unet_weights_destroy (reference
+ * src/infer/unet.cuh:90-146, unet.cu:1336,1475).  The handle owns a prepared copy of every
+ * weight (repacked for the kernels), so the caller's tensors may be freed after create.
+ *   names / dev_ptrs / numels: n fp16 device tensors keyed by the diffusers state-dict names
+ *     the reference reads (unet.cu `w.get("...")`); numels may be NULL (no size check);
+ *   depths: transformer layers per Transformer2D at the 1x / 1/2x / 1/4x levels ({0, 2, 10} for
+ *     SDXL; NULL = SDXL) and mid_depth (10 for SDXL) — reduced depths serve tests.
+ * Returns DLM_ERR_NOT_FOUND (naming the tensor in dlm_last_error) when a weight is missing.
+ */
+int dlm_unet_create(const int* depths, int mid_depth, int n, const char* const* names,
+                    const void* const* dev_ptrs, const int64_t* numels, void** handle, void* stream);
+int dlm_unet_destroy(void* handle);
+
+/* One UNet step for a batch of B latents (CFG cond/uncond stacked as B = 2, unet.cuh:137-146):
+ *   latent [B, 4, H, W], ehs [B, 77, 2048], text_embeds [B, 1280], time_ids [6] (shared),
+ *   noise_out [B, 4, H, W]; all fp16 device tensors, NCHW as the reference.
+ * H and W are the latent size (128 for 1024^2 images); H/4 and W/4 must tile by 128 pixels.
+ * The first call for a (B, H, W) plans the step (static activation arena, all launch
+ * parameters) and captures it as a CUDA graph; later calls replay it with no allocation. */
+int dlm_unet_forward(void* handle, int B, int H, int W, const void* latent, float timestep,
+                     const void* ehs, const void* text_embeds, const void* time_ids, void* noise_out,
+                     void* stream);
+
+/* Enables (default) or disables CUDA-graph replay of the step. */
+int dlm_unet_set_graph(void* handle, int enable);
+
+/* Test hook (the reference's unet_set_stage_hook, unet.cuh:53-54): device pointer and NHWC
+ * geometry of a stage output of the last forward ("temb_final", "conv_in_out",
+ * "down_block_{0,1,2}_out", "mid_block_out", "up_block_{0,1,2}_out"). */
+int dlm_unet_stage(void* handle, const char* name, const void** ptr, int* C, int* H, int* W);
+
+/* Activation arena bytes, prepared weight bytes, kernel launches per step. */
+int dlm_unet_info(void* handle, int64_t* arena_bytes, int64_t* weight_bytes, int* num_launches);
 
 #ifdef __cplusplus
 }  /* extern "C" */
