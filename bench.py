@@ -1,0 +1,358 @@
+#!/usr/bin/env python
+"""bench.py — the north-star workload: one SDXL UNet step at 1024x1024 (128x128 latent) with
+the CFG pair stacked as batch 2, random-init weights of the SDXL architecture, synthetic seeded
+inputs.  One process per GPU; every GPU runs its own replica on its own CFG pair (replica data
+parallelism, no collective on the path), so `value` (UNet steps/s) is the whole-job aggregate.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints ONE JSON line on rank 0.  Legs of our arm:
+  value        K steps replayed from the CUDA graph with inputs resident in HBM, CUDA events on
+               the launching stream, barrier + synchronize on both sides, max over ranks;
+  e2e          the same steps through dlm_unet_forward_host with pinned HOST buffers: every step
+               copies latent / text conditioning in and the noise prediction out;
+  roofline     the dominant kernel class (tcgen05 GEMM / implicit-GEMM conv) timed per launch
+               with CUDA events in one eager step right after the timed region;
+  cpu_baseline the CPU fp32 oracle of the same step (oracle/sdxl_unet.py) on this host's cores
+               (rank 0, N = 1 only).
+`--impl reference` times the reference's CPU path for this workload: the reference has no CPU
+UNet (its UNet is CUDA-only and its golden path needs diffusers + pretrained weights), so the
+arm is the fp32 restatement (`kind: port`) on all host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "UNet steps/s per GPU at 1024² CFG-b2; images/s at 1/2/4/8 B200; % fp16 TC peak"
+UNIT = "steps/s"
+LATENT = 128
+BATCH = 2
+STEPS_PER_IMAGE = 20
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--legs", choices=["all", "device"], default="all",
+                    help="'device' stops after the device-resident timed leg (for ncu launch lists)")
+    return ap.parse_args()
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d.get("bf16_tflops", 1590.0), d.get("bf16_tflops_sustained", 1400.0), \
+            d.get("hbm_gbs", 6650.0), "measured"
+    return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+def config(n):
+    return {
+        "workload": "SDXL UNet2DConditionModel step, 1024x1024 image (latent 128x128), CFG pair as batch 2",
+        "model": "sdxl-unet (2.57 G params, random-init)",
+        "global_batch": BATCH * n,
+        "latent": [LATENT, LATENT],
+        "parallelism": f"replica-dp{n}",
+        "steps_per_image": STEPS_PER_IMAGE,
+        "l2": "inputs larger than L2: every step streams 5.1 GB of weights and a 0.58 GB "
+              "activation arena through the 126 MB L2",
+    }
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_indices):
+        self.idx = set(gpu_indices)
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return None
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except Exception:
+            self.p.kill()
+        self.f.flush()
+        rows = []
+        for line in Path(self.f.name).read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                if int(parts[0]) not in self.idx:
+                    continue
+                rows.append(parts)
+            except ValueError:
+                continue
+        os.unlink(self.f.name)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[k] for r in rows for k in range(4) if "Active" in r[5 + k]
+                          and "Not" not in r[5 + k]})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def make_inputs(device, seed=6):
+    import torch
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    lat = torch.randn(1, 4, LATENT, LATENT, generator=g).expand(BATCH, -1, -1, -1).contiguous()
+    ehs = torch.randn(BATCH, 77, 2048, generator=g)
+    te = torch.randn(BATCH, 1280, generator=g)
+    tid = torch.tensor([1024.0, 1024.0, 0.0, 0.0, 1024.0, 1024.0])
+    host = [t.half().contiguous() for t in (lat, ehs, te, tid)]
+    if torch.cuda.is_available():
+        host = [t.pin_memory() for t in host]
+    dev = [t.to(device) for t in host]
+    return host, dev
+
+
+def cpu_oracle_step(sd_gpu, host_inputs, timestep=999.0):
+    """One UNet step of the CPU fp32 oracle on the same weights / inputs; returns (seconds, threads)."""
+    import torch
+    from oracle.sdxl_unet import UNetConfig, unet_forward
+    torch.set_num_threads(os.cpu_count() or 1)
+    sdf = {k: v.float().cpu() for k, v in sd_gpu.items()}
+    lat, ehs, te, tid = host_inputs
+    with torch.no_grad():
+        t0 = time.perf_counter()
+        unet_forward(sdf, lat.float(), timestep, ehs.float(), te.float(), tid.float(), UNetConfig())
+        dt = time.perf_counter() - t0
+    return dt, torch.get_num_threads()
+
+
+def run_reference(args, ws, rank):
+    if rank != 0:
+        return 0
+    import torch
+    from dollama_b200.unet import random_weights
+    from oracle.sdxl_unet import UNetConfig, unet_forward
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    sd = random_weights(seed=7, device=dev)
+    sdf = {k: v.float().cpu() for k, v in sd.items()}
+    del sd
+    host, _ = make_inputs("cpu")
+    lat, ehs, te, tid = (t.float() for t in host)
+    steps, warm = max(1, min(args.steps, 2)), max(0, min(args.warmup, 1))
+    with torch.no_grad():
+        for _ in range(warm):
+            unet_forward(sdf, lat, 999.0, ehs, te, tid, UNetConfig())
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            unet_forward(sdf, lat, 999.0, ehs, te, tid, UNetConfig())
+        dt = time.perf_counter() - t0
+    v = steps / dt
+    sample = (f"{steps} full UNet steps (B=2, 128x128 latent, all 70 transformer blocks) after "
+              f"{warm} warm-up, fp32 torch on {threads} host threads")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": ws,
+        "steps": steps, "warmup": warm, "ms_per_step": 1000.0 / v, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config(1),
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference's UNet exists only as CUDA + cuBLAS (src/infer/unet.cu); its CPU "
+                "golden path needs diffusers and pretrained weights, absent here; this arm is the "
+                "CPU fp32 restatement of the same step",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    args = parse()
+    ws, rank, local = dist_env()
+    if args.impl == "reference":
+        return run_reference(args, ws, rank)
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    if ws > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    from dollama_b200.unet import SDXLUNet, random_weights
+    from dollama_b200 import _lib as L
+
+    dev = torch.device("cuda", local)
+    sd = random_weights(seed=7, device=dev)
+    net = SDXLUNet(sd)
+    keep_sd = (rank == 0 and ws == 1 and not args.no_cpu_baseline)
+    if not keep_sd:
+        del sd
+        sd = None
+    host, (lat, ehs, te, tid) = make_inputs(dev)
+    out = torch.empty_like(lat)
+    stream = torch.cuda.current_stream(dev)
+    ts = [999.0 - 50.0 * i for i in range(STEPS_PER_IMAGE)]
+
+    def barrier():
+        if ws > 1:
+            dist.barrier()
+
+    # ---------------------------------------------------------------- device-resident leg
+    for i in range(max(3, args.warmup)):
+        net(lat, ts[i % len(ts)], ehs, te, tid, out)
+    torch.cuda.synchronize()
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    gpu_ids = [int(x) for x in vis.split(",")] if vis else list(range(max(ws, 1)))
+    sampler = ClockSampler(gpu_ids if rank == 0 else []) if rank == 0 else None
+    time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("dlm_timed")
+    e0.record(stream)
+    for i in range(args.steps):
+        net(lat, ts[i % len(ts)], ehs, te, tid, out)
+    e1.record(stream)
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop() if sampler else None
+    ms_local = e0.elapsed_time(e1)
+    t = torch.tensor([ms_local], device=dev, dtype=torch.float64)
+    if ws > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_total = float(t.item())
+    ms_step = ms_total / args.steps
+    value = ws * args.steps / (ms_total / 1000.0)
+    finite = bool(torch.isfinite(out).all().item())
+
+    if args.legs == "device":
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws,
+                              "steps": args.steps, "ms_per_step": ms_step, "legs": "device"}))
+        if ws > 1:
+            dist.destroy_process_group()
+        net.close()
+        return 0
+
+    # ---------------------------------------------------------------- end-to-end leg (host buffers)
+    hl, he, ht, hi = host
+    hout = torch.empty(tuple(lat.shape), dtype=torch.float16).pin_memory()
+    for i in range(max(3, args.warmup)):
+        net.forward_host(hl, ts[i % len(ts)], he, ht, hi, hout)
+    barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for i in range(args.steps):
+        net.forward_host(hl, ts[i % len(ts)], he, ht, hi, hout)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    t = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+    if ws > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_value = ws * args.steps / (float(t.item()) / 1000.0)
+    h2d = sum(x.numel() * x.element_size() for x in host)
+    d2h = hout.numel() * hout.element_size()
+
+    # ---------------------------------------------------------------- dominant-kernel roofline
+    ops = net.time_ops()
+    info = net.info()
+    burst, sustained, hbm, peak_src = peaks()
+    g = ops["gemm"]
+    gemm_tf = g["flops"] / (g["ms"] / 1000.0) / 1e12 if g["ms"] > 0 else 0.0
+    step_flops = sum(v["flops"] for v in ops.values())
+    prof = ROOT / "profiles" / "gemm_tc_kernel_unet_step.md"
+    traffic = None
+    if prof.exists():
+        for line in prof.read_text().splitlines():
+            if line.startswith("traffic_bytes_per_launch:"):
+                try:
+                    traffic = float(line.split(":", 1)[1].strip())
+                except ValueError:
+                    traffic = None
+    roofline = {
+        "kernel": "gemm_tc_kernel (tcgen05 GEMM + implicit-GEMM conv), all launches of one step",
+        "bound": "tensor", "achieved": gemm_tf, "peak": sustained, "unit": "TFLOP/s",
+        "frac": gemm_tf / sustained, "traffic": traffic,
+        "peak_source": f"{peak_src} bf16_tflops_sustained (kernel timed inside a long step)",
+        "frac_of_burst_peak": gemm_tf / burst,
+        "launches": g["launches"], "avg_launch_us": 1000.0 * g["ms"] / max(1, g["launches"]),
+        "algorithmic_flops_per_launch": g["flops"] / max(1, g["launches"]),
+        "step": {"flops": step_flops, "achieved_tflops": step_flops / (ms_step / 1000.0) / 1e12,
+                 "frac_of_sustained": step_flops / (ms_step / 1000.0) / 1e12 / sustained},
+        "by_class_ms": {k: round(v["ms"], 4) for k, v in ops.items()},
+    }
+
+    # ---------------------------------------------------------------- CPU baseline (rank 0, N=1)
+    cpu = None
+    if keep_sd:
+        try:
+            dt, thr = cpu_oracle_step(sd, host)
+            cpu = {"value": 1.0 / dt, "unit": UNIT, "cores": thr, "kind": "port",
+                   "sample": "1 full UNet step (B=2, 128x128 latent, 70 transformer blocks), "
+                             "CPU fp32 torch oracle, same weights and inputs"}
+        except Exception as exc:  # pragma: no cover - reported, not fatal
+            cpu = {"value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+                   "sample": f"failed: {exc}"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+            "warmup": max(3, args.warmup), "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+            "config": config(ws),
+            "images_per_s": value / STEPS_PER_IMAGE,
+            "pct_fp16_tc_peak": 100.0 * roofline["step"]["achieved_tflops"] / sustained,
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+            "gpu_launches": args.steps * (info["launches_per_step"] + 1),
+            "output_finite": finite,
+        }
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    net.close()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -56,6 +56,13 @@ _SIGS = {
     "dlm_unet_forward": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_float, c_void_p,
                                  c_void_p, c_void_p, c_void_p, c_void_p]),
     "dlm_unet_set_graph": (c_int, [c_void_p, c_int]),
+    "dlm_unet_weight_count": (c_int, [ctypes.POINTER(c_int), c_int]),
+    "dlm_unet_weight_info": (c_int, [ctypes.POINTER(c_int), c_int, c_int, ctypes.c_char_p, c_int,
+                                     ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(c_int)]),
+    "dlm_unet_forward_host": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_float, c_void_p,
+                                      c_void_p, c_void_p, c_void_p, c_void_p]),
+    "dlm_unet_time_ops": (c_int, [c_void_p, ctypes.POINTER(ctypes.c_double),
+                                  ctypes.POINTER(ctypes.c_double), ctypes.POINTER(c_int), c_void_p]),
     "dlm_unet_stage": (c_int, [c_void_p, c_char_p, ctypes.POINTER(c_void_p), ctypes.POINTER(c_int),
                                ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
     "dlm_unet_info": (c_int, [c_void_p, ctypes.POINTER(ctypes.c_int64),

@@ -124,6 +124,7 @@ int gemm_plan_dense(GemmOp* op, const __half* A, int lda, const __half* W, int M
   fill_epilogue(p, epi, p.N);
   p.status = device_status_ptr();
   op->bn = bn;
+  op->k_true = K;
   const int tiles = p.m_tiles * p.n_tiles;
   op->grid = tiles < num_sms() ? tiles : num_sms();
   return DLM_OK;
@@ -195,6 +196,7 @@ int gemm_plan_conv(GemmOp* op, int Nb, int oH, int oW, const ConvSource* srcs, i
   fill_epilogue(p, epi, p.N);
   p.status = device_status_ptr();
   op->bn = bn;
+  op->k_true = ktot;
   const int tiles = p.m_tiles * p.n_tiles;
   op->grid = tiles < num_sms() ? tiles : num_sms();
   return DLM_OK;

@@ -16,6 +16,7 @@ struct GemmOp {
   GemmParams p;
   int bn = 0;
   int grid = 0;
+  long long k_true = 0;  // reduction length before padding to 64 (host-side bookkeeping)
 };
 
 struct GemmEpilogue {

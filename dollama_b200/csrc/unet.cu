@@ -135,7 +135,7 @@ struct WeightSpec {
   std::vector<int64_t> shape;
 };
 
-static std::vector<WeightSpec> unet_weight_specs(const UNetCfg& cfg) {
+std::vector<WeightSpec> unet_weight_specs(const UNetCfg& cfg) {
   std::vector<WeightSpec> S;
   auto lin = [&](const std::string& n, int o, int i, bool bias = true) {
     S.push_back({n + ".weight", {o, i}});
@@ -240,6 +240,7 @@ void UNetModel::release_plan() {
   B_ = H_ = W_ = 0;
   seq_.clear();
   gemm_ops_.clear();
+  gemm_flops_.clear();
   attn_ops_.clear();
   gn_ops_.clear();
   ln_ops_.clear();
@@ -518,8 +519,9 @@ __half* UNetModel::act(size_t elems) {
   return reinterpret_cast<__half*>(static_cast<char*>(abuf_) + off);
 }
 
-void UNetModel::push_gemm(const GemmOp& g) {
+void UNetModel::push_gemm(const GemmOp& g, double flops) {
   gemm_ops_.push_back(g);
+  gemm_flops_.push_back(flops >= 0.0 ? flops : 2.0 * g.p.M * static_cast<double>(g.p.N) * g.k_true);
   seq_.push_back({OpKind::Gemm, static_cast<int>(gemm_ops_.size() - 1)});
 }
 void UNetModel::push_attn(const AttnOp& a) {
@@ -707,6 +709,7 @@ int UNetModel::build(bool dry) {
   aoff_ = 0;
   seq_.clear();
   gemm_ops_.clear();
+  gemm_flops_.clear();
   attn_ops_.clear();
   gn_ops_.clear();
   ln_ops_.clear();
@@ -822,7 +825,7 @@ int UNetModel::build(bool dry) {
     e.bias = W("conv_in.bias");
     int rc = gemm_plan_conv(&g, B, H0, W0, &s0, 1, W("conv_in.packed"), C0, x0, C0, e);
     if (rc != DLM_OK) return rc;
-    push_gemm(g);
+    push_gemm(g, 2.0 * P0 * C0 * 36);  // algorithmic: 4 real input channels
   }
   stages_["conv_in_out"] = {x0, C0, H0, W0};
   struct Skip {
@@ -942,7 +945,7 @@ int UNetModel::build(bool dry) {
       e.bias = W("conv_out.bias_pad");
       rc = gemm_plan_conv(&g, B, H0, W0, &s0, 1, W("conv_out.packed"), 32, out32_, 32, e);
       if (rc != DLM_OK) return rc;
-      push_gemm(g);
+      push_gemm(g, 2.0 * P0 * 4 * 9 * C0);  // algorithmic: 4 real output channels
       const __half* o32 = out32_;
       __half* no = noise_out_;
       push_custom([=](cudaStream_t s) {
@@ -1024,31 +1027,110 @@ int UNetModel::forward(int B, int H, int Wd, const __half* latent, float timeste
   DLM_CHECK_CUDA(cudaMemcpyAsync(te_, te, static_cast<size_t>(B) * kTextDim * 2,
                                  cudaMemcpyDeviceToDevice, s));
   DLM_CHECK_CUDA(cudaMemcpyAsync(tid_, tid, 6 * 2, cudaMemcpyDeviceToDevice, s));
-  set_scalar_kernel<<<1, 1, 0, s>>>(d_t_, timestep);
-  DLM_CHECK_CUDA(cudaGetLastError());
-  if (use_graph_) {
-    if (!gexec_) {
-      if (!cap_stream_) DLM_CHECK_CUDA(cudaStreamCreateWithFlags(&cap_stream_, cudaStreamNonBlocking));
-      cudaGraph_t graph = nullptr;
-      DLM_CHECK_CUDA(cudaStreamBeginCapture(cap_stream_, cudaStreamCaptureModeThreadLocal));
-      rc = run_ops(cap_stream_);
-      cudaError_t ce = cudaStreamEndCapture(cap_stream_, &graph);
-      if (rc != DLM_OK) {
-        if (graph) cudaGraphDestroy(graph);
-        return rc;
-      }
-      DLM_CHECK_CUDA(ce);
-      ce = cudaGraphInstantiate(&gexec_, graph, 0);
-      cudaGraphDestroy(graph);
-      DLM_CHECK_CUDA(ce);
-    }
-    DLM_CHECK_CUDA(cudaGraphLaunch(gexec_, s));
-  } else {
-    rc = run_ops(s);
-    if (rc != DLM_OK) return rc;
-  }
+  rc = launch_step(timestep, s);
+  if (rc != DLM_OK) return rc;
   DLM_CHECK_CUDA(cudaMemcpyAsync(noise_out, noise_out_, lat * 2, cudaMemcpyDeviceToDevice, s));
   return DLM_OK;
+}
+
+int UNetModel::forward_host(int B, int H, int Wd, const __half* latent, float timestep,
+                            const __half* ehs, const __half* te, const __half* tid, __half* noise_out,
+                            cudaStream_t s) {
+  DLM_REQUIRE(latent && ehs && te && tid && noise_out, DLM_ERR_INVALID,
+              "unet_forward_host: null input");
+  int rc = plan(B, H, Wd);
+  if (rc != DLM_OK) return rc;
+  const size_t lat = static_cast<size_t>(B) * 4 * H * Wd;
+  DLM_CHECK_CUDA(cudaMemcpyAsync(lat_in_, latent, lat * 2, cudaMemcpyHostToDevice, s));
+  DLM_CHECK_CUDA(cudaMemcpyAsync(ehs_, ehs, static_cast<size_t>(B) * kCtxTokens * kCtxDim * 2,
+                                 cudaMemcpyHostToDevice, s));
+  DLM_CHECK_CUDA(cudaMemcpyAsync(te_, te, static_cast<size_t>(B) * kTextDim * 2,
+                                 cudaMemcpyHostToDevice, s));
+  DLM_CHECK_CUDA(cudaMemcpyAsync(tid_, tid, 6 * 2, cudaMemcpyHostToDevice, s));
+  rc = launch_step(timestep, s);
+  if (rc != DLM_OK) return rc;
+  DLM_CHECK_CUDA(cudaMemcpyAsync(noise_out, noise_out_, lat * 2, cudaMemcpyDeviceToHost, s));
+  DLM_CHECK_CUDA(cudaStreamSynchronize(s));
+  return DLM_OK;
+}
+
+int UNetModel::launch_step(float timestep, cudaStream_t s) {
+  set_scalar_kernel<<<1, 1, 0, s>>>(d_t_, timestep);
+  DLM_CHECK_CUDA(cudaGetLastError());
+  if (!use_graph_) return run_ops(s);
+  if (!gexec_) {
+    if (!cap_stream_) DLM_CHECK_CUDA(cudaStreamCreateWithFlags(&cap_stream_, cudaStreamNonBlocking));
+    cudaGraph_t graph = nullptr;
+    DLM_CHECK_CUDA(cudaStreamBeginCapture(cap_stream_, cudaStreamCaptureModeThreadLocal));
+    int rc = run_ops(cap_stream_);
+    cudaError_t ce = cudaStreamEndCapture(cap_stream_, &graph);
+    if (rc != DLM_OK) {
+      if (graph) cudaGraphDestroy(graph);
+      return rc;
+    }
+    DLM_CHECK_CUDA(ce);
+    ce = cudaGraphInstantiate(&gexec_, graph, 0);
+    cudaGraphDestroy(graph);
+    DLM_CHECK_CUDA(ce);
+  }
+  DLM_CHECK_CUDA(cudaGraphLaunch(gexec_, s));
+  return DLM_OK;
+}
+
+// Runs the planned step once, eagerly, with a CUDA event between consecutive launches, and
+// accumulates device time and algorithmic FLOPs per op class.  Measurement only: every op of the
+// step runs, in order, on the current arena contents.
+int UNetModel::time_ops(cudaStream_t s, double* ms, double* flops, int* count) {
+  DLM_REQUIRE(abuf_ != nullptr, DLM_ERR_INVALID, "unet_time_ops: run a forward first");
+  for (int k = 0; k < kNumOpClasses; ++k) {
+    ms[k] = 0.0;
+    flops[k] = 0.0;
+    count[k] = 0;
+  }
+  std::vector<cudaEvent_t> ev(seq_.size() + 1);
+  for (auto& e : ev) DLM_CHECK_CUDA(cudaEventCreate(&e));
+  int rc = DLM_OK;
+  DLM_CHECK_CUDA(cudaEventRecord(ev[0], s));
+  for (size_t i = 0; i < seq_.size() && rc == DLM_OK; ++i) {
+    const OpRef& o = seq_[i];
+    switch (o.kind) {
+      case OpKind::Gemm: rc = gemm_launch(gemm_ops_[o.idx], s); break;
+      case OpKind::Attn: rc = attn_launch(attn_ops_[o.idx], s); break;
+      case OpKind::Gn: rc = gn_launch(gn_ops_[o.idx], s); break;
+      case OpKind::Ln: {
+        const LnArgs& l = ln_ops_[o.idx];
+        rc = layer_norm(l.x, l.g, l.b, l.out, l.rows, l.C, l.eps, s);
+        break;
+      }
+      case OpKind::Custom: rc = custom_[o.idx](s); break;
+    }
+    if (cudaEventRecord(ev[i + 1], s) != cudaSuccess) rc = DLM_ERR_CUDA;
+  }
+  if (rc == DLM_OK && cudaStreamSynchronize(s) != cudaSuccess) rc = DLM_ERR_CUDA;
+  for (size_t i = 0; i < seq_.size() && rc == DLM_OK; ++i) {
+    float t = 0.0f;
+    cudaEventElapsedTime(&t, ev[i], ev[i + 1]);
+    const OpRef& o = seq_[i];
+    int k = 4;
+    double f = 0.0;
+    if (o.kind == OpKind::Gemm) {
+      k = 0;
+      f = gemm_flops_[o.idx];
+    } else if (o.kind == OpKind::Attn) {
+      k = 1;
+      const AttnParams& p = attn_ops_[o.idx].p;
+      f = 4.0 * p.B * p.H * static_cast<double>(p.Sq) * p.Sk * 64;
+    } else if (o.kind == OpKind::Gn) {
+      k = 2;
+    } else if (o.kind == OpKind::Ln) {
+      k = 3;
+    }
+    ms[k] += t;
+    flops[k] += f;
+    count[k] += o.kind == OpKind::Gn ? 2 : 1;
+  }
+  for (auto& e : ev) cudaEventDestroy(e);
+  return rc;
 }
 
 int UNetModel::stage(const std::string& name, const __half** ptr, int* C, int* H, int* Wd) const {
@@ -1126,6 +1208,61 @@ int dlm_unet_info(void* handle, int64_t* arena_bytes, int64_t* weight_bytes, int
   if (arena_bytes) *arena_bytes = static_cast<int64_t>(m->arena_bytes());
   if (weight_bytes) *weight_bytes = static_cast<int64_t>(m->weight_bytes());
   if (num_launches) *num_launches = m->num_launches();
+  return DLM_OK;
+}
+
+}  // extern "C"
+
+extern "C" {
+
+int dlm_unet_forward_host(void* handle, int B, int H, int W, const void* latent_host, float timestep,
+                          const void* ehs_host, const void* text_embeds_host,
+                          const void* time_ids_host, void* noise_out_host, void* stream) {
+  DLM_REQUIRE(handle != nullptr, DLM_ERR_INVALID, "unet_forward_host: null handle");
+  if (B == 0 || H == 0 || W == 0) return DLM_OK;
+  return static_cast<dlm::UNetModel*>(handle)->forward_host(
+      B, H, W, static_cast<const __half*>(latent_host), timestep,
+      static_cast<const __half*>(ehs_host), static_cast<const __half*>(text_embeds_host),
+      static_cast<const __half*>(time_ids_host), static_cast<__half*>(noise_out_host),
+      static_cast<cudaStream_t>(stream));
+}
+
+int dlm_unet_time_ops(void* handle, double* ms, double* flops, int* count, void* stream) {
+  DLM_REQUIRE(handle && ms && flops && count, DLM_ERR_INVALID, "unet_time_ops: null argument");
+  return static_cast<dlm::UNetModel*>(handle)->time_ops(static_cast<cudaStream_t>(stream), ms, flops,
+                                                       count);
+}
+
+}  // extern "C"
+
+extern "C" {
+
+int dlm_unet_weight_count(const int* depths, int mid_depth) {
+  dlm::UNetCfg cfg;
+  if (depths) {
+    for (int i = 0; i < 3; ++i) cfg.depth[i] = depths[i];
+    cfg.mid_depth = mid_depth;
+  }
+  return static_cast<int>(dlm::unet_weight_specs(cfg).size());
+}
+
+int dlm_unet_weight_info(const int* depths, int mid_depth, int index, char* name, int name_cap,
+                         int64_t* shape, int* ndim) {
+  DLM_REQUIRE(name && shape && ndim && name_cap > 0, DLM_ERR_INVALID, "unet_weight_info: null argument");
+  dlm::UNetCfg cfg;
+  if (depths) {
+    for (int i = 0; i < 3; ++i) cfg.depth[i] = depths[i];
+    cfg.mid_depth = mid_depth;
+  }
+  const auto specs = dlm::unet_weight_specs(cfg);
+  DLM_REQUIRE(index >= 0 && index < static_cast<int>(specs.size()), DLM_ERR_INVALID,
+              "unet_weight_info: index %d out of range", index);
+  const auto& sp = specs[index];
+  DLM_REQUIRE(static_cast<int>(sp.name.size()) < name_cap, DLM_ERR_INVALID,
+              "unet_weight_info: name buffer too small");
+  std::memcpy(name, sp.name.c_str(), sp.name.size() + 1);
+  *ndim = static_cast<int>(sp.shape.size());
+  for (int i = 0; i < 4; ++i) shape[i] = i < *ndim ? sp.shape[i] : 0;
   return DLM_OK;
 }
 

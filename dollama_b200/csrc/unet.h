@@ -42,6 +42,11 @@ class UNetModel {
              const int64_t* numels, cudaStream_t s);
   int forward(int B, int H, int W, const __half* latent, float timestep, const __half* ehs,
               const __half* te, const __half* tid, __half* noise_out, cudaStream_t s);
+  // Same step with pinned/pageable HOST inputs and output; returns after the result is on host.
+  int forward_host(int B, int H, int W, const __half* latent, float timestep, const __half* ehs,
+                   const __half* te, const __half* tid, __half* noise_out, cudaStream_t s);
+  static constexpr int kNumOpClasses = 5;  // gemm, attention, groupnorm, layernorm, other
+  int time_ops(cudaStream_t s, double* ms, double* flops, int* count);
   void set_graph(bool on) {
     if (on != use_graph_ && gexec_) {
       cudaGraphExecDestroy(gexec_);
@@ -78,6 +83,7 @@ class UNetModel {
   int build(bool dry);
   void release_plan();
   int run_ops(cudaStream_t s);
+  int launch_step(float timestep, cudaStream_t s);
   int plan_gn(const __half* x1, int C1, const __half* x2, int C2, int HW, const std::string& wprefix,
               float eps, bool silu, __half* out);
   int plan_resnet(const ResnetInfo& rs, const __half* x1, int C1, const __half* x2, int C2, int H,
@@ -87,7 +93,7 @@ class UNetModel {
                   const GemmEpilogue& e);
   int plan_attn(const __half* q, int ldq, const __half* k, int ldk, const __half* v, int ldv,
                 __half* o, int ldo, int heads, int Sq, int Sk);
-  void push_gemm(const GemmOp& g);
+  void push_gemm(const GemmOp& g, double flops = -1.0);
   void push_attn(const AttnOp& a);
   void push_gn(const GnOp& g);
   void push_ln(const LnArgs& l);
@@ -108,6 +114,7 @@ class UNetModel {
   size_t aoff_ = 0, arena_bytes_ = 0;
   std::vector<OpRef> seq_;
   std::vector<GemmOp> gemm_ops_;
+  std::vector<double> gemm_flops_;
   std::vector<AttnOp> attn_ops_;
   std::vector<GnOp> gn_ops_;
   std::vector<LnArgs> ln_ops_;

@@ -1,0 +1,98 @@
+"""Single-op timing tool for the B200 kernels (CUDA events, warm-up, L2-sized inputs).
+
+    python -m dollama_b200.kernel_bench gemm --m 8192 --n 640 --k 640
+    python -m dollama_b200.kernel_bench conv --n 8 --cin 320 --h 128 --w 128 --cout 320
+    python -m dollama_b200.kernel_bench attn --b 2 --heads 10 --sq 4096 --sk 4096
+
+Prints one JSON line: shape, microseconds per launch, achieved TFLOP/s and the fraction of the
+measured bf16 peak (MEASURED_PEAKS.json next to the repository, when present).  Used for the
+per-kernel ncu captures under profiles/.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+from pathlib import Path
+
+import torch
+
+from . import _lib as L
+
+
+def _p(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _s():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _time(fn, iters, warm=3):
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iters
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("op", choices=["gemm", "conv", "attn"])
+    ap.add_argument("--m", type=int, default=8192)
+    ap.add_argument("--n", type=int, default=640)
+    ap.add_argument("--k", type=int, default=640)
+    ap.add_argument("--cin", type=int, default=320)
+    ap.add_argument("--h", type=int, default=128)
+    ap.add_argument("--w", type=int, default=128)
+    ap.add_argument("--cout", type=int, default=320)
+    ap.add_argument("--b", type=int, default=2)
+    ap.add_argument("--heads", type=int, default=10)
+    ap.add_argument("--sq", type=int, default=4096)
+    ap.add_argument("--sk", type=int, default=4096)
+    ap.add_argument("--iters", type=int, default=20)
+    a = ap.parse_args(argv)
+    torch.manual_seed(0)
+    dev = "cuda"
+    if a.op == "gemm":
+        A = torch.randn(a.m, a.k, device=dev).half()
+        W = (torch.randn(a.n, a.k, device=dev) * a.k ** -0.5).half()
+        C = torch.empty(a.m, a.n, device=dev, dtype=torch.half)
+        fn = lambda: L.call("dlm_launch_gemm_fp16", _p(A), _p(W), _p(C), a.m, a.n, a.k, 1.0, 0.0, 0, 1, _s())
+        flops = 2.0 * a.m * a.n * a.k
+        shape = {"m": a.m, "n": a.n, "k": a.k}
+    elif a.op == "conv":
+        x = torch.randn(a.n, a.h, a.w, a.cin, device=dev).half()
+        w = (torch.randn(a.cout, 3, 3, a.cin, device=dev) * (9 * a.cin) ** -0.5).half()
+        b = torch.zeros(a.cout, device=dev).half()
+        o = torch.empty(a.n, a.h, a.w, a.cout, device=dev, dtype=torch.half)
+        fn = lambda: L.call("dlm_conv2d_nhwc", _p(x), a.n, a.h, a.w, a.cin, _p(w), _p(b), _p(o), a.cout,
+                            3, 1, None, 0, _s())
+        flops = 2.0 * a.n * a.h * a.w * a.cout * 9 * a.cin
+        shape = {"n": a.n, "cin": a.cin, "h": a.h, "w": a.w, "cout": a.cout, "k": 3}
+    else:
+        q = torch.randn(a.b, a.heads, a.sq, 64, device=dev).half()
+        k = torch.randn(a.b, a.heads, a.sk, 64, device=dev).half()
+        v = torch.randn_like(k)
+        o = torch.empty_like(q)
+        fn = lambda: L.call("dlm_launch_attention", _p(q), _p(k), _p(v), _p(o), a.b, a.heads, a.sq, a.sk,
+                            64, 0.125, _s())
+        flops = 4.0 * a.b * a.heads * a.sq * a.sk * 64
+        shape = {"b": a.b, "heads": a.heads, "sq": a.sq, "sk": a.sk, "dh": 64}
+    ms = _time(fn, a.iters)
+    peak = None
+    pk = Path(__file__).resolve().parent.parent / "MEASURED_PEAKS.json"
+    if pk.exists():
+        peak = json.loads(pk.read_text()).get("bf16_tflops")
+    tf = flops / (ms / 1e3) / 1e12
+    print(json.dumps({"op": a.op, **shape, "us": ms * 1e3, "tflops": tf,
+                      "frac_of_measured_bf16_burst": (tf / peak) if peak else None}))
+
+
+if __name__ == "__main__":
+    main()

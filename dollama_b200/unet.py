@@ -8,6 +8,7 @@ module only marshals torch CUDA tensors' pointers.
 from __future__ import annotations
 
 import ctypes
+import math
 
 import torch
 
@@ -61,6 +62,31 @@ class SDXLUNet:
 
     __call__ = forward
 
+    def forward_host(self, latent, timestep: float, ehs, text_embeds, time_ids, out, stream=None):
+        """The step on HOST tensors (pinned for full speed): copies in, runs, copies `out` back and
+        returns after the result is on the host (the reference loop's per-step boundary)."""
+        B, _, H, W = latent.shape
+        self._last_b = B
+        for t in (latent, ehs, text_embeds, time_ids, out):
+            if t.is_cuda or t.dtype != torch.float16 or not t.is_contiguous():
+                raise ValueError("forward_host takes contiguous fp16 host tensors")
+        L.call("dlm_unet_forward_host", self._h, B, H, W, ctypes.c_void_p(latent.data_ptr()),
+               float(timestep), ctypes.c_void_p(ehs.data_ptr()),
+               ctypes.c_void_p(text_embeds.data_ptr()), ctypes.c_void_p(time_ids.data_ptr()),
+               ctypes.c_void_p(out.data_ptr()), _stream_ptr(stream))
+        return out
+
+    OP_CLASSES = ("gemm", "attention", "groupnorm", "layernorm", "other")
+
+    def time_ops(self, stream=None) -> dict:
+        """Per op class: device ms, algorithmic FLOPs and launches of one eager step."""
+        ms = (ctypes.c_double * 5)()
+        fl = (ctypes.c_double * 5)()
+        cnt = (ctypes.c_int * 5)()
+        L.call("dlm_unet_time_ops", self._h, ms, fl, cnt, _stream_ptr(stream))
+        return {k: {"ms": ms[i], "flops": fl[i], "launches": cnt[i]}
+                for i, k in enumerate(self.OP_CLASSES)}
+
     def set_graph(self, enable: bool) -> None:
         L.call("dlm_unet_set_graph", self._h, 1 if enable else 0)
 
@@ -95,3 +121,45 @@ class SDXLUNet:
             self.close()
         except Exception:
             pass
+
+
+def weight_spec(depths=(0, 2, 10), mid_depth: int = 10) -> dict:
+    """name -> shape of every tensor dlm_unet_create expects (from the C library)."""
+    lib = L.lib()
+    d = (ctypes.c_int * 3)(*depths)
+    n = lib.dlm_unet_weight_count(d, int(mid_depth))
+    out = {}
+    buf = ctypes.create_string_buffer(256)
+    shape = (ctypes.c_int64 * 4)()
+    nd = ctypes.c_int()
+    for i in range(n):
+        L.call("dlm_unet_weight_info", d, int(mid_depth), i, buf, 256, shape, ctypes.byref(nd))
+        out[buf.value.decode()] = tuple(shape[j] for j in range(nd.value))
+    return out
+
+
+_CONV_SUFFIXES = ("conv1", "conv2", "conv_shortcut", "conv_in", "conv_out", "downsamplers.0.conv",
+                  "upsamplers.0.conv")
+
+
+def random_weights(depths=(0, 2, 10), mid_depth: int = 10, seed: int = 7, device="cuda") -> dict:
+    """Synthetic random-init weights of the named architecture, generated on `device`:
+    conv weights / biases Kaiming-uniform U(+-1/sqrt(fan_in)), Linear weights and biases
+    N(0, 0.02), norm gammas 1 + N(0, 0.05), betas N(0, 0.05) (fp16)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    spec = weight_spec(depths, mid_depth)
+    sd = {}
+    for name, shape in sorted(spec.items()):
+        base, kind = name.rsplit(".", 1)
+        if base.endswith(_CONV_SUFFIXES):
+            w = spec[base + ".weight"]
+            bound = 1.0 / math.sqrt(w[1] * w[2] * w[3])
+            t = (torch.rand(shape, generator=g, device=device) * 2 - 1) * bound
+        elif len(shape) == 1 and base.rsplit(".", 1)[-1] in ("norm", "norm1", "norm2", "norm3",
+                                                              "conv_norm_out"):
+            t = (1.0 if kind == "weight" else 0.0) + 0.05 * torch.randn(shape, generator=g,
+                                                                        device=device)
+        else:
+            t = 0.02 * torch.randn(shape, generator=g, device=device)
+        sd[name] = t.half()
+    return sd

@@ -162,6 +162,26 @@ int dlm_unet_forward(void* handle, int B, int H, int W, const void* latent, floa
                      const void* ehs, const void* text_embeds, const void* time_ids, void* noise_out,
                      void* stream);
 
+/* The same step called with HOST buffers, as the reference's diffusion loop drives it
+ * (src/infer/diffusion.cu:896-986: H2D of the latent before the UNet, D2H of the noise
+ * prediction after): copies the inputs in, runs the step, copies noise_out back and returns
+ * once it is on the host (synchronizes `stream`).  Pinned host memory gives full copy speed. */
+int dlm_unet_forward_host(void* handle, int B, int H, int W, const void* latent_host, float timestep,
+                          const void* ehs_host, const void* text_embeds_host,
+                          const void* time_ids_host, void* noise_out_host, void* stream);
+
+/* Measurement helper: runs the planned step once eagerly with a CUDA event between launches and
+ * returns per op class (0 GEMM/conv, 1 attention, 2 GroupNorm, 3 LayerNorm, 4 other) the
+ * device milliseconds, the algorithmic FLOPs and the launch count (arrays of 5).  Requires a
+ * previous dlm_unet_forward for the same shape. */
+int dlm_unet_time_ops(void* handle, double* ms, double* flops, int* count, void* stream);
+
+/* The weight set dlm_unet_create expects for the given depths (NULL = SDXL): count, then per
+ * index its state-dict name and shape (ndim <= 4; shape padded with 0). */
+int dlm_unet_weight_count(const int* depths, int mid_depth);
+int dlm_unet_weight_info(const int* depths, int mid_depth, int index, char* name, int name_cap,
+                         int64_t* shape, int* ndim);
+
 /* Enables (default) or disables CUDA-graph replay of the step. */
 int dlm_unet_set_graph(void* handle, int enable);
 
