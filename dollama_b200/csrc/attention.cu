@@ -4,17 +4,19 @@
 // attention.cu:393, attention_fast.cu:58): out = softmax(Q K^T * scale) V with an fp32 online
 // softmax and P rounded to fp16 for the P.V product (as attention_fast.cu:238 does).
 //
-// One CTA = one (batch, head, 128-query tile); 192 threads:
-//   warps 0..3  softmax: thread r owns query row r (TMEM lane r).  Per 128-key tile j it reads
-//               S_j from TMEM (two passes of 4 x 32 columns: row max, then exp2 / row sum),
-//               writes P_j (fp16) into a 128-byte-swizzled K-major shared tile, then folds the
-//               previous tile's P.V result O_{j-1} (TMEM, 64 columns) into its fp32 register
-//               accumulator with the running rescale;
-//   warp 4      TMA producer: Q once, then K_j / V_j into a KV_STAGES ring;
-//   warp 5      TMEM owner + single-thread MMA issuer: S_j = Q K_j^T (M=128, N=128, K=64) into
-//               S[j%2]; O_j = P_j V_j (M=128, N=64, K=128, V as an MN-major operand) into O[j%2].
-// S and O are double-buffered in TMEM (2x128 + 2x64 of 512 columns) so that S_{j+1} and
-// P_j V_j run on the tensor core while the softmax warps work on tile j.
+// One CTA = one (batch, head) and two 128-query tiles T0, T1 that share every K/V tile
+// (320 threads, one CTA per SM, all 512 TMEM columns):
+//   warps 0..3 / 4..7  softmax of T0 / T1: thread r of the warpgroup owns query row r (TMEM
+//               lane r).  Per 128-key tile j: pass 1 reads S_j (TMEM) for the row max; the
+//               previous P.V result O_{j-1} is folded into the fp32 register accumulator with
+//               the running rescale; pass 2 computes p = 2^(s*c - m*c), the fp32 row sum, and
+//               stores P_j (fp16) into a 128-byte-swizzled K-major shared tile;
+//   warp 8      TMA producer: Q (both tiles) once, then K_j / V_j through a 3-stage ring;
+//   warp 9      TMEM owner + single-thread MMA issuer: S_j^t = Q_t K_j^T (M=128, N=128, K=64)
+//               and O_j^t = P_j^t V_j (M=128, N=64, K=128, V as an MN-major operand).
+// While one tile's softmax runs, the tensor core computes the other tile's S and P.V, so the
+// MMA latency hides behind softmax work (the two warpgroups ping-pong).
+// TMEM columns: S^0 [0,128), S^1 [128,256), O^0 [256,384) (2 x 64), O^1 [384,512) (2 x 64).
 //
 // Q/K/V/O are addressed through 4D tensor maps {64 (d), heads, seq, batch} with arbitrary
 // strides, so the same kernel reads the token-major [B*S, ld] projections of the UNet (head h at
@@ -29,29 +31,30 @@ namespace dlm {
 
 namespace {
 
-constexpr int kQ = 128;        // queries per CTA
+constexpr int kQT = 128;       // queries per tile (one softmax warpgroup)
+constexpr int kQ = 2 * kQT;    // queries per CTA
 constexpr int kKV = 128;       // keys per tile
 constexpr int kD = 64;         // head dim
 constexpr int kKVStages = 3;
-constexpr int kAttnThreads = 192;
-constexpr int kTileBytes = kQ * kD * 2;          // 16 KB (Q, K or V tile)
-constexpr int kPBytes = kQ * kKV * 2;            // 32 KB
+constexpr int kAttnThreads = 320;
+constexpr int kTileBytes = kQT * kD * 2;         // 16 KB (Q, K or V tile)
+constexpr int kPBytes = kQT * kKV * 2;           // 32 KB
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS0 = 0, kColO0 = 256;     // S[b] at 128*b, O[b] at 256 + 64*b
 
-constexpr int kSmemQ = 0;
-constexpr int kSmemK = kSmemQ + kTileBytes;
+constexpr int kSmemQ = 0;                                   // 2 tiles
+constexpr int kSmemK = kSmemQ + 2 * kTileBytes;
 constexpr int kSmemV = kSmemK + kKVStages * kTileBytes;
-constexpr int kSmemP = kSmemV + kKVStages * kTileBytes;
+constexpr int kSmemP = kSmemV + kKVStages * kTileBytes;     // 2 tiles
 constexpr int kSmemBar = kSmemP + 2 * kPBytes;
 constexpr int kAttnSmem = kSmemBar + 256 + 1024;
+static_assert(kAttnSmem <= 226 * 1024, "shared memory");
 
 __device__ __forceinline__ void store_p_chunk(uint8_t* pbuf, int row, int chunk32,
                                               const uint32_t (&h)[16]) {
   // keys [32*chunk32, +32) of `row`: four 16-byte chunks, 128B-swizzled K-major layout with
   // two 64-key column blocks of 16 KB each.
   const int blk = chunk32 >> 1;
-  uint8_t* base = pbuf + blk * (kQ * 128) + row * 128;
+  uint8_t* base = pbuf + blk * (kQT * 128) + row * 128;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int c16 = ((chunk32 & 1) * 4 + i) ^ (row & 7);
@@ -71,25 +74,25 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint8_t* sV = smem + kSmemV;
   uint8_t* sP = smem + kSmemP;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kSmemBar);
-  uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;
-  uint64_t* v_full = k_full + kKVStages;
-  uint64_t* kv_empty = v_full + kKVStages;
-  uint64_t* s_full = kv_empty + kKVStages;  // [2]
-  uint64_t* p_full = s_full + 2;            // [2]
-  uint64_t* o_full = p_full + 2;            // [2]
-  uint64_t* o_empty = o_full + 2;           // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_empty + 2);
+  uint64_t* q_full = bars;                    // Q of both tiles
+  uint64_t* k_full = bars + 1;                // [stages]
+  uint64_t* v_full = k_full + kKVStages;      // [stages]
+  uint64_t* kv_empty = v_full + kKVStages;    // [stages]
+  uint64_t* s_full = kv_empty + kKVStages;    // [tile]      S_j^t ready
+  uint64_t* p_full = s_full + 2;              // [tile]      P_j^t stored, S_j^t consumed
+  uint64_t* o_full = p_full + 2;              // [tile][2]   O_j^t ready
+  uint64_t* o_empty = o_full + 4;             // [tile][2]   O_j^t folded
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_empty + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int q_tiles = (p.Sq + kQ - 1) / kQ;
-  const int qt = blockIdx.x % q_tiles;
-  const int bh = blockIdx.x / q_tiles;
+  const int q_blocks = (p.Sq + kQ - 1) / kQ;
+  const int qb = blockIdx.x % q_blocks;
+  const int bh = blockIdx.x / q_blocks;
   const int h = bh % p.H;
   const int b = bh / p.H;
-  const int q0 = qt * kQ;
+  const int q0 = qb * kQ;
   const int n_tiles = (p.Sk + kKV - 1) / kKV;
 
   if (threadIdx.x == 0) {
@@ -97,18 +100,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     for (int s = 0; s < kKVStages; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&v_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&kv_empty[s], 2);  // released by P.V of both tiles
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], kQ);
-      mbar_init(&o_full[i], 1);
-      mbar_init(&o_empty[i], kQ);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], kQT);
+      mbar_init(&o_full[2 * t], 1);
+      mbar_init(&o_full[2 * t + 1], 1);
+      mbar_init(&o_empty[2 * t], kQT);
+      mbar_init(&o_empty[2 * t + 1], kQT);
     }
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
   }
@@ -117,14 +122,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
-      mbar_arrive_expect_tx(q_full, kTileBytes);
+      mbar_arrive_expect_tx(q_full, 2 * kTileBytes);
       tma_load_4d(sQ, &tmQ, q_full, 0, h, q0, b);
+      tma_load_4d(sQ + kTileBytes, &tmQ, q_full, 0, h, q0 + kQT, b);
       int stage = 0;
       uint32_t phase = 0;
       for (int j = 0; j < n_tiles; ++j) {
@@ -139,58 +145,73 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc_s = idesc_f16_f32(kQ, kKV, false);
-      constexpr uint32_t idesc_o = idesc_f16_f32(kQ, kD, true);
-      const uint32_t q_addr = smem_u32(sQ);
+      constexpr uint32_t idesc_s = idesc_f16_f32(kQT, kKV, false);
+      constexpr uint32_t idesc_o = idesc_f16_f32(kQT, kD, true);
       bool ok = mbar_wait(q_full, 0, abort_flag, p.status, kDevTimeoutMma);
-      // S_j for j = 0, 1
-      auto issue_s = [&](int j) -> bool {
+      auto issue_s = [&](int t, int j) -> bool {
         const int st = j % kKVStages;
-        const uint32_t ph = (j / kKVStages) & 1;
-        if (!mbar_wait(&k_full[st], ph, abort_flag, p.status, kDevTimeoutMma)) return false;
+        if (!mbar_wait(&k_full[st], (j / kKVStages) & 1, abort_flag, p.status, kDevTimeoutMma))
+          return false;
         tc_fence_after();
+        const uint32_t q_addr = smem_u32(sQ + t * kTileBytes);
         const uint32_t k_addr = smem_u32(sK + st * kTileBytes);
-        const uint32_t d = tbase + kColS0 + (j & 1) * kKV;
 #pragma unroll
         for (int k = 0; k < kD / 16; ++k) {
-          umma_f16_ss(d, sw128_desc(q_addr + k * 32, 16, 1024), sw128_desc(k_addr + k * 32, 16, 1024),
-                      idesc_s, k != 0 ? 1u : 0u);
+          umma_f16_ss(tbase + t * kKV, sw128_desc(q_addr + k * 32, 16, 1024),
+                      sw128_desc(k_addr + k * 32, 16, 1024), idesc_s, k != 0 ? 1u : 0u);
         }
-        umma_commit(&s_full[j & 1]);
+        umma_commit(&s_full[t]);
         return true;
       };
-      if (ok) ok = issue_s(0);
-      if (ok && n_tiles > 1) ok = issue_s(1);
-      for (int j = 0; j < n_tiles && ok; ++j) {
+      auto issue_pv = [&](int t, int j) -> bool {
         const int st = j % kKVStages;
-        const uint32_t ph = (j / kKVStages) & 1;
-        if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, abort_flag, p.status, kDevTimeoutMma)) break;
-        if (!mbar_wait(&v_full[st], ph, abort_flag, p.status, kDevTimeoutMma)) break;
-        if (j >= 2 &&
-            !mbar_wait(&o_empty[j & 1], ((j - 2) >> 1) & 1, abort_flag, p.status, kDevTimeoutMma))
-          break;
+        if (!mbar_wait(&v_full[st], (j / kKVStages) & 1, abort_flag, p.status, kDevTimeoutMma))
+          return false;
+        if (j >= 2 && !mbar_wait(&o_empty[2 * t + (j & 1)], ((j - 2) >> 1) & 1, abort_flag,
+                                 p.status, kDevTimeoutMma))
+          return false;
         tc_fence_after();
-        const uint32_t p_addr = smem_u32(sP + (j & 1) * kPBytes);
+        const uint32_t p_addr = smem_u32(sP + t * kPBytes);
         const uint32_t v_addr = smem_u32(sV + st * kTileBytes);
-        const uint32_t d = tbase + kColO0 + (j & 1) * kD;
+        const uint32_t d = tbase + 256 + t * 128 + (j & 1) * kD;
 #pragma unroll
         for (int ks = 0; ks < kKV / 16; ++ks) {
-          const uint64_t ad = sw128_desc(p_addr + (ks >> 2) * (kQ * 128) + (ks & 3) * 32, 16, 1024);
+          const uint64_t ad = sw128_desc(p_addr + (ks >> 2) * (kQT * 128) + (ks & 3) * 32, 16, 1024);
           const uint64_t bd = sw128_desc(v_addr + ks * 2048, 1024, 1024);
           umma_f16_ss(d, ad, bd, idesc_o, ks != 0 ? 1u : 0u);
         }
-        umma_commit(&o_full[j & 1]);
+        umma_commit(&o_full[2 * t + (j & 1)]);
         umma_commit(&kv_empty[st]);
-        if (j + 2 < n_tiles) ok = issue_s(j + 2);
+        return true;
+      };
+      if (ok) ok = issue_s(0, 0);
+      if (ok) ok = issue_s(1, 0);
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (!mbar_wait(&p_full[t], j & 1, abort_flag, p.status, kDevTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (j + 1 < n_tiles && !issue_s(t, j + 1)) {
+            ok = false;
+            break;
+          }
+          if (!issue_pv(t, j)) ok = false;
+        }
       }
     }
   } else {
-    // ------------------------------------------------------------ softmax warps 0..3
-    const int row = warp * 32 + lane;  // TMEM lane == query row within the tile
-    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    // ------------------------------------------------------------ softmax warps 0..7
+    const int t = warp >> 2;                       // query tile of this warpgroup
+    const int row = (warp & 3) * 32 + lane;        // TMEM lane == query row within the tile
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t ts = tbase + lane_off + t * kKV;
+    const uint32_t to = tbase + lane_off + 256 + t * 128;
+    uint8_t* pbuf = sP + t * kPBytes;
     const float c = p.scale_log2;
     float m_run = -INFINITY, l_run = 0.0f, alpha_prev = 1.0f;
     float acc[kD];
@@ -199,85 +220,110 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     bool ok = true;
 
     auto fold_o = [&](int j, float alpha) -> bool {
-      if (!mbar_wait(&o_full[j & 1], (j >> 1) & 1, abort_flag, p.status, kDevTimeoutSoftmax))
+      if (!mbar_wait(&o_full[2 * t + (j & 1)], (j >> 1) & 1, abort_flag, p.status,
+                     kDevTimeoutSoftmax))
         return false;
       tc_fence_after();
-      const uint32_t ta = tbase + lane_off + kColO0 + (j & 1) * kD;
-      uint32_t r[32];
+      uint32_t r0[32], r1[32];
+      tmem_ld_32x32b_x32(to + (j & 1) * kD, r0);
+      tmem_ld_32x32b_x32(to + (j & 1) * kD + 32, r1);
+      tmem_ld_wait();
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        tmem_ld_32x32b_x32(ta + half * 32, r);
-        tmem_ld_wait();
-#pragma unroll
-        for (int q = 0; q < 32; ++q) acc[half * 32 + q] = acc[half * 32 + q] * alpha + __uint_as_float(r[q]);
+      for (int q = 0; q < 32; ++q) {
+        acc[q] = fmaf(acc[q], alpha, __uint_as_float(r0[q]));
+        acc[32 + q] = fmaf(acc[32 + q], alpha, __uint_as_float(r1[q]));
       }
       tc_fence_before();
-      mbar_arrive(&o_empty[j & 1]);
+      mbar_arrive(&o_empty[2 * t + (j & 1)]);
       return true;
     };
 
     for (int j = 0; j < n_tiles; ++j) {
-      if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1, abort_flag, p.status, kDevTimeoutSoftmax)) {
+      if (!mbar_wait(&s_full[t], j & 1, abort_flag, p.status, kDevTimeoutSoftmax)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const uint32_t ts = tbase + lane_off + kColS0 + (j & 1) * kKV;
       const int valid = p.Sk - j * kKV;  // keys of this tile that exist (may exceed 128)
-      // pass 1: row max
-      float mx = m_run;
-      uint32_t r[32];
+      const bool full_tile = valid >= kKV;
+      // pass 1: row max over 128 columns, two TMEM loads in flight, four independent chains
+      float mx0 = m_run, mx1 = m_run, mx2 = m_run, mx3 = m_run;
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        tmem_ld_32x32b_x32(ts + cc * 32, r);
+      for (int cc = 0; cc < 4; cc += 2) {
+        uint32_t ra[32], rb[32];
+        tmem_ld_32x32b_x32(ts + cc * 32, ra);
+        tmem_ld_32x32b_x32(ts + cc * 32 + 32, rb);
         tmem_ld_wait();
+        if (full_tile) {
 #pragma unroll
-        for (int q = 0; q < 32; ++q) {
-          const float s = (cc * 32 + q < valid) ? __uint_as_float(r[q]) : -INFINITY;
-          mx = fmaxf(mx, s);
+          for (int q = 0; q < 32; q += 2) {
+            mx0 = fmaxf(mx0, __uint_as_float(ra[q]));
+            mx1 = fmaxf(mx1, __uint_as_float(ra[q + 1]));
+            mx2 = fmaxf(mx2, __uint_as_float(rb[q]));
+            mx3 = fmaxf(mx3, __uint_as_float(rb[q + 1]));
+          }
+        } else {
+#pragma unroll
+          for (int q = 0; q < 32; ++q) {
+            if (cc * 32 + q < valid) mx0 = fmaxf(mx0, __uint_as_float(ra[q]));
+            if (cc * 32 + 32 + q < valid) mx1 = fmaxf(mx1, __uint_as_float(rb[q]));
+          }
         }
       }
+      const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
       const float alpha = fast_exp2((m_run - mx) * c);  // m_run = -inf on the first tile -> 0
       const float mc = mx * c;
-      // pass 2: p = exp2(s*c - m*c), row sum, fp16 P into shared memory
-      float sum = 0.0f;
-      uint8_t* pbuf = sP + (j & 1) * kPBytes;
+      // fold O_{j-1}: also guarantees P.V of tile j-1 finished reading the P buffer
+      if (j >= 1 && !fold_o(j - 1, alpha_prev)) {
+        ok = false;
+        break;
+      }
+      // pass 2: p = exp2(s*c - m*c), fp32 row sum, fp16 P into shared memory
+      float sum0 = 0.0f, sum1 = 0.0f, sum2 = 0.0f, sum3 = 0.0f;
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        tmem_ld_32x32b_x32(ts + cc * 32, r);
+      for (int cc = 0; cc < 4; cc += 2) {
+        uint32_t ra[32], rb[32];
+        tmem_ld_32x32b_x32(ts + cc * 32, ra);
+        tmem_ld_32x32b_x32(ts + cc * 32 + 32, rb);
         tmem_ld_wait();
-        uint32_t hp[16];
 #pragma unroll
-        for (int q = 0; q < 32; q += 2) {
-          const float s0 = (cc * 32 + q < valid) ? __uint_as_float(r[q]) : -INFINITY;
-          const float s1 = (cc * 32 + q + 1 < valid) ? __uint_as_float(r[q + 1]) : -INFINITY;
-          const float e0 = fast_exp2(fmaf(s0, c, -mc));
-          const float e1 = fast_exp2(fmaf(s1, c, -mc));
-          const __half2 hh = __floats2half2_rn(e0, e1);
-          const float2 back = __half22float2(hh);
-          sum += back.x + back.y;  // the sum matches the fp16 P that multiplies V
-          hp[q >> 1] = *reinterpret_cast<const uint32_t*>(&hh);
+        for (int half = 0; half < 2; ++half) {
+          const uint32_t* r = half ? rb : ra;
+          const int col0 = (cc + half) * 32;
+          uint32_t hp[16];
+#pragma unroll
+          for (int q = 0; q < 32; q += 2) {
+            float e0 = fast_exp2(fmaf(__uint_as_float(r[q]), c, -mc));
+            float e1 = fast_exp2(fmaf(__uint_as_float(r[q + 1]), c, -mc));
+            if (!full_tile) {
+              if (col0 + q >= valid) e0 = 0.0f;
+              if (col0 + q + 1 >= valid) e1 = 0.0f;
+            }
+            if (q & 2) {
+              sum2 += e0;
+              sum3 += e1;
+            } else {
+              sum0 += e0;
+              sum1 += e1;
+            }
+            hp[q >> 1] = pack_half2(e0, e1);
+          }
+          store_p_chunk(pbuf, row, cc + half, hp);
         }
-        store_p_chunk(pbuf, row, cc, hp);
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(&p_full[j & 1]);
-      l_run = l_run * alpha + sum;
+      mbar_arrive(&p_full[t]);
+      l_run = fmaf(l_run, alpha, (sum0 + sum1) + (sum2 + sum3));
       m_run = mx;
-      if (j >= 1) {
-        if (!fold_o(j - 1, alpha_prev)) {
-          ok = false;
-          break;
-        }
-      }
       alpha_prev = alpha;
     }
     if (ok && n_tiles > 0) ok = fold_o(n_tiles - 1, alpha_prev);
-    if (ok && q0 + row < p.Sq) {
+    const int qrow = q0 + t * kQT + row;
+    if (ok && qrow < p.Sq) {
       const float inv = 1.0f / l_run;
       __half* dst = p.out + static_cast<size_t>(b) * p.o_sb + static_cast<size_t>(h) * p.o_sh +
-                    static_cast<size_t>(q0 + row) * p.o_ss;
+                    static_cast<size_t>(qrow) * p.o_ss;
 #pragma unroll
       for (int d = 0; d < kD; d += 8) {
         uint4 v;
@@ -294,7 +340,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   tc_fence_before();
   __syncthreads();
   if (*abort_flag) drain_sleep(200000);
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tbase, kTmemCols);
   }

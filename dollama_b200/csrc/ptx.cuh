@@ -262,6 +262,13 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// 2^x for two fp16 values at once (ex2.approx.f16x2; -inf -> 0).
+__device__ __forceinline__ uint32_t ex2_half2(uint32_t x) {
+  uint32_t y;
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
 
 __device__ __forceinline__ float gelu_erf_f(float x) {
