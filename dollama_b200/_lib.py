@@ -47,6 +47,10 @@ _SIGS = {
     "dlm_group_norm_nhwc": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_void_p,
                                     c_void_p, c_float, c_int, c_int, c_void_p, c_void_p, c_size_t,
                                     c_void_p]),
+    "dlm_group_norm_nhwc_noalloc_capacity": (c_size_t, []),
+    "dlm_group_norm_nhwc_noalloc": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int,
+                                            c_void_p, c_void_p, c_float, c_int, c_int, c_void_p,
+                                            c_void_p]),
     "dlm_launch_layer_norm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_float,
                                       c_void_p]),
     "dlm_unet_create": (c_int, [ctypes.POINTER(c_int), c_int, c_int, ctypes.POINTER(c_char_p),

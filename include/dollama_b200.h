@@ -132,6 +132,20 @@ int dlm_group_norm_nhwc(const void* x1, int C1, const void* x2, int C2, int N, i
                         const void* gamma, const void* beta, float eps, int groups, int silu,
                         void* out, void* scratch, size_t scratch_bytes, void* stream);
 
+/* The same GroupNorm for callers that cannot allocate device memory (no counterpart in the
+ * reference): a host whose device memory is entirely owned by its own pre-reserved arena, or a
+ * loop that must not pay cudaMalloc's implicit synchronisation, cannot hand dlm_group_norm_nhwc a
+ * scratch buffer.  This entry point keeps the partial sums in a static device array of the
+ * library (dlm_group_norm_nhwc_noalloc_capacity() float2 entries, 256 KiB, one copy per GPU that
+ * loads the library, held until exit) and allocates nothing.  Problems needing more partial sums
+ * are rejected with DLM_ERR_INVALID.  All calls share the array: calls that overlap on the GPU
+ * race and must be serialised.  The first call on a device looks up the array's device address
+ * (with that device current) and should come before any stream capture. */
+size_t dlm_group_norm_nhwc_noalloc_capacity(void);
+int dlm_group_norm_nhwc_noalloc(const void* x1, int C1, const void* x2, int C2, int N, int HW,
+                                const void* gamma, const void* beta, float eps, int groups,
+                                int silu, void* out, void* stream);
+
 /* LayerNorm over the last dim of [rows, C] (reference src/kernels/layernorm.cuh:51-57);
  * gamma / beta may be NULL.  C % 8 == 0, C <= 2048. */
 int dlm_launch_layer_norm(const void* in, const void* gamma, const void* beta, void* out, int rows,
