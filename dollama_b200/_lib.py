@@ -53,6 +53,12 @@ _SIGS = {
                                             c_void_p]),
     "dlm_launch_layer_norm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_float,
                                       c_void_p]),
+    "dlm_ternary_pack": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p]),
+    "dlm_quantize_act_i8": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p]),
+    "dlm_ternary_gemm_i8": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
+                                    c_int, c_void_p]),
+    "dlm_bitlinear": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p,
+                              c_void_p, c_void_p]),
     "dlm_unet_create": (c_int, [ctypes.POINTER(c_int), c_int, c_int, ctypes.POINTER(c_char_p),
                                 ctypes.POINTER(c_void_p), ctypes.POINTER(ctypes.c_int64),
                                 ctypes.POINTER(c_void_p), c_void_p]),

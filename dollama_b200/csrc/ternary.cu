@@ -1,0 +1,237 @@
+// BitNet ternary-weight x int8-activation linear (the tag LM's BitLinear), bit-exact with the
+// reference's integer path (src/models/bitnet.hpp: quantize_weight_ternary :70-109,
+// quantize_activation_int8 :123-165, BitNet::bitlinear :447-471).
+//
+// Weights are quantized once (per output row: alpha = mean|w| in double, q = clamp(round(w/alpha),
+// -1, 1)) and stored as 2-bit codes, 16 per 32-bit word (00 = 0, 01 = +1, 11 = -1), i.e. 1/16 of
+// the fp32 bytes; activations are quantized per token (scale = max|x|/127, q = clamp(round(x/scale),
+// -127, 127)).  Both quantizers run in double with explicit round-to-nearest operations, in the
+// same order as the reference, so codes and scales are identical.
+//
+// The GEMM keeps the reference's exact arithmetic: int32 accumulation (|acc| <= 127 * K fits for
+// K < 2^24) and y = float(double(acc) * double(alpha_n) * double(scale_m)).  Each CTA computes a
+// 32-token x 64-output tile: the weight chunk is expanded to int8 once in shared memory (rows padded
+// by 16 bytes, so 16-byte reads of consecutive rows hit distinct banks) and amortised over the 32
+// tokens; the inner loop is 16-byte shared loads + dp4a.  Packed weight rows are read with
+// coalesced 16-byte loads.
+#include <cstdint>
+
+#include "common.h"
+
+namespace dlm {
+
+namespace {
+
+constexpr int kTM = 32;       // tokens per CTA
+constexpr int kTN = 64;       // outputs per CTA
+constexpr int kKC = 256;      // K chunk (elements)
+constexpr int kRow = kKC + 16;  // padded smem row (bytes)
+constexpr int kThreads = 256;
+
+// One thread per output row: exact per-row ternary quantization, then 2-bit packing.
+__global__ void ternary_pack_kernel(const float* __restrict__ w, int N, int K,
+                                    uint32_t* __restrict__ packed, float* __restrict__ alpha) {
+  const int n = blockIdx.x * blockDim.x + threadIdx.x;
+  if (n >= N) return;
+  const float* row = w + static_cast<size_t>(n) * K;
+  double sum_abs = 0.0;
+  for (int i = 0; i < K; ++i) sum_abs = __dadd_rn(sum_abs, fabs(static_cast<double>(row[i])));
+  const double a = __ddiv_rn(sum_abs, static_cast<double>(K));
+  alpha[n] = static_cast<float>(a);
+  const double inv = a == 0.0 ? 0.0 : __ddiv_rn(1.0, a);
+  uint32_t* out = packed + static_cast<size_t>(n) * (K / 16);
+  for (int w16 = 0; w16 < K / 16; ++w16) {
+    uint32_t word = 0;
+    for (int j = 0; j < 16; ++j) {
+      uint32_t code = 0;
+      if (a != 0.0) {
+        double r = round(__dmul_rn(static_cast<double>(row[w16 * 16 + j]), inv));
+        if (r > 1.0) r = 1.0;
+        if (r < -1.0) r = -1.0;
+        code = r > 0.0 ? 1u : (r < 0.0 ? 3u : 0u);
+      }
+      word |= code << (2 * j);
+    }
+    out[w16] = word;
+  }
+}
+
+// One warp per token: exact absmax int8 quantization.
+__global__ void quant_act_kernel(const float* __restrict__ x, int M, int K, int8_t* __restrict__ xq,
+                                 float* __restrict__ xscale) {
+  const int m = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (m >= M) return;
+  const float* row = x + static_cast<size_t>(m) * K;
+  double amax = 0.0;
+  for (int i = lane; i < K; i += 32) amax = fmax(amax, fabs(static_cast<double>(row[i])));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmax(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const double scale = __ddiv_rn(amax, 127.0);
+  const double inv = scale == 0.0 ? 0.0 : __ddiv_rn(1.0, scale);
+  if (lane == 0) xscale[m] = static_cast<float>(scale);
+  int8_t* q = xq + static_cast<size_t>(m) * K;
+  for (int i = lane; i < K; i += 32) {
+    int v = 0;
+    if (scale != 0.0) {
+      double r = round(__dmul_rn(static_cast<double>(row[i]), inv));
+      if (r > 127.0) r = 127.0;
+      if (r < -127.0) r = -127.0;
+      v = static_cast<int>(r);
+    }
+    q[i] = static_cast<int8_t>(v);
+  }
+}
+
+// 4 two-bit codes (one byte) -> 4 int8 lanes {0, +1, -1}.
+__device__ __forceinline__ uint32_t decode4(uint32_t b) {
+  const uint32_t t = (b & 0x03u) | ((b & 0x0Cu) << 6) | ((b & 0x30u) << 12) | ((b & 0xC0u) << 18);
+  const uint32_t lo = t & 0x01010101u;
+  const uint32_t hi = (t >> 1) & 0x01010101u;
+  return lo | (hi * 0xFEu);
+}
+
+__global__ void __launch_bounds__(kThreads)
+    ternary_gemm_kernel(const uint32_t* __restrict__ wp, const float* __restrict__ alpha,
+                        const int8_t* __restrict__ xq, const float* __restrict__ xscale,
+                        float* __restrict__ y, int M, int N, int K) {
+  __shared__ __align__(16) int8_t sw[kTN * kRow];
+  __shared__ __align__(16) int8_t sx[kTM * kRow];
+  const int n0 = blockIdx.x * kTN, m0 = blockIdx.y * kTM;
+  const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;  // outputs n0 + tx + 16i, tokens m0 + ty + 16j
+  int acc[2][4];
+#pragma unroll
+  for (int j = 0; j < 2; ++j)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[j][i] = 0;
+  const int wwords = K / 16;
+  for (int k0 = 0; k0 < K; k0 += kKC) {
+    const int kc = min(kKC, K - k0);  // multiple of 16
+    // expand the weight chunk: 64 rows x kc/16 words, four words (64 codes) per 16-byte load
+    const int wq = kc / 64;           // uint4 per row (kc multiple of 64 on this path)
+    for (int idx = tid; idx < kTN * wq; idx += kThreads) {
+      const int r = idx / wq, c = idx - r * wq;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (n0 + r < N)
+        v = __ldg(reinterpret_cast<const uint4*>(wp + static_cast<size_t>(n0 + r) * wwords + k0 / 16) + c);
+      const uint32_t words[4] = {v.x, v.y, v.z, v.w};
+      uint32_t* dst = reinterpret_cast<uint32_t*>(sw + r * kRow + c * 64);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t wd = words[q];
+        dst[4 * q + 0] = decode4(wd & 0xFFu);
+        dst[4 * q + 1] = decode4((wd >> 8) & 0xFFu);
+        dst[4 * q + 2] = decode4((wd >> 16) & 0xFFu);
+        dst[4 * q + 3] = decode4(wd >> 24);
+      }
+    }
+    // activations: 32 rows x kc bytes, 16-byte loads
+    const int xv = kc / 16;
+    for (int idx = tid; idx < kTM * xv; idx += kThreads) {
+      const int r = idx / xv, c = idx - r * xv;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (m0 + r < M) v = __ldg(reinterpret_cast<const uint4*>(xq + static_cast<size_t>(m0 + r) * K + k0) + c);
+      *reinterpret_cast<uint4*>(sx + r * kRow + c * 16) = v;
+    }
+    __syncthreads();
+    for (int k = 0; k < kc; k += 16) {
+      uint4 xv4[2], wv4[4];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) xv4[j] = *reinterpret_cast<const uint4*>(sx + (ty + 16 * j) * kRow + k);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) wv4[i] = *reinterpret_cast<const uint4*>(sw + (tx + 16 * i) * kRow + k);
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          int a = acc[j][i];
+          a = __dp4a(static_cast<int>(xv4[j].x), static_cast<int>(wv4[i].x), a);
+          a = __dp4a(static_cast<int>(xv4[j].y), static_cast<int>(wv4[i].y), a);
+          a = __dp4a(static_cast<int>(xv4[j].z), static_cast<int>(wv4[i].z), a);
+          a = __dp4a(static_cast<int>(xv4[j].w), static_cast<int>(wv4[i].w), a);
+          acc[j][i] = a;
+        }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int m = m0 + ty + 16 * j;
+    if (m >= M) continue;
+    const double s = static_cast<double>(xscale[m]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int n = n0 + tx + 16 * i;
+      if (n >= N) continue;
+      const double v = __dmul_rn(__dmul_rn(static_cast<double>(acc[j][i]), static_cast<double>(alpha[n])), s);
+      y[static_cast<size_t>(m) * N + n] = static_cast<float>(v);
+    }
+  }
+}
+
+}  // namespace
+
+int ternary_pack(const float* w, int N, int K, uint32_t* packed, float* alpha, cudaStream_t s) {
+  DLM_REQUIRE(w && packed && alpha, DLM_ERR_INVALID, "ternary_pack: null pointer");
+  DLM_REQUIRE(N > 0 && K > 0 && K % 64 == 0, DLM_ERR_INVALID, "ternary_pack: K=%d must be a multiple of 64", K);
+  ternary_pack_kernel<<<(N + 127) / 128, 128, 0, s>>>(w, N, K, packed, alpha);
+  DLM_CHECK_CUDA(cudaGetLastError());
+  return DLM_OK;
+}
+
+int quantize_act_i8(const float* x, int M, int K, int8_t* xq, float* xscale, cudaStream_t s) {
+  DLM_REQUIRE(x && xq && xscale, DLM_ERR_INVALID, "quantize_act_i8: null pointer");
+  DLM_REQUIRE(M > 0 && K > 0, DLM_ERR_INVALID, "quantize_act_i8: empty");
+  const int warps = 8;
+  quant_act_kernel<<<(M + warps - 1) / warps, warps * 32, 0, s>>>(x, M, K, xq, xscale);
+  DLM_CHECK_CUDA(cudaGetLastError());
+  return DLM_OK;
+}
+
+int ternary_gemm_i8(const uint32_t* wp, const float* alpha, const int8_t* xq, const float* xscale,
+                    float* y, int M, int N, int K, cudaStream_t s) {
+  DLM_REQUIRE(wp && alpha && xq && xscale && y, DLM_ERR_INVALID, "ternary_gemm_i8: null pointer");
+  DLM_REQUIRE(K % 64 == 0 && K < (1 << 24), DLM_ERR_INVALID,
+              "ternary_gemm_i8: K=%d must be a multiple of 64", K);
+  DLM_REQUIRE((reinterpret_cast<uintptr_t>(wp) & 15) == 0 && (reinterpret_cast<uintptr_t>(xq) & 15) == 0,
+              DLM_ERR_INVALID, "ternary_gemm_i8: packed weights / activations must be 16-byte aligned");
+  dim3 grid((N + kTN - 1) / kTN, (M + kTM - 1) / kTM);
+  ternary_gemm_kernel<<<grid, kThreads, 0, s>>>(wp, alpha, xq, xscale, y, M, N, K);
+  DLM_CHECK_CUDA(cudaGetLastError());
+  return DLM_OK;
+}
+
+}  // namespace dlm
+
+extern "C" {
+
+int dlm_ternary_pack(const float* w, int N, int K, void* w_packed2b, float* row_scale, void* stream) {
+  if (N == 0 || K == 0) return DLM_OK;
+  return dlm::ternary_pack(w, N, K, static_cast<uint32_t*>(w_packed2b), row_scale,
+                           static_cast<cudaStream_t>(stream));
+}
+
+int dlm_quantize_act_i8(const float* x, int M, int K, int8_t* xq, float* x_scale, void* stream) {
+  if (M == 0 || K == 0) return DLM_OK;
+  return dlm::quantize_act_i8(x, M, K, xq, x_scale, static_cast<cudaStream_t>(stream));
+}
+
+int dlm_ternary_gemm_i8(const void* w_packed2b, const float* row_scale, const int8_t* x,
+                        const float* x_scale, float* y, int M, int N, int K, void* stream) {
+  if (M == 0 || N == 0 || K == 0) return DLM_OK;
+  return dlm::ternary_gemm_i8(static_cast<const uint32_t*>(w_packed2b), row_scale, x, x_scale, y, M,
+                              N, K, static_cast<cudaStream_t>(stream));
+}
+
+int dlm_bitlinear(const void* w_packed2b, const float* row_scale, const float* x, float* y, int M,
+                  int N, int K, int8_t* xq_scratch, float* xscale_scratch, void* stream) {
+  if (M == 0 || N == 0 || K == 0) return DLM_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc = dlm::quantize_act_i8(x, M, K, xq_scratch, xscale_scratch, s);
+  if (rc != DLM_OK) return rc;
+  return dlm::ternary_gemm_i8(static_cast<const uint32_t*>(w_packed2b), row_scale, xq_scratch,
+                              xscale_scratch, y, M, N, K, s);
+}
+
+}  // extern "C"

@@ -43,7 +43,7 @@ def _time(fn, iters, warm=3):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("op", choices=["gemm", "conv", "attn"])
+    ap.add_argument("op", choices=["gemm", "conv", "attn", "ternary"])
     ap.add_argument("--m", type=int, default=8192)
     ap.add_argument("--n", type=int, default=640)
     ap.add_argument("--k", type=int, default=640)
@@ -75,6 +75,19 @@ def main(argv=None):
                             3, 1, None, 0, _s())
         flops = 2.0 * a.n * a.h * a.w * a.cout * 9 * a.cin
         shape = {"n": a.n, "cin": a.cin, "h": a.h, "w": a.w, "cout": a.cout, "k": 3}
+    elif a.op == "ternary":
+        w = (torch.randn(a.n, a.k, device=dev) * 0.05).float()
+        packed = torch.zeros(a.n * a.k // 16, dtype=torch.int32, device=dev)
+        alpha = torch.zeros(a.n, dtype=torch.float32, device=dev)
+        L.call("dlm_ternary_pack", _p(w), a.n, a.k, _p(packed), _p(alpha), _s())
+        xq = torch.randint(-127, 128, (a.m, a.k), dtype=torch.int8, device=dev)
+        xs = torch.rand(a.m, device=dev)
+        y = torch.empty(a.m, a.n, dtype=torch.float32, device=dev)
+        fn = lambda: L.call("dlm_ternary_gemm_i8", _p(packed), _p(alpha), _p(xq), _p(xs), _p(y), a.m, a.n,
+                            a.k, _s())
+        flops = 2.0 * a.m * a.n * a.k  # int8 ops
+        shape = {"m": a.m, "n": a.n, "k": a.k,
+                 "bytes": a.n * a.k / 4 + a.m * a.k + 4 * a.m * a.n + 4 * (a.m + a.n)}
     else:
         q = torch.randn(a.b, a.heads, a.sq, 64, device=dev).half()
         k = torch.randn(a.b, a.heads, a.sk, 64, device=dev).half()
@@ -90,6 +103,8 @@ def main(argv=None):
     if pk.exists():
         peak = json.loads(pk.read_text()).get("bf16_tflops")
     tf = flops / (ms / 1e3) / 1e12
+    if "bytes" in shape:
+        shape["gbs"] = shape["bytes"] / (ms / 1e3) / 1e9
     print(json.dumps({"op": a.op, **shape, "us": ms * 1e3, "tflops": tf,
                       "frac_of_measured_bf16_burst": (tf / peak) if peak else None}))
 

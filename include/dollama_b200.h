@@ -151,6 +151,25 @@ int dlm_group_norm_nhwc_noalloc(const void* x1, int C1, const void* x2, int C2, 
 int dlm_launch_layer_norm(const void* in, const void* gamma, const void* beta, void* out, int rows,
                           int C, float eps, void* stream);
 
+/* ------------------------------------------------------------------ BitNet ternary x int8 linear
+ *
+ * Bit-exact with the reference's integer BitLinear (src/models/bitnet.hpp:447-471, a host loop
+ * there; no GPU kernel exists in the reference, README_en.md:143):
+ *   y[m, n] = float( double(sum_k wq[n,k] * xq[m,k]) * double(alpha_n) * double(scale_m) )
+ * with alpha_n = mean|w[n,:]| and wq = clamp(round(w/alpha), -1, 1) per output row
+ * (quantize_weight_ternary, bitnet.hpp:70-109) and scale_m = max|x[m,:]|/127,
+ * xq = clamp(round(x/scale), -127, 127) per token (quantize_activation_int8, bitnet.hpp:123-165).
+ * Packed weights: [N, K/16] uint32, 16 two-bit codes per word (00 = 0, 01 = +1, 11 = -1,
+ * code j at bits 2j); K % 64 == 0; packed weights and activations 16-byte aligned.
+ */
+int dlm_ternary_pack(const float* w, int N, int K, void* w_packed2b, float* row_scale, void* stream);
+int dlm_quantize_act_i8(const float* x, int M, int K, int8_t* xq, float* x_scale, void* stream);
+int dlm_ternary_gemm_i8(const void* w_packed2b, const float* row_scale, const int8_t* x,
+                        const float* x_scale, float* y, int M, int N, int K, void* stream);
+/* quantize_act_i8 + ternary_gemm_i8: BitNet::bitlinear for M tokens (scratch: M*K bytes, M floats). */
+int dlm_bitlinear(const void* w_packed2b, const float* row_scale, const float* x, float* y, int M,
+                  int N, int K, int8_t* xq_scratch, float* xscale_scratch, void* stream);
+
 /* ------------------------------------------------------------------ SDXL UNet (model level)
  *
  * Replaces unet_weights_create / launch_unet_batched / unet_weights_destroy (reference

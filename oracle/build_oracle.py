@@ -1,0 +1,54 @@
+"""Build recipe of the test oracles (test infrastructure only).
+
+* oracle/_build/liboracle_bitnet.so — the plain-C restatement (bitnet_oracle.c), always built;
+* oracle/_ref/libref_bitnet.so      — the reference's own BitNet integer path, compiled from
+  its header where it lies (src/models/bitnet.hpp under the reference tree) through
+  ref_bitnet_shim.cpp, built only when the reference tree exists (it does not on GPU boxes,
+  which use the prebuilt file).  Outputs go only to oracle/_ref/ (git-ignored).
+
+Usage:  python oracle/build_oracle.py
+"""
+from __future__ import annotations
+
+import os
+import subprocess
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+BUILD = HERE / "_build"
+REF_OUT = HERE / "_ref"
+REFERENCE = Path(os.environ.get("DOLLAMA_REFERENCE", "/root/reference"))
+
+
+def _run(cmd):
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"{' '.join(cmd)}\n{r.stdout}\n{r.stderr}")
+
+
+def _stale(out: Path, *srcs: Path) -> bool:
+    return not out.exists() or any(out.stat().st_mtime < s.stat().st_mtime for s in srcs)
+
+
+def build() -> dict:
+    BUILD.mkdir(exist_ok=True)
+    out = {}
+    lib = BUILD / "liboracle_bitnet.so"
+    src = HERE / "bitnet_oracle.c"
+    if _stale(lib, src):
+        _run(["gcc", "-O2", "-fPIC", "-shared", "-std=c11", "-o", str(lib), str(src), "-lm"])
+    out["oracle_bitnet"] = str(lib)
+    hdr = REFERENCE / "src" / "models" / "bitnet.hpp"
+    if hdr.exists():
+        REF_OUT.mkdir(exist_ok=True)
+        ref = REF_OUT / "libref_bitnet.so"
+        shim = HERE / "ref_bitnet_shim.cpp"
+        if _stale(ref, shim, hdr):
+            _run(["g++", "-O2", "-fPIC", "-shared", "-std=c++17", "-I", str(REFERENCE / "src"),
+                  "-o", str(ref), str(shim)])
+        out["ref_bitnet"] = str(ref)
+    return out
+
+
+if __name__ == "__main__":
+    print(build())
