@@ -25,34 +25,114 @@ int launch_bn(const GemmOp& op, cudaStream_t s) {
   return DLM_OK;
 }
 
-// Relative cost of one 128 x BN tile per unit of K: MMA time grows with BN; narrow tiles are
-// bound by shared-memory operand bandwidth (A + B bytes per MMA); plus a fixed per-tile cost.
+template <int BN>
+int launch_bn2(const GemmOp& op, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(op.grid, 1, 1);
+  cfg.blockDim = dim3(kGemmThreads, 1, 1);
+  cfg.dynamicSmemBytes = gemm2_smem_bytes(BN);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  DLM_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc2_kernel<BN>, op.tmA[0], op.tmA[1], op.tmA[2],
+                                    op.tmB, op.p));
+  return DLM_OK;
+}
+
+// Tile choice, calibrated on B200 sweeps of the UNet shapes (single CTA vs CTA pair, every N
+// tile).  The single-CTA kernel is bound by how fast TMA can pull operands from L2 into one SM
+// (about 70-85 B/clock with every SM loading), which narrow tiles hit first; its relative cost per
+// k-block and unit of N is modelled as max(BN, (128 + BN) / 2) + 24 per tile, times the number of
+// waves.  The CTA pair halves B traffic per SM but measured faster only for wide-N problems with
+// few row tiles (N >= 2560, M <= 4096, BN = 256: +5-7%), so it is used there alone.
 double tile_cost(int bn) {
   const double mma = bn;
   const double smem = 0.5 * (128 + bn);
   return (mma > smem ? mma : smem) + 24.0;
 }
 
-int pick_bn(int M, int N) {
-  static const int cands[] = {256, 192, 160, 128, 64};
-  const int sms = num_sms();
-  const int m_tiles = (M + kGemmBM - 1) / kGemmBM;
-  int best = 128;
-  double best_cost = 1e30;
-  for (int bn : cands) {
-    const int n_tiles = (N + bn - 1) / bn;
-    const long tiles = static_cast<long>(m_tiles) * n_tiles;
-    const long waves = (tiles + sms - 1) / sms;
-    const double cost = waves * tile_cost(bn);
-    if (cost < best_cost - 1e-9) {
-      best_cost = cost;
-      best = bn;
-    }
+// Largest number of CTA pairs of gemm_tc2_kernel<BN> co-resident on the current device (clusters
+// are placed within a GPC, so an SM without a free partner in its GPC cannot host a pair).
+template <int BN>
+int max_pairs_bn() {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * num_sms(), 1, 1);
+  cfg.blockDim = dim3(kGemmThreads, 1, 1);
+  cfg.dynamicSmemBytes = gemm2_smem_bytes(BN);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaFuncSetAttribute(gemm_tc2_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       gemm2_smem_bytes(BN));
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, gemm_tc2_kernel<BN>, &cfg) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    n = num_sms() / 2;
   }
-  return best;
+  return n;
 }
 
-bool bn_supported(int bn) { return bn == 256 || bn == 192 || bn == 160 || bn == 128 || bn == 64; }
+int max_pairs(int bn) {
+  static int cache[64][4] = {{0}};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int slot = bn == 256 ? 0 : bn == 192 ? 1 : bn == 160 ? 2 : 3;
+  if (dev < 0 || dev >= 64) return num_sms() / 2;
+  if (cache[dev][slot] == 0) {
+    cache[dev][slot] = bn == 256 ? max_pairs_bn<256>() : bn == 192 ? max_pairs_bn<192>()
+                     : bn == 160 ? max_pairs_bn<160>() : max_pairs_bn<128>();
+  }
+  return cache[dev][slot];
+}
+
+// Chooses single-CTA vs CTA-pair and the N tile.
+void pick_tile(int M, int N, int force_bn, int force_mode, int* bn_out, bool* pair_out) {
+  static const int single[] = {256, 192, 160, 128, 64};
+  static const int paired[] = {256, 192, 160, 128};
+  const int sms = num_sms();
+  const bool want_pair = force_mode == 2 || (force_mode == 0 && N >= 2560 && M <= 4096 && M > kGemmBM);
+  if (want_pair && M > kGemmBM) {
+    int bn = force_bn ? force_bn : 256;
+    bool ok = false;
+    for (int c : paired) ok = ok || c == bn;
+    if (ok) {
+      *bn_out = bn;
+      *pair_out = true;
+      return;
+    }
+  }
+  const long mt = (M + kGemmBM - 1) / kGemmBM;
+  double best = 1e30;
+  int bn_best = 128;
+  for (int bn : single) {
+    if (force_bn && bn != force_bn) continue;
+    const long tiles = mt * ((N + bn - 1) / bn);
+    const double c = ((tiles + sms - 1) / sms) * tile_cost(bn);
+    if (c < best - 1e-9) {
+      best = c;
+      bn_best = bn;
+    }
+  }
+  *bn_out = bn_best;
+  *pair_out = false;
+}
+
+int g_force_mode = 0;  // test hook: 0 auto, 1 single CTA, 2 CTA pair
+int g_force_bn = 0;    // test hook: forced N tile (0 = cost model)
+
+bool bn_supported(int bn, bool pair) {
+  if (pair) return bn == 256 || bn == 192 || bn == 160 || bn == 128;
+  return bn == 256 || bn == 192 || bn == 160 || bn == 128 || bn == 64;
+}
 
 void fill_epilogue(GemmParams& p, const GemmEpilogue& e, int N) {
   p.flags = e.flags;
@@ -64,6 +144,14 @@ void fill_epilogue(GemmParams& p, const GemmEpilogue& e, int N) {
   p.ldb2 = e.ldb2 > 0 ? e.ldb2 : N;
   p.resid = e.resid;
   p.ldr = e.ldr;
+  p.stats_out = e.stats_out;
+  p.stats_in = e.stats_in;
+  p.stats_in_parts = e.stats_in_parts;
+  p.stats_in_tile = e.stats_in_tile;
+  p.ln_C = e.ln_C;
+  p.ln_eps = e.ln_eps;
+  p.ln_u = e.ln_u;
+  p.ln_v = e.ln_v;
 }
 
 int check_epilogue(const GemmEpilogue& e, int N, __half* C, int ldc) {
@@ -85,8 +173,15 @@ int check_epilogue(const GemmEpilogue& e, int N, __half* C, int ldc) {
                     e.ldr % 8 == 0,
                 DLM_ERR_INVALID, "gemm: residual must be 16-byte aligned with ldr %% 8 == 0");
   if (e.flags & DLM_EPI_GEGLU)
-    DLM_REQUIRE(!(e.flags & DLM_EPI_RESID) && N % 64 == 0, DLM_ERR_INVALID,
-                "gemm: GEGLU needs N %% 64 == 0 and no residual");
+    DLM_REQUIRE(!(e.flags & DLM_EPI_RESID) && !(e.flags & kEpiRowStats) && N % 64 == 0,
+                DLM_ERR_INVALID, "gemm: GEGLU needs N %% 64 == 0, no residual, no row statistics");
+  if (e.flags & kEpiRowStats)
+    DLM_REQUIRE(e.stats_out != nullptr, DLM_ERR_INVALID, "gemm: row statistics need a buffer");
+  if (e.flags & kEpiLnFold)
+    DLM_REQUIRE(e.stats_in && e.ln_u && e.ln_v && e.stats_in_parts > 0 && e.stats_in_tile > 0 &&
+                    e.ln_C > 0 && (reinterpret_cast<uintptr_t>(e.ln_u) & 15) == 0 &&
+                    (reinterpret_cast<uintptr_t>(e.ln_v) & 15) == 0,
+                DLM_ERR_INVALID, "gemm: LayerNorm fold needs statistics and 16-byte aligned u / v");
   return DLM_OK;
 }
 
@@ -105,28 +200,33 @@ int gemm_plan_dense(GemmOp* op, const __half* A, int lda, const __half* W, int M
               DLM_ERR_INVALID, "gemm: operands must be 16-byte aligned");
   int rc = check_epilogue(epi, N, C, ldc);
   if (rc != DLM_OK) return rc;
-  const int bn = force_bn ? force_bn : pick_bn(M, N);
-  DLM_REQUIRE(bn_supported(bn), DLM_ERR_INVALID, "gemm: unsupported tile width %d", bn);
+  int bn = 0;
+  bool pair = false;
+  pick_tile(M, N, force_bn ? force_bn : g_force_bn, g_force_mode, &bn, &pair);
+  DLM_REQUIRE(bn_supported(bn, pair), DLM_ERR_INVALID, "gemm: unsupported tile width %d", bn);
   std::memset(op, 0, sizeof(*op));
   if (!tmap_2d_f16(&op->tmA[0], A, M, K, lda, kGemmBM, kGemmBK)) return DLM_ERR_CUDA;
   op->tmA[1] = op->tmA[0];
   op->tmA[2] = op->tmA[0];
-  if (!tmap_2d_f16(&op->tmB, W, N, K, K, bn, kGemmBK)) return DLM_ERR_CUDA;
+  if (!tmap_2d_f16(&op->tmB, W, N, K, K, pair ? bn / 2 : bn, kGemmBK)) return DLM_ERR_CUDA;
   GemmParams& p = op->p;
   p.M = M;
   p.N = N;
   p.num_kb = (K + kGemmBK - 1) / kGemmBK;
-  p.m_tiles = (M + kGemmBM - 1) / kGemmBM;
+  p.m_tiles = (M + (pair ? 2 : 1) * kGemmBM - 1) / ((pair ? 2 : 1) * kGemmBM);
   p.n_tiles = (N + bn - 1) / bn;
+  p.stats_ld = p.n_tiles;
   p.amode = 0;
   p.out = C;
   p.ldo = ldc;
   fill_epilogue(p, epi, p.N);
   p.status = device_status_ptr();
   op->bn = bn;
+  op->pair = pair;
   op->k_true = K;
   const int tiles = p.m_tiles * p.n_tiles;
-  op->grid = tiles < num_sms() ? tiles : num_sms();
+  const int slots = pair ? max_pairs(bn) : num_sms();
+  op->grid = (tiles < slots ? tiles : slots) * (pair ? 2 : 1);
   return DLM_OK;
 }
 
@@ -145,8 +245,10 @@ int gemm_plan_conv(GemmOp* op, int Nb, int oH, int oW, const ConvSource* srcs, i
   int rc = check_epilogue(epi, Cout, C, ldc);
   if (rc != DLM_OK) return rc;
   const int M = Nb * oH * oW;
-  const int bn = force_bn ? force_bn : pick_bn(M, Cout);
-  DLM_REQUIRE(bn_supported(bn), DLM_ERR_INVALID, "conv: unsupported tile width %d", bn);
+  int bn = 0;
+  bool pair = false;
+  pick_tile(M, Cout, force_bn ? force_bn : g_force_bn, g_force_mode, &bn, &pair);
+  DLM_REQUIRE(bn_supported(bn, pair), DLM_ERR_INVALID, "conv: unsupported tile width %d", bn);
   std::memset(op, 0, sizeof(*op));
   GemmParams& p = op->p;
   long ktot = 0;
@@ -179,12 +281,13 @@ int gemm_plan_conv(GemmOp* op, int Nb, int oH, int oW, const ConvSource* srcs, i
     ktot += static_cast<long>(cs.kind == 1 ? 1 : 9) * cs.C;
   }
   for (int s = nsrc; s < 3; ++s) op->tmA[s] = op->tmA[0];
-  if (!tmap_2d_f16(&op->tmB, W, Cout, ktot, ktot, bn, kGemmBK)) return DLM_ERR_CUDA;
+  if (!tmap_2d_f16(&op->tmB, W, Cout, ktot, ktot, pair ? bn / 2 : bn, kGemmBK)) return DLM_ERR_CUDA;
   p.M = M;
   p.N = Cout;
   p.num_kb = static_cast<int>(ktot / 64);
-  p.m_tiles = M / kGemmBM;
+  p.m_tiles = pair ? (M + 2 * kGemmBM - 1) / (2 * kGemmBM) : M / kGemmBM;
   p.n_tiles = (Cout + bn - 1) / bn;
+  p.stats_ld = p.n_tiles;
   p.amode = 1;
   p.oH = oH;
   p.oW = oW;
@@ -196,9 +299,11 @@ int gemm_plan_conv(GemmOp* op, int Nb, int oH, int oW, const ConvSource* srcs, i
   fill_epilogue(p, epi, p.N);
   p.status = device_status_ptr();
   op->bn = bn;
+  op->pair = pair;
   op->k_true = ktot;
   const int tiles = p.m_tiles * p.n_tiles;
-  op->grid = tiles < num_sms() ? tiles : num_sms();
+  const int slots = pair ? max_pairs(bn) : num_sms();
+  op->grid = (tiles < slots ? tiles : slots) * (pair ? 2 : 1);
   return DLM_OK;
 }
 
@@ -213,10 +318,31 @@ int gemm_prepare_kernels() {
   DLM_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<160>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm_smem_bytes(160)));
   DLM_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm_smem_bytes(128)));
   DLM_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm_smem_bytes(64)));
+  DLM_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm2_smem_bytes(256)));
+  DLM_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<192>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm2_smem_bytes(192)));
+  DLM_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<160>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm2_smem_bytes(160)));
+  DLM_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm2_smem_bytes(128)));
   return DLM_OK;
 }
 
 int gemm_launch(const GemmOp& op, cudaStream_t s) {
+  if (op.pair) {
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+      int rc = gemm_prepare_kernels();
+      if (rc != DLM_OK) return rc;
+      attr_set[dev] = true;
+    }
+    switch (op.bn) {
+      case 256: return launch_bn2<256>(op, s);
+      case 192: return launch_bn2<192>(op, s);
+      case 160: return launch_bn2<160>(op, s);
+      case 128: return launch_bn2<128>(op, s);
+      default: set_error("gemm: op not planned"); return DLM_ERR_INVALID;
+    }
+  }
   switch (op.bn) {
     case 256: return launch_bn<256>(op, s);
     case 192: return launch_bn<192>(op, s);
@@ -230,6 +356,17 @@ int gemm_launch(const GemmOp& op, cudaStream_t s) {
 }  // namespace dlm
 
 extern "C" {
+
+int dlm_gemm_set_tile_mode(int mode) {
+  const int kernel = mode & 15, bn = mode >> 4;
+  DLM_REQUIRE(kernel >= 0 && kernel <= 2, DLM_ERR_INVALID,
+              "gemm_set_tile_mode: low bits 0 auto, 1 single, 2 pair");
+  DLM_REQUIRE(bn == 0 || bn == 64 || bn == 128 || bn == 160 || bn == 192 || bn == 256,
+              DLM_ERR_INVALID, "gemm_set_tile_mode: forced tile width %d", bn);
+  dlm::g_force_mode = kernel;
+  dlm::g_force_bn = bn;
+  return DLM_OK;
+}
 
 int dlm_gemm_fp16_ex(const void* A, int lda, const void* W, void* C, int ldc, int M, int N, int K,
                      unsigned flags, const void* bias, const void* bias2d, int rows_per_img,

@@ -15,6 +15,7 @@ struct GemmOp {
   CUtensorMap tmB;
   GemmParams p;
   int bn = 0;
+  bool pair = false;  // CTA-pair (cta_group::2) kernel
   int grid = 0;
   long long k_true = 0;  // reduction length before padding to 64 (host-side bookkeeping)
 };
@@ -29,6 +30,13 @@ struct GemmEpilogue {
   int ldb2 = 0;  // row stride of bias2d (0 = N)
   const __half* resid = nullptr;
   int ldr = 0;
+  // internal modes (kEpiRowStats / kEpiLnFold in flags)
+  float2* stats_out = nullptr;      // [M, n_tiles] (mean, M2) per row and N tile of the output
+  const float2* stats_in = nullptr; // producer statistics of the A operand rows
+  int stats_in_parts = 0, stats_in_tile = 0, ln_C = 0;
+  float ln_eps = 1e-5f;
+  const float* ln_u = nullptr;      // [N] sum_k W'[n,k]
+  const float* ln_v = nullptr;      // [N] sum_k beta[k] W[n,k] + bias[n]
 };
 
 // One source of an implicit-GEMM conv K segment.

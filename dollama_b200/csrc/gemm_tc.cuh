@@ -51,8 +51,25 @@ struct GemmParams {
   int ldb2;  // row stride of bias2d
   const __half* resid;
   int ldr;
+  // row statistics of the fp16 output (kEpiRowStats): per row and N tile, (mean, M2) of the tile's
+  // stored values, at stats_out[row * stats_ld + n_tile]
+  float2* stats_out;
+  int stats_ld;
+  // LayerNorm fold (kEpiLnFold): the A operand is the raw x whose LayerNorm the reference applies;
+  // W was prescaled by gamma, and  out = rstd * (acc - mean * ln_u[n]) + ln_v[n]  with mean / rstd
+  // merged from the producer's row statistics stats_in[row * stats_in_parts + i] (tiles of
+  // stats_in_tile columns over ln_C columns)
+  const float2* stats_in;
+  int stats_in_parts, stats_in_tile, ln_C;
+  float ln_eps;
+  const float* ln_u;
+  const float* ln_v;
   int* status;
 };
+
+// Internal epilogue flags (beyond the public DLM_EPI_* bits).
+constexpr unsigned kEpiRowStats = 1u << 8;
+constexpr unsigned kEpiLnFold = 1u << 9;
 
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;
@@ -91,6 +108,150 @@ __device__ __forceinline__ void load_half8_nc(const __half* p, float* f) {
     f[2 * i] = t.x;
     f[2 * i + 1] = t.y;
   }
+}
+
+// Chan's parallel merge of (count, mean, M2) statistics.
+__device__ __forceinline__ void chan_merge(float& n_a, float& mean_a, float& m2_a, float n_b,
+                                           float mean_b, float m2_b) {
+  const float n = n_a + n_b;
+  const float delta = mean_b - mean_a;
+  const float f = n_b / n;
+  mean_a = fmaf(delta, f, mean_a);
+  m2_a = m2_a + m2_b + delta * delta * n_a * f;
+  n_a = n;
+}
+
+// Epilogue of one 128 x BN accumulator held in TMEM (this warp's 32 lanes starting at t_row):
+// LayerNorm fold, alpha scaling, bias / per-image bias / SiLU / GEGLU / residual, fp16 stores,
+// optional row statistics of the stored values.
+template <int BN>
+__device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t t_row, int row, int n0) {
+  const bool row_ok = row < p.M;
+  float ln_mean = 0.0f, ln_rstd = 1.0f;
+  if ((p.flags & kEpiLnFold) && row_ok) {
+    float cnt = 0.0f, mean = 0.0f, m2 = 0.0f;
+    const float2* st = p.stats_in + static_cast<size_t>(row) * p.stats_in_parts;
+    for (int i = 0; i < p.stats_in_parts; ++i) {
+      const int c = min(p.stats_in_tile, p.ln_C - i * p.stats_in_tile);
+      const float2 v = st[i];
+      if (i == 0) {
+        cnt = static_cast<float>(c);
+        mean = v.x;
+        m2 = v.y;
+      } else {
+        chan_merge(cnt, mean, m2, static_cast<float>(c), v.x, v.y);
+      }
+    }
+    ln_mean = mean;
+    ln_rstd = rsqrtf(fmaxf(m2 / static_cast<float>(p.ln_C), 0.0f) + p.ln_eps);
+  }
+  float s_cnt = 0.0f, s_mean = 0.0f, s_m2 = 0.0f;  // row statistics of this tile's outputs
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 32) {
+    if (n0 + c >= p.N) break;
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(t_row + c, r);
+    tmem_ld_wait();
+    if (!row_ok) continue;
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
+    const int n = n0 + c;
+    if (p.flags & kEpiLnFold) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        const float4 u4 = __ldg(reinterpret_cast<const float4*>(p.ln_u + n + j));
+        const float4 w4 = __ldg(reinterpret_cast<const float4*>(p.ln_v + n + j));
+        v[j] = fmaf(ln_rstd, v[j] - ln_mean * u4.x, w4.x);
+        v[j + 1] = fmaf(ln_rstd, v[j + 1] - ln_mean * u4.y, w4.y);
+        v[j + 2] = fmaf(ln_rstd, v[j + 2] - ln_mean * u4.z, w4.z);
+        v[j + 3] = fmaf(ln_rstd, v[j + 3] - ln_mean * u4.w, w4.w);
+      }
+    }
+    if (p.flags & DLM_EPI_BIAS) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) {
+        float b[8];
+        load_half8(p.bias + n + j, b);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) v[j + q] += b[q];
+      }
+    }
+    if (p.flags & DLM_EPI_BIAS2D) {
+      const __half* b2 = p.bias2d + static_cast<size_t>(row / p.rows_per_img) * p.ldb2 + n;
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) {
+        float b[8];
+        load_half8(b2 + j, b);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) v[j + q] += b[q];
+      }
+    }
+    if (p.flags & DLM_EPI_SILU) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = silu_f(v[j]);
+    }
+    if (p.flags & DLM_EPI_GEGLU) {
+      uint32_t o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float a0 = v[4 * j] * gelu_erf_f(v[4 * j + 1]);
+        const float a1 = v[4 * j + 2] * gelu_erf_f(v[4 * j + 3]);
+        o[j] = pack_half2(a0, a1);
+      }
+      uint4* dst = reinterpret_cast<uint4*>(p.out + static_cast<size_t>(row) * p.ldo + (n >> 1));
+      dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+      dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+    } else {
+      if (p.flags & DLM_EPI_RESID) {
+        const __half* rs = p.resid + static_cast<size_t>(row) * p.ldr + n;
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+          float b[8];
+          load_half8_nc(rs + j, b);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) v[j + q] += p.resid_scale * b[q];
+        }
+      }
+      uint32_t o[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) o[j] = pack_half2(v[2 * j], v[2 * j + 1]);
+      uint4* dst = reinterpret_cast<uint4*>(p.out + static_cast<size_t>(row) * p.ldo + n);
+      dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+      dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+      dst[2] = make_uint4(o[8], o[9], o[10], o[11]);
+      dst[3] = make_uint4(o[12], o[13], o[14], o[15]);
+      if (p.flags & kEpiRowStats) {
+        // statistics of the values as stored (fp16), chunk by chunk, merged with Chan's formula
+        float f[32];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&o[j]));
+          f[2 * j] = t.x;
+          f[2 * j + 1] = t.y;
+        }
+        float sum = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) sum += f[j];
+        const float cm = sum * (1.0f / 32.0f);
+        float m2 = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float d = f[j] - cm;
+          m2 = fmaf(d, d, m2);
+        }
+        if (s_cnt == 0.0f) {
+          s_cnt = 32.0f;
+          s_mean = cm;
+          s_m2 = m2;
+        } else {
+          chan_merge(s_cnt, s_mean, s_m2, 32.0f, cm, m2);
+        }
+      }
+    }
+  }
+  if ((p.flags & kEpiRowStats) && row_ok)
+    p.stats_out[static_cast<size_t>(row) * p.stats_ld + n0 / BN] = make_float2(s_mean, s_m2);
 }
 
 template <int BN>
@@ -268,75 +429,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int m0 = (t / p.n_tiles) * kGemmBM;
       const int n0 = (t % p.n_tiles) * BN;
       const int row = m0 + quad * 32 + lane;
-      const bool row_ok = row < p.M;
       const uint32_t t_row = tbase + (static_cast<uint32_t>(quad * 32) << 16) +
                              static_cast<uint32_t>(acc * BN);
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        if (n0 + c >= p.N) break;
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(t_row + c, r);
-        tmem_ld_wait();
-        if (!row_ok) continue;
-        float v[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
-        const int n = n0 + c;
-        if (p.flags & DLM_EPI_BIAS) {
-#pragma unroll
-          for (int j = 0; j < 32; j += 8) {
-            float b[8];
-            load_half8(p.bias + n + j, b);
-#pragma unroll
-            for (int q = 0; q < 8; ++q) v[j + q] += b[q];
-          }
-        }
-        if (p.flags & DLM_EPI_BIAS2D) {
-          const __half* b2 = p.bias2d + static_cast<size_t>(row / p.rows_per_img) * p.ldb2 + n;
-#pragma unroll
-          for (int j = 0; j < 32; j += 8) {
-            float b[8];
-            load_half8(b2 + j, b);
-#pragma unroll
-            for (int q = 0; q < 8; ++q) v[j + q] += b[q];
-          }
-        }
-        if (p.flags & DLM_EPI_SILU) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = silu_f(v[j]);
-        }
-        if (p.flags & DLM_EPI_GEGLU) {
-          uint32_t o[8];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float a0 = v[4 * j] * gelu_erf_f(v[4 * j + 1]);
-            const float a1 = v[4 * j + 2] * gelu_erf_f(v[4 * j + 3]);
-            o[j] = pack_half2(a0, a1);
-          }
-          uint4* dst = reinterpret_cast<uint4*>(p.out + static_cast<size_t>(row) * p.ldo + (n >> 1));
-          dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
-          dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
-        } else {
-          if (p.flags & DLM_EPI_RESID) {
-            const __half* rs = p.resid + static_cast<size_t>(row) * p.ldr + n;
-#pragma unroll
-            for (int j = 0; j < 32; j += 8) {
-              float b[8];
-              load_half8_nc(rs + j, b);
-#pragma unroll
-              for (int q = 0; q < 8; ++q) v[j + q] += p.resid_scale * b[q];
-            }
-          }
-          uint32_t o[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) o[j] = pack_half2(v[2 * j], v[2 * j + 1]);
-          uint4* dst = reinterpret_cast<uint4*>(p.out + static_cast<size_t>(row) * p.ldo + n);
-          dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
-          dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
-          dst[2] = make_uint4(o[8], o[9], o[10], o[11]);
-          dst[3] = make_uint4(o[12], o[13], o[14], o[15]);
-        }
-      }
+      epilogue_tile<BN>(p, t_row, row, n0);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -350,6 +445,213 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tbase, TMEM_COLS);
+  }
+}
+
+
+// ======================================================================================
+// CTA-pair variant (tcgen05 cta_group::2): a cluster of two CTAs on two SMs computes a
+// 256 x BN tile.  Each CTA TMA-loads its own 128 rows of A and its half (BN/2 rows) of B into
+// its own shared memory; the bulk copies of both CTAs complete on the even CTA's `full` barrier;
+// the even CTA issues tcgen05.mma.cta_group::2 (M = 256, N = BN) and commits to the `empty` and
+// `tfull` barriers of both CTAs (multicast commit).  Each CTA's TMEM holds its 128 rows of the
+// accumulator (two buffers of BN columns); each CTA runs the epilogue for its rows and both signal
+// the even CTA's `tempty`.  Per SM this moves half of B through L2 and shared memory compared with
+// the single-CTA kernel, which is what lets the tensor core run at full rate for BN = 256.
+// Loads carry no multicast qualifier: every CTA fetches its own operands.
+// ======================================================================================
+
+__host__ __device__ constexpr int gemm2_stage_bytes(int BN) { return (kGemmBM + BN / 2) * kGemmBK * 2; }
+__host__ __device__ constexpr int gemm2_stages(int BN) {
+  return ((225 * 1024 - 2048) / gemm2_stage_bytes(BN)) > 8 ? 8
+                                                             : ((225 * 1024 - 2048) / gemm2_stage_bytes(BN));
+}
+__host__ __device__ constexpr int gemm2_smem_bytes(int BN) {
+  return gemm2_stages(BN) * gemm2_stage_bytes(BN) + 1024 + 256;
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
+                    const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB,
+                    const GemmParams p) {
+  constexpr int BNH = BN / 2;
+  constexpr int A_BYTES = kGemmBM * kGemmBK * 2;
+  constexpr int B_BYTES = BNH * kGemmBK * 2;
+  constexpr int STAGES = gemm2_stages(BN);
+  constexpr uint32_t TMEM_COLS = gemm_tmem_cols(BN);
+  static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "pair UMMA N");
+  static_assert(BNH % 8 == 0, "B half must hold whole 8-row swizzle atoms");
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 8);  // 4 epilogue warps in each of the two CTAs
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA0);
+    if (p.amode == 1) {
+      tma_prefetch_desc(&tmA1);
+      tma_prefetch_desc(&tmA2);
+    }
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc2(tmem_slot, TMEM_COLS);
+    tmem_relinquish2();
+  }
+  tc_fence_before();
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  const int num_tiles = p.m_tiles * p.n_tiles;  // m tiles of 256 rows
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = pair; t < num_tiles && ok; t += npairs) {
+        const int m0 = (t / p.n_tiles) * (2 * kGemmBM) + static_cast<int>(rank) * kGemmBM;
+        const int nb = (t % p.n_tiles) * BN + static_cast<int>(rank) * BNH;
+        int img = 0, oh0 = 0, ow0 = 0;
+        if (p.amode == 1) {
+          const int hw = p.oH * p.oW;
+          img = m0 / hw;
+          const int rem = m0 - img * hw;
+          oh0 = rem / p.oW;
+          ow0 = rem - oh0 * p.oW;
+        }
+        int kb = 0;
+        const int nseg = p.amode == 0 ? 1 : p.nseg;
+        for (int s = 0; s < nseg && ok; ++s) {
+          const ConvSeg sg = p.seg[s];
+          const CUtensorMap* am = p.amode == 0 ? &tmA0 : (sg.map == 0 ? &tmA0 : (sg.map == 1 ? &tmA1 : &tmA2));
+          const int ntaps = p.amode == 0 ? 1 : (sg.kind == 1 ? 1 : 9);
+          const int ncb = p.amode == 0 ? p.num_kb : sg.cblocks;
+          for (int tap = 0; tap < ntaps && ok; ++tap) {
+            const int kh = tap / 3, kw = tap - (tap / 3) * 3;
+            for (int cb = 0; cb < ncb; ++cb) {
+              if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status, kDevTimeoutProducer)) {
+                ok = false;
+                break;
+              }
+              if (leader) mbar_arrive_expect_tx(&full[stage], 2 * (A_BYTES + B_BYTES));
+              const uint32_t fb = pair_leader_addr(&full[stage]);
+              uint8_t* dstA = sA + stage * A_BYTES;
+              if (p.amode == 0) {
+                tma2_load_2d(dstA, am, fb, cb * kGemmBK, m0);
+              } else if (sg.kind == 0) {
+                tma2_load_4d(dstA, am, fb, cb * 64, ow0 + kw - 1, oh0 + kh - 1, img);
+              } else if (sg.kind == 1) {
+                tma2_load_4d(dstA, am, fb, cb * 64, ow0, oh0, img);
+              } else {
+                const int pr = (kh == 1) ? 0 : 1, dr = (kh == 0) ? -1 : 0;
+                const int pc = (kw == 1) ? 0 : 1, dc = (kw == 0) ? -1 : 0;
+                tma2_load_5d(dstA, am, fb, cb * 64, ow0 + dc, oh0 + dr, img, pr * 2 + pc);
+              }
+              tma2_load_2d(sB + stage * B_BYTES, &tmB, fb, kb * kGemmBK, nb);
+              ++kb;
+              if (++stage == STAGES) {
+                stage = 0;
+                phase ^= 1;
+              }
+            }
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (even CTA)
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(2 * kGemmBM, BN, false);
+      int stage = 0;
+      uint32_t phase = 0;
+      int i = 0;
+      bool ok = true;
+      for (int t = pair; t < num_tiles && ok; t += npairs, ++i) {
+        const int acc = i & 1;
+        const uint32_t acc_phase = (i >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, p.status, kDevTimeoutMma)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tbase + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.status, kDevTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + stage * A_BYTES);
+          const uint32_t b_base = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+          for (int k = 0; k < kGemmBK / 16; ++k) {
+            umma2_f16_ss(d_tmem, sw128_desc(a_base + k * 32, 16, 1024),
+                         sw128_desc(b_base + k * 32, 16, 1024), idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma2_commit_mc(&empty[stage], 0x3);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (ok) umma2_commit_mc(&tfull[acc], 0x3);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 2..5, both CTAs)
+    const int quad = warp & 3;
+    int i = 0;
+    for (int t = pair; t < num_tiles; t += npairs, ++i) {
+      const int acc = i & 1;
+      const uint32_t acc_phase = (i >> 1) & 1;
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status, kDevTimeoutEpilogue)) break;
+      tc_fence_after();
+      const int m0 = (t / p.n_tiles) * (2 * kGemmBM) + static_cast<int>(rank) * kGemmBM;
+      const int n0 = (t % p.n_tiles) * BN;
+      const int row = m0 + quad * 32 + lane;
+      const uint32_t t_row = tbase + (static_cast<uint32_t>(quad * 32) << 16) +
+                             static_cast<uint32_t>(acc * BN);
+      epilogue_tile<BN>(p, t_row, row, n0);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(&tempty[acc], 0);
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync_all();
+  if (*abort_flag) drain_sleep(200000);
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc2(tbase, TMEM_COLS);
   }
 }
 

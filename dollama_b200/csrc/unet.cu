@@ -115,6 +115,35 @@ __global__ void add_half_kernel(const __half* __restrict__ a, const __half* __re
   if (i < n) y[i] = __float2half_rn(__half2float(a[i]) + __half2float(b[i]));
 }
 
+// LayerNorm fold of a consumer weight, in place, one warp per output row n:
+//   W'[n,k] = fp16(W[n,k] * gamma[k]);  u[n] = sum_k W'[n,k];  v[n] = sum_k beta[k] W[n,k] + bias[n]
+// so that  LN(x) W^T + bias = rstd * (x W'^T - mean * u) + v.
+__global__ void ln_fold_kernel(__half* __restrict__ w, int N, int K, const __half* __restrict__ gamma,
+                               const __half* __restrict__ beta, const __half* __restrict__ bias,
+                               float* __restrict__ u, float* __restrict__ v) {
+  const int n = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (n >= N) return;
+  __half* row = w + static_cast<size_t>(n) * K;
+  double su = 0.0, sv = 0.0;
+  for (int k = lane; k < K; k += 32) {
+    const float x = __half2float(row[k]);
+    const __half wp = __float2half_rn(x * __half2float(gamma[k]));
+    row[k] = wp;
+    su += static_cast<double>(__half2float(wp));
+    sv += static_cast<double>(__half2float(beta[k])) * static_cast<double>(x);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    su += __shfl_xor_sync(0xffffffffu, su, o);
+    sv += __shfl_xor_sync(0xffffffffu, sv, o);
+  }
+  if (lane == 0) {
+    u[n] = static_cast<float>(su);
+    v[n] = static_cast<float>(sv + (bias ? static_cast<double>(__half2float(bias[n])) : 0.0));
+  }
+}
+
 int blocks_for(size_t n, int t) { return static_cast<int>((n + t - 1) / t); }
 
 constexpr int kCtxTokens = 77;
@@ -479,6 +508,27 @@ int UNetModel::prepare_weights(cudaStream_t s) {
       w_[b + "ff.geglu.weight"] = gw;
       w_[b + "ff.geglu.bias"] = gb;
       if (!copy(b + "ff.net.2.weight", static_cast<size_t>(c) * ff)) return fail("ff2");
+      // fold the three LayerNorms into the weights of the GEMMs that consume them
+      struct Fold {
+        const char* wname;
+        const char* norm;
+        int rows;
+        const char* bias;
+      };
+      const Fold folds[3] = {{"attn1.qkv", "norm1", 3 * c, nullptr},
+                             {"attn2.to_q.weight", "norm2", c, nullptr},
+                             {"ff.geglu.weight", "norm3", 2 * ff, "ff.geglu.bias"}};
+      for (const Fold& f : folds) {
+        float* fu = reinterpret_cast<float*>(wtake(2 * static_cast<size_t>(f.rows)));
+        float* fv = reinterpret_cast<float*>(wtake(2 * static_cast<size_t>(f.rows)));
+        if (!fu || !fv) return fail("ln fold");
+        ln_fold_kernel<<<blocks_for(static_cast<size_t>(f.rows) * 32, 256), 256, 0, s>>>(
+            w_[b + f.wname], f.rows, c, W(b + f.norm + ".weight"), W(b + f.norm + ".bias"),
+            f.bias ? W(b + f.bias) : nullptr, fu, fv);
+        DLM_CHECK_CUDA(cudaGetLastError());
+        wf_[b + f.wname + ".u"] = fu;
+        wf_[b + f.wname + ".v"] = fv;
+      }
     }
     return DLM_OK;
   };
@@ -507,6 +557,11 @@ int UNetModel::prepare_weights(cudaStream_t s) {
 const __half* UNetModel::W(const std::string& n) const {
   auto it = w_.find(n);
   return it == w_.end() ? nullptr : it->second;
+}
+
+const float* UNetModel::WF(const std::string& n) const {
+  auto it = wf_.find(n);
+  return it == wf_.end() ? nullptr : it->second;
 }
 
 // ================================================================== plan
@@ -613,11 +668,12 @@ int UNetModel::plan_resnet(const ResnetInfo& rs, const __half* x1, int C1, const
 }
 
 int UNetModel::plan_linear(const __half* A, int lda, const __half* Wt, int M, int N, int K, __half* C,
-                           int ldc, const GemmEpilogue& e) {
+                           int ldc, const GemmEpilogue& e, int* bn_out) {
   if (dry_) return DLM_OK;
   GemmOp g;
   int rc = gemm_plan_dense(&g, A, lda, Wt, M, N, K, C, ldc, e);
   if (rc != DLM_OK) return rc;
+  if (bn_out) *bn_out = g.bn;
   push_gemm(g);
   return DLM_OK;
 }
@@ -642,40 +698,58 @@ int UNetModel::plan_attn(const __half* q, int ldq, const __half* k, int ldk, con
 }
 
 // Transformer2D, in place on x [B*HW, C] (token-major == NHWC).
+// Transformer2D, in place on x [B*HW, C] (token-major == NHWC).
+// The three LayerNorms of each block are folded into the GEMMs that consume them (q/k/v, cross q,
+// GEGLU proj): their weights were prescaled by gamma at load, they read the raw hidden state h,
+// and their epilogue applies  rstd * (acc - mean * u) + v  with the row mean / rstd merged from
+// the (mean, M2) statistics that the GEMM which last wrote h emitted from its epilogue.  No
+// LayerNorm kernel runs and no normalised copy of h is written.
 int UNetModel::plan_t2d(const std::string& p, __half* x, int C, int H, int Wd, int layers) {
   const int S = H * Wd, M = B_ * S, heads = C / 64;
   __half* g = t_gn_;     // [M, C]
   __half* h = t_h_;      // [M, C] running hidden state
-  __half* n = t_n_;      // [M, C] LN output
   __half* qkv = t_qkv_;  // [M, 3C]
   __half* ao = t_ao_;    // [M, C] attention output
   __half* kv = t_kv_;    // [B*77, 2C]
   __half* ff = t_ff_;    // [M, 4C]
+  int stats_bn = 0;      // N tile of the GEMM that last wrote h (its statistics tiles)
   int rc = plan_gn(x, C, nullptr, 0, S, p + "norm", 1e-6f, false, g);
   if (rc != DLM_OK) return rc;
   GemmEpilogue eb;
-  eb.flags = DLM_EPI_BIAS;
+  eb.flags = DLM_EPI_BIAS | kEpiRowStats;
+  eb.stats_out = ln_stats_;
   if (!dry_) eb.bias = W(p + "proj_in.bias");
-  rc = plan_linear(g, C, W(p + "proj_in.weight"), M, C, C, h, C, eb);
+  rc = plan_linear(g, C, W(p + "proj_in.weight"), M, C, C, h, C, eb, &stats_bn);
   if (rc != DLM_OK) return rc;
+  auto ln_fold = [&](const std::string& wname, unsigned extra) {
+    GemmEpilogue e;
+    e.flags = kEpiLnFold | extra;
+    e.stats_in = ln_stats_;
+    e.stats_in_tile = stats_bn > 0 ? stats_bn : C;
+    e.stats_in_parts = (C + e.stats_in_tile - 1) / e.stats_in_tile;
+    e.ln_C = C;
+    e.ln_eps = 1e-5f;
+    e.ln_u = WF(wname + ".u");
+    e.ln_v = WF(wname + ".v");
+    return e;
+  };
   for (int l = 0; l < layers; ++l) {
     const std::string b = p + "transformer_blocks." + std::to_string(l) + ".";
-    // self attention
-    if (!dry_) push_ln({h, W(b + "norm1.weight"), W(b + "norm1.bias"), n, M, C, 1e-5f});
-    rc = plan_linear(n, C, W(b + "attn1.qkv"), M, 3 * C, C, qkv, 3 * C, GemmEpilogue{});
+    // self attention: LN1 folded into the q/k/v GEMM
+    rc = plan_linear(h, C, W(b + "attn1.qkv"), M, 3 * C, C, qkv, 3 * C, ln_fold(b + "attn1.qkv", 0));
     if (rc != DLM_OK) return rc;
     rc = plan_attn(qkv, 3 * C, qkv + C, 3 * C, qkv + 2 * C, 3 * C, ao, C, heads, S, S);
     if (rc != DLM_OK) return rc;
     GemmEpilogue er;
-    er.flags = DLM_EPI_BIAS | DLM_EPI_RESID;
+    er.flags = DLM_EPI_BIAS | DLM_EPI_RESID | kEpiRowStats;
     er.resid = h;
     er.ldr = C;
+    er.stats_out = ln_stats_;
     if (!dry_) er.bias = W(b + "attn1.to_out.0.bias");
-    rc = plan_linear(ao, C, W(b + "attn1.to_out.0.weight"), M, C, C, h, C, er);
+    rc = plan_linear(ao, C, W(b + "attn1.to_out.0.weight"), M, C, C, h, C, er, &stats_bn);
     if (rc != DLM_OK) return rc;
-    // cross attention
-    if (!dry_) push_ln({h, W(b + "norm2.weight"), W(b + "norm2.bias"), n, M, C, 1e-5f});
-    rc = plan_linear(n, C, W(b + "attn2.to_q.weight"), M, C, C, qkv, C, GemmEpilogue{});
+    // cross attention: LN2 folded into the q GEMM
+    rc = plan_linear(h, C, W(b + "attn2.to_q.weight"), M, C, C, qkv, C, ln_fold(b + "attn2.to_q.weight", 0));
     if (rc != DLM_OK) return rc;
     rc = plan_linear(ehs_, kCtxDim, W(b + "attn2.kv"), B_ * kCtxTokens, 2 * C, kCtxDim, kv, 2 * C,
                      GemmEpilogue{});
@@ -683,17 +757,14 @@ int UNetModel::plan_t2d(const std::string& p, __half* x, int C, int H, int Wd, i
     rc = plan_attn(qkv, C, kv, 2 * C, kv + C, 2 * C, ao, C, heads, S, kCtxTokens);
     if (rc != DLM_OK) return rc;
     if (!dry_) er.bias = W(b + "attn2.to_out.0.bias");
-    rc = plan_linear(ao, C, W(b + "attn2.to_out.0.weight"), M, C, C, h, C, er);
+    rc = plan_linear(ao, C, W(b + "attn2.to_out.0.weight"), M, C, C, h, C, er, &stats_bn);
     if (rc != DLM_OK) return rc;
-    // GEGLU feed-forward
-    if (!dry_) push_ln({h, W(b + "norm3.weight"), W(b + "norm3.bias"), n, M, C, 1e-5f});
-    GemmEpilogue eg;
-    eg.flags = DLM_EPI_BIAS | DLM_EPI_GEGLU;
-    if (!dry_) eg.bias = W(b + "ff.geglu.bias");
-    rc = plan_linear(n, C, W(b + "ff.geglu.weight"), M, 8 * C, C, ff, 4 * C, eg);
+    // GEGLU feed-forward: LN3 folded into the proj GEMM (its bias folded into v)
+    rc = plan_linear(h, C, W(b + "ff.geglu.weight"), M, 8 * C, C, ff, 4 * C,
+                     ln_fold(b + "ff.geglu.weight", DLM_EPI_GEGLU));
     if (rc != DLM_OK) return rc;
     if (!dry_) er.bias = W(b + "ff.net.2.bias");
-    rc = plan_linear(ff, 4 * C, W(b + "ff.net.2.weight"), M, C, 4 * C, h, C, er);
+    rc = plan_linear(ff, 4 * C, W(b + "ff.net.2.weight"), M, C, 4 * C, h, C, er, &stats_bn);
     if (rc != DLM_OK) return rc;
   }
   GemmEpilogue eo;
@@ -752,6 +823,8 @@ int UNetModel::build(bool dry) {
   t_ao_ = act(tMC);
   t_kv_ = act(static_cast<size_t>(B) * kCtxTokens * 2 * C2);
   t_ff_ = act(4 * tMC);
+  // per-row (mean, M2) statistics tiles of the hidden state, at most C / 64 tiles per row
+  ln_stats_ = reinterpret_cast<float2*>(act(4 * (tMC / 64 + 64) * 2));
   planes_ = act(std::max(P0 * C0, P1 * C1));
   upbuf_ = act(std::max(P1 * C2, P0 * C1));
   out32_ = act(P0 * 32);

@@ -77,6 +77,7 @@ class UNetModel {
   int prepare_weights(cudaStream_t s);
   const __half* src(const std::string& n) const;
   const __half* W(const std::string& n) const;
+  const float* WF(const std::string& n) const;
   __half* wtake(size_t elems);
   __half* act(size_t elems);
   int plan(int B, int H, int W);
@@ -90,7 +91,7 @@ class UNetModel {
                   int W, __half* out);
   int plan_t2d(const std::string& p, __half* x, int C, int H, int W, int layers);
   int plan_linear(const __half* A, int lda, const __half* Wt, int M, int N, int K, __half* C, int ldc,
-                  const GemmEpilogue& e);
+                  const GemmEpilogue& e, int* bn_out = nullptr);
   int plan_attn(const __half* q, int ldq, const __half* k, int ldk, const __half* v, int ldv,
                 __half* o, int ldo, int heads, int Sq, int Sk);
   void push_gemm(const GemmOp& g, double flops = -1.0);
@@ -103,6 +104,7 @@ class UNetModel {
   // weights
   std::unordered_map<std::string, const __half*> src_;  // caller's tensors (create only)
   std::unordered_map<std::string, __half*> w_;          // prepared tensors
+  std::unordered_map<std::string, float*> wf_;          // prepared fp32 vectors (LN fold u / v)
   void* wbuf_ = nullptr;
   size_t wcap_ = 0, woff_ = 0;
   std::vector<ResnetInfo> resnets_;
@@ -132,6 +134,7 @@ class UNetModel {
          *t_kv_ = nullptr, *t_ff_ = nullptr;
   __half *planes_ = nullptr, *upbuf_ = nullptr, *out32_ = nullptr;
   float2* gn_partials_ = nullptr;
+  float2* ln_stats_ = nullptr;
   size_t gn_partial_cap_ = 0;
 };
 

@@ -78,6 +78,12 @@ int dlm_gemm_fp16_ex(const void* A, int lda, const void* W, void* C, int ldc, in
                      unsigned flags, const void* bias, const void* bias2d, int rows_per_img,
                      const void* residual, int ldr, void* stream);
 
+/* Tile-kernel selection for the GEMM / conv entry points planned after the call (process-wide):
+ * mode & 15: 0 = automatic (cost model), 1 = single-CTA kernel only, 2 = CTA-pair
+ * (cta_group::2) kernel where M > 128; mode >> 4: forced N tile width (0 = cost model; 64, 128,
+ * 160, 192, 256).  For tests and A/B measurements. */
+int dlm_gemm_set_tile_mode(int mode);
+
 /* ------------------------------------------------------------------ conv2d (implicit GEMM)
  *
  * Replaces launch_conv2d (reference src/kernels/conv2d.cuh:38-40, conv2d.cu:757) for the

@@ -40,6 +40,13 @@ def run_conv(x_nchw, w, b, ksize, stride):
     return out.permute(0, 3, 1, 2)
 
 
+@pytest.fixture(params=[0, 1, 2], ids=["auto", "single", "pair"])
+def tile_mode(request):
+    L.call("dlm_gemm_set_tile_mode", request.param)
+    yield request.param
+    L.call("dlm_gemm_set_tile_mode", 0)
+
+
 @pytest.mark.parametrize("N,Cin,H,W,Cout,k,s", [
     (1, 64, 16, 16, 64, 3, 1),
     (2, 320, 32, 32, 320, 3, 1),
@@ -49,7 +56,7 @@ def run_conv(x_nchw, w, b, ksize, stride):
     (2, 320, 64, 64, 320, 3, 2),
     (2, 640, 32, 32, 1280, 1, 1),
 ])
-def test_conv(N, Cin, H, W, Cout, k, s):
+def test_conv(N, Cin, H, W, Cout, k, s, tile_mode):
     g = torch.Generator().manual_seed(N * 1000 + Cin + H)
     x = torch.randn(N, Cin, H, W, generator=g).half().cuda()
     bound = (Cin * k * k) ** -0.5

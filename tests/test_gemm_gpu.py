@@ -28,11 +28,18 @@ def _rand(*shape, scale=1.0, seed=0):
     return (torch.randn(*shape, generator=g) * scale).half().cuda()
 
 
+@pytest.fixture(params=[0, 1, 2], ids=["auto", "single", "pair"])
+def tile_mode(request):
+    L.call("dlm_gemm_set_tile_mode", request.param)
+    yield request.param
+    L.call("dlm_gemm_set_tile_mode", 0)
+
+
 @pytest.mark.parametrize("M,N,K", [(128, 128, 64), (256, 320, 640), (8192, 640, 640),
                                    (2048, 1280, 1280), (154, 1280, 2048), (300, 96, 72),
                                    (8192, 1920, 640), (2048, 10240, 1280),
                                    (2, 1280, 2816), (64, 256, 128)])
-def test_gemm_plain(M, N, K):
+def test_gemm_plain(M, N, K, tile_mode):
     A = _rand(M, K, seed=1)
     W = _rand(N, K, scale=K ** -0.5, seed=2)
     C = torch.empty(M, N, dtype=torch.float16, device="cuda")
@@ -43,7 +50,7 @@ def test_gemm_plain(M, N, K):
     assert err < 2e-3, f"max rel err {err}"
 
 
-def test_gemm_bias_resid_inplace():
+def test_gemm_bias_resid_inplace(tile_mode):
     M, N, K = 1024, 640, 640
     A = _rand(M, K, seed=3)
     W = _rand(N, K, scale=K ** -0.5, seed=4)
@@ -56,7 +63,7 @@ def test_gemm_bias_resid_inplace():
     assert max_rel_err(X, ref) < 2e-3
 
 
-def test_gemm_geglu_interleaved():
+def test_gemm_geglu_interleaved(tile_mode):
     M, C = 512, 320
     ff = 4 * C
     A = _rand(M, C, seed=7)
@@ -74,7 +81,7 @@ def test_gemm_geglu_interleaved():
     assert max_rel_err(out, ref) < 2e-3
 
 
-def test_gemm_bias2d_silu():
+def test_gemm_bias2d_silu(tile_mode):
     M, N, K, rows = 512, 256, 128, 128
     A = _rand(M, K, seed=10)
     W = _rand(N, K, scale=K ** -0.5, seed=11)
