@@ -121,6 +121,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
+  griddep_launch_dependents();
+  griddep_wait();  // q / k / v are written by the previous kernel
 
   if (warp == 8) {
     // ------------------------------------------------------------ TMA producer
@@ -405,8 +407,17 @@ int attn_launch(const AttnOp& op, cudaStream_t s) {
                                         kAttnSmem));
     attr_set[dev] = true;
   }
-  attn_fwd_kernel<<<op.grid, kAttnThreads, kAttnSmem, s>>>(op.tmQ, op.tmK, op.tmV, op.p);
-  DLM_CHECK_CUDA(cudaGetLastError());
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(op.grid, 1, 1);
+  cfg.blockDim = dim3(kAttnThreads, 1, 1);
+  cfg.dynamicSmemBytes = kAttnSmem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  DLM_CHECK_CUDA(cudaLaunchKernelEx(&cfg, attn_fwd_kernel, op.tmQ, op.tmK, op.tmV, op.p));
   return DLM_OK;
 }
 

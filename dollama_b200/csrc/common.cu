@@ -1,5 +1,6 @@
 // Host-side common pieces (see common.h) and the library-level C-ABI entry points.
 #include <cstdarg>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -29,6 +30,16 @@ void set_error(const char* fmt, ...) {
   va_start(ap, fmt);
   vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
   va_end(ap);
+}
+
+bool pdl_enabled() {
+  // Programmatic dependent launch is opt-in (DLM_PDL=1): measured on B200 it lengthened the UNet
+  // step (early-resident dependent CTAs wait on griddepcontrol while the primary drains).
+  static const bool on = [] {
+    const char* e = std::getenv("DLM_PDL");
+    return e && e[0] == '1';
+  }();
+  return on;
 }
 
 int num_sms() {

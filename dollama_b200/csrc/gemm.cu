@@ -19,9 +19,18 @@ int launch_bn(const GemmOp& op, cudaStream_t s) {
                                         gemm_smem_bytes(BN)));
     attr_set[dev] = true;
   }
-  gemm_tc_kernel<BN><<<op.grid, kGemmThreads, gemm_smem_bytes(BN), s>>>(op.tmA[0], op.tmA[1],
-                                                                         op.tmA[2], op.tmB, op.p);
-  DLM_CHECK_CUDA(cudaGetLastError());
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(op.grid, 1, 1);
+  cfg.blockDim = dim3(kGemmThreads, 1, 1);
+  cfg.dynamicSmemBytes = gemm_smem_bytes(BN);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  DLM_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN>, op.tmA[0], op.tmA[1], op.tmA[2],
+                                    op.tmB, op.tmC, op.p));
   return DLM_OK;
 }
 
@@ -32,15 +41,17 @@ int launch_bn2(const GemmOp& op, cudaStream_t s) {
   cfg.blockDim = dim3(kGemmThreads, 1, 1);
   cfg.dynamicSmemBytes = gemm2_smem_bytes(BN);
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
   DLM_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc2_kernel<BN>, op.tmA[0], op.tmA[1], op.tmA[2],
-                                    op.tmB, op.p));
+                                    op.tmB, op.tmC, op.p));
   return DLM_OK;
 }
 
@@ -134,6 +145,18 @@ bool bn_supported(int bn, bool pair) {
   return bn == 256 || bn == 192 || bn == 160 || bn == 128 || bn == 64;
 }
 
+// Output map for the staged epilogue: boxes of 32 rows x 32 columns (64-byte swizzle), or
+// 32 rows x 16 columns (32-byte swizzle) for GEGLU's half-width output.
+bool make_out_map(CUtensorMap* m, const __half* C, int M, int N, int ldc, unsigned flags) {
+  const bool geglu = (flags & DLM_EPI_GEGLU) != 0;
+  const uint64_t cols = geglu ? N / 2 : N;
+  const uint64_t dims[2] = {cols, static_cast<uint64_t>(M)};
+  const uint64_t strides[1] = {static_cast<uint64_t>(ldc) * 2};
+  const uint32_t box[2] = {geglu ? 16u : 32u, 32u};
+  return encode_tmap(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, C, dims, strides, box,
+                     geglu ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B);
+}
+
 void fill_epilogue(GemmParams& p, const GemmEpilogue& e, int N) {
   p.flags = e.flags;
   p.alpha = e.alpha;
@@ -209,6 +232,7 @@ int gemm_plan_dense(GemmOp* op, const __half* A, int lda, const __half* W, int M
   op->tmA[1] = op->tmA[0];
   op->tmA[2] = op->tmA[0];
   if (!tmap_2d_f16(&op->tmB, W, N, K, K, pair ? bn / 2 : bn, kGemmBK)) return DLM_ERR_CUDA;
+  if (!make_out_map(&op->tmC, C, M, N, ldc, epi.flags)) return DLM_ERR_CUDA;
   GemmParams& p = op->p;
   p.M = M;
   p.N = N;
@@ -282,6 +306,7 @@ int gemm_plan_conv(GemmOp* op, int Nb, int oH, int oW, const ConvSource* srcs, i
   }
   for (int s = nsrc; s < 3; ++s) op->tmA[s] = op->tmA[0];
   if (!tmap_2d_f16(&op->tmB, W, Cout, ktot, ktot, pair ? bn / 2 : bn, kGemmBK)) return DLM_ERR_CUDA;
+  if (!make_out_map(&op->tmC, C, M, Cout, ldc, epi.flags)) return DLM_ERR_CUDA;
   p.M = M;
   p.N = Cout;
   p.num_kb = static_cast<int>(ktot / 64);

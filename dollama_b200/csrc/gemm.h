@@ -13,6 +13,7 @@ namespace dlm {
 struct GemmOp {
   CUtensorMap tmA[3];
   CUtensorMap tmB;
+  CUtensorMap tmC;  // output, 32-row boxes for the staged epilogue stores
   GemmParams p;
   int bn = 0;
   bool pair = false;  // CTA-pair (cta_group::2) kernel

@@ -76,12 +76,17 @@ constexpr int kGemmBK = 64;
 constexpr int kGemmThreads = 192;
 
 __host__ __device__ constexpr int gemm_stage_bytes(int BN) { return (kGemmBM + BN) * kGemmBK * 2; }
+// Epilogue staging: each of the 4 epilogue warps owns two 2 KB buffers (32 rows x 32 fp16 columns,
+// 64-byte swizzled) through which its outputs leave by TMA bulk stores.
+constexpr int kStageBytesPerWarp = 4096;
+constexpr int kEpiStageBytes = 4 * kStageBytesPerWarp;
 __host__ __device__ constexpr int gemm_stages(int BN) {
-  return ((225 * 1024 - 2048) / gemm_stage_bytes(BN)) > 8 ? 8
-                                                            : ((225 * 1024 - 2048) / gemm_stage_bytes(BN));
+  return ((225 * 1024 - 2048 - kEpiStageBytes) / gemm_stage_bytes(BN)) > 8
+             ? 8
+             : ((225 * 1024 - 2048 - kEpiStageBytes) / gemm_stage_bytes(BN));
 }
 __host__ __device__ constexpr int gemm_smem_bytes(int BN) {
-  return gemm_stages(BN) * gemm_stage_bytes(BN) + 1024 + 256;
+  return gemm_stages(BN) * gemm_stage_bytes(BN) + kEpiStageBytes + 1024 + 256;
 }
 __host__ __device__ constexpr uint32_t gemm_tmem_cols(int BN) {
   return (2 * BN) <= 32 ? 32 : (2 * BN) <= 64 ? 64 : (2 * BN) <= 128 ? 128 : (2 * BN) <= 256 ? 256 : 512;
@@ -121,12 +126,20 @@ __device__ __forceinline__ void chan_merge(float& n_a, float& mean_a, float& m2_
   n_a = n;
 }
 
-// Epilogue of one 128 x BN accumulator held in TMEM (this warp's 32 lanes starting at t_row):
-// LayerNorm fold, alpha scaling, bias / per-image bias / SiLU / GEGLU / residual, fp16 stores,
-// optional row statistics of the stored values.
+// Epilogue of one 128 x BN accumulator held in TMEM (this warp's 32 lanes starting at t_row,
+// output rows m_base .. m_base+31): LayerNorm fold, alpha scaling, bias / per-image bias / SiLU /
+// GEGLU / residual, optional row statistics of the stored values.  Each 32-column chunk leaves
+// through the warp's shared-memory staging buffer (swizzled so that row-per-thread writes and
+// the bulk copy are bank-conflict free) as one TMA bulk store of 32 rows x 32 columns (16 for
+// GEGLU); the residual chunk is read with coalesced 16-byte loads and transposed through the same
+// buffer.  Rows >= M are clipped by the store.
 template <int BN>
-__device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t t_row, int row, int n0) {
+__device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t t_row, int row, int n0,
+                                              int m_base, uint8_t* stage, const CUtensorMap* tmC,
+                                              int& sbuf) {
+  const int lane = threadIdx.x & 31;
   const bool row_ok = row < p.M;
+  const bool geglu = (p.flags & DLM_EPI_GEGLU) != 0;
   float ln_mean = 0.0f, ln_rstd = 1.0f;
   if ((p.flags & kEpiLnFold) && row_ok) {
     float cnt = 0.0f, mean = 0.0f, m2 = 0.0f;
@@ -145,6 +158,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t t_ro
     ln_mean = mean;
     ln_rstd = rsqrtf(fmaxf(m2 / static_cast<float>(p.ln_C), 0.0f) + p.ln_eps);
   }
+  const int img = (row_ok ? row : p.M - 1) / p.rows_per_img;
   float s_cnt = 0.0f, s_mean = 0.0f, s_m2 = 0.0f;  // row statistics of this tile's outputs
 #pragma unroll 1
   for (int c = 0; c < BN; c += 32) {
@@ -152,7 +166,6 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t t_ro
     uint32_t r[32];
     tmem_ld_32x32b_x32(t_row + c, r);
     tmem_ld_wait();
-    if (!row_ok) continue;
     float v[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
@@ -178,7 +191,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t t_ro
       }
     }
     if (p.flags & DLM_EPI_BIAS2D) {
-      const __half* b2 = p.bias2d + static_cast<size_t>(row / p.rows_per_img) * p.ldb2 + n;
+      const __half* b2 = p.bias2d + static_cast<size_t>(img) * p.ldb2 + n;
 #pragma unroll
       for (int j = 0; j < 32; j += 8) {
         float b[8];
@@ -191,7 +204,11 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t t_ro
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = silu_f(v[j]);
     }
-    if (p.flags & DLM_EPI_GEGLU) {
+    uint8_t* buf = stage + sbuf * 2048;
+    // the bulk store that last used this buffer must have finished reading it
+    if (lane == 0) bulk_wait_read_le1();
+    __syncwarp();
+    if (geglu) {
       uint32_t o[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
@@ -199,29 +216,47 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t t_ro
         const float a1 = v[4 * j + 2] * gelu_erf_f(v[4 * j + 3]);
         o[j] = pack_half2(a0, a1);
       }
-      uint4* dst = reinterpret_cast<uint4*>(p.out + static_cast<size_t>(row) * p.ldo + (n >> 1));
-      dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
-      dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+      // 32-byte rows, 32-byte swizzle: 16-byte chunk q of row r at q ^ ((r >> 2) & 1)
+      uint8_t* rb = buf + lane * 32;
+      const int sw = (lane >> 2) & 1;
+      *reinterpret_cast<uint4*>(rb + ((0 ^ sw) * 16)) = make_uint4(o[0], o[1], o[2], o[3]);
+      *reinterpret_cast<uint4*>(rb + ((1 ^ sw) * 16)) = make_uint4(o[4], o[5], o[6], o[7]);
     } else {
+      // 64-byte rows, 64-byte swizzle: 16-byte chunk q of row r at q ^ ((r >> 1) & 3)
       if (p.flags & DLM_EPI_RESID) {
-        const __half* rs = p.resid + static_cast<size_t>(row) * p.ldr + n;
 #pragma unroll
-        for (int j = 0; j < 32; j += 8) {
-          float b[8];
-          load_half8_nc(rs + j, b);
-#pragma unroll
-          for (int q = 0; q < 8; ++q) v[j + q] += p.resid_scale * b[q];
+        for (int i = 0; i < 4; ++i) {
+          const int rr = (lane >> 2) + 8 * i, q = lane & 3;
+          const int grow = m_base + rr;
+          uint4 u = make_uint4(0, 0, 0, 0);
+          if (grow < p.M)
+            u = *reinterpret_cast<const uint4*>(p.resid + static_cast<size_t>(grow) * p.ldr + n + q * 8);
+          *reinterpret_cast<uint4*>(buf + rr * 64 + ((q ^ ((rr >> 1) & 3)) * 16)) = u;
         }
+        __syncwarp();
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 u = *reinterpret_cast<const uint4*>(buf + lane * 64 + ((q ^ ((lane >> 1) & 3)) * 16));
+          const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float2 t = __half22float2(h[k]);
+            v[q * 8 + 2 * k] += p.resid_scale * t.x;
+            v[q * 8 + 2 * k + 1] += p.resid_scale * t.y;
+          }
+        }
+        __syncwarp();
       }
       uint32_t o[16];
 #pragma unroll
       for (int j = 0; j < 16; ++j) o[j] = pack_half2(v[2 * j], v[2 * j + 1]);
-      uint4* dst = reinterpret_cast<uint4*>(p.out + static_cast<size_t>(row) * p.ldo + n);
-      dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
-      dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
-      dst[2] = make_uint4(o[8], o[9], o[10], o[11]);
-      dst[3] = make_uint4(o[12], o[13], o[14], o[15]);
-      if (p.flags & kEpiRowStats) {
+      uint8_t* rb = buf + lane * 64;
+      const int sw = (lane >> 1) & 3;
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        *reinterpret_cast<uint4*>(rb + ((q ^ sw) * 16)) =
+            make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+      if ((p.flags & kEpiRowStats) && row_ok) {
         // statistics of the values as stored (fp16), chunk by chunk, merged with Chan's formula
         float f[32];
 #pragma unroll
@@ -249,6 +284,13 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t t_ro
         }
       }
     }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(tmC, buf, geglu ? (n >> 1) : n, m_base);
+      bulk_commit_group();
+    }
+    sbuf ^= 1;
   }
   if ((p.flags & kEpiRowStats) && row_ok)
     p.stats_out[static_cast<size_t>(row) * p.stats_ld + n0 / BN] = make_float2(s_mean, s_m2);
@@ -258,7 +300,7 @@ template <int BN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
                    const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB,
-                   const GemmParams p) {
+                   const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
   constexpr int A_BYTES = kGemmBM * kGemmBK * 2;
   constexpr int B_BYTES = BN * kGemmBK * 2;
   constexpr int STAGES = gemm_stages(BN);
@@ -271,7 +313,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint8_t* sEpi = sB + STAGES * B_BYTES;  // 1024-aligned: stage sizes are multiples of 1 KB
+  uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + kEpiStageBytes);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -309,6 +352,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
+  griddep_launch_dependents();
+  griddep_wait();  // inputs of this GEMM are written by the previous kernel
 
   const int num_tiles = p.m_tiles * p.n_tiles;
 
@@ -418,8 +463,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else {
     // ------------------------------------------------------------ epilogue (warps 2..5)
     const int quad = warp & 3;
-    const int out_cols = (p.flags & DLM_EPI_GEGLU) ? (p.N >> 1) : p.N;
-    (void)out_cols;
+    int sbuf = 0;
     int i = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++i) {
       const int acc = i & 1;
@@ -431,11 +475,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int row = m0 + quad * 32 + lane;
       const uint32_t t_row = tbase + (static_cast<uint32_t>(quad * 32) << 16) +
                              static_cast<uint32_t>(acc * BN);
-      epilogue_tile<BN>(p, t_row, row, n0);
+      epilogue_tile<BN>(p, t_row, row, n0, m0 + quad * 32, sEpi + (warp - 2) * kStageBytesPerWarp,
+                        &tmC, sbuf);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
     }
+    if (lane == 0) bulk_wait_all();
   }
 
   __syncwarp();
@@ -463,18 +509,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
 __host__ __device__ constexpr int gemm2_stage_bytes(int BN) { return (kGemmBM + BN / 2) * kGemmBK * 2; }
 __host__ __device__ constexpr int gemm2_stages(int BN) {
-  return ((225 * 1024 - 2048) / gemm2_stage_bytes(BN)) > 8 ? 8
-                                                             : ((225 * 1024 - 2048) / gemm2_stage_bytes(BN));
+  return ((225 * 1024 - 2048 - kEpiStageBytes) / gemm2_stage_bytes(BN)) > 8
+             ? 8
+             : ((225 * 1024 - 2048 - kEpiStageBytes) / gemm2_stage_bytes(BN));
 }
 __host__ __device__ constexpr int gemm2_smem_bytes(int BN) {
-  return gemm2_stages(BN) * gemm2_stage_bytes(BN) + 1024 + 256;
+  return gemm2_stages(BN) * gemm2_stage_bytes(BN) + kEpiStageBytes + 1024 + 256;
 }
 
 template <int BN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
                     const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB,
-                    const GemmParams p) {
+                    const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
   constexpr int BNH = BN / 2;
   constexpr int A_BYTES = kGemmBM * kGemmBK * 2;
   constexpr int B_BYTES = BNH * kGemmBK * 2;
@@ -488,7 +535,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint8_t* sEpi = sB + STAGES * B_BYTES;  // 1024-aligned: stage sizes are multiples of 1 KB
+  uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + kEpiStageBytes);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -530,6 +578,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   cluster_sync_all();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
+  griddep_launch_dependents();
+  griddep_wait();  // inputs of this GEMM are written by the previous kernel
   const int num_tiles = p.m_tiles * p.n_tiles;  // m tiles of 256 rows
 
   if (warp == 0) {
@@ -627,6 +677,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else {
     // ------------------------------------------------------------ epilogue (warps 2..5, both CTAs)
     const int quad = warp & 3;
+    int sbuf = 0;
     int i = 0;
     for (int t = pair; t < num_tiles; t += npairs, ++i) {
       const int acc = i & 1;
@@ -638,11 +689,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int row = m0 + quad * 32 + lane;
       const uint32_t t_row = tbase + (static_cast<uint32_t>(quad * 32) << 16) +
                              static_cast<uint32_t>(acc * BN);
-      epilogue_tile<BN>(p, t_row, row, n0);
+      epilogue_tile<BN>(p, t_row, row, n0, m0 + quad * 32, sEpi + (warp - 2) * kStageBytesPerWarp,
+                        &tmC, sbuf);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(&tempty[acc], 0);
     }
+    if (lane == 0) bulk_wait_all();
   }
 
   __syncwarp();

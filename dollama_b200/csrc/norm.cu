@@ -40,6 +40,8 @@ __global__ void __launch_bounds__(kStatThreads)
     gn_stats_kernel(const __half* __restrict__ x1, int C1, const __half* __restrict__ x2, int C2,
                     int HW, int pix_per_chunk, float2* __restrict__ partials) {
   extern __shared__ float sh[];  // [PL][C] sums then [PL][C] sumsq
+  griddep_launch_dependents();
+  griddep_wait();
   const int C = C1 + C2;
   const int nvec = C >> 3;
   const int chunk = blockIdx.x, n = blockIdx.y, chunks = gridDim.x;
@@ -94,6 +96,8 @@ __global__ void __launch_bounds__(256)
                     const __half* __restrict__ gamma, const __half* __restrict__ beta, float eps,
                     int silu, int pix_per_block, __half* __restrict__ out) {
   __shared__ float s_mean[kGroups], s_rstd[kGroups];
+  griddep_launch_dependents();
+  griddep_wait();
   const int C = C1 + C2;
   const int n = blockIdx.y;
   if (threadIdx.x < kGroups) {
@@ -152,6 +156,8 @@ __global__ void __launch_bounds__(256)
     layer_norm_kernel(const __half* __restrict__ x, const __half* __restrict__ gamma,
                       const __half* __restrict__ beta, __half* __restrict__ out, int rows, int C,
                       float eps) {
+  griddep_launch_dependents();
+  griddep_wait();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= rows) return;
@@ -265,14 +271,25 @@ int gn_launch(const GnOp& op, cudaStream_t s) {
     DLM_CHECK_CUDA(cudaFuncSetAttribute(gn_stats_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         op.stat_smem));
   }
-  gn_stats_kernel<<<dim3(op.chunks, op.N), kStatThreads, op.stat_smem, s>>>(
-      op.x1, op.C1, op.x2, op.C2, op.HW, op.pix_per_chunk, op.partials);
-  DLM_CHECK_CUDA(cudaGetLastError());
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(op.chunks, op.N, 1);
+  cfg.blockDim = dim3(kStatThreads, 1, 1);
+  cfg.dynamicSmemBytes = op.stat_smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  DLM_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gn_stats_kernel, op.x1, op.C1, op.x2, op.C2, op.HW,
+                                    op.pix_per_chunk, op.partials));
   const int blocks = (op.HW + op.pix_per_block - 1) / op.pix_per_block;
-  gn_apply_kernel<<<dim3(blocks, op.N), 256, 0, s>>>(op.x1, op.C1, op.x2, op.C2, op.HW, op.partials,
-                                                     op.chunks, op.gamma, op.beta, op.eps,
-                                                     op.silu ? 1 : 0, op.pix_per_block, op.out);
-  DLM_CHECK_CUDA(cudaGetLastError());
+  cfg.gridDim = dim3(blocks, op.N, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  DLM_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gn_apply_kernel, op.x1, op.C1, op.x2, op.C2, op.HW,
+                                    static_cast<const float2*>(op.partials), op.chunks, op.gamma,
+                                    op.beta, op.eps, op.silu ? 1 : 0, op.pix_per_block, op.out));
   return DLM_OK;
 }
 

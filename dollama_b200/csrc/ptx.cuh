@@ -147,6 +147,29 @@ __device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* tm, ui
       : "memory");
 }
 
+// Tiled TMA store of a shared-memory box to global memory (bulk-group completion).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* tm, const void* src, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(tm)),
+      "r"(smem_u32(src)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// Wait until at most one bulk group of this thread still reads shared memory.
+__device__ __forceinline__ void bulk_wait_read_le1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
+
+// Wait until every bulk group of this thread has completed.
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
 // Generic-proxy shared-memory writes -> visible to the async proxy (tensor core reads).
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -352,6 +375,16 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N, bool b_mn_maj
   return (1u << 4) | (static_cast<uint32_t>(b_mn_major ? 1 : 0) << 16) |
          (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
+
+// ---------------------------------------------------------------- programmatic dependent launch
+// The next kernel in the stream may start launching now (its own griddep_wait holds it before it
+// touches memory this grid writes).
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+// Wait until the previous kernel in the stream has completed and its writes are visible
+// (returns at once when this kernel was launched without programmatic serialization).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // ---------------------------------------------------------------- small math
 // 2^x with the hardware approximation (ex2.approx.ftz.f32, max relative error ~2^-22).

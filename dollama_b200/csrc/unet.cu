@@ -19,6 +19,8 @@
 //   * all tensor maps / launch parameters are built once per (B, H, W) plan over a static
 //     activation arena; the step replays as one CUDA graph (no allocation, no host sync).
 #include <cmath>
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <unordered_map>
@@ -463,7 +465,15 @@ int UNetModel::prepare_weights(cudaStream_t s) {
     w_[p + ".packed"] = d;
     if (!copy(p + ".bias", c)) return fail("upsampler bias");
   }
-  // transformers
+  // transformers: one buffer for the k/v weights of all cross-attentions
+  kv_total_ = 0;
+  for (int lvl = 1; lvl < 3; ++lvl) kv_total_ += 2 * 2 * kC[lvl] * cfg_.depth[lvl];
+  kv_total_ += 2 * kC[2] * cfg_.mid_depth;
+  for (int u = 0; u < 2; ++u) kv_total_ += 3 * 2 * kC[2 - u] * cfg_.depth[2 - u];
+  kv_all_w_ = wtake(static_cast<size_t>(kv_total_) * kCtxDim);
+  if (!kv_all_w_) return fail("kv concat");
+  kv_cursor_ = 0;
+  kv_off_.clear();
   auto prep_t2d = [&](const std::string& p, int c, int layers) -> int {
     for (const char* nn : {"norm.weight", "norm.bias", "proj_in.bias", "proj_out.bias"})
       if (!copy(p + nn, c)) return fail("t2d vec");
@@ -485,12 +495,15 @@ int UNetModel::prepare_weights(cudaStream_t s) {
       if (!copy(b + "attn1.to_out.0.weight", cc) || !copy(b + "attn2.to_q.weight", cc) ||
           !copy(b + "attn2.to_out.0.weight", cc))
         return fail("attn weights");
+      // cross-attention k / v weights of every block are rows of ONE matrix (all blocks' k/v
+      // projections of the text context become a single GEMM per step)
       const size_t kv1 = static_cast<size_t>(c) * kCtxDim;
-      __half* kv = wtake(2 * kv1);
-      if (!kv) return fail("kv");
+      if (kv_cursor_ + 2 * c > kv_total_) return fail("kv concat overflow");
+      __half* kv = kv_all_w_ + static_cast<size_t>(kv_cursor_) * kCtxDim;
       DLM_CHECK_CUDA(cudaMemcpyAsync(kv, src(b + "attn2.to_k.weight"), kv1 * 2, cudaMemcpyDeviceToDevice, s));
       DLM_CHECK_CUDA(cudaMemcpyAsync(kv + kv1, src(b + "attn2.to_v.weight"), kv1 * 2, cudaMemcpyDeviceToDevice, s));
-      w_[b + "attn2.kv"] = kv;
+      kv_off_[b] = kv_cursor_;
+      kv_cursor_ += 2 * c;
       // GEGLU proj: interleave rows (hidden_j, gate_j) so one output tile holds both halves
       const int ff = 4 * c;
       __half* gw = wtake(static_cast<size_t>(2 * ff) * c);
@@ -710,7 +723,6 @@ int UNetModel::plan_t2d(const std::string& p, __half* x, int C, int H, int Wd, i
   __half* h = t_h_;      // [M, C] running hidden state
   __half* qkv = t_qkv_;  // [M, 3C]
   __half* ao = t_ao_;    // [M, C] attention output
-  __half* kv = t_kv_;    // [B*77, 2C]
   __half* ff = t_ff_;    // [M, 4C]
   int stats_bn = 0;      // N tile of the GEMM that last wrote h (its statistics tiles)
   int rc = plan_gn(x, C, nullptr, 0, S, p + "norm", 1e-6f, false, g);
@@ -751,10 +763,8 @@ int UNetModel::plan_t2d(const std::string& p, __half* x, int C, int H, int Wd, i
     // cross attention: LN2 folded into the q GEMM
     rc = plan_linear(h, C, W(b + "attn2.to_q.weight"), M, C, C, qkv, C, ln_fold(b + "attn2.to_q.weight", 0));
     if (rc != DLM_OK) return rc;
-    rc = plan_linear(ehs_, kCtxDim, W(b + "attn2.kv"), B_ * kCtxTokens, 2 * C, kCtxDim, kv, 2 * C,
-                     GemmEpilogue{});
-    if (rc != DLM_OK) return rc;
-    rc = plan_attn(qkv, C, kv, 2 * C, kv + C, 2 * C, ao, C, heads, S, kCtxTokens);
+    const __half* kvb = kv_all_act_ + (dry_ ? 0 : kv_off_.at(b));
+    rc = plan_attn(qkv, C, kvb, kv_total_, kvb + C, kv_total_, ao, C, heads, S, kCtxTokens);
     if (rc != DLM_OK) return rc;
     if (!dry_) er.bias = W(b + "attn2.to_out.0.bias");
     rc = plan_linear(ao, C, W(b + "attn2.to_out.0.weight"), M, C, C, h, C, er, &stats_bn);
@@ -821,7 +831,7 @@ int UNetModel::build(bool dry) {
   t_n_ = act(tMC);
   t_qkv_ = act(3 * tMC);
   t_ao_ = act(tMC);
-  t_kv_ = act(static_cast<size_t>(B) * kCtxTokens * 2 * C2);
+  kv_all_act_ = act(static_cast<size_t>(B) * kCtxTokens * kv_total_);
   t_ff_ = act(4 * tMC);
   // per-row (mean, M2) statistics tiles of the hidden state, at most C / 64 tiles per row
   ln_stats_ = reinterpret_cast<float2*>(act(4 * (tMC / 64 + 64) * 2));
@@ -880,6 +890,12 @@ int UNetModel::build(bool dry) {
     if (!dry_) et.bias = W("temb_proj.bias");
     rc = plan_linear(temb_silu, kTembDim, W("temb_proj.weight"), B, temb_total_, kTembDim, tproj_,
                      temb_total_, et);
+    if (rc != DLM_OK) return rc;
+  }
+  // ---- k / v of the text context for every cross-attention of the step: one GEMM
+  {
+    int rc = plan_linear(ehs_, kCtxDim, kv_all_w_, B * kCtxTokens, kv_total_, kCtxDim, kv_all_act_,
+                         kv_total_, GemmEpilogue{});
     if (rc != DLM_OK) return rc;
   }
   // ---- conv_in (latent NCHW -> NHWC padded to 64 channels)
@@ -1160,6 +1176,10 @@ int UNetModel::time_ops(cudaStream_t s, double* ms, double* flops, int* count) {
     flops[k] = 0.0;
     count[k] = 0;
   }
+  // DLM_OP_TABLE=<path>: also write the per-launch timings of this step as CSV
+  const char* table_path = std::getenv("DLM_OP_TABLE");
+  FILE* table = table_path ? std::fopen(table_path, "w") : nullptr;
+  if (table) std::fprintf(table, "kind,M,N,K,bn,pair,amode,flags,us\n");
   std::vector<cudaEvent_t> ev(seq_.size() + 1);
   for (auto& e : ev) DLM_CHECK_CUDA(cudaEventCreate(&e));
   int rc = DLM_OK;
@@ -1201,7 +1221,23 @@ int UNetModel::time_ops(cudaStream_t s, double* ms, double* flops, int* count) {
     ms[k] += t;
     flops[k] += f;
     count[k] += o.kind == OpKind::Gn ? 2 : 1;
+    if (table) {
+      // one line per launch: class, shape, tile choice, epilogue flags, microseconds
+      if (o.kind == OpKind::Gemm) {
+        const GemmOp& g = gemm_ops_[o.idx];
+        std::fprintf(table, "gemm,%d,%d,%lld,%d,%d,%d,0x%x,%.2f\n", g.p.M, g.p.N, g.k_true, g.bn,
+                     g.pair ? 1 : 0, g.p.amode, g.p.flags, 1000.0 * t);
+      } else if (o.kind == OpKind::Attn) {
+        const AttnParams& a = attn_ops_[o.idx].p;
+        std::fprintf(table, "attn,%d,%d,%d,%d,0,0,0,%.2f\n", a.B * a.H, a.Sq, a.Sk, 64, 1000.0 * t);
+      } else {
+        std::fprintf(table, "%s,0,0,0,0,0,0,0,%.2f\n",
+                     o.kind == OpKind::Gn ? "groupnorm" : o.kind == OpKind::Ln ? "layernorm" : "other",
+                     1000.0 * t);
+      }
+    }
   }
+  if (table) std::fclose(table);
   for (auto& e : ev) cudaEventDestroy(e);
   return rc;
 }

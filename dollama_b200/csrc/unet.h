@@ -108,6 +108,9 @@ class UNetModel {
   void* wbuf_ = nullptr;
   size_t wcap_ = 0, woff_ = 0;
   std::vector<ResnetInfo> resnets_;
+  __half* kv_all_w_ = nullptr;                          // [kv_total_, 2048] all cross k/v weights
+  int kv_total_ = 0, kv_cursor_ = 0;
+  std::unordered_map<std::string, int> kv_off_;         // block prefix -> row offset in kv_all_w_
   int temb_total_ = 0;
   // plan
   int B_ = 0, H_ = 0, W_ = 0;
@@ -131,7 +134,7 @@ class UNetModel {
   __half *lat64_ = nullptr, *tproj_ = nullptr;
   __half *scratch_a_ = nullptr, *scratch_b_ = nullptr, *scratch_c_ = nullptr;
   __half *t_gn_ = nullptr, *t_h_ = nullptr, *t_n_ = nullptr, *t_qkv_ = nullptr, *t_ao_ = nullptr,
-         *t_kv_ = nullptr, *t_ff_ = nullptr;
+         *t_ff_ = nullptr, *kv_all_act_ = nullptr;
   __half *planes_ = nullptr, *upbuf_ = nullptr, *out32_ = nullptr;
   float2* gn_partials_ = nullptr;
   float2* ln_stats_ = nullptr;
