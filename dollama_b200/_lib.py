@@ -78,6 +78,21 @@ _SIGS = {
                                ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
     "dlm_unet_info": (c_int, [c_void_p, ctypes.POINTER(ctypes.c_int64),
                               ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(c_int)]),
+    "dlm_vae_create": (c_int, [c_int, ctypes.POINTER(c_char_p), ctypes.POINTER(c_void_p),
+                               ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(c_void_p), c_void_p]),
+    "dlm_vae_destroy": (c_int, [c_void_p]),
+    "dlm_vae_decode": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),
+    "dlm_vae_decode_host": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),
+    "dlm_vae_set_graph": (c_int, [c_void_p, c_int]),
+    "dlm_vae_stage": (c_int, [c_void_p, c_char_p, ctypes.POINTER(c_void_p), ctypes.POINTER(c_int),
+                              ctypes.POINTER(c_int), ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
+    "dlm_vae_info": (c_int, [c_void_p, ctypes.POINTER(ctypes.c_int64),
+                             ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(c_int)]),
+    "dlm_vae_time_ops": (c_int, [c_void_p, ctypes.POINTER(ctypes.c_double),
+                                 ctypes.POINTER(ctypes.c_double), ctypes.POINTER(c_int), c_void_p]),
+    "dlm_vae_weight_count": (c_int, []),
+    "dlm_vae_weight_info": (c_int, [c_int, ctypes.c_char_p, c_int, ctypes.POINTER(ctypes.c_int64),
+                                    ctypes.POINTER(c_int)]),
 }
 
 EPI_BIAS = 1

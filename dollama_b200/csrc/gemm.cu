@@ -148,6 +148,13 @@ bool bn_supported(int bn, bool pair) {
 // Output map for the staged epilogue: boxes of 32 rows x 32 columns (64-byte swizzle), or
 // 32 rows x 16 columns (32-byte swizzle) for GEGLU's half-width output.
 bool make_out_map(CUtensorMap* m, const __half* C, int M, int N, int ldc, unsigned flags) {
+  if (flags & kEpiOutF32) {
+    const uint64_t dims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(M)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(ldc) * 4};
+    const uint32_t box[2] = {16u, 32u};
+    return encode_tmap(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, C, dims, strides, box,
+                       CU_TENSOR_MAP_SWIZZLE_64B);
+  }
   const bool geglu = (flags & DLM_EPI_GEGLU) != 0;
   const uint64_t cols = geglu ? N / 2 : N;
   const uint64_t dims[2] = {cols, static_cast<uint64_t>(M)};
@@ -199,7 +206,14 @@ int check_epilogue(const GemmEpilogue& e, int N, __half* C, int ldc) {
     DLM_REQUIRE(!(e.flags & DLM_EPI_RESID) && !(e.flags & kEpiRowStats) && N % 64 == 0,
                 DLM_ERR_INVALID, "gemm: GEGLU needs N %% 64 == 0, no residual, no row statistics");
   if (e.flags & kEpiRowStats)
-    DLM_REQUIRE(e.stats_out != nullptr, DLM_ERR_INVALID, "gemm: row statistics need a buffer");
+    DLM_REQUIRE(e.stats_out != nullptr && !(e.flags & kEpiOutF32), DLM_ERR_INVALID,
+                "gemm: row statistics need a buffer and an fp16 output");
+  if (e.flags & kEpiOutF32)
+    DLM_REQUIRE(!(e.flags & DLM_EPI_GEGLU) && ldc % 4 == 0, DLM_ERR_INVALID,
+                "gemm: fp32 output needs ldc %% 4 == 0 and no GEGLU");
+  if (e.flags & kEpiResidF32)
+    DLM_REQUIRE((e.flags & DLM_EPI_RESID) && e.ldr % 4 == 0, DLM_ERR_INVALID,
+                "gemm: fp32 residual needs ldr %% 4 == 0");
   if (e.flags & kEpiLnFold)
     DLM_REQUIRE(e.stats_in && e.ln_u && e.ln_v && e.stats_in_parts > 0 && e.stats_in_tile > 0 &&
                     e.ln_C > 0 && (reinterpret_cast<uintptr_t>(e.ln_u) & 15) == 0 &&
@@ -211,7 +225,9 @@ int check_epilogue(const GemmEpilogue& e, int N, __half* C, int ldc) {
 }  // namespace
 
 int gemm_plan_dense(GemmOp* op, const __half* A, int lda, const __half* W, int M, int N, int K,
-                    __half* C, int ldc, const GemmEpilogue& epi, int force_bn) {
+                    __half* C, int ldc, const GemmEpilogue& epi, int force_bn, int ldw) {
+  if (ldw == 0) ldw = K;
+  DLM_REQUIRE(ldw >= K && ldw % 8 == 0, DLM_ERR_INVALID, "gemm: ldw=%d must be >= K and a multiple of 8", ldw);
   DLM_REQUIRE(op != nullptr && A != nullptr && W != nullptr, DLM_ERR_INVALID,
               "gemm: null operand");
   DLM_REQUIRE(M > 0 && N > 0 && K > 0, DLM_ERR_INVALID, "gemm: empty problem");
@@ -231,7 +247,7 @@ int gemm_plan_dense(GemmOp* op, const __half* A, int lda, const __half* W, int M
   if (!tmap_2d_f16(&op->tmA[0], A, M, K, lda, kGemmBM, kGemmBK)) return DLM_ERR_CUDA;
   op->tmA[1] = op->tmA[0];
   op->tmA[2] = op->tmA[0];
-  if (!tmap_2d_f16(&op->tmB, W, N, K, K, pair ? bn / 2 : bn, kGemmBK)) return DLM_ERR_CUDA;
+  if (!tmap_2d_f16(&op->tmB, W, N, K, ldw, pair ? bn / 2 : bn, kGemmBK)) return DLM_ERR_CUDA;
   if (!make_out_map(&op->tmC, C, M, N, ldc, epi.flags)) return DLM_ERR_CUDA;
   GemmParams& p = op->p;
   p.M = M;

@@ -49,7 +49,7 @@ struct ConvSource {
 
 // Dense: C[M, ldc] = epi(A[M, K] (row stride lda) * W[N, K]^T).
 int gemm_plan_dense(GemmOp* op, const __half* A, int lda, const __half* W, int M, int N, int K,
-                    __half* C, int ldc, const GemmEpilogue& epi, int force_bn = 0);
+                    __half* C, int ldc, const GemmEpilogue& epi, int force_bn = 0, int ldw = 0);
 
 // Implicit-GEMM conv producing NHWC out[Nb, oH, oW, Cout] (row stride ldc) from up to three
 // K segments; W is [Cout, sum(taps_s * C_s)] with the K index ordered (segment, tap, channel).

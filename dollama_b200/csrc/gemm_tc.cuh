@@ -70,6 +70,8 @@ struct GemmParams {
 // Internal epilogue flags (beyond the public DLM_EPI_* bits).
 constexpr unsigned kEpiRowStats = 1u << 8;
 constexpr unsigned kEpiLnFold = 1u << 9;
+constexpr unsigned kEpiOutF32 = 1u << 10;    // output stored as fp32 (p.out points to float)
+constexpr unsigned kEpiResidF32 = 1u << 11;  // residual read as fp32 (p.resid points to float)
 
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;
@@ -223,7 +225,19 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t t_ro
       *reinterpret_cast<uint4*>(rb + ((1 ^ sw) * 16)) = make_uint4(o[4], o[5], o[6], o[7]);
     } else {
       // 64-byte rows, 64-byte swizzle: 16-byte chunk q of row r at q ^ ((r >> 1) & 3)
-      if (p.flags & DLM_EPI_RESID) {
+      if ((p.flags & DLM_EPI_RESID) && (p.flags & kEpiResidF32)) {
+        if (row_ok) {
+          const float* rs = reinterpret_cast<const float*>(p.resid) + static_cast<size_t>(row) * p.ldr + n;
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            const float4 t = *reinterpret_cast<const float4*>(rs + j);
+            v[j] += p.resid_scale * t.x;
+            v[j + 1] += p.resid_scale * t.y;
+            v[j + 2] += p.resid_scale * t.z;
+            v[j + 3] += p.resid_scale * t.w;
+          }
+        }
+      } else if (p.flags & DLM_EPI_RESID) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int rr = (lane >> 2) + 8 * i, q = lane & 3;
@@ -246,6 +260,33 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t t_ro
           }
         }
         __syncwarp();
+      }
+      if (p.flags & kEpiOutF32) {
+        // fp32 output: two halves of 16 columns, each 32 rows x 64 bytes through one staging
+        // buffer and one bulk store (the second half uses the other buffer)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint8_t* hb = stage + sbuf * 2048;
+          if (h == 1) {
+            if (lane == 0) bulk_wait_read_le1();
+            __syncwarp();
+          }
+          uint8_t* rb = hb + lane * 64;
+          const int sw = (lane >> 1) & 3;
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            *reinterpret_cast<float4*>(rb + ((q ^ sw) * 16)) =
+                make_float4(v[16 * h + 4 * q], v[16 * h + 4 * q + 1], v[16 * h + 4 * q + 2],
+                            v[16 * h + 4 * q + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(tmC, hb, n + 16 * h, m_base);
+            bulk_commit_group();
+          }
+          sbuf ^= 1;
+        }
+        continue;
       }
       uint32_t o[16];
 #pragma unroll

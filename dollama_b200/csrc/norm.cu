@@ -35,9 +35,24 @@ __device__ __forceinline__ void load8(const __half* p, float* f) {
   }
 }
 
-// partials[(n * chunks + chunk) * 32 + g] = (sum, sumsq)
+__device__ __forceinline__ void load8(const float* p, float* f) {
+  const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+  const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+  f[0] = a.x;
+  f[1] = a.y;
+  f[2] = a.z;
+  f[3] = a.w;
+  f[4] = b.x;
+  f[5] = b.y;
+  f[6] = b.z;
+  f[7] = b.w;
+}
+
+// partials[(n * chunks + chunk) * 32 + g] = (sum, sumsq).  T = __half or float (fp32 input: the
+// VAE's full-resolution residual stream).
+template <typename T>
 __global__ void __launch_bounds__(kStatThreads)
-    gn_stats_kernel(const __half* __restrict__ x1, int C1, const __half* __restrict__ x2, int C2,
+    gn_stats_kernel(const T* __restrict__ x1, int C1, const T* __restrict__ x2, int C2,
                     int HW, int pix_per_chunk, float2* __restrict__ partials) {
   extern __shared__ float sh[];  // [PL][C] sums then [PL][C] sumsq
   griddep_launch_dependents();
@@ -90,8 +105,9 @@ __global__ void __launch_bounds__(kStatThreads)
 }
 
 // Each block handles `pix_per_block` pixels of image n = blockIdx.y.
+template <typename T>
 __global__ void __launch_bounds__(256)
-    gn_apply_kernel(const __half* __restrict__ x1, int C1, const __half* __restrict__ x2, int C2,
+    gn_apply_kernel(const T* __restrict__ x1, int C1, const T* __restrict__ x2, int C2,
                     int HW, const float2* __restrict__ partials, int chunks,
                     const __half* __restrict__ gamma, const __half* __restrict__ beta, float eps,
                     int silu, int pix_per_block, __half* __restrict__ out) {
@@ -260,6 +276,19 @@ int gn_plan(GnOp* op, const __half* x1, int C1, const __half* x2, int C2, int N,
   return DLM_OK;
 }
 
+int gn_plan_f32(GnOp* op, const float* x, int C, int N, int HW, const __half* gamma,
+                const __half* beta, float eps, bool silu, __half* out, float2* partials,
+                size_t partial_cap) {
+  DLM_REQUIRE(x != nullptr, DLM_ERR_INVALID, "gn: null input");
+  // plan as a single-source fp16 problem of the same geometry, then read fp32
+  int rc = gn_plan(op, reinterpret_cast<const __half*>(x), C, nullptr, 0, N, HW, gamma, beta, eps,
+                   silu, out, partials, partial_cap);
+  if (rc != DLM_OK) return rc;
+  op->xf = x;
+  op->x1 = nullptr;
+  return DLM_OK;
+}
+
 size_t gn_partial_elems(int N, int HW) {
   const int sms = 148 * 2;  // generous bound for any SM count up to 296
   (void)HW;
@@ -267,10 +296,8 @@ size_t gn_partial_elems(int N, int HW) {
 }
 
 int gn_launch(const GnOp& op, cudaStream_t s) {
-  if (op.stat_smem > 48 * 1024) {
-    DLM_CHECK_CUDA(cudaFuncSetAttribute(gn_stats_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        op.stat_smem));
-  }
+  // stat_smem <= 2 * 256 * 8 floats * 4 B (PL * C <= 256 * 8 for C / 8 < 256) or 2 * C * 4 B
+  // (C <= 4096): always within the 48 KB default, no attribute needed.
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -281,15 +308,29 @@ int gn_launch(const GnOp& op, cudaStream_t s) {
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
-  DLM_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gn_stats_kernel, op.x1, op.C1, op.x2, op.C2, op.HW,
-                                    op.pix_per_chunk, op.partials));
+  if (op.xf) {
+    DLM_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gn_stats_kernel<float>, op.xf, op.C1,
+                                      static_cast<const float*>(nullptr), 0, op.HW,
+                                      op.pix_per_chunk, op.partials));
+  } else {
+    DLM_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gn_stats_kernel<__half>, op.x1, op.C1, op.x2, op.C2,
+                                      op.HW, op.pix_per_chunk, op.partials));
+  }
   const int blocks = (op.HW + op.pix_per_block - 1) / op.pix_per_block;
   cfg.gridDim = dim3(blocks, op.N, 1);
   cfg.blockDim = dim3(256, 1, 1);
   cfg.dynamicSmemBytes = 0;
-  DLM_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gn_apply_kernel, op.x1, op.C1, op.x2, op.C2, op.HW,
-                                    static_cast<const float2*>(op.partials), op.chunks, op.gamma,
-                                    op.beta, op.eps, op.silu ? 1 : 0, op.pix_per_block, op.out));
+  if (op.xf) {
+    DLM_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gn_apply_kernel<float>, op.xf, op.C1,
+                                      static_cast<const float*>(nullptr), 0, op.HW,
+                                      static_cast<const float2*>(op.partials), op.chunks, op.gamma,
+                                      op.beta, op.eps, op.silu ? 1 : 0, op.pix_per_block, op.out));
+  } else {
+    DLM_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gn_apply_kernel<__half>, op.x1, op.C1, op.x2, op.C2,
+                                      op.HW, static_cast<const float2*>(op.partials), op.chunks,
+                                      op.gamma, op.beta, op.eps, op.silu ? 1 : 0, op.pix_per_block,
+                                      op.out));
+  }
   return DLM_OK;
 }
 

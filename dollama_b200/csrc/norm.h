@@ -8,6 +8,7 @@
 namespace dlm {
 
 struct GnOp {
+  const float* xf = nullptr;  // fp32 single-source input (then x1 / x2 are unused)
   const __half* x1 = nullptr;
   const __half* x2 = nullptr;
   int C1 = 0, C2 = 0, N = 0, HW = 0;
@@ -25,6 +26,10 @@ struct GnOp {
 int gn_plan(GnOp* op, const __half* x1, int C1, const __half* x2, int C2, int N, int HW,
             const __half* gamma, const __half* beta, float eps, bool silu, __half* out,
             float2* partials, size_t partial_cap);
+// Same with an fp32 input [N, HW, C] (single source).
+int gn_plan_f32(GnOp* op, const float* x, int C, int N, int HW, const __half* gamma,
+                const __half* beta, float eps, bool silu, __half* out, float2* partials,
+                size_t partial_cap);
 size_t gn_partial_elems(int N, int HW);
 int gn_launch(const GnOp& op, cudaStream_t s);
 

@@ -73,50 +73,6 @@ __global__ void silu_kernel(const __half* __restrict__ x, __half* __restrict__ y
 
 __global__ void set_scalar_kernel(float* p, float v) { *p = v; }
 
-// NCHW [B, Cin, H, W] -> NHWC [B, H, W, Cpad] with zero channels beyond Cin.
-__global__ void nchw_to_nhwc_pad_kernel(const __half* __restrict__ in, __half* __restrict__ out,
-                                        int B, int Cin, int HW, int Cpad) {
-  const size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x;
-  const size_t total = static_cast<size_t>(B) * HW;
-  if (i >= total) return;
-  const int b = static_cast<int>(i / HW), p = static_cast<int>(i % HW);
-  __half* o = out + i * Cpad;
-  for (int c = 0; c < Cpad; ++c)
-    o[c] = c < Cin ? in[(static_cast<size_t>(b) * Cin + c) * HW + p] : __float2half_rn(0.0f);
-}
-
-// NHWC [B, HW, ld] (first Cout channels) -> NCHW [B, Cout, HW]
-__global__ void nhwc_to_nchw_narrow_kernel(const __half* __restrict__ in, int ld,
-                                           __half* __restrict__ out, int B, int Cout, int HW) {
-  const size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x;
-  const size_t total = static_cast<size_t>(B) * HW;
-  if (i >= total) return;
-  const int b = static_cast<int>(i / HW), p = static_cast<int>(i % HW);
-  for (int c = 0; c < Cout; ++c) out[(static_cast<size_t>(b) * Cout + c) * HW + p] = in[i * ld + c];
-}
-
-// p[o, kh, kw, i] (row stride ldp) = w[o, i, kh, kw] for o < Cout, i < Cin; zero for the padding
-// rows o in [Cout, Cout_pad) and channels i in [Cin, Cin_pad).
-__global__ void pack_conv_pad_kernel(const __half* __restrict__ w, __half* __restrict__ p, int Cout,
-                                     int Cout_pad, int Cin, int Cin_pad, int KK, int ldp) {
-  const size_t total = static_cast<size_t>(Cout_pad) * KK * Cin_pad;
-  for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
-       idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
-    const int i = static_cast<int>(idx % Cin_pad);
-    const int tap = static_cast<int>((idx / Cin_pad) % KK);
-    const int o = static_cast<int>(idx / (static_cast<size_t>(Cin_pad) * KK));
-    __half v = __float2half_rn(0.0f);
-    if (o < Cout && i < Cin) v = w[(static_cast<size_t>(o) * Cin + i) * KK + tap];
-    p[static_cast<size_t>(o) * ldp + static_cast<size_t>(tap) * Cin_pad + i] = v;
-  }
-}
-
-__global__ void add_half_kernel(const __half* __restrict__ a, const __half* __restrict__ b,
-                                __half* __restrict__ y, int n) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n) y[i] = __float2half_rn(__half2float(a[i]) + __half2float(b[i]));
-}
-
 // LayerNorm fold of a consumer weight, in place, one warp per output row n:
 //   W'[n,k] = fp16(W[n,k] * gamma[k]);  u[n] = sum_k W'[n,k];  v[n] = sum_k beta[k] W[n,k] + bias[n]
 // so that  LN(x) W^T + bias = rstd * (x W'^T - mean * u) + v.
@@ -262,20 +218,10 @@ UNetModel::~UNetModel() {
 }
 
 void UNetModel::release_plan() {
-  if (gexec_) cudaGraphExecDestroy(gexec_);
-  gexec_ = nullptr;
-  if (cap_stream_) cudaStreamDestroy(cap_stream_);
-  cap_stream_ = nullptr;
+  ops_.clear();
   if (abuf_) cudaFree(abuf_);
   abuf_ = nullptr;
   B_ = H_ = W_ = 0;
-  seq_.clear();
-  gemm_ops_.clear();
-  gemm_flops_.clear();
-  attn_ops_.clear();
-  gn_ops_.clear();
-  ln_ops_.clear();
-  custom_.clear();
   stages_.clear();
 }
 
@@ -337,10 +283,7 @@ int UNetModel::prepare_weights(cudaStream_t s) {
   };
   auto pack = [&](const std::string& name, __half* dst, int cout, int cout_pad, int cin, int cin_pad,
                   int kk, int ldp) -> bool {
-    const size_t total = static_cast<size_t>(cout_pad) * kk * cin_pad;
-    pack_conv_pad_kernel<<<std::min<size_t>((total + 255) / 256, 4096), 256, 0, s>>>(
-        src(name), dst, cout, cout_pad, cin, cin_pad, kk, ldp);
-    return cudaGetLastError() == cudaSuccess;
+    return pack_conv_pad(src(name), dst, cout, cout_pad, cin, cin_pad, kk, ldp, s) == DLM_OK;
   };
   auto fail = [&](const char* what) {
     set_error("unet prepare: %s", what);
@@ -419,9 +362,8 @@ int UNetModel::prepare_weights(cudaStream_t s) {
                                    src(p + "time_emb_proj.weight"),
                                    static_cast<size_t>(co) * kTembDim * 2, cudaMemcpyDeviceToDevice, s));
     // time_emb_proj.bias + conv1.bias: both are added to every pixel of conv1's output
-    add_half_kernel<<<blocks_for(co, 256), 256, 0, s>>>(src(p + "time_emb_proj.bias"),
-                                                       src(p + "conv1.bias"), tb + rs.temb_off, co);
-    DLM_CHECK_CUDA(cudaGetLastError());
+    int rc = add_f16(src(p + "time_emb_proj.bias"), src(p + "conv1.bias"), tb + rs.temb_off, co, s);
+    if (rc != DLM_OK) return rc;
     for (const char* nn : {"norm1.weight", "norm1.bias"})
       if (!copy(p + nn, ci)) return fail("resnet norm1");
     for (const char* nn : {"norm2.weight", "norm2.bias"})
@@ -440,9 +382,8 @@ int UNetModel::prepare_weights(cudaStream_t s) {
       DLM_CHECK_CUDA(cudaMemcpy2DAsync(w2 + 9 * co, static_cast<size_t>(k2) * 2,
                                        src(p + "conv_shortcut.weight"), static_cast<size_t>(ci) * 2,
                                        static_cast<size_t>(ci) * 2, co, cudaMemcpyDeviceToDevice, s));
-      add_half_kernel<<<blocks_for(co, 256), 256, 0, s>>>(src(p + "conv2.bias"),
-                                                         src(p + "conv_shortcut.bias"), b2, co);
-      DLM_CHECK_CUDA(cudaGetLastError());
+      rc = add_f16(src(p + "conv2.bias"), src(p + "conv_shortcut.bias"), b2, co, s);
+      if (rc != DLM_OK) return rc;
     } else {
       DLM_CHECK_CUDA(cudaMemcpyAsync(b2, src(p + "conv2.bias"), co * 2, cudaMemcpyDeviceToDevice, s));
     }
@@ -579,35 +520,7 @@ const float* UNetModel::WF(const std::string& n) const {
 
 // ================================================================== plan
 
-__half* UNetModel::act(size_t elems) {
-  const size_t bytes = ((elems * 2 + 255) / 256) * 256;
-  const size_t off = aoff_;
-  aoff_ += bytes;
-  if (dry_) return reinterpret_cast<__half*>(static_cast<uintptr_t>(0x100000000ull + off));
-  return reinterpret_cast<__half*>(static_cast<char*>(abuf_) + off);
-}
-
-void UNetModel::push_gemm(const GemmOp& g, double flops) {
-  gemm_ops_.push_back(g);
-  gemm_flops_.push_back(flops >= 0.0 ? flops : 2.0 * g.p.M * static_cast<double>(g.p.N) * g.k_true);
-  seq_.push_back({OpKind::Gemm, static_cast<int>(gemm_ops_.size() - 1)});
-}
-void UNetModel::push_attn(const AttnOp& a) {
-  attn_ops_.push_back(a);
-  seq_.push_back({OpKind::Attn, static_cast<int>(attn_ops_.size() - 1)});
-}
-void UNetModel::push_gn(const GnOp& g) {
-  gn_ops_.push_back(g);
-  seq_.push_back({OpKind::Gn, static_cast<int>(gn_ops_.size() - 1)});
-}
-void UNetModel::push_ln(const LnArgs& l) {
-  ln_ops_.push_back(l);
-  seq_.push_back({OpKind::Ln, static_cast<int>(ln_ops_.size() - 1)});
-}
-void UNetModel::push_custom(std::function<int(cudaStream_t)> f) {
-  custom_.push_back(std::move(f));
-  seq_.push_back({OpKind::Custom, static_cast<int>(custom_.size() - 1)});
-}
+__half* UNetModel::act(size_t elems) { return arena_.take<__half>(elems); }
 
 #define PLAN_CHECK(expr)            \
   do {                              \
@@ -787,14 +700,8 @@ int UNetModel::plan_t2d(const std::string& p, __half* x, int C, int H, int Wd, i
 
 int UNetModel::build(bool dry) {
   dry_ = dry;
-  aoff_ = 0;
-  seq_.clear();
-  gemm_ops_.clear();
-  gemm_flops_.clear();
-  attn_ops_.clear();
-  gn_ops_.clear();
-  ln_ops_.clear();
-  custom_.clear();
+  arena_.begin(dry, abuf_);
+  ops_.clear();
   stages_.clear();
   const int B = B_, H0 = H_, W0 = W_;
   const int C0 = kC[0], C1 = kC[1], C2 = kC[2];
@@ -904,8 +811,7 @@ int UNetModel::build(bool dry) {
     const __half* li = lat_in_;
     __half* l64 = lat64_;
     push_custom([=](cudaStream_t s) {
-      nchw_to_nhwc_pad_kernel<<<blocks_for(P0, 256), 256, 0, s>>>(li, l64, B, 4, H0 * W0, 64);
-      return cudaGetLastError() == cudaSuccess ? DLM_OK : DLM_ERR_CUDA;
+      return nchw_to_nhwc_pad(li, l64, B, 4, H0 * W0, 64, s);
     });
     GemmOp g;
     ConvSource s0{0, lat64_, 64};
@@ -1038,8 +944,7 @@ int UNetModel::build(bool dry) {
       const __half* o32 = out32_;
       __half* no = noise_out_;
       push_custom([=](cudaStream_t s) {
-        nhwc_to_nchw_narrow_kernel<<<blocks_for(P0, 256), 256, 0, s>>>(o32, 32, no, B, 4, H0 * W0);
-        return cudaGetLastError() == cudaSuccess ? DLM_OK : DLM_ERR_CUDA;
+        return nhwc_to_nchw_narrow(o32, 32, no, B, 4, H0 * W0, s);
       });
     }
   }
@@ -1066,7 +971,7 @@ int UNetModel::plan(int B, int H, int Wd) {
     release_plan();
     return rc;
   }
-  const size_t bytes = aoff_ + 4096;
+  const size_t bytes = arena_.used() + 4096;
   if (cudaMalloc(&abuf_, bytes) != cudaSuccess) {
     cudaGetLastError();
     release_plan();
@@ -1081,25 +986,6 @@ int UNetModel::plan(int B, int H, int Wd) {
   if (rc != DLM_OK) {
     release_plan();
     return rc;
-  }
-  return DLM_OK;
-}
-
-int UNetModel::run_ops(cudaStream_t s) {
-  for (const OpRef& o : seq_) {
-    int rc = DLM_OK;
-    switch (o.kind) {
-      case OpKind::Gemm: rc = gemm_launch(gemm_ops_[o.idx], s); break;
-      case OpKind::Attn: rc = attn_launch(attn_ops_[o.idx], s); break;
-      case OpKind::Gn: rc = gn_launch(gn_ops_[o.idx], s); break;
-      case OpKind::Ln: {
-        const LnArgs& l = ln_ops_[o.idx];
-        rc = layer_norm(l.x, l.g, l.b, l.out, l.rows, l.C, l.eps, s);
-        break;
-      }
-      case OpKind::Custom: rc = custom_[o.idx](s); break;
-    }
-    if (rc != DLM_OK) return rc;
   }
   return DLM_OK;
 }
@@ -1146,24 +1032,7 @@ int UNetModel::forward_host(int B, int H, int Wd, const __half* latent, float ti
 int UNetModel::launch_step(float timestep, cudaStream_t s) {
   set_scalar_kernel<<<1, 1, 0, s>>>(d_t_, timestep);
   DLM_CHECK_CUDA(cudaGetLastError());
-  if (!use_graph_) return run_ops(s);
-  if (!gexec_) {
-    if (!cap_stream_) DLM_CHECK_CUDA(cudaStreamCreateWithFlags(&cap_stream_, cudaStreamNonBlocking));
-    cudaGraph_t graph = nullptr;
-    DLM_CHECK_CUDA(cudaStreamBeginCapture(cap_stream_, cudaStreamCaptureModeThreadLocal));
-    int rc = run_ops(cap_stream_);
-    cudaError_t ce = cudaStreamEndCapture(cap_stream_, &graph);
-    if (rc != DLM_OK) {
-      if (graph) cudaGraphDestroy(graph);
-      return rc;
-    }
-    DLM_CHECK_CUDA(ce);
-    ce = cudaGraphInstantiate(&gexec_, graph, 0);
-    cudaGraphDestroy(graph);
-    DLM_CHECK_CUDA(ce);
-  }
-  DLM_CHECK_CUDA(cudaGraphLaunch(gexec_, s));
-  return DLM_OK;
+  return ops_.replay(s, use_graph_);
 }
 
 // Runs the planned step once, eagerly, with a CUDA event between consecutive launches, and
@@ -1171,75 +1040,7 @@ int UNetModel::launch_step(float timestep, cudaStream_t s) {
 // step runs, in order, on the current arena contents.
 int UNetModel::time_ops(cudaStream_t s, double* ms, double* flops, int* count) {
   DLM_REQUIRE(abuf_ != nullptr, DLM_ERR_INVALID, "unet_time_ops: run a forward first");
-  for (int k = 0; k < kNumOpClasses; ++k) {
-    ms[k] = 0.0;
-    flops[k] = 0.0;
-    count[k] = 0;
-  }
-  // DLM_OP_TABLE=<path>: also write the per-launch timings of this step as CSV
-  const char* table_path = std::getenv("DLM_OP_TABLE");
-  FILE* table = table_path ? std::fopen(table_path, "w") : nullptr;
-  if (table) std::fprintf(table, "kind,M,N,K,bn,pair,amode,flags,us\n");
-  std::vector<cudaEvent_t> ev(seq_.size() + 1);
-  for (auto& e : ev) DLM_CHECK_CUDA(cudaEventCreate(&e));
-  int rc = DLM_OK;
-  DLM_CHECK_CUDA(cudaEventRecord(ev[0], s));
-  for (size_t i = 0; i < seq_.size() && rc == DLM_OK; ++i) {
-    const OpRef& o = seq_[i];
-    switch (o.kind) {
-      case OpKind::Gemm: rc = gemm_launch(gemm_ops_[o.idx], s); break;
-      case OpKind::Attn: rc = attn_launch(attn_ops_[o.idx], s); break;
-      case OpKind::Gn: rc = gn_launch(gn_ops_[o.idx], s); break;
-      case OpKind::Ln: {
-        const LnArgs& l = ln_ops_[o.idx];
-        rc = layer_norm(l.x, l.g, l.b, l.out, l.rows, l.C, l.eps, s);
-        break;
-      }
-      case OpKind::Custom: rc = custom_[o.idx](s); break;
-    }
-    if (cudaEventRecord(ev[i + 1], s) != cudaSuccess) rc = DLM_ERR_CUDA;
-  }
-  if (rc == DLM_OK && cudaStreamSynchronize(s) != cudaSuccess) rc = DLM_ERR_CUDA;
-  for (size_t i = 0; i < seq_.size() && rc == DLM_OK; ++i) {
-    float t = 0.0f;
-    cudaEventElapsedTime(&t, ev[i], ev[i + 1]);
-    const OpRef& o = seq_[i];
-    int k = 4;
-    double f = 0.0;
-    if (o.kind == OpKind::Gemm) {
-      k = 0;
-      f = gemm_flops_[o.idx];
-    } else if (o.kind == OpKind::Attn) {
-      k = 1;
-      const AttnParams& p = attn_ops_[o.idx].p;
-      f = 4.0 * p.B * p.H * static_cast<double>(p.Sq) * p.Sk * 64;
-    } else if (o.kind == OpKind::Gn) {
-      k = 2;
-    } else if (o.kind == OpKind::Ln) {
-      k = 3;
-    }
-    ms[k] += t;
-    flops[k] += f;
-    count[k] += o.kind == OpKind::Gn ? 2 : 1;
-    if (table) {
-      // one line per launch: class, shape, tile choice, epilogue flags, microseconds
-      if (o.kind == OpKind::Gemm) {
-        const GemmOp& g = gemm_ops_[o.idx];
-        std::fprintf(table, "gemm,%d,%d,%lld,%d,%d,%d,0x%x,%.2f\n", g.p.M, g.p.N, g.k_true, g.bn,
-                     g.pair ? 1 : 0, g.p.amode, g.p.flags, 1000.0 * t);
-      } else if (o.kind == OpKind::Attn) {
-        const AttnParams& a = attn_ops_[o.idx].p;
-        std::fprintf(table, "attn,%d,%d,%d,%d,0,0,0,%.2f\n", a.B * a.H, a.Sq, a.Sk, 64, 1000.0 * t);
-      } else {
-        std::fprintf(table, "%s,0,0,0,0,0,0,0,%.2f\n",
-                     o.kind == OpKind::Gn ? "groupnorm" : o.kind == OpKind::Ln ? "layernorm" : "other",
-                     1000.0 * t);
-      }
-    }
-  }
-  if (table) std::fclose(table);
-  for (auto& e : ev) cudaEventDestroy(e);
-  return rc;
+  return ops_.time(s, ms, flops, count);
 }
 
 int UNetModel::stage(const std::string& name, const __half** ptr, int* C, int* H, int* Wd) const {

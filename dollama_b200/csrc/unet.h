@@ -12,6 +12,7 @@
 #include "common.h"
 #include "gemm.h"
 #include "norm.h"
+#include "plan.h"
 
 namespace dlm {
 
@@ -26,15 +27,6 @@ struct ResnetInfo {
   int temb_off;  // column offset of this resnet in the concatenated time-embedding projection
 };
 
-struct LnArgs {
-  const __half* x;
-  const __half* g;
-  const __half* b;
-  __half* out;
-  int rows, C;
-  float eps;
-};
-
 class UNetModel {
  public:
   ~UNetModel();
@@ -45,30 +37,18 @@ class UNetModel {
   // Same step with pinned/pageable HOST inputs and output; returns after the result is on host.
   int forward_host(int B, int H, int W, const __half* latent, float timestep, const __half* ehs,
                    const __half* te, const __half* tid, __half* noise_out, cudaStream_t s);
-  static constexpr int kNumOpClasses = 5;  // gemm, attention, groupnorm, layernorm, other
+  static constexpr int kNumOpClasses = OpPlan::kNumClasses;
   int time_ops(cudaStream_t s, double* ms, double* flops, int* count);
   void set_graph(bool on) {
-    if (on != use_graph_ && gexec_) {
-      cudaGraphExecDestroy(gexec_);
-      gexec_ = nullptr;
-    }
+    if (on != use_graph_) ops_.drop_graph();
     use_graph_ = on;
   }
   int stage(const std::string& name, const __half** ptr, int* C, int* H, int* W) const;
   size_t arena_bytes() const { return arena_bytes_; }
   size_t weight_bytes() const { return woff_; }
-  int num_launches() const {
-    int n = 0;
-    for (const auto& o : seq_) n += o.kind == OpKind::Gn ? 2 : 1;
-    return n;
-  }
+  int num_launches() const { return ops_.num_launches(); }
 
  private:
-  enum class OpKind { Gemm, Attn, Gn, Ln, Custom };
-  struct OpRef {
-    OpKind kind;
-    int idx;
-  };
   struct StageInfo {
     const __half* ptr;
     int C, H, W;
@@ -83,7 +63,6 @@ class UNetModel {
   int plan(int B, int H, int W);
   int build(bool dry);
   void release_plan();
-  int run_ops(cudaStream_t s);
   int launch_step(float timestep, cudaStream_t s);
   int plan_gn(const __half* x1, int C1, const __half* x2, int C2, int HW, const std::string& wprefix,
               float eps, bool silu, __half* out);
@@ -94,11 +73,11 @@ class UNetModel {
                   const GemmEpilogue& e, int* bn_out = nullptr);
   int plan_attn(const __half* q, int ldq, const __half* k, int ldk, const __half* v, int ldv,
                 __half* o, int ldo, int heads, int Sq, int Sk);
-  void push_gemm(const GemmOp& g, double flops = -1.0);
-  void push_attn(const AttnOp& a);
-  void push_gn(const GnOp& g);
-  void push_ln(const LnArgs& l);
-  void push_custom(std::function<int(cudaStream_t)> f);
+  void push_gemm(const GemmOp& g, double flops = -1.0) { ops_.push_gemm(g, flops); }
+  void push_attn(const AttnOp& a) { ops_.push_attn(a); }
+  void push_gn(const GnOp& g) { ops_.push_gn(g); }
+  void push_ln(const LnArgs& l) { ops_.push_ln(l); }
+  void push_custom(std::function<int(cudaStream_t)> f) { ops_.push_custom(std::move(f)); }
 
   UNetCfg cfg_;
   // weights
@@ -116,18 +95,11 @@ class UNetModel {
   int B_ = 0, H_ = 0, W_ = 0;
   bool dry_ = false;
   void* abuf_ = nullptr;
-  size_t aoff_ = 0, arena_bytes_ = 0;
-  std::vector<OpRef> seq_;
-  std::vector<GemmOp> gemm_ops_;
-  std::vector<double> gemm_flops_;
-  std::vector<AttnOp> attn_ops_;
-  std::vector<GnOp> gn_ops_;
-  std::vector<LnArgs> ln_ops_;
-  std::vector<std::function<int(cudaStream_t)>> custom_;
+  size_t arena_bytes_ = 0;
+  ActArena arena_;
+  OpPlan ops_;
   std::unordered_map<std::string, StageInfo> stages_;
   bool use_graph_ = true;
-  cudaGraphExec_t gexec_ = nullptr;
-  cudaStream_t cap_stream_ = nullptr;
   // buffers inside the arena
   float* d_t_ = nullptr;
   __half *tid_ = nullptr, *te_ = nullptr, *ehs_ = nullptr, *lat_in_ = nullptr, *noise_out_ = nullptr;

@@ -232,6 +232,48 @@ int dlm_unet_stage(void* handle, const char* name, const void** ptr, int* C, int
 /* Activation arena bytes, prepared weight bytes, kernel launches per step. */
 int dlm_unet_info(void* handle, int64_t* arena_bytes, int64_t* weight_bytes, int* num_launches);
 
+/* ---------------------------------------------------------------- SDXL VAE decoder
+ * Resident-weight handle of the AutoencoderKL decoder.  Replaces vae_weights_create /
+ * vae_weights_destroy / launch_vae_decode(handle, d_latent, d_image_out)
+ * (src/kernels/vae_decode.cuh:66-75): the caller passes the state dict as (name, device pointer,
+ * element count) triples of fp16 tensors (decoder.* and post_quant_conv.*; the 140 names of
+ * dlm_vae_weight_info); the handle copies and repacks them, so the caller's buffers may be freed
+ * after create returns.  DLM_ERR_NOT_FOUND names a missing tensor in dlm_last_error. */
+int dlm_vae_create(int n, const char* const* names, const void* const* dev_ptrs,
+                   const int64_t* numels, void** handle, void* stream);
+int dlm_vae_destroy(void* handle);
+
+/* latent [B, 4, h, w] fp16 NCHW (already divided by the VAE scaling factor, as the reference's
+ * caller does at src/infer/diffusion.cu:979-986) -> image [B, 3, 8h, 8w] fp16 NCHW, both device
+ * pointers.  w must be a multiple of 128 or divide 128 (then 128 / w must divide h), and
+ * h * w <= 32768.  The first call for a (B, h, w) plans the decode (static arena) and captures it
+ * as a CUDA graph; later calls replay it. */
+int dlm_vae_decode(void* handle, int B, int h, int w, const void* latent, void* image, void* stream);
+
+/* Same decode with HOST latent / image: copies in, decodes, copies the image back and returns once
+ * it is on the host (synchronizes `stream`). */
+int dlm_vae_decode_host(void* handle, int B, int h, int w, const void* latent_host, void* image_host,
+                        void* stream);
+
+/* Enables (default) or disables CUDA-graph replay of the decode. */
+int dlm_vae_set_graph(void* handle, int enable);
+
+/* Test hook (the reference's dbg_stat points, vae_decode.cu:736-866): device pointer, dtype
+ * (0 fp16, 1 fp32) and NHWC geometry of a stage output of the last decode ("mid_block_out",
+ * "up_block_{0,1,2,3}_out"). */
+int dlm_vae_stage(void* handle, const char* name, const void** ptr, int* dtype, int* C, int* H,
+                  int* W);
+
+/* Activation arena bytes, prepared weight bytes, kernel launches per decode. */
+int dlm_vae_info(void* handle, int64_t* arena_bytes, int64_t* weight_bytes, int* num_launches);
+
+/* Per op class device ms / algorithmic FLOPs / launches of one eager decode (as dlm_unet_time_ops). */
+int dlm_vae_time_ops(void* handle, double* ms, double* flops, int* count, void* stream);
+
+/* The weight set dlm_vae_create expects: count, then per index its name and shape (ndim <= 4). */
+int dlm_vae_weight_count(void);
+int dlm_vae_weight_info(int index, char* name, int name_cap, int64_t* shape, int* ndim);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif
