@@ -12,10 +12,11 @@
 //   * the static array holds kNoAllocPartials float2 (256 KiB); dlm_group_norm_nhwc_noalloc rejects
 //     problems whose partial sums would not fit (an error, nothing is launched);
 //   * every GPU that loads the library holds its own copy of the array until the process exits;
-//   * every call shares the array and leaves the last call's partial sums in it.  Nothing has to
-//     start at zero: the statistics pass writes every partial it later reads.  Calls whose work
-//     overlaps on the GPU (different streams, or other threads) race on the array and give
-//     wrong results — serialise them;
+//   * every call shares the array and leaves the last call's partial sums in it.  The array also
+//     holds the statistics pass's per-image arrival counters, which must be zero when a launch
+//     starts: static device memory starts zeroed and every launch leaves its counters at zero.
+//     Calls whose work overlaps on the GPU (different streams, or other threads) race on the
+//     array and give wrong results — serialise them;
 //   * the array's device address is looked up (cudaGetSymbolAddress) by the first call on each
 //     device, with that device current; that first call should come before any stream capture.
 #include <mutex>

@@ -125,16 +125,24 @@ __global__ void add_f16_kernel(const __half* __restrict__ a, const __half* __res
   if (i < n) y[i] = __float2half_rn(__half2float(a[i]) + __half2float(b[i]));
 }
 
-// NCHW [B, Cin, HW] -> NHWC [B, HW, Cpad] with zero channels beyond Cin.
+// NCHW [B, Cin, HW] -> NHWC [B, HW, Cpad] with zero channels beyond Cin; one thread per pixel,
+// 16-byte stores (Cpad % 8 == 0), reads coalesced across the threads of a warp.
 __global__ void nchw_to_nhwc_pad_kernel(const __half* __restrict__ in, __half* __restrict__ out,
                                         int B, int Cin, int HW, int Cpad) {
   const size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x;
   const size_t total = static_cast<size_t>(B) * HW;
   if (i >= total) return;
   const int b = static_cast<int>(i / HW), p = static_cast<int>(i % HW);
-  __half* o = out + i * Cpad;
-  for (int c = 0; c < Cpad; ++c)
-    o[c] = c < Cin ? in[(static_cast<size_t>(b) * Cin + c) * HW + p] : __float2half_rn(0.0f);
+  uint4* o = reinterpret_cast<uint4*>(out + i * Cpad);
+  for (int c0 = 0; c0 < Cpad; c0 += 8) {
+    __align__(16) __half h[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = c0 + j;
+      h[j] = c < Cin ? in[(static_cast<size_t>(b) * Cin + c) * HW + p] : __float2half_rn(0.0f);
+    }
+    o[c0 / 8] = *reinterpret_cast<const uint4*>(h);
+  }
 }
 
 // NHWC [B, HW, ld] (first Cout channels) -> NCHW [B, Cout, HW]
@@ -204,16 +212,16 @@ __global__ void upsample2x_f32_to_f16_kernel(const float4* __restrict__ in, uint
 }
 
 // In-place row softmax of fp16 scores [rows, cols] (already scaled), fp32 arithmetic; one
-// 256-thread block per row, the row held in registers (cols <= 256 * 8 * kSoftmaxVec).
-constexpr int kSoftmaxVec = 16;
+// 256-thread block per row, the row held in registers (VEC x 8 values per thread, cols <= 2048 VEC).
+template <int VEC>
 __global__ void __launch_bounds__(256) softmax_rows_kernel(__half* __restrict__ s, int cols) {
   __shared__ float red[8];
   __half* row = s + static_cast<size_t>(blockIdx.x) * cols;
   const int n8 = cols / 8;
-  float v[kSoftmaxVec][8];
+  float v[VEC][8];
   float mx = -INFINITY;
 #pragma unroll
-  for (int k = 0; k < kSoftmaxVec; ++k) {
+  for (int k = 0; k < VEC; ++k) {
     const int i = threadIdx.x + 256 * k;
     if (i < n8) {
       const uint4 u = *reinterpret_cast<const uint4*>(row + 8 * i);
@@ -237,7 +245,7 @@ __global__ void __launch_bounds__(256) softmax_rows_kernel(__half* __restrict__ 
   __syncthreads();
   float sum = 0.0f;
 #pragma unroll
-  for (int k = 0; k < kSoftmaxVec; ++k) {
+  for (int k = 0; k < VEC; ++k) {
     const int i = threadIdx.x + 256 * k;
     if (i < n8) {
 #pragma unroll
@@ -256,7 +264,7 @@ __global__ void __launch_bounds__(256) softmax_rows_kernel(__half* __restrict__ 
   for (int w = 0; w < 8; ++w) sum += red[w];
   const float inv = 1.0f / sum;
 #pragma unroll
-  for (int k = 0; k < kSoftmaxVec; ++k) {
+  for (int k = 0; k < VEC; ++k) {
     const int i = threadIdx.x + 256 * k;
     if (i < n8) {
       uint32_t o[4];
@@ -269,6 +277,7 @@ __global__ void __launch_bounds__(256) softmax_rows_kernel(__half* __restrict__ 
     }
   }
 }
+constexpr int kSoftmaxMaxCols = 256 * 8 * 16;
 
 int grid_for(size_t total, int threads) {
   size_t g = (total + threads - 1) / threads;
@@ -331,6 +340,8 @@ int add_f16(const __half* a, const __half* b, __half* y, int n, cudaStream_t s) 
 }
 
 int nchw_to_nhwc_pad(const __half* in, __half* out, int B, int Cin, int HW, int Cpad, cudaStream_t s) {
+  DLM_REQUIRE(Cpad % 8 == 0 && Cpad >= Cin && (reinterpret_cast<uintptr_t>(out) & 15) == 0,
+              DLM_ERR_INVALID, "nchw_to_nhwc_pad: Cpad=%d must be a multiple of 8 and >= Cin", Cpad);
   const size_t total = static_cast<size_t>(B) * HW;
   nchw_to_nhwc_pad_kernel<<<static_cast<int>((total + 255) / 256), 256, 0, s>>>(in, out, B, Cin, HW, Cpad);
   DLM_CHECK_CUDA(cudaGetLastError());
@@ -370,9 +381,19 @@ int upsample2x_f32_to_f16(const float* in, __half* out, int N, int H, int W, int
 }
 
 int softmax_rows_f16(__half* s_, int rows, int cols, cudaStream_t s) {
-  DLM_REQUIRE(cols % 8 == 0 && cols <= 256 * 8 * kSoftmaxVec, DLM_ERR_INVALID,
-              "softmax_rows: cols=%d must be a multiple of 8 and <= %d", cols, 256 * 8 * kSoftmaxVec);
-  softmax_rows_kernel<<<rows, 256, 0, s>>>(s_, cols);
+  DLM_REQUIRE(cols % 8 == 0 && cols <= kSoftmaxMaxCols, DLM_ERR_INVALID,
+              "softmax_rows: cols=%d must be a multiple of 8 and <= %d", cols, kSoftmaxMaxCols);
+  const int vec = (cols / 8 + 255) / 256;
+  if (vec <= 1)
+    softmax_rows_kernel<1><<<rows, 256, 0, s>>>(s_, cols);
+  else if (vec <= 2)
+    softmax_rows_kernel<2><<<rows, 256, 0, s>>>(s_, cols);
+  else if (vec <= 4)
+    softmax_rows_kernel<4><<<rows, 256, 0, s>>>(s_, cols);
+  else if (vec <= 8)
+    softmax_rows_kernel<8><<<rows, 256, 0, s>>>(s_, cols);
+  else
+    softmax_rows_kernel<16><<<rows, 256, 0, s>>>(s_, cols);
   DLM_CHECK_CUDA(cudaGetLastError());
   return DLM_OK;
 }

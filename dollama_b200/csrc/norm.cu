@@ -48,13 +48,24 @@ __device__ __forceinline__ void load8(const float* p, float* f) {
   f[7] = b.w;
 }
 
-// partials[(n * chunks + chunk) * 32 + g] = (sum, sumsq).  T = __half or float (fp32 input: the
-// VAE's full-resolution residual stream).
+constexpr int kStatUnroll = 8;   // independent pixel loads in flight per thread (stats)
+constexpr int kApplyUnroll = 4;  // independent 16-byte loads in flight per thread (apply)
+constexpr int kFoldSets = kStatThreads / kGroups;
+
+// Statistics pass.  Block (chunk, n) reduces pixels [chunk * pix_per_chunk, ...) of image n to
+// per-group (sum, sum of squares) in fp32 and writes partials[(n * chunks + chunk) * 32 + g].
+// The block that finishes last for image n (arrival counter, counters[n]) folds that image's
+// partials in a fixed order in fp64, writes mean_rstd[n * 32 + g] = (mean, rstd) and resets the
+// counter to zero for the next launch.  The fold order does not depend on which block is last,
+// so the result is deterministic.  T = __half or float (fp32 input: the VAE's fp32 carries).
 template <typename T>
 __global__ void __launch_bounds__(kStatThreads)
     gn_stats_kernel(const T* __restrict__ x1, int C1, const T* __restrict__ x2, int C2,
-                    int HW, int pix_per_chunk, float2* __restrict__ partials) {
+                    int HW, int pix_per_chunk, float2* __restrict__ partials,
+                    float2* __restrict__ mean_rstd, unsigned* __restrict__ counters, float eps) {
   extern __shared__ float sh[];  // [PL][C] sums then [PL][C] sumsq
+  __shared__ double s_fold[2][kFoldSets][kGroups];
+  __shared__ int s_last;
   griddep_launch_dependents();
   griddep_wait();
   const int C = C1 + C2;
@@ -68,16 +79,29 @@ __global__ void __launch_bounds__(kStatThreads)
   for (int t = threadIdx.x; t < PL * nvec; t += blockDim.x) {
     const int cv = t % nvec, pl = t / nvec;
     const int c = cv * 8;
+    const T* base = c < C1 ? x1 + c : x2 + (c - C1);
+    const int ld = c < C1 ? C1 : C2;
     float a[8], q[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) a[i] = q[i] = 0.0f;
-    for (int pix = p0 + pl; pix < p1; pix += PL) {
+    const size_t img = static_cast<size_t>(n) * HW;
+    int pix = p0 + pl;
+    // full groups of kStatUnroll pixels: all loads issued before the first use
+    for (; pix + (kStatUnroll - 1) * PL < p1; pix += kStatUnroll * PL) {
+      float f[kStatUnroll][8];
+#pragma unroll
+      for (int u = 0; u < kStatUnroll; ++u) load8(base + (img + pix + u * PL) * ld, f[u]);
+#pragma unroll
+      for (int u = 0; u < kStatUnroll; ++u)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          a[i] += f[u][i];
+          q[i] = fmaf(f[u][i], f[u][i], q[i]);
+        }
+    }
+    for (; pix < p1; pix += PL) {
       float f[8];
-      const size_t row = static_cast<size_t>(n) * HW + pix;
-      if (c < C1)
-        load8(x1 + row * C1 + c, f);
-      else
-        load8(x2 + row * C2 + (c - C1), f);
+      load8(base + (img + pix) * ld, f);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         a[i] += f[i];
@@ -102,67 +126,110 @@ __global__ void __launch_bounds__(kStatThreads)
       }
     partials[(static_cast<size_t>(n) * chunks + chunk) * kGroups + g] = make_float2(a, q);
   }
-}
-
-// Each block handles `pix_per_block` pixels of image n = blockIdx.y.
-template <typename T>
-__global__ void __launch_bounds__(256)
-    gn_apply_kernel(const T* __restrict__ x1, int C1, const T* __restrict__ x2, int C2,
-                    int HW, const float2* __restrict__ partials, int chunks,
-                    const __half* __restrict__ gamma, const __half* __restrict__ beta, float eps,
-                    int silu, int pix_per_block, __half* __restrict__ out) {
-  __shared__ float s_mean[kGroups], s_rstd[kGroups];
-  griddep_launch_dependents();
-  griddep_wait();
-  const int C = C1 + C2;
-  const int n = blockIdx.y;
+  // publish this block's partials, then count it in
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(&counters[n], 1u) == static_cast<unsigned>(chunks - 1);
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  {
+    const int g = threadIdx.x % kGroups, set = threadIdx.x / kGroups;
+    double a = 0.0, q = 0.0;
+    const float2* pp = partials + static_cast<size_t>(n) * chunks * kGroups + g;
+#pragma unroll 8
+    for (int k = set; k < chunks; k += kFoldSets) {
+      const float2 v = __ldcg(pp + static_cast<size_t>(k) * kGroups);
+      a += v.x;
+      q += v.y;
+    }
+    s_fold[0][set][g] = a;
+    s_fold[1][set][g] = q;
+  }
+  __syncthreads();
   if (threadIdx.x < kGroups) {
     const int g = threadIdx.x;
     double a = 0.0, q = 0.0;
-    const float2* pp = partials + static_cast<size_t>(n) * chunks * kGroups + g;
-    for (int k = 0; k < chunks; ++k) {
-      const float2 v = pp[static_cast<size_t>(k) * kGroups];
-      a += v.x;
-      q += v.y;
+    for (int k = 0; k < kFoldSets; ++k) {
+      a += s_fold[0][k][g];
+      q += s_fold[1][k][g];
     }
     const double cnt = static_cast<double>(HW) * (C / kGroups);
     const double mean = a / cnt;
     double var = q / cnt - mean * mean;
     if (var < 0.0) var = 0.0;
-    s_mean[g] = static_cast<float>(mean);
-    s_rstd[g] = static_cast<float>(1.0 / sqrt(var + static_cast<double>(eps)));
+    mean_rstd[n * kGroups + g] =
+        make_float2(static_cast<float>(mean), static_cast<float>(1.0 / sqrt(var + static_cast<double>(eps))));
+    if (g == 0) counters[n] = 0u;
   }
-  __syncthreads();
+}
+
+// Apply pass: block (b, n) writes pixels [b * pix_per_block, ...) of image n as
+// y = (x - mean) * rstd * gamma + beta (optional SiLU), fp16.  Each thread owns one 8-channel
+// vector (its per-channel scale rstd * gamma and shift beta - mean * rstd * gamma stay in
+// registers) and walks the block's pixels with stride PL = 256 / (C / 8).
+template <typename T>
+__global__ void __launch_bounds__(256)
+    gn_apply_kernel(const T* __restrict__ x1, int C1, const T* __restrict__ x2, int C2,
+                    int HW, const float2* __restrict__ mean_rstd, const __half* __restrict__ gamma,
+                    const __half* __restrict__ beta, int silu, int pix_per_block,
+                    __half* __restrict__ out) {
+  griddep_launch_dependents();
+  griddep_wait();
+  const int C = C1 + C2;
+  const int n = blockIdx.y;
   const int nvec = C >> 3;
   const int cpg = C / kGroups;
+  const int PL = nvec >= static_cast<int>(blockDim.x) ? 1 : blockDim.x / nvec;
   const int p0 = blockIdx.x * pix_per_block;
   const int p1 = min(HW, p0 + pix_per_block);
-  const size_t total = static_cast<size_t>(p1 - p0) * nvec;
-  for (size_t t = threadIdx.x; t < total; t += blockDim.x) {
-    const int cv = static_cast<int>(t % nvec);
-    const int pix = p0 + static_cast<int>(t / nvec);
+  const size_t img = static_cast<size_t>(n) * HW;
+  for (int w = threadIdx.x; w < PL * nvec; w += blockDim.x) {
+    const int cv = w % nvec, pl = w / nvec;
     const int c = cv * 8;
-    const size_t row = static_cast<size_t>(n) * HW + pix;
-    float f[8], gm[8], bt[8];
-    if (c < C1)
-      load8(x1 + row * C1 + c, f);
-    else
-      load8(x2 + row * C2 + (c - C1), f);
-    load8(gamma + c, gm);
-    load8(beta + c, bt);
-    uint32_t o[4];
+    float sc[8], sh[8];
+    {
+      float gm[8], bt[8];
+      load8(gamma + c, gm);
+      load8(beta + c, bt);
 #pragma unroll
-    for (int i = 0; i < 8; i += 2) {
-      const int g0 = (c + i) / cpg, g1 = (c + i + 1) / cpg;
-      float y0 = (f[i] - s_mean[g0]) * s_rstd[g0] * gm[i] + bt[i];
-      float y1 = (f[i + 1] - s_mean[g1]) * s_rstd[g1] * gm[i + 1] + bt[i + 1];
-      if (silu) {
-        y0 = silu_f(y0);
-        y1 = silu_f(y1);
+      for (int i = 0; i < 8; ++i) {
+        const float2 mr = __ldg(mean_rstd + n * kGroups + (c + i) / cpg);
+        sc[i] = mr.y * gm[i];
+        sh[i] = bt[i] - mr.x * sc[i];
       }
-      o[i >> 1] = pack_half2(y0, y1);
     }
-    *reinterpret_cast<uint4*>(out + row * C + c) = make_uint4(o[0], o[1], o[2], o[3]);
+    const T* src = c < C1 ? x1 + c : x2 + (c - C1);
+    const int ld = c < C1 ? C1 : C2;
+    __half* dst = out + c;
+    auto emit = [&](int pix, const float* f) {
+      uint32_t o[4];
+#pragma unroll
+      for (int i = 0; i < 8; i += 2) {
+        float y0 = fmaf(f[i], sc[i], sh[i]);
+        float y1 = fmaf(f[i + 1], sc[i + 1], sh[i + 1]);
+        if (silu) {
+          y0 = silu_f(y0);
+          y1 = silu_f(y1);
+        }
+        o[i >> 1] = pack_half2(y0, y1);
+      }
+      *reinterpret_cast<uint4*>(dst + (img + pix) * C) = make_uint4(o[0], o[1], o[2], o[3]);
+    };
+    int pix = p0 + pl;
+    // full groups of kApplyUnroll pixels: all loads issued before the first use
+    for (; pix + (kApplyUnroll - 1) * PL < p1; pix += kApplyUnroll * PL) {
+      float f[kApplyUnroll][8];
+#pragma unroll
+      for (int u = 0; u < kApplyUnroll; ++u) load8(src + (img + pix + u * PL) * ld, f[u]);
+#pragma unroll
+      for (int u = 0; u < kApplyUnroll; ++u) emit(pix + u * PL, f[u]);
+    }
+    for (; pix < p1; pix += PL) {
+      float f[8];
+      load8(src + (img + pix) * ld, f);
+      emit(pix, f);
+    }
   }
 }
 
@@ -237,6 +304,18 @@ __global__ void __launch_bounds__(256)
 
 }  // namespace
 
+// Scratch layout (float2 units): [N * 32 (mean, rstd)] [counters: N unsigned, padded to 32 float2]
+// [partials: N * chunks * 32].  The fixed-size head does not depend on the SM count.
+size_t gn_head_elems(int N) { return static_cast<size_t>(N) * kGroups + ((N + 63) / 64) * 32; }
+
+int gn_chunks(int N, int HW, int sms, int* ppc_out) {
+  int chunks = (2 * sms + N - 1) / N;
+  int ppc = (HW + chunks - 1) / chunks;
+  if (ppc < 8) ppc = 8;
+  *ppc_out = ppc;
+  return (HW + ppc - 1) / ppc;
+}
+
 int gn_plan(GnOp* op, const __half* x1, int C1, const __half* x2, int C2, int N, int HW,
             const __half* gamma, const __half* beta, float eps, bool silu, __half* out,
             float2* partials, size_t partial_cap) {
@@ -245,14 +324,13 @@ int gn_plan(GnOp* op, const __half* x1, int C1, const __half* x2, int C2, int N,
   DLM_REQUIRE(C % kGroups == 0 && C1 % 8 == 0 && C2 % 8 == 0 && (C2 == 0 || x2 != nullptr),
               DLM_ERR_INVALID, "gn: channels %d+%d must be multiples of 8 and of 32 in total", C1, C2);
   DLM_REQUIRE(C <= 4096, DLM_ERR_INVALID, "gn: at most 4096 channels");
+  DLM_REQUIRE(N > 0 && HW > 0 && N <= 65535, DLM_ERR_INVALID, "gn: bad batch %d / pixels %d", N, HW);
   const int sms = num_sms();
-  int chunks = (4 * sms + N - 1) / N;
-  int ppc = (HW + chunks - 1) / chunks;
-  if (ppc < 8) ppc = 8;
-  chunks = (HW + ppc - 1) / ppc;
-  DLM_REQUIRE(static_cast<size_t>(N) * chunks * kGroups <= partial_cap, DLM_ERR_NOMEM,
-              "gn: partial buffer too small (%zu < %zu)", partial_cap,
-              static_cast<size_t>(N) * chunks * kGroups);
+  int ppc = 0;
+  const int chunks = gn_chunks(N, HW, sms, &ppc);
+  const size_t need = gn_head_elems(N) + static_cast<size_t>(N) * chunks * kGroups;
+  DLM_REQUIRE(need <= partial_cap, DLM_ERR_NOMEM, "gn: partial buffer too small (%zu < %zu)",
+              partial_cap, need);
   op->x1 = x1;
   op->x2 = x2;
   op->C1 = C1;
@@ -264,13 +342,16 @@ int gn_plan(GnOp* op, const __half* x1, int C1, const __half* x2, int C2, int N,
   op->eps = eps;
   op->silu = silu;
   op->out = out;
-  op->partials = partials;
+  op->mean_rstd = partials;
+  op->counters = reinterpret_cast<unsigned*>(partials + static_cast<size_t>(N) * kGroups);
+  op->partials = partials + gn_head_elems(N);
   op->chunks = chunks;
   op->pix_per_chunk = ppc;
   const int nvec = C / 8;
   const int PL = nvec >= kStatThreads ? 1 : kStatThreads / nvec;
   op->stat_smem = 2 * PL * C * static_cast<int>(sizeof(float));
-  int ppb = (HW + (2 * sms + N - 1) / N - 1) / ((2 * sms + N - 1) / N);
+  const int per_img = (2 * sms + N - 1) / N;
+  int ppb = (HW + per_img - 1) / per_img;
   if (ppb < 4) ppb = 4;
   op->pix_per_block = ppb;
   return DLM_OK;
@@ -291,13 +372,17 @@ int gn_plan_f32(GnOp* op, const float* x, int C, int N, int HW, const __half* ga
 
 size_t gn_partial_elems(int N, int HW) {
   const int sms = 148 * 2;  // generous bound for any SM count up to 296
-  (void)HW;
-  return static_cast<size_t>(N) * ((4 * sms + N - 1) / N + 1) * kGroups;
+  int ppc = 0;
+  const int chunks = gn_chunks(N, HW > 0 ? HW : 1, sms, &ppc);
+  const int chunks_any = (2 * sms + N - 1) / N;  // upper bound for any HW
+  return gn_head_elems(N) + static_cast<size_t>(N) * (chunks > chunks_any ? chunks : chunks_any) * kGroups;
 }
+
+size_t gn_counter_bytes(int N) { return static_cast<size_t>(N) * sizeof(unsigned); }
 
 int gn_launch(const GnOp& op, cudaStream_t s) {
   // stat_smem <= 2 * 256 * 8 floats * 4 B (PL * C <= 256 * 8 for C / 8 < 256) or 2 * C * 4 B
-  // (C <= 4096): always within the 48 KB default, no attribute needed.
+  // (C <= 4096): within the 48 KB default together with the 4 KB fold buffer.
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -311,10 +396,12 @@ int gn_launch(const GnOp& op, cudaStream_t s) {
   if (op.xf) {
     DLM_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gn_stats_kernel<float>, op.xf, op.C1,
                                       static_cast<const float*>(nullptr), 0, op.HW,
-                                      op.pix_per_chunk, op.partials));
+                                      op.pix_per_chunk, op.partials, op.mean_rstd, op.counters,
+                                      op.eps));
   } else {
     DLM_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gn_stats_kernel<__half>, op.x1, op.C1, op.x2, op.C2,
-                                      op.HW, op.pix_per_chunk, op.partials));
+                                      op.HW, op.pix_per_chunk, op.partials, op.mean_rstd,
+                                      op.counters, op.eps));
   }
   const int blocks = (op.HW + op.pix_per_block - 1) / op.pix_per_block;
   cfg.gridDim = dim3(blocks, op.N, 1);
@@ -323,13 +410,12 @@ int gn_launch(const GnOp& op, cudaStream_t s) {
   if (op.xf) {
     DLM_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gn_apply_kernel<float>, op.xf, op.C1,
                                       static_cast<const float*>(nullptr), 0, op.HW,
-                                      static_cast<const float2*>(op.partials), op.chunks, op.gamma,
-                                      op.beta, op.eps, op.silu ? 1 : 0, op.pix_per_block, op.out));
+                                      static_cast<const float2*>(op.mean_rstd), op.gamma, op.beta,
+                                      op.silu ? 1 : 0, op.pix_per_block, op.out));
   } else {
     DLM_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gn_apply_kernel<__half>, op.x1, op.C1, op.x2, op.C2,
-                                      op.HW, static_cast<const float2*>(op.partials), op.chunks,
-                                      op.gamma, op.beta, op.eps, op.silu ? 1 : 0, op.pix_per_block,
-                                      op.out));
+                                      op.HW, static_cast<const float2*>(op.mean_rstd), op.gamma,
+                                      op.beta, op.silu ? 1 : 0, op.pix_per_block, op.out));
   }
   return DLM_OK;
 }
@@ -366,6 +452,9 @@ int dlm_group_norm_nhwc(const void* x1, int C1, const void* x2, int C2, int N, i
                         eps, silu != 0, static_cast<__half*>(out), static_cast<float2*>(scratch),
                         scratch_bytes / sizeof(float2));
   if (rc != DLM_OK) return rc;
+  // the caller's scratch may hold anything: start the arrival counters at zero
+  DLM_CHECK_CUDA(cudaMemsetAsync(op.counters, 0, dlm::gn_counter_bytes(N),
+                                 static_cast<cudaStream_t>(stream)));
   return dlm::gn_launch(op, static_cast<cudaStream_t>(stream));
 }
 

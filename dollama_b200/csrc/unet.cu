@@ -987,6 +987,9 @@ int UNetModel::plan(int B, int H, int Wd) {
     release_plan();
     return rc;
   }
+  // GroupNorm's arrival counters start at zero (each launch leaves them at zero)
+  DLM_CHECK_CUDA(cudaMemset(gn_partials_, 0, gn_partial_cap_ * sizeof(float2)));
+  DLM_CHECK_CUDA(cudaDeviceSynchronize());
   return DLM_OK;
 }
 

@@ -130,8 +130,9 @@ int dlm_attention_tokens(const void* q, int ldq, const void* k, int ldk, const v
  * (x2 may be NULL with C2 = 0), optionally followed by SiLU; out is [N, HW, C1 + C2].
  * Replaces launch_group_norm / launch_group_norm_mb / launch_group_norm_silu (reference
  * src/kernels/groupnorm.cuh:51-108) and the up-path concat (src/infer/unet.cu:250).
- * Deterministic (fixed-order reductions).  `scratch` holds the per-chunk partial sums:
- * dlm_group_norm_nhwc_scratch_bytes(N, HW) bytes.
+ * Deterministic (fixed-order reductions).  `scratch` holds the per-chunk partial sums, the
+ * per-image statistics and arrival counters: dlm_group_norm_nhwc_scratch_bytes(N, HW) bytes of any
+ * content (the call zeroes the counters on `stream` before its two kernels).
  */
 size_t dlm_group_norm_nhwc_scratch_bytes(int N, int HW);
 int dlm_group_norm_nhwc(const void* x1, int C1, const void* x2, int C2, int N, int HW,
