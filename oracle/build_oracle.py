@@ -1,6 +1,7 @@
 """Build recipe of the test oracles (test infrastructure only).
 
-* oracle/_build/liboracle_bitnet.so — the plain-C restatement (bitnet_oracle.c), always built;
+* oracle/_build/liboracle_bitnet.so — the plain-C restatements (bitnet_oracle.c: quantizers and
+  BitLinear; bitnet_lm.c: LM forward and greedy decode), always built;
 * oracle/_ref/libref_bitnet.so      — the reference's own BitNet integer path, compiled from
   its header where it lies (src/models/bitnet.hpp under the reference tree) through
   ref_bitnet_shim.cpp, built only when the reference tree exists (it does not on GPU boxes,
@@ -34,9 +35,12 @@ def build() -> dict:
     BUILD.mkdir(exist_ok=True)
     out = {}
     lib = BUILD / "liboracle_bitnet.so"
-    src = HERE / "bitnet_oracle.c"
-    if _stale(lib, src):
-        _run(["gcc", "-O2", "-fPIC", "-shared", "-std=c11", "-o", str(lib), str(src), "-lm"])
+    srcs = [HERE / "bitnet_oracle.c", HERE / "bitnet_lm.c"]
+    if _stale(lib, *srcs):
+        # no -ffast-math / -mfma: double expressions are evaluated exactly as written, like the
+        # reference's own build of the same formulas
+        _run(["gcc", "-O2", "-fPIC", "-shared", "-std=c11", "-ffp-contract=off", "-o", str(lib)]
+             + [str(x) for x in srcs] + ["-lm"])
     out["oracle_bitnet"] = str(lib)
     hdr = REFERENCE / "src" / "models" / "bitnet.hpp"
     if hdr.exists():
@@ -44,8 +48,8 @@ def build() -> dict:
         ref = REF_OUT / "libref_bitnet.so"
         shim = HERE / "ref_bitnet_shim.cpp"
         if _stale(ref, shim, hdr):
-            _run(["g++", "-O2", "-fPIC", "-shared", "-std=c++17", "-I", str(REFERENCE / "src"),
-                  "-o", str(ref), str(shim)])
+            _run(["g++", "-O2", "-fPIC", "-shared", "-std=c++17", "-ffp-contract=off",
+                  "-I", str(REFERENCE / "src"), "-o", str(ref), str(shim)])
         out["ref_bitnet"] = str(ref)
     return out
 
