@@ -78,6 +78,16 @@ _SIGS = {
                                ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
     "dlm_unet_info": (c_int, [c_void_p, ctypes.POINTER(ctypes.c_int64),
                               ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(c_int)]),
+    "dlm_bitnet_create": (c_int, [c_void_p, c_int, ctypes.POINTER(c_char_p), ctypes.POINTER(c_void_p),
+                                  ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(c_void_p),
+                                  c_void_p]),
+    "dlm_bitnet_destroy": (c_int, [c_void_p]),
+    "dlm_bitnet_forward": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p]),
+    "dlm_bitnet_generate": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p,
+                                    c_void_p]),
+    "dlm_bitnet_weight_count": (c_int, [c_void_p]),
+    "dlm_bitnet_weight_info": (c_int, [c_void_p, c_int, ctypes.c_char_p, c_int,
+                                       ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(c_int)]),
     "dlm_vae_create": (c_int, [c_int, ctypes.POINTER(c_char_p), ctypes.POINTER(c_void_p),
                                ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(c_void_p), c_void_p]),
     "dlm_vae_destroy": (c_int, [c_void_p]),

@@ -16,7 +16,7 @@
 // coalesced 16-byte loads.
 #include <cstdint>
 
-#include "common.h"
+#include "ternary.h"
 
 namespace dlm {
 
@@ -39,6 +39,41 @@ __global__ void ternary_pack_kernel(const float* __restrict__ w, int N, int K,
   const double a = __ddiv_rn(sum_abs, static_cast<double>(K));
   alpha[n] = static_cast<float>(a);
   const double inv = a == 0.0 ? 0.0 : __ddiv_rn(1.0, a);
+  uint32_t* out = packed + static_cast<size_t>(n) * (K / 16);
+  for (int w16 = 0; w16 < K / 16; ++w16) {
+    uint32_t word = 0;
+    for (int j = 0; j < 16; ++j) {
+      uint32_t code = 0;
+      if (a != 0.0) {
+        double r = round(__dmul_rn(static_cast<double>(row[w16 * 16 + j]), inv));
+        if (r > 1.0) r = 1.0;
+        if (r < -1.0) r = -1.0;
+        code = r > 0.0 ? 1u : (r < 0.0 ? 3u : 0u);
+      }
+      word |= code << (2 * j);
+    }
+    out[w16] = word;
+  }
+}
+
+// Per-tensor alpha: sum |w| over the whole tensor in row-major order, one thread (load time only),
+// so the double sum rounds exactly as a sequential loop.
+__global__ void tensor_absmean_kernel(const float* __restrict__ w, size_t n, double* __restrict__ out) {
+  double sum_abs = 0.0;
+  for (size_t i = 0; i < n; ++i) sum_abs = __dadd_rn(sum_abs, fabs(static_cast<double>(w[i])));
+  *out = __ddiv_rn(sum_abs, static_cast<double>(n));
+}
+
+// Packs every row with the given alpha (one thread per row).
+__global__ void ternary_pack_alpha_kernel(const float* __restrict__ w, int N, int K,
+                                          const double* __restrict__ alpha_in,
+                                          uint32_t* __restrict__ packed, float* __restrict__ alpha) {
+  const int n = blockIdx.x * blockDim.x + threadIdx.x;
+  if (n >= N) return;
+  const double a = *alpha_in;
+  alpha[n] = static_cast<float>(a);
+  const double inv = a == 0.0 ? 0.0 : __ddiv_rn(1.0, a);
+  const float* row = w + static_cast<size_t>(n) * K;
   uint32_t* out = packed + static_cast<size_t>(n) * (K / 16);
   for (int w16 = 0; w16 < K / 16; ++w16) {
     uint32_t word = 0;
@@ -94,7 +129,7 @@ __device__ __forceinline__ uint32_t decode4(uint32_t b) {
 __global__ void __launch_bounds__(kThreads)
     ternary_gemm_kernel(const uint32_t* __restrict__ wp, const float* __restrict__ alpha,
                         const int8_t* __restrict__ xq, const float* __restrict__ xscale,
-                        float* __restrict__ y, int M, int N, int K) {
+                        float* __restrict__ y, int M, int N, int K, int accumulate) {
   __shared__ __align__(16) int8_t sw[kTN * kRow];
   __shared__ __align__(16) int8_t sx[kTM * kRow];
   const int n0 = blockIdx.x * kTN, m0 = blockIdx.y * kTM;
@@ -165,7 +200,9 @@ __global__ void __launch_bounds__(kThreads)
       const int n = n0 + tx + 16 * i;
       if (n >= N) continue;
       const double v = __dmul_rn(__dmul_rn(static_cast<double>(acc[j][i]), static_cast<double>(alpha[n])), s);
-      y[static_cast<size_t>(m) * N + n] = static_cast<float>(v);
+      float* dst = y + static_cast<size_t>(m) * N + n;
+      // accumulate: the residual update h += bitlinear(x) as one float add (bitnet.hpp:579-583)
+      *dst = accumulate ? __fadd_rn(*dst, __double2float_rn(v)) : __double2float_rn(v);
     }
   }
 }
@@ -180,6 +217,17 @@ int ternary_pack(const float* w, int N, int K, uint32_t* packed, float* alpha, c
   return DLM_OK;
 }
 
+int ternary_pack_per_tensor(const float* w, int N, int K, uint32_t* packed, float* alpha,
+                            double* scratch, cudaStream_t s) {
+  DLM_REQUIRE(w && packed && alpha && scratch, DLM_ERR_INVALID, "ternary_pack: null pointer");
+  DLM_REQUIRE(N > 0 && K > 0 && K % 64 == 0, DLM_ERR_INVALID, "ternary_pack: K=%d must be a multiple of 64", K);
+  tensor_absmean_kernel<<<1, 1, 0, s>>>(w, static_cast<size_t>(N) * K, scratch);
+  DLM_CHECK_CUDA(cudaGetLastError());
+  ternary_pack_alpha_kernel<<<(N + 127) / 128, 128, 0, s>>>(w, N, K, scratch, packed, alpha);
+  DLM_CHECK_CUDA(cudaGetLastError());
+  return DLM_OK;
+}
+
 int quantize_act_i8(const float* x, int M, int K, int8_t* xq, float* xscale, cudaStream_t s) {
   DLM_REQUIRE(x && xq && xscale, DLM_ERR_INVALID, "quantize_act_i8: null pointer");
   DLM_REQUIRE(M > 0 && K > 0, DLM_ERR_INVALID, "quantize_act_i8: empty");
@@ -190,14 +238,14 @@ int quantize_act_i8(const float* x, int M, int K, int8_t* xq, float* xscale, cud
 }
 
 int ternary_gemm_i8(const uint32_t* wp, const float* alpha, const int8_t* xq, const float* xscale,
-                    float* y, int M, int N, int K, cudaStream_t s) {
+                    float* y, int M, int N, int K, cudaStream_t s, bool accumulate) {
   DLM_REQUIRE(wp && alpha && xq && xscale && y, DLM_ERR_INVALID, "ternary_gemm_i8: null pointer");
   DLM_REQUIRE(K % 64 == 0 && K < (1 << 24), DLM_ERR_INVALID,
               "ternary_gemm_i8: K=%d must be a multiple of 64", K);
   DLM_REQUIRE((reinterpret_cast<uintptr_t>(wp) & 15) == 0 && (reinterpret_cast<uintptr_t>(xq) & 15) == 0,
               DLM_ERR_INVALID, "ternary_gemm_i8: packed weights / activations must be 16-byte aligned");
   dim3 grid((N + kTN - 1) / kTN, (M + kTM - 1) / kTM);
-  ternary_gemm_kernel<<<grid, kThreads, 0, s>>>(wp, alpha, xq, xscale, y, M, N, K);
+  ternary_gemm_kernel<<<grid, kThreads, 0, s>>>(wp, alpha, xq, xscale, y, M, N, K, accumulate ? 1 : 0);
   DLM_CHECK_CUDA(cudaGetLastError());
   return DLM_OK;
 }

@@ -177,6 +177,43 @@ int dlm_ternary_gemm_i8(const void* w_packed2b, const float* row_scale, const in
 int dlm_bitlinear(const void* w_packed2b, const float* row_scale, const float* x, float* y, int M,
                   int N, int K, int8_t* xq_scratch, float* xscale_scratch, void* stream);
 
+/* ---------------------------------------------------------------- BitNet tag LM (model level)
+ *
+ * The ternary LM around BitLinear: BitNet::forward (reference src/models/bitnet.hpp:376-440) with
+ * the greedy decode rule of src/infer/bitnet.hpp:282-318 (argmax of the last position, ties to the
+ * smallest id, stop before <eos> = 2 or at max_len tokens), batched over sequences with a K/V
+ * cache.  Dimensions are parameters (the reference compiles them in, src/models/bitnet_config.hpp);
+ * head_dim is 64.  The reference's double-precision context arithmetic is reproduced operation by
+ * operation; BitLinear is exact. */
+typedef struct dlm_bitnet_config {
+  int vocab, d_model, n_layers, n_heads, ffn_dim, max_seq;
+  double rope_base, rms_eps;
+  int per_tensor_scale; /* 0: one ternary scale per output row (the reference); 1: per tensor */
+} dlm_bitnet_config;
+
+/* fp32 state dict (host or device pointers): "embed" [vocab, d], "final_norm" [d],
+ * "layers.N.{attn_norm, wq, wk, wv, wo, ffn_norm, w_gate, w_up, w_down}" (the reference loader's
+ * names, src/infer/bitnet.hpp:116-135).  BitLinear weights are quantized and 2-bit packed here. */
+int dlm_bitnet_create(const dlm_bitnet_config* cfg, int n, const char* const* names,
+                      const float* const* weights, const int64_t* numels, void** handle, void* stream);
+int dlm_bitnet_destroy(void* handle);
+
+/* logits [B, S, vocab] of every position of tokens [B, S] (BitNet::forward per sequence; host or
+ * device pointers).  DLM_ERR_INVALID for ids outside [0, vocab) or S > max_seq. */
+int dlm_bitnet_forward(void* handle, const int* tokens, int B, int S, float* logits, void* stream);
+
+/* Greedy decode of prompts [B, P] (host or device) to at most max_len tokens per sequence
+ * (max_len <= max_seq): out [B, max_len - P] the generated ids (without <eos>), out_len [B] their
+ * counts.  One prefill over all prompt positions, then one decode pass per token (CUDA graph).
+ * Returns when the results are in out / out_len. */
+int dlm_bitnet_generate(void* handle, const int* prompts, int B, int P, int max_len, int* out,
+                        int* out_len, void* stream);
+
+/* The weight set dlm_bitnet_create expects for cfg: count, then per index its name and shape. */
+int dlm_bitnet_weight_count(const dlm_bitnet_config* cfg);
+int dlm_bitnet_weight_info(const dlm_bitnet_config* cfg, int index, char* name, int name_cap,
+                           int64_t* shape, int* ndim);
+
 /* ------------------------------------------------------------------ SDXL UNet (model level)
  *
  * Replaces unet_weights_create / launch_unet_batched / unet_weights_destroy (reference

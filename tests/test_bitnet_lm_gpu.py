@@ -1,0 +1,105 @@
+"""BitNet tag LM on the GPU (C ABI) against the C oracle of BitNet::forward (oracle/bitnet_lm.c,
+itself pinned bit for bit to the reference's compiled forward) and against the reference's own
+golden logits (tests/golden/bitnet_lm_ref.npz).
+
+The LM reproduces the reference's double-precision context arithmetic operation by operation and
+BitLinear exactly; the one source of last-bit differences is CUDA's double exp (softmax, SiLU)
+against the host C library's.  So logits are compared bit for bit where possible and otherwise
+within LOGIT_TOL of max|logit|, and greedy tokens must be identical.
+"""
+import hashlib
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from oracle import bitnet as B
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 1e-5
+GOLD = Path(__file__).resolve().parent / "golden" / "bitnet_lm_ref.npz"
+SMALL = B.lm_config(vocab=300, d_model=128, n_layers=2, n_heads=2, ffn_dim=192, max_seq=24)
+
+
+def _gpu(cfg, w):
+    from dollama_b200.bitnet_lm import BitNetConfig, BitNetLM
+    return BitNetLM(BitNetConfig(**cfg), w)
+
+
+def _cmp(got, ref):
+    eq = float(np.mean(got == ref))
+    err = float(np.max(np.abs(got - ref)) / max(np.max(np.abs(ref)), 1e-30))
+    print(f"logits: {100 * eq:.3f}% bit-identical, max rel err {err:.2e}")
+    assert err <= LOGIT_TOL
+    return eq
+
+
+@pytest.mark.parametrize("kind,per_tensor", [("normal", 0), ("ternary", 0), ("ternary", 1)])
+def test_forward_matches_oracle(kind, per_tensor):
+    cfg = dict(SMALL, per_tensor_scale=per_tensor)
+    w = B.lm_random_weights(cfg, seed=3, kind=kind)
+    toks = np.random.default_rng(4).integers(0, cfg["vocab"], size=(3, 10)).astype(np.int32)
+    lm = _gpu(cfg, w)
+    got = lm.forward(toks)
+    o = B.OracleLM(cfg, w)
+    ref = np.stack([o.forward(t) for t in toks])
+    assert _cmp(got, ref) > 0.99
+    lm.close()
+
+
+@pytest.mark.parametrize("case", [0, 1])
+def test_forward_matches_reference_golden(case):
+    g = np.load(GOLD)
+    d = [int(x) for x in g["dims"]]
+    cfg = B.lm_config(vocab=d[0], d_model=d[1], n_layers=d[2], n_heads=d[3], ffn_dim=d[4],
+                      max_seq=d[5])
+    w = B.lm_random_weights(cfg, seed=int(g[f"wseed{case}"]), kind=str(g[f"kind{case}"]))
+    lm = _gpu(cfg, w)
+    logits = lm.forward(g[f"tokens{case}"][None])[0]
+    _cmp(logits[0], g[f"first{case}"])
+    _cmp(logits[-1], g[f"last{case}"])
+    same = hashlib.sha256(logits.tobytes()).hexdigest() == str(g[f"sha{case}"])
+    print("whole logits bit-identical to the reference:", same)
+    lm.close()
+
+
+def test_generate_matches_oracle_with_eos_stops():
+    # a long <eos> (id 2) embedding row makes <eos> win at state-dependent steps, so sequences
+    # stop at different lengths (0, 6 and 19 of 19 here)
+    cfg = B.lm_config(vocab=64, d_model=128, n_layers=2, n_heads=2, ffn_dim=128, max_seq=24)
+    w = B.lm_random_weights(cfg, seed=8, kind="normal")
+    w["embed"][B.TOK_EOS] *= 30.0
+    prompts = np.random.default_rng(9).integers(3, cfg["vocab"], size=(16, 5)).astype(np.int32)
+    lm = _gpu(cfg, w)
+    got = lm.generate(prompts, max_len=24)
+    o = B.OracleLM(cfg, w)
+    ref = [o.generate(p, 24) for p in prompts]
+    assert got == ref
+    assert len({len(r) for r in ref}) > 2      # the stops really differ between sequences
+    lm.close()
+
+
+def test_generate_baseline_dims_matches_oracle():
+    """BASELINE config 5 dims (vocab 16000, d 512, 8 layers, FFN 1536), 64 prompt + 64 greedy
+    tokens, ternary weights; 8 sequences on the GPU, two of them re-derived by the oracle."""
+    cfg = B.lm_config()
+    w = B.lm_random_weights(cfg, seed=10, kind="ternary")
+    prompts = np.random.default_rng(11).integers(0, cfg["vocab"], size=(8, 64)).astype(np.int32)
+    lm = _gpu(cfg, w)
+    got = lm.generate(prompts, max_len=128)
+    o = B.OracleLM(cfg, w)
+    for b in (0, 5):
+        assert got[b] == o.generate(prompts[b], 128)
+    lm.close()
+
+
+def test_invalid_tokens_rejected():
+    from dollama_b200 import _lib as L
+    w = B.lm_random_weights(SMALL, seed=1)
+    lm = _gpu(SMALL, w)
+    with pytest.raises(L.DlmError):
+        lm.forward(np.array([[0, SMALL["vocab"]]], dtype=np.int32))
+    with pytest.raises(L.DlmError):
+        lm.generate(np.zeros((1, 4), dtype=np.int32), max_len=SMALL["max_seq"] + 1)
+    lm.close()
