@@ -3,6 +3,9 @@
     python -m dollama_b200.kernel_bench gemm --m 8192 --n 640 --k 640
     python -m dollama_b200.kernel_bench conv --n 8 --cin 320 --h 128 --w 128 --cout 320
     python -m dollama_b200.kernel_bench attn --b 2 --heads 10 --sq 4096 --sk 4096
+    python -m dollama_b200.kernel_bench gn --n 1 --h 512 --w 512 --cin 512
+    python -m dollama_b200.kernel_bench vae --h 128 --w 128            # whole decode (graph)
+    python -m dollama_b200.kernel_bench lm --b 256 --sq 64 --sk 128    # prefill 64 + greedy to 128
 
 Prints one JSON line: shape, microseconds per launch, achieved TFLOP/s and the fraction of the
 measured bf16 peak (MEASURED_PEAKS.json next to the repository, when present).  Used for the
@@ -43,7 +46,7 @@ def _time(fn, iters, warm=3):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("op", choices=["gemm", "conv", "attn", "ternary"])
+    ap.add_argument("op", choices=["gemm", "conv", "attn", "ternary", "gn", "vae", "lm"])
     ap.add_argument("--m", type=int, default=8192)
     ap.add_argument("--n", type=int, default=640)
     ap.add_argument("--k", type=int, default=640)
@@ -56,7 +59,11 @@ def main(argv=None):
     ap.add_argument("--sq", type=int, default=4096)
     ap.add_argument("--sk", type=int, default=4096)
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--tile-mode", type=int, default=0,
+                    help="GEMM tile choice: 0 auto, 1 single CTA, 2 CTA pair (+16 * forced N tile)")
     a = ap.parse_args(argv)
+    if a.tile_mode:
+        L.call("dlm_gemm_set_tile_mode", a.tile_mode)
     torch.manual_seed(0)
     dev = "cuda"
     if a.op == "gemm":
@@ -88,6 +95,37 @@ def main(argv=None):
         flops = 2.0 * a.m * a.n * a.k  # int8 ops
         shape = {"m": a.m, "n": a.n, "k": a.k,
                  "bytes": a.n * a.k / 4 + a.m * a.k + 4 * a.m * a.n + 4 * (a.m + a.n)}
+    elif a.op == "vae":
+        from .vae import SDXLVAEDecoder, random_weights
+        dec = SDXLVAEDecoder(random_weights(seed=9))
+        lat = torch.randn(1, 4, a.h, a.w, device=dev).half()
+        img = dec(lat)
+        fn = lambda: dec(lat, out=img)
+        flops = 10.47e12 * (a.h * a.w) / (128 * 128)
+        shape = {"latent": [1, 4, a.h, a.w], "launches": dec.info()["launches_per_decode"]}
+    elif a.op == "lm":
+        from .bitnet_lm import BitNetConfig, BitNetLM, random_weights
+        cfg = BitNetConfig(max_seq=max(a.sk, 1))
+        lm = BitNetLM(cfg, random_weights(cfg, seed=10))
+        prompts = torch.randint(0, cfg.vocab, (a.b, a.sq), dtype=torch.int32, device=dev)
+        out = torch.zeros(a.b, max(a.sk - a.sq, 1), dtype=torch.int32, device=dev)
+        lens = torch.zeros(a.b, dtype=torch.int32, device=dev)
+        fn = lambda: lm.generate_device(prompts, a.sk, out, lens)
+        flops = 0.0
+        shape = {"sequences": a.b, "prompt": a.sq, "max_len": a.sk,
+                 "generated_tokens": a.b * (a.sk - a.sq)}
+    elif a.op == "gn":
+        # GroupNorm(32) + SiLU over NHWC fp16 [n, h*w, cin]: two launches (statistics, apply)
+        x = torch.randn(a.n, a.h * a.w, a.cin, device=dev).half()
+        g = torch.ones(a.cin, device=dev).half()
+        bt = torch.zeros(a.cin, device=dev).half()
+        o = torch.empty_like(x)
+        sb = L.lib().dlm_group_norm_nhwc_scratch_bytes(a.n, a.h * a.w)
+        scr = torch.empty(sb, dtype=torch.uint8, device=dev)
+        fn = lambda: L.call("dlm_group_norm_nhwc", _p(x), a.cin, None, 0, a.n, a.h * a.w, _p(g), _p(bt),
+                            1e-6, 32, 1, _p(o), _p(scr), sb, _s())
+        flops = 0.0
+        shape = {"n": a.n, "hw": a.h * a.w, "c": a.cin, "bytes": 3.0 * x.numel() * 2}
     else:
         q = torch.randn(a.b, a.heads, a.sq, 64, device=dev).half()
         k = torch.randn(a.b, a.heads, a.sk, 64, device=dev).half()
@@ -102,11 +140,13 @@ def main(argv=None):
     pk = Path(__file__).resolve().parent.parent / "MEASURED_PEAKS.json"
     if pk.exists():
         peak = json.loads(pk.read_text()).get("bf16_tflops")
-    tf = flops / (ms / 1e3) / 1e12
+    tf = flops / (ms / 1e3) / 1e12 if flops else None
     if "bytes" in shape:
         shape["gbs"] = shape["bytes"] / (ms / 1e3) / 1e9
+    if "generated_tokens" in shape:
+        shape["tokens_per_s"] = shape["generated_tokens"] / (ms / 1e3)
     print(json.dumps({"op": a.op, **shape, "us": ms * 1e3, "tflops": tf,
-                      "frac_of_measured_bf16_burst": (tf / peak) if peak else None}))
+                      "frac_of_measured_bf16_burst": (tf / peak) if (peak and tf) else None}))
 
 
 if __name__ == "__main__":
