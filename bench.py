@@ -131,6 +131,24 @@ def dist_env():
     return ws, rank, local
 
 
+def max_over_ranks(ms_local: float, ws: int, device=None) -> float:
+    """The timed duration of the whole job: the maximum of every rank's device-timed duration
+    (one all-reduce MAX; a plain value when there is one rank)."""
+    if ws <= 1:
+        return float(ms_local)
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([float(ms_local)], dtype=torch.float64,
+                     device=device if device is not None else "cpu")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def job_throughput(ws: int, steps: int, ms_total: float) -> float:
+    """Whole-job steps/s: every rank runs `steps` steps of its own replica (weak scaling)."""
+    return ws * steps / (ms_total / 1000.0)
+
+
 def make_inputs(device, seed=6):
     import torch
     g = torch.Generator(device="cpu").manual_seed(seed)
@@ -251,13 +269,9 @@ def main():
     torch.cuda.synchronize()
     barrier()
     clocks = sampler.stop() if sampler else None
-    ms_local = e0.elapsed_time(e1)
-    t = torch.tensor([ms_local], device=dev, dtype=torch.float64)
-    if ws > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_total = float(t.item())
+    ms_total = max_over_ranks(e0.elapsed_time(e1), ws, dev)
     ms_step = ms_total / args.steps
-    value = ws * args.steps / (ms_total / 1000.0)
+    value = job_throughput(ws, args.steps, ms_total)
     finite = bool(torch.isfinite(out).all().item())
 
     if args.legs == "device":
@@ -282,10 +296,7 @@ def main():
     e1.record(stream)
     torch.cuda.synchronize()
     barrier()
-    t = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
-    if ws > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e_value = ws * args.steps / (float(t.item()) / 1000.0)
+    e2e_value = job_throughput(ws, args.steps, max_over_ranks(e0.elapsed_time(e1), ws, dev))
     h2d = sum(x.numel() * x.element_size() for x in host)
     d2h = hout.numel() * hout.element_size()
 

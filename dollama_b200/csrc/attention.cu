@@ -10,7 +10,10 @@
 //               lane r).  Per 128-key tile j: pass 1 reads S_j (TMEM) for the row max; the
 //               previous P.V result O_{j-1} is folded into the fp32 register accumulator with
 //               the running rescale; pass 2 computes p = 2^(s*c - m*c), the fp32 row sum, and
-//               stores P_j (fp16) into a 128-byte-swizzled K-major shared tile;
+//               stores P_j (fp16) into a 128-byte-swizzled K-major shared tile.  The softmax is
+//               bound by instruction issue and MUFU latency with two warps per scheduler, so the
+//               scale / shift, the row sum and the O rescale run as packed f32x2 FMA / add and
+//               the row max as three-input max (half the instructions of scalar code);
 //   warp 8      TMA producer: Q (both tiles) once, then K_j / V_j through a 3-stage ring;
 //   warp 9      TMEM owner + single-thread MMA issuer: S_j^t = Q_t K_j^T (M=128, N=128, K=64)
 //               and O_j^t = P_j^t V_j (M=128, N=64, K=128, V as an MN-major operand).
@@ -230,10 +233,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tmem_ld_32x32b_x32(to + (j & 1) * kD, r0);
       tmem_ld_32x32b_x32(to + (j & 1) * kD + 32, r1);
       tmem_ld_wait();
+      const uint64_t a2 = f2_pack(alpha, alpha);
 #pragma unroll
-      for (int q = 0; q < 32; ++q) {
-        acc[q] = fmaf(acc[q], alpha, __uint_as_float(r0[q]));
-        acc[32 + q] = fmaf(acc[32 + q], alpha, __uint_as_float(r1[q]));
+      for (int q = 0; q < 32; q += 2) {
+        uint64_t v = f2_fma(f2_pack(acc[q], acc[q + 1]), a2,
+                            f2_pack(__uint_as_float(r0[q]), __uint_as_float(r0[q + 1])));
+        f2_unpack(v, acc[q], acc[q + 1]);
+        v = f2_fma(f2_pack(acc[32 + q], acc[33 + q]), a2,
+                   f2_pack(__uint_as_float(r1[q]), __uint_as_float(r1[q + 1])));
+        f2_unpack(v, acc[32 + q], acc[33 + q]);
       }
       tc_fence_before();
       mbar_arrive(&o_empty[2 * t + (j & 1)]);
@@ -258,11 +266,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tmem_ld_wait();
         if (full_tile) {
 #pragma unroll
-          for (int q = 0; q < 32; q += 2) {
-            mx0 = fmaxf(mx0, __uint_as_float(ra[q]));
-            mx1 = fmaxf(mx1, __uint_as_float(ra[q + 1]));
-            mx2 = fmaxf(mx2, __uint_as_float(rb[q]));
-            mx3 = fmaxf(mx3, __uint_as_float(rb[q + 1]));
+          for (int q = 0; q < 32; q += 4) {
+            mx0 = max3f(mx0, __uint_as_float(ra[q]), __uint_as_float(ra[q + 1]));
+            mx1 = max3f(mx1, __uint_as_float(ra[q + 2]), __uint_as_float(ra[q + 3]));
+            mx2 = max3f(mx2, __uint_as_float(rb[q]), __uint_as_float(rb[q + 1]));
+            mx3 = max3f(mx3, __uint_as_float(rb[q + 2]), __uint_as_float(rb[q + 3]));
           }
         } else {
 #pragma unroll
@@ -281,7 +289,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         break;
       }
       // pass 2: p = exp2(s*c - m*c), fp32 row sum, fp16 P into shared memory
-      float sum0 = 0.0f, sum1 = 0.0f, sum2 = 0.0f, sum3 = 0.0f;
+      const uint64_t c2 = f2_pack(c, c), nmc2 = f2_pack(-mc, -mc);
+      uint64_t sumA = f2_pack(0.0f, 0.0f), sumB = sumA;
 #pragma unroll
       for (int cc = 0; cc < 4; cc += 2) {
         uint32_t ra[32], rb[32];
@@ -295,24 +304,27 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           uint32_t hp[16];
 #pragma unroll
           for (int q = 0; q < 32; q += 2) {
-            float e0 = fast_exp2(fmaf(__uint_as_float(r[q]), c, -mc));
-            float e1 = fast_exp2(fmaf(__uint_as_float(r[q + 1]), c, -mc));
+            float x0, x1;
+            f2_unpack(f2_fma(f2_pack(__uint_as_float(r[q]), __uint_as_float(r[q + 1])), c2, nmc2),
+                      x0, x1);
+            float e0 = fast_exp2(x0);
+            float e1 = fast_exp2(x1);
             if (!full_tile) {
               if (col0 + q >= valid) e0 = 0.0f;
               if (col0 + q + 1 >= valid) e1 = 0.0f;
             }
-            if (q & 2) {
-              sum2 += e0;
-              sum3 += e1;
-            } else {
-              sum0 += e0;
-              sum1 += e1;
-            }
+            if (q & 2)
+              sumB = f2_add(sumB, f2_pack(e0, e1));
+            else
+              sumA = f2_add(sumA, f2_pack(e0, e1));
             hp[q >> 1] = pack_half2(e0, e1);
           }
           store_p_chunk(pbuf, row, cc + half, hp);
         }
       }
+      float sum0, sum1, sum2, sum3;
+      f2_unpack(sumA, sum0, sum1);
+      f2_unpack(sumB, sum2, sum3);
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&p_full[t]);
