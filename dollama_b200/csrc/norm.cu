@@ -49,8 +49,10 @@ __device__ __forceinline__ void load8(const float* p, float* f) {
 }
 
 constexpr int kStatUnroll = 8;   // independent pixel loads in flight per thread (stats)
-constexpr int kApplyUnroll = 4;  // independent 16-byte loads in flight per thread (apply)
+constexpr int kApplyUnroll = 2;  // independent 16-byte loads in flight per thread (apply)
 constexpr int kFoldSets = kStatThreads / kGroups;
+constexpr int kBlocksPerSm = 4;  // stats / apply blocks per SM (16 warps each way would leave
+                                 // the passes latency bound)
 
 // Statistics pass.  Block (chunk, n) reduces pixels [chunk * pix_per_chunk, ...) of image n to
 // per-group (sum, sum of squares) in fp32 and writes partials[(n * chunks + chunk) * 32 + g].
@@ -59,7 +61,7 @@ constexpr int kFoldSets = kStatThreads / kGroups;
 // counter to zero for the next launch.  The fold order does not depend on which block is last,
 // so the result is deterministic.  T = __half or float (fp32 input: the VAE's fp32 carries).
 template <typename T>
-__global__ void __launch_bounds__(kStatThreads)
+__global__ void __launch_bounds__(kStatThreads, kBlocksPerSm)
     gn_stats_kernel(const T* __restrict__ x1, int C1, const T* __restrict__ x2, int C2,
                     int HW, int pix_per_chunk, float2* __restrict__ partials,
                     float2* __restrict__ mean_rstd, unsigned* __restrict__ counters, float eps) {
@@ -87,12 +89,14 @@ __global__ void __launch_bounds__(kStatThreads)
     const size_t img = static_cast<size_t>(n) * HW;
     int pix = p0 + pl;
     // full groups of kStatUnroll pixels: all loads issued before the first use
-    for (; pix + (kStatUnroll - 1) * PL < p1; pix += kStatUnroll * PL) {
-      float f[kStatUnroll][8];
+    // fp32 rows are twice the bytes: half the pixels in flight keep the same bytes per thread
+    constexpr int U = sizeof(T) == 4 ? kStatUnroll / 2 : kStatUnroll;
+    for (; pix + (U - 1) * PL < p1; pix += U * PL) {
+      float f[U][8];
 #pragma unroll
-      for (int u = 0; u < kStatUnroll; ++u) load8(base + (img + pix + u * PL) * ld, f[u]);
+      for (int u = 0; u < U; ++u) load8(base + (img + pix + u * PL) * ld, f[u]);
 #pragma unroll
-      for (int u = 0; u < kStatUnroll; ++u)
+      for (int u = 0; u < U; ++u)
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           a[i] += f[u][i];
@@ -137,7 +141,7 @@ __global__ void __launch_bounds__(kStatThreads)
     const int g = threadIdx.x % kGroups, set = threadIdx.x / kGroups;
     double a = 0.0, q = 0.0;
     const float2* pp = partials + static_cast<size_t>(n) * chunks * kGroups + g;
-#pragma unroll 8
+#pragma unroll 16
     for (int k = set; k < chunks; k += kFoldSets) {
       const float2 v = __ldcg(pp + static_cast<size_t>(k) * kGroups);
       a += v.x;
@@ -169,7 +173,7 @@ __global__ void __launch_bounds__(kStatThreads)
 // vector (its per-channel scale rstd * gamma and shift beta - mean * rstd * gamma stay in
 // registers) and walks the block's pixels with stride PL = 256 / (C / 8).
 template <typename T>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, kBlocksPerSm)
     gn_apply_kernel(const T* __restrict__ x1, int C1, const T* __restrict__ x2, int C2,
                     int HW, const float2* __restrict__ mean_rstd, const __half* __restrict__ gamma,
                     const __half* __restrict__ beta, int silu, int pix_per_block,
@@ -309,7 +313,7 @@ __global__ void __launch_bounds__(256)
 size_t gn_head_elems(int N) { return static_cast<size_t>(N) * kGroups + ((N + 63) / 64) * 32; }
 
 int gn_chunks(int N, int HW, int sms, int* ppc_out) {
-  int chunks = (2 * sms + N - 1) / N;
+  int chunks = (kBlocksPerSm * sms + N - 1) / N;
   int ppc = (HW + chunks - 1) / chunks;
   if (ppc < 8) ppc = 8;
   *ppc_out = ppc;
@@ -350,7 +354,7 @@ int gn_plan(GnOp* op, const __half* x1, int C1, const __half* x2, int C2, int N,
   const int nvec = C / 8;
   const int PL = nvec >= kStatThreads ? 1 : kStatThreads / nvec;
   op->stat_smem = 2 * PL * C * static_cast<int>(sizeof(float));
-  const int per_img = (2 * sms + N - 1) / N;
+  const int per_img = (kBlocksPerSm * sms + N - 1) / N;
   int ppb = (HW + per_img - 1) / per_img;
   if (ppb < 4) ppb = 4;
   op->pix_per_block = ppb;
@@ -374,7 +378,7 @@ size_t gn_partial_elems(int N, int HW) {
   const int sms = 148 * 2;  // generous bound for any SM count up to 296
   int ppc = 0;
   const int chunks = gn_chunks(N, HW > 0 ? HW : 1, sms, &ppc);
-  const int chunks_any = (2 * sms + N - 1) / N;  // upper bound for any HW
+  const int chunks_any = (kBlocksPerSm * sms + N - 1) / N;  // upper bound for any HW
   return gn_head_elems(N) + static_cast<size_t>(N) * (chunks > chunks_any ? chunks : chunks_any) * kGroups;
 }
 
