@@ -34,6 +34,10 @@ _SIGS = {
     "dlm_gemm_fp16_ex": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
                                  c_uint, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p]),
     "dlm_gemm_set_tile_mode": (c_int, [c_int]),
+    "dlm_gemm_workspace_bytes": (ctypes.c_size_t, []),
+    "dlm_gemm_fp16_ws": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
+                                 ctypes.c_uint, c_void_p, c_void_p, c_int, c_void_p, ctypes.c_size_t,
+                                 c_void_p]),
     "dlm_conv2d_nhwc_scratch_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int, c_int]),
     "dlm_conv2d_nhwc": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p,
                                 c_void_p, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),

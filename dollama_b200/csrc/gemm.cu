@@ -137,8 +137,38 @@ void pick_tile(int M, int N, int force_bn, int force_mode, int* bn_out, bool* pa
   *pair_out = false;
 }
 
-int g_force_mode = 0;  // test hook: 0 auto, 1 single CTA, 2 CTA pair
+int g_force_mode = 0;  // test hook: 0 auto, 1 single CTA, 2 CTA pair, 3 stream-K
 int g_force_bn = 0;    // test hook: forced N tile (0 = cost model)
+
+// Stream-K choice (single-CTA kernel over all SMs).  Only on request (tile mode 3): B200 sweeps
+// of the UNet shapes (M = 2048 / 8192 linears, long-K convs) measured the single-CTA stream-K
+// launch 1.3-3x slower than whole tiles, because with every SM loading 128 x 256 tiles the
+// aggregate L2 -> SM traffic (about 9 TB/s here) rather than the idle SMs bounds these launches;
+// splitting K does not reduce that traffic, larger (CTA-pair) tiles do.  Returns the N tile for
+// stream-K, or 0.
+int pick_stream_k(long m_tiles, int N, int num_kb, int bn, bool pair, const GemmEpilogue& e,
+                  int force_mode, int force_bn) {
+  const int sms = num_sms();
+  if (e.sk_ws == nullptr) return 0;
+  auto fits = [&](int b) {
+    return static_cast<size_t>(sms) * kGemmBM * b * 4 + gemm_sk_flag_bytes() <= e.sk_ws_bytes;
+  };
+  int best = 0;
+  long best_units = 0;
+  for (int b : {256, 192, 160, 128}) {
+    if (force_bn && b != force_bn) continue;
+    const long units = (m_tiles * ((N + b - 1) / b) * num_kb + sms - 1) / sms;
+    if (best == 0 || units < best_units) {
+      best = b;
+      best_units = units;
+    }
+  }
+  if (best == 0 || !fits(best)) return 0;
+  (void)bn;
+  (void)pair;
+  (void)best_units;
+  return force_mode == 3 ? best : 0;
+}
 
 bool bn_supported(int bn, bool pair) {
   if (pair) return bn == 256 || bn == 192 || bn == 160 || bn == 128;
@@ -222,7 +252,28 @@ int check_epilogue(const GemmEpilogue& e, int N, __half* C, int ldc) {
   return DLM_OK;
 }
 
+// Grid of a planned op: whole tiles (at most one CTA / pair per SM), or stream-K over every SM
+// with the workspace's flag head and partial slots.
+void set_grid(GemmOp* op, bool stream_k, const GemmEpilogue& e) {
+  GemmParams& p = op->p;
+  if (stream_k) {
+    p.sk_ctas = num_sms();
+    p.sk_flags = static_cast<int*>(e.sk_ws);
+    p.sk_ws = reinterpret_cast<float*>(static_cast<char*>(e.sk_ws) + gemm_sk_flag_bytes());
+    op->grid = p.sk_ctas;
+    return;
+  }
+  const int tiles = p.m_tiles * p.n_tiles;
+  const int slots = op->pair ? max_pairs(op->bn) : num_sms();
+  op->grid = (tiles < slots ? tiles : slots) * (op->pair ? 2 : 1);
+}
+
 }  // namespace
+
+size_t gemm_sk_flag_bytes() { return ((static_cast<size_t>(num_sms()) * 4 + 255) / 256) * 256; }
+size_t gemm_sk_workspace_bytes() {
+  return gemm_sk_flag_bytes() + static_cast<size_t>(num_sms()) * kGemmBM * 256 * 4;
+}
 
 int gemm_plan_dense(GemmOp* op, const __half* A, int lda, const __half* W, int M, int N, int K,
                     __half* C, int ldc, const GemmEpilogue& epi, int force_bn, int ldw) {
@@ -242,6 +293,12 @@ int gemm_plan_dense(GemmOp* op, const __half* A, int lda, const __half* W, int M
   int bn = 0;
   bool pair = false;
   pick_tile(M, N, force_bn ? force_bn : g_force_bn, g_force_mode, &bn, &pair);
+  const int sk_bn = pick_stream_k((M + kGemmBM - 1) / kGemmBM, N, (K + kGemmBK - 1) / kGemmBK, bn,
+                                  pair, epi, g_force_mode, force_bn ? force_bn : g_force_bn);
+  if (sk_bn) {
+    bn = sk_bn;
+    pair = false;
+  }
   DLM_REQUIRE(bn_supported(bn, pair), DLM_ERR_INVALID, "gemm: unsupported tile width %d", bn);
   std::memset(op, 0, sizeof(*op));
   if (!tmap_2d_f16(&op->tmA[0], A, M, K, lda, kGemmBM, kGemmBK)) return DLM_ERR_CUDA;
@@ -264,9 +321,7 @@ int gemm_plan_dense(GemmOp* op, const __half* A, int lda, const __half* W, int M
   op->bn = bn;
   op->pair = pair;
   op->k_true = K;
-  const int tiles = p.m_tiles * p.n_tiles;
-  const int slots = pair ? max_pairs(bn) : num_sms();
-  op->grid = (tiles < slots ? tiles : slots) * (pair ? 2 : 1);
+  set_grid(op, sk_bn != 0, epi);
   return DLM_OK;
 }
 
@@ -288,6 +343,14 @@ int gemm_plan_conv(GemmOp* op, int Nb, int oH, int oW, const ConvSource* srcs, i
   int bn = 0;
   bool pair = false;
   pick_tile(M, Cout, force_bn ? force_bn : g_force_bn, g_force_mode, &bn, &pair);
+  long ktot_blocks = 0;
+  for (int s = 0; s < nsrc; ++s) ktot_blocks += static_cast<long>(srcs[s].kind == 1 ? 1 : 9) * (srcs[s].C / 64);
+  const int sk_bn = pick_stream_k(M / kGemmBM, Cout, static_cast<int>(ktot_blocks), bn, pair, epi,
+                                  g_force_mode, force_bn ? force_bn : g_force_bn);
+  if (sk_bn) {
+    bn = sk_bn;
+    pair = false;
+  }
   DLM_REQUIRE(bn_supported(bn, pair), DLM_ERR_INVALID, "conv: unsupported tile width %d", bn);
   std::memset(op, 0, sizeof(*op));
   GemmParams& p = op->p;
@@ -342,9 +405,7 @@ int gemm_plan_conv(GemmOp* op, int Nb, int oH, int oW, const ConvSource* srcs, i
   op->bn = bn;
   op->pair = pair;
   op->k_true = ktot;
-  const int tiles = p.m_tiles * p.n_tiles;
-  const int slots = pair ? max_pairs(bn) : num_sms();
-  op->grid = (tiles < slots ? tiles : slots) * (pair ? 2 : 1);
+  set_grid(op, sk_bn != 0, epi);
   return DLM_OK;
 }
 
@@ -400,8 +461,8 @@ extern "C" {
 
 int dlm_gemm_set_tile_mode(int mode) {
   const int kernel = mode & 15, bn = mode >> 4;
-  DLM_REQUIRE(kernel >= 0 && kernel <= 2, DLM_ERR_INVALID,
-              "gemm_set_tile_mode: low bits 0 auto, 1 single, 2 pair");
+  DLM_REQUIRE(kernel >= 0 && kernel <= 3, DLM_ERR_INVALID,
+              "gemm_set_tile_mode: low bits 0 auto, 1 single, 2 pair, 3 stream-K");
   DLM_REQUIRE(bn == 0 || bn == 64 || bn == 128 || bn == 160 || bn == 192 || bn == 256,
               DLM_ERR_INVALID, "gemm_set_tile_mode: forced tile width %d", bn);
   dlm::g_force_mode = kernel;
@@ -420,6 +481,31 @@ int dlm_gemm_fp16_ex(const void* A, int lda, const void* W, void* C, int ldc, in
   e.rows_per_img = rows_per_img;
   e.resid = static_cast<const __half*>(residual);
   e.ldr = ldr;
+  dlm::GemmOp op;
+  int rc = dlm::gemm_plan_dense(&op, static_cast<const __half*>(A), lda,
+                                static_cast<const __half*>(W), M, N, K, static_cast<__half*>(C),
+                                ldc, e);
+  if (rc != DLM_OK) return rc;
+  return dlm::gemm_launch(op, static_cast<cudaStream_t>(stream));
+}
+
+size_t dlm_gemm_workspace_bytes(void) { return dlm::gemm_sk_workspace_bytes(); }
+
+int dlm_gemm_fp16_ws(const void* A, int lda, const void* W, void* C, int ldc, int M, int N, int K,
+                     unsigned flags, const void* bias, const void* residual, int ldr, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+  if (M == 0 || N == 0 || K == 0) return DLM_OK;
+  DLM_REQUIRE(workspace == nullptr || (reinterpret_cast<uintptr_t>(workspace) & 255) == 0,
+              DLM_ERR_INVALID, "gemm_fp16_ws: workspace must be 256-byte aligned");
+  DLM_REQUIRE(!(flags & ~(DLM_EPI_BIAS | DLM_EPI_RESID | DLM_EPI_GEGLU | DLM_EPI_SILU)),
+              DLM_ERR_INVALID, "gemm_fp16_ws: flags");
+  dlm::GemmEpilogue e;
+  e.flags = flags;
+  e.bias = static_cast<const __half*>(bias);
+  e.resid = static_cast<const __half*>(residual);
+  e.ldr = ldr;
+  e.sk_ws = workspace;
+  e.sk_ws_bytes = workspace ? workspace_bytes : 0;
   dlm::GemmOp op;
   int rc = dlm::gemm_plan_dense(&op, static_cast<const __half*>(A), lda,
                                 static_cast<const __half*>(W), M, N, K, static_cast<__half*>(C),

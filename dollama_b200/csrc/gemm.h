@@ -38,6 +38,12 @@ struct GemmEpilogue {
   float ln_eps = 1e-5f;
   const float* ln_u = nullptr;      // [N] sum_k W'[n,k]
   const float* ln_v = nullptr;      // [N] sum_k beta[k] W[n,k] + bias[n]
+  // stream-K workspace (optional): gemm_sk_workspace_bytes() bytes whose first
+  // gemm_sk_flag_bytes() are zero before the first launch (every launch leaves them zero).  When
+  // present, the planner may split the k-block iterations of a launch with fewer tiles than SMs
+  // over all SMs.  Launches sharing a workspace must not overlap on the GPU.
+  void* sk_ws = nullptr;
+  size_t sk_ws_bytes = 0;
 };
 
 // One source of an implicit-GEMM conv K segment.
@@ -58,6 +64,10 @@ int gemm_plan_conv(GemmOp* op, int Nb, int oH, int oW, const ConvSource* srcs, i
                    int force_bn = 0);
 
 int gemm_launch(const GemmOp& op, cudaStream_t stream);
+
+// Size of a stream-K workspace for this device, and of its flag head (zero between launches).
+size_t gemm_sk_workspace_bytes();
+size_t gemm_sk_flag_bytes();
 
 // Sets kernel attributes of every variant on the current device (call before graph capture).
 int gemm_prepare_kernels();

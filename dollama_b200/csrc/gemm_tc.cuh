@@ -65,6 +65,16 @@ struct GemmParams {
   const float* ln_u;
   const float* ln_v;
   int* status;
+  // stream-K (sk_ctas > 0, single-CTA kernel only): the m_tiles * n_tiles * num_kb k-block
+  // iterations are split evenly over sk_ctas CTAs (the whole grid, all resident at once), so a
+  // launch with fewer tiles than SMs still keeps every SM busy.  A tile cut between CTAs is
+  // finished by the CTA holding its first k-block (its owner, which reaches that segment last):
+  // it adds, in CTA order, the fp32 partial accumulators that the following CTAs wrote to
+  // sk_ws[cta] (always their first segment) and released through sk_flags[cta], then clears those
+  // flags for the next launch.
+  int sk_ctas;
+  float* sk_ws;   // [sk_ctas][128][BN] fp32
+  int* sk_flags;  // [sk_ctas], zero between launches
 };
 
 // Internal epilogue flags (beyond the public DLM_EPI_* bits).
@@ -72,6 +82,49 @@ constexpr unsigned kEpiRowStats = 1u << 8;
 constexpr unsigned kEpiLnFold = 1u << 9;
 constexpr unsigned kEpiOutF32 = 1u << 10;    // output stored as fp32 (p.out points to float)
 constexpr unsigned kEpiResidF32 = 1u << 11;  // residual read as fp32 (p.resid points to float)
+
+// Contiguous k-block iteration range [a, b) of CTA `cta` under stream-K.
+__device__ __forceinline__ void sk_range(const GemmParams& p, int cta, long long& a, long long& b) {
+  const long long total = static_cast<long long>(p.m_tiles) * p.n_tiles * p.num_kb;
+  const long long q = total / p.sk_ctas, r = total % p.sk_ctas;
+  a = cta * q + (cta < r ? cta : r);
+  b = a + q + (cta < r ? 1 : 0);
+}
+
+// One unit of a CTA's work: k-blocks [kb0, kb1) of one output tile.
+struct TileSeg {
+  int tile, kb0, kb1;
+};
+
+// This CTA's work, identical in the producer, MMA and epilogue warps: whole tiles with stride
+// gridDim (kb0 = 0, kb1 = num_kb), or under stream-K the tile segments of its iteration range.
+struct SegIter {
+  long long it, it1;
+  int t;
+  __device__ __forceinline__ void init(const GemmParams& p) {
+    if (p.sk_ctas > 0)
+      sk_range(p, blockIdx.x, it, it1);
+    else
+      t = blockIdx.x;
+  }
+  __device__ __forceinline__ bool next(const GemmParams& p, TileSeg& sg) {
+    if (p.sk_ctas > 0) {
+      if (it >= it1) return false;
+      sg.tile = static_cast<int>(it / p.num_kb);
+      sg.kb0 = static_cast<int>(it - static_cast<long long>(sg.tile) * p.num_kb);
+      const long long end = it1 - it + sg.kb0;
+      sg.kb1 = end < p.num_kb ? static_cast<int>(end) : p.num_kb;
+      it += sg.kb1 - sg.kb0;
+      return true;
+    }
+    if (t >= p.m_tiles * p.n_tiles) return false;
+    sg.tile = t;
+    sg.kb0 = 0;
+    sg.kb1 = p.num_kb;
+    t += gridDim.x;
+    return true;
+  }
+};
 
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;
@@ -138,7 +191,8 @@ __device__ __forceinline__ void chan_merge(float& n_a, float& mean_a, float& m2_
 template <int BN>
 __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t t_row, int row, int n0,
                                               int m_base, uint8_t* stage, const CUtensorMap* tmC,
-                                              int& sbuf) {
+                                              int& sbuf, int sk_c0 = 0, int sk_c1 = 0,
+                                              int r_in_tile = 0) {
   const int lane = threadIdx.x & 31;
   const bool row_ok = row < p.M;
   const bool geglu = (p.flags & DLM_EPI_GEGLU) != 0;
@@ -170,7 +224,22 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t t_ro
     tmem_ld_wait();
     float v[32];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+    // stream-K owner: add the other CTAs' partial accumulators of this row, in CTA order
+    for (int cc = sk_c0; cc < sk_c1; ++cc) {
+      const float4* src = reinterpret_cast<const float4*>(
+          p.sk_ws + (static_cast<size_t>(cc) * kGemmBM + r_in_tile) * BN + c);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 t4 = __ldcg(src + j);
+        v[4 * j] += t4.x;
+        v[4 * j + 1] += t4.y;
+        v[4 * j + 2] += t4.z;
+        v[4 * j + 3] += t4.w;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] *= p.alpha;
     const int n = n0 + c;
     if (p.flags & kEpiLnFold) {
 #pragma unroll
@@ -337,6 +406,24 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t t_ro
     p.stats_out[static_cast<size_t>(row) * p.stats_ld + n0 / BN] = make_float2(s_mean, s_m2);
 }
 
+// Stream-K contributor: this CTA's fp32 partial accumulator of its 32 rows of a cut tile, to its
+// workspace slot sk_ws[blockIdx.x] (128 contiguous bytes per lane and 32-column chunk).
+template <int BN>
+__device__ __forceinline__ void epilogue_partial(const GemmParams& p, uint32_t t_row, int r_in_tile) {
+  float* dst = p.sk_ws + (static_cast<size_t>(blockIdx.x) * kGemmBM + r_in_tile) * BN;
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 32) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(t_row + c, r);
+    tmem_ld_wait();
+    float4* d4 = reinterpret_cast<float4*>(dst + c);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      __stcg(d4 + j, make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                 __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])));
+  }
+}
+
 template <int BN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
@@ -359,7 +446,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* sk_bar = tempty + 2;  // stream-K: the four epilogue warps meet here
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sk_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -374,6 +462,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], 4);
     }
+    mbar_init(sk_bar, 4);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -396,19 +485,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   griddep_launch_dependents();
   griddep_wait();  // inputs of this GEMM are written by the previous kernel
 
-  const int num_tiles = p.m_tiles * p.n_tiles;
-
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        const int m0 = (t / p.n_tiles) * kGemmBM;
-        const int n0 = (t % p.n_tiles) * BN;
+      SegIter si;
+      si.init(p);
+      TileSeg sg;
+      while (ok && si.next(p, sg)) {
+        const int m0 = (sg.tile / p.n_tiles) * kGemmBM;
+        const int n0 = (sg.tile % p.n_tiles) * BN;
         if (p.amode == 0) {
-          for (int kb = 0; kb < p.num_kb; ++kb) {
+          for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
             if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status, kDevTimeoutProducer)) {
               ok = false;
               break;
@@ -427,37 +517,46 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const int rem = m0 - img * hw;
           const int oh0 = rem / p.oW;
           const int ow0 = rem - oh0 * p.oW;
-          int kb = 0;
-          for (int s = 0; s < p.nseg && ok; ++s) {
-            const ConvSeg sg = p.seg[s];
-            const CUtensorMap* am = sg.map == 0 ? &tmA0 : (sg.map == 1 ? &tmA1 : &tmA2);
-            const int ntaps = sg.kind == 1 ? 1 : 9;
-            for (int tap = 0; tap < ntaps && ok; ++tap) {
-              const int kh = tap / 3, kw = tap - (tap / 3) * 3;
-              for (int cb = 0; cb < sg.cblocks; ++cb) {
-                if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status, kDevTimeoutProducer)) {
-                  ok = false;
-                  break;
-                }
-                mbar_arrive_expect_tx(&full[stage], A_BYTES + B_BYTES);
-                uint8_t* dstA = sA + stage * A_BYTES;
-                if (sg.kind == 0) {
-                  tma_load_4d(dstA, am, &full[stage], cb * 64, ow0 + kw - 1, oh0 + kh - 1, img);
-                } else if (sg.kind == 1) {
-                  tma_load_4d(dstA, am, &full[stage], cb * 64, ow0, oh0, img);
-                } else {
-                  // input row 2*oh + kh - 1: kh=0 -> odd plane, row oh-1; kh=1 -> even, oh;
-                  // kh=2 -> odd, oh.  Same for columns.
-                  const int pr = (kh == 1) ? 0 : 1, dr = (kh == 0) ? -1 : 0;
-                  const int pc = (kw == 1) ? 0 : 1, dc = (kw == 0) ? -1 : 0;
-                  tma_load_5d(dstA, am, &full[stage], cb * 64, ow0 + dc, oh0 + dr, img, pr * 2 + pc);
-                }
-                tma_load_2d(sB + stage * B_BYTES, &tmB, &full[stage], kb * kGemmBK, n0);
-                ++kb;
-                if (++stage == STAGES) {
-                  stage = 0;
-                  phase ^= 1;
-                }
+          // k-block kb0 -> (segment, tap, channel block); K order is (segment, tap, channel)
+          int sidx = 0, base = 0;
+          while (sidx < p.nseg - 1 &&
+                 base + (p.seg[sidx].kind == 1 ? 1 : 9) * p.seg[sidx].cblocks <= sg.kb0) {
+            base += (p.seg[sidx].kind == 1 ? 1 : 9) * p.seg[sidx].cblocks;
+            ++sidx;
+          }
+          int tap = (sg.kb0 - base) / p.seg[sidx].cblocks;
+          int cb = (sg.kb0 - base) - tap * p.seg[sidx].cblocks;
+          for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
+            const ConvSeg cs = p.seg[sidx];
+            const CUtensorMap* am = cs.map == 0 ? &tmA0 : (cs.map == 1 ? &tmA1 : &tmA2);
+            const int kh = tap / 3, kw = tap - (tap / 3) * 3;
+            if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status, kDevTimeoutProducer)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&full[stage], A_BYTES + B_BYTES);
+            uint8_t* dstA = sA + stage * A_BYTES;
+            if (cs.kind == 0) {
+              tma_load_4d(dstA, am, &full[stage], cb * 64, ow0 + kw - 1, oh0 + kh - 1, img);
+            } else if (cs.kind == 1) {
+              tma_load_4d(dstA, am, &full[stage], cb * 64, ow0, oh0, img);
+            } else {
+              // input row 2*oh + kh - 1: kh=0 -> odd plane, row oh-1; kh=1 -> even, oh;
+              // kh=2 -> odd, oh.  Same for columns.
+              const int pr = (kh == 1) ? 0 : 1, dr = (kh == 0) ? -1 : 0;
+              const int pc = (kw == 1) ? 0 : 1, dc = (kw == 0) ? -1 : 0;
+              tma_load_5d(dstA, am, &full[stage], cb * 64, ow0 + dc, oh0 + dr, img, pr * 2 + pc);
+            }
+            tma_load_2d(sB + stage * B_BYTES, &tmB, &full[stage], kb * kGemmBK, n0);
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1;
+            }
+            if (++cb == cs.cblocks) {
+              cb = 0;
+              if (++tap == (cs.kind == 1 ? 1 : 9)) {
+                tap = 0;
+                ++sidx;
               }
             }
           }
@@ -472,13 +571,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t phase = 0;
       int i = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++i) {
+      SegIter si;
+      si.init(p);
+      TileSeg sg;
+      while (ok && si.next(p, sg)) {
         const int acc = i & 1;
         const uint32_t acc_phase = (i >> 1) & 1;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, p.status, kDevTimeoutMma)) break;
         tc_fence_after();
         const uint32_t d_tmem = tbase + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < p.num_kb; ++kb) {
+        for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, p.status, kDevTimeoutMma)) {
             ok = false;
             break;
@@ -490,7 +592,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           for (int k = 0; k < kGemmBK / 16; ++k) {
             const uint64_t ad = sw128_desc(a_base + k * 32, 16, 1024);
             const uint64_t bd = sw128_desc(b_base + k * 32, 16, 1024);
-            umma_f16_ss(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            umma_f16_ss(d_tmem, ad, bd, idesc, (kb != sg.kb0 || k != 0) ? 1u : 0u);
           }
           umma_commit(&empty[stage]);
           if (++stage == STAGES) {
@@ -499,28 +601,77 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
         if (ok) umma_commit(&tfull[acc]);
+        ++i;
       }
     }
   } else {
     // ------------------------------------------------------------ epilogue (warps 2..5)
     const int quad = warp & 3;
+    const int r_in_tile = quad * 32 + lane;
     int sbuf = 0;
     int i = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++i) {
+    uint32_t sk_phase = 0;
+    SegIter si;
+    si.init(p);
+    TileSeg sg;
+    // the four epilogue warps meet (bounded) before a stream-K flag changes hands
+    auto sk_meet = [&]() -> bool {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(sk_bar);
+      const bool okm = mbar_wait(sk_bar, sk_phase, abort_flag, p.status, kDevTimeoutEpilogue);
+      sk_phase ^= 1;
+      return okm;
+    };
+    bool ok = true;
+    while (ok && si.next(p, sg)) {
       const int acc = i & 1;
       const uint32_t acc_phase = (i >> 1) & 1;
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status, kDevTimeoutEpilogue)) break;
       tc_fence_after();
-      const int m0 = (t / p.n_tiles) * kGemmBM;
-      const int n0 = (t % p.n_tiles) * BN;
-      const int row = m0 + quad * 32 + lane;
+      const int m0 = (sg.tile / p.n_tiles) * kGemmBM;
+      const int n0 = (sg.tile % p.n_tiles) * BN;
+      const int row = m0 + r_in_tile;
       const uint32_t t_row = tbase + (static_cast<uint32_t>(quad * 32) << 16) +
                              static_cast<uint32_t>(acc * BN);
-      epilogue_tile<BN>(p, t_row, row, n0, m0 + quad * 32, sEpi + (warp - 2) * kStageBytesPerWarp,
-                        &tmC, sbuf);
+      if (p.sk_ctas > 0 && sg.kb0 > 0) {
+        // contributor: hand the partial accumulator to the tile's owner
+        epilogue_partial<BN>(p, t_row, r_in_tile);
+        __threadfence();
+        ok = sk_meet();
+        if (ok && warp == 2 && lane == 0) {
+          __threadfence();
+          flag_store_release(p.sk_flags + blockIdx.x, 1);
+        }
+      } else {
+        int c0 = blockIdx.x + 1, c1 = c0;
+        if (p.sk_ctas > 0 && sg.kb1 < p.num_kb) {
+          // owner of a cut tile: its contributors are the following CTAs whose ranges start
+          // inside it
+          const long long tile_end = static_cast<long long>(sg.tile + 1) * p.num_kb;
+          while (c1 < p.sk_ctas) {
+            long long a, b;
+            sk_range(p, c1, a, b);
+            if (a >= tile_end) break;
+            ++c1;
+          }
+          for (int cc = c0; cc < c1 && ok; ++cc)
+            ok = flag_wait_acquire(p.sk_flags + cc, 1, abort_flag, p.status, kDevTimeoutStreamK);
+        }
+        if (ok) {
+          epilogue_tile<BN>(p, t_row, row, n0, m0 + quad * 32, sEpi + (warp - 2) * kStageBytesPerWarp,
+                            &tmC, sbuf, c0, c1, r_in_tile);
+          if (c1 > c0) {
+            // every warp has read the partials: clear the flags for the next launch
+            ok = sk_meet();
+            if (ok && warp == 2)
+              for (int cc = c0 + lane; cc < c1; cc += 32) p.sk_flags[cc] = 0;
+          }
+        }
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
+      ++i;
     }
     if (lane == 0) bulk_wait_all();
   }

@@ -23,6 +23,7 @@ enum DeviceStatus : int {
   kDevTimeoutMma = 2,
   kDevTimeoutEpilogue = 3,
   kDevTimeoutSoftmax = 4,
+  kDevTimeoutStreamK = 5,  // a stream-K tile owner gave up waiting for a partial accumulator
 };
 
 }  // namespace dlm
@@ -94,6 +95,32 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
       }
     }
   }
+}
+
+// Waits (bounded) until the global flag holds `want`, with acquire semantics: every write the
+// signalling thread made before its release store is visible afterwards.
+__device__ __forceinline__ bool flag_wait_acquire(const int* flag, int want, volatile int* abort_flag,
+                                                  int* status, int code) {
+  const unsigned long long t0 = globaltimer_ns();
+  uint32_t it = 0;
+  while (true) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+    if (v == want) return true;
+    __nanosleep(64);
+    if ((++it & 15u) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+        if (status) atomicCAS(status, 0, code);
+        *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void flag_store_release(int* flag, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(flag), "r"(v) : "memory");
 }
 
 // Sleep for about `ns` nanoseconds (used on the abort path so that bulk copies and MMAs

@@ -60,7 +60,8 @@ def main(argv=None):
     ap.add_argument("--sk", type=int, default=4096)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--tile-mode", type=int, default=0,
-                    help="GEMM tile choice: 0 auto, 1 single CTA, 2 CTA pair (+16 * forced N tile)")
+                    help="GEMM tile choice: 0 auto, 1 single CTA, 2 CTA pair, 3 stream-K "
+                         "(+16 * forced N tile)")
     a = ap.parse_args(argv)
     if a.tile_mode:
         L.call("dlm_gemm_set_tile_mode", a.tile_mode)
@@ -70,7 +71,10 @@ def main(argv=None):
         A = torch.randn(a.m, a.k, device=dev).half()
         W = (torch.randn(a.n, a.k, device=dev) * a.k ** -0.5).half()
         C = torch.empty(a.m, a.n, device=dev, dtype=torch.half)
-        fn = lambda: L.call("dlm_launch_gemm_fp16", _p(A), _p(W), _p(C), a.m, a.n, a.k, 1.0, 0.0, 0, 1, _s())
+        nws = L.lib().dlm_gemm_workspace_bytes()
+        ws = torch.zeros(nws, dtype=torch.uint8, device=dev)  # stream-K workspace
+        fn = lambda: L.call("dlm_gemm_fp16_ws", _p(A), a.k, _p(W), _p(C), a.n, a.m, a.n, a.k, 0,
+                            None, None, 0, _p(ws), nws, _s())
         flops = 2.0 * a.m * a.n * a.k
         shape = {"m": a.m, "n": a.n, "k": a.k}
     elif a.op == "conv":

@@ -78,10 +78,22 @@ int dlm_gemm_fp16_ex(const void* A, int lda, const void* W, void* C, int ldc, in
                      unsigned flags, const void* bias, const void* bias2d, int rows_per_img,
                      const void* residual, int ldr, void* stream);
 
+/* The same fused linear with a stream-K workspace: when the launch has fewer output tiles than
+ * SMs, its k-block iterations may be split over every SM, the CTAs that hold a tile's later
+ * k-blocks handing fp32 partial sums to the CTA holding its first ones through `workspace`
+ * (dlm_gemm_workspace_bytes() bytes, 256-byte aligned, ZEROED once before its first use; every
+ * call leaves it ready for the next).  Calls sharing a workspace must not overlap on the GPU.
+ * flags: DLM_EPI_BIAS / RESID / GEGLU / SILU.  workspace == NULL behaves as dlm_gemm_fp16_ex. */
+size_t dlm_gemm_workspace_bytes(void);
+int dlm_gemm_fp16_ws(const void* A, int lda, const void* W, void* C, int ldc, int M, int N, int K,
+                     unsigned flags, const void* bias, const void* residual, int ldr, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
 /* Tile-kernel selection for the GEMM / conv entry points planned after the call (process-wide):
  * mode & 15: 0 = automatic (cost model), 1 = single-CTA kernel only, 2 = CTA-pair
- * (cta_group::2) kernel where M > 128; mode >> 4: forced N tile width (0 = cost model; 64, 128,
- * 160, 192, 256).  For tests and A/B measurements. */
+ * (cta_group::2) kernel where M > 128, 3 = stream-K over all SMs (where a workspace is given);
+ * mode >> 4: forced N tile width (0 = cost model; 64, 128, 160, 192, 256).  For tests and A/B
+ * measurements. */
 int dlm_gemm_set_tile_mode(int mode);
 
 /* ------------------------------------------------------------------ conv2d (implicit GEMM)

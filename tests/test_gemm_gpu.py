@@ -106,3 +106,63 @@ def test_gemm_unsupported_trans():
     rc = L.lib().dlm_launch_gemm_fp16(_ptr(A), _ptr(A), _ptr(A), 128, 64, 64, 1.0, 0.0, 1, 1,
                                       _stream())
     assert rc == -4
+
+
+# ---------------------------------------------------------------- stream-K
+
+@pytest.fixture(scope="module")
+def sk_workspace():
+    nbytes = L.lib().dlm_gemm_workspace_bytes()
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    return ws, nbytes
+
+
+@pytest.mark.parametrize("mode", [3, 3 + 16 * 160, 3 + 16 * 128, 0], ids=["sk256", "sk160", "sk128", "auto"])
+@pytest.mark.parametrize("M,N,K", [(2048, 1280, 5120),   # tiles cut between two or three CTAs
+                                   (300, 320, 1280),     # partial M and N tiles
+                                   (128, 256, 8192),     # one tile over 128 CTAs (one k-block each)
+                                   (256, 512, 128),      # fewer k-blocks than CTAs: idle CTAs
+                                   (8192, 640, 2560)])
+def test_gemm_stream_k(M, N, K, mode, sk_workspace):
+    ws, nbytes = sk_workspace
+    L.call("dlm_gemm_set_tile_mode", mode)
+    try:
+        A = _rand(M, K, seed=11)
+        W = _rand(N, K, scale=K ** -0.5, seed=12)
+        b = _rand(N, seed=13)
+        X = _rand(M, N, seed=14)
+        ref = X.float() + A.float() @ W.float().t() + b.float()
+        outs = []
+        for _ in range(2):   # the second launch checks that the first left the flags clear
+            C = X.clone()
+            L.call("dlm_gemm_fp16_ws", _ptr(A), K, _ptr(W), _ptr(C), N, M, N, K,
+                   L.EPI_BIAS | L.EPI_RESID, _ptr(b), _ptr(C), N, _ptr(ws), nbytes, _stream())
+            torch.cuda.synchronize()
+            outs.append(C)
+        assert torch.equal(outs[0], outs[1])   # fixed-order partial sums: deterministic
+        err = max_rel_err(outs[0], ref)
+        assert err < 2e-3, f"max rel err {err}"
+        code = ctypes.c_int()
+        L.call("dlm_get_device_status", ctypes.byref(code), 1, _stream())
+        assert code.value == 0
+    finally:
+        L.call("dlm_gemm_set_tile_mode", 0)
+
+
+def test_gemm_stream_k_geglu(sk_workspace):
+    ws, nbytes = sk_workspace
+    L.call("dlm_gemm_set_tile_mode", 3)
+    try:
+        M, N, K = 512, 1024, 4096
+        A = _rand(M, K, seed=21)
+        W = _rand(N, K, scale=K ** -0.5, seed=22)
+        b = _rand(N, seed=23)
+        C = torch.empty(M, N // 2, dtype=torch.float16, device="cuda")
+        L.call("dlm_gemm_fp16_ws", _ptr(A), K, _ptr(W), _ptr(C), N // 2, M, N, K,
+               L.EPI_BIAS | L.EPI_GEGLU, _ptr(b), None, 0, _ptr(ws), nbytes, _stream())
+        torch.cuda.synchronize()
+        y = A.float() @ W.float().t() + b.float()
+        ref = y[:, 0::2] * torch.nn.functional.gelu(y[:, 1::2])
+        assert max_rel_err(C, ref) < 2e-3
+    finally:
+        L.call("dlm_gemm_set_tile_mode", 0)
