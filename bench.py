@@ -329,6 +329,31 @@ def main():
         "by_class_ms": {k: round(v["ms"], 4) for k, v in ops.items()},
     }
 
+    # ---------------------------------------------------------------- whole image (txt2img)
+    # 20 Euler steps with CFG on the device + the VAE decode (dlm_sdxl_generate): one image per
+    # replica, no host round trip between steps
+    from dollama_b200.pipeline import euler_schedule, generate
+    from dollama_b200.vae import SDXLVAEDecoder, random_weights as vae_weights
+    vae = SDXLVAEDecoder(vae_weights(seed=9, device=dev))
+    sig, _ = euler_schedule(STEPS_PER_IMAGE)
+    g = torch.Generator(device="cpu").manual_seed(8)
+    init = (torch.randn(1, 4, LATENT, LATENT, generator=g) * sig[0]).to(dev)
+    generate(net, vae, init, ehs, te, tid, steps=STEPS_PER_IMAGE, guidance=7.5)  # warm-up
+    barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    img = generate(net, vae, init, ehs, te, tid, steps=STEPS_PER_IMAGE, guidance=7.5)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    img_ms = max_over_ranks(e0.elapsed_time(e1), ws, dev)
+    txt2img = {"ms_per_image": img_ms, "images_per_s": ws * 1000.0 / img_ms,
+               "steps": STEPS_PER_IMAGE, "guidance": 7.5,
+               "note": "dlm_sdxl_generate: 20 UNet steps (CFG batch 2) + Euler on the device + "
+                       "VAE decode to [1, 3, 1024, 1024]; text encoders not included",
+               "image_finite": bool(torch.isfinite(img).all().item())}
+    vae.close()
+
     # ---------------------------------------------------------------- CPU baseline (rank 0, N=1)
     cpu = None
     if keep_sd:
@@ -348,6 +373,7 @@ def main():
             "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
             "config": config(ws),
             "images_per_s": value / STEPS_PER_IMAGE,
+            "txt2img": txt2img,
             "pct_fp16_tc_peak": 100.0 * roofline["step"]["achieved_tflops"] / sustained,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},

@@ -92,6 +92,12 @@ _SIGS = {
     "dlm_bitnet_weight_count": (c_int, [c_void_p]),
     "dlm_bitnet_weight_info": (c_int, [c_void_p, c_int, ctypes.c_char_p, c_int,
                                        ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(c_int)]),
+    "dlm_sdxl_schedule": (c_int, [c_int, ctypes.POINTER(ctypes.c_float),
+                                  ctypes.POINTER(ctypes.c_float)]),
+    "dlm_sdxl_denoise": (c_int, [c_void_p, c_int, c_int, c_void_p, c_int, c_float, c_void_p,
+                                 c_void_p, c_void_p, c_void_p, c_void_p]),
+    "dlm_sdxl_generate": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_int, c_float,
+                                  c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_void_p]),
     "dlm_vae_create": (c_int, [c_int, ctypes.POINTER(c_char_p), ctypes.POINTER(c_void_p),
                                ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(c_void_p), c_void_p]),
     "dlm_vae_destroy": (c_int, [c_void_p]),

@@ -282,6 +282,26 @@ int dlm_unet_stage(void* handle, const char* name, const void** ptr, int* C, int
 /* Activation arena bytes, prepared weight bytes, kernel launches per step. */
 int dlm_unet_info(void* handle, int64_t* arena_bytes, int64_t* weight_bytes, int* num_launches);
 
+/* ---------------------------------------------------------------- SDXL denoising loop
+ *
+ * The txt2img loop of the reference's DiffusionPipeline::generate_txt2img
+ * (src/infer/diffusion.cu:896-988) on the device, without its per-step host round trip: Euler
+ * (epsilon prediction) over the SDXL schedule of src/infer/scheduler.hpp (scaled_linear betas
+ * 0.00085..0.012, 1000 training steps, "leading" spacing, steps_offset 1), classifier-free
+ * guidance e = e_uncond + g * (e_cond - e_uncond), the UNet run at batch 2 (cond, uncond).
+ * init_latent [1, 4, H, W] fp32 is the starting latent (randn * sigmas[0], as the reference
+ * draws it); ehs [2, 77, 2048], text_embeds [2, 1280] (cond first), time_ids [6] fp16; device
+ * pointers.  Enqueued on `stream`. */
+int dlm_sdxl_schedule(int steps, float* sigmas /* [steps + 1] */, float* timesteps /* [steps] */);
+int dlm_sdxl_denoise(void* unet, int H, int W, const float* init_latent, int steps, float guidance,
+                     const void* ehs, const void* text_embeds, const void* time_ids,
+                     float* latent_out, void* stream);
+/* The same loop followed by the VAE decode of fp16(latent / vae_scaling) (diffusion.cu:979-988):
+ * image [1, 3, 8H, 8W] fp16. */
+int dlm_sdxl_generate(void* unet, void* vae, int H, int W, const float* init_latent, int steps,
+                      float guidance, const void* ehs, const void* text_embeds, const void* time_ids,
+                      float vae_scaling, void* image, void* stream);
+
 /* ---------------------------------------------------------------- SDXL VAE decoder
  * Resident-weight handle of the AutoencoderKL decoder.  Replaces vae_weights_create /
  * vae_weights_destroy / launch_vae_decode(handle, d_latent, d_image_out)
