@@ -46,6 +46,10 @@ _SIGS = {
     "dlm_nhwc_to_nchw": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
     "dlm_launch_attention": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
                                      c_int, c_int, c_float, c_void_p]),
+    "dlm_attention_workspace_bytes": (ctypes.c_size_t, [c_int, c_int, c_int]),
+    "dlm_launch_attention_ws": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
+                                        c_int, c_int, c_float, c_void_p, ctypes.c_size_t,
+                                        c_void_p]),
     "dlm_attention_tokens": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p,
                                      c_int, c_int, c_int, c_int, c_int, c_int, c_float, c_void_p]),
     "dlm_group_norm_nhwc_scratch_bytes": (c_size_t, [c_int, c_int]),

@@ -66,6 +66,68 @@ __device__ __forceinline__ void store_p_chunk(uint8_t* pbuf, int row, int chunk3
   }
 }
 
+// Work of one CTA: KV tiles [j0, j1) of one group (a 256-query block of one (batch, head));
+// `whole` when that is every tile of the group.
+struct AttnSeg {
+  int group, j0, j1;
+  bool whole;
+};
+
+__device__ __forceinline__ void attn_range(long long total, int ctas, int cta, long long& a,
+                                           long long& b) {
+  const long long q = total / ctas, r = total % ctas;
+  a = cta * q + (cta < r ? cta : r);
+  b = a + q + (cta < r ? 1 : 0);
+}
+
+// CTA whose stream-K range holds tile-step `it`.
+__device__ __forceinline__ int attn_cta_of(long long total, int ctas, long long it) {
+  const long long q = total / ctas, r = total % ctas;
+  const long long big = r * (q + 1);
+  return it < big ? static_cast<int>(it / (q + 1)) : static_cast<int>(r + (it - big) / q);
+}
+
+// This CTA's segments, identical in every role: one whole group per CTA, or under stream-K the
+// group pieces of its contiguous range of the groups * n_t tile-steps.
+template <bool kSK>
+struct AttnSegIter {
+  int it, it1, n_t;
+  __device__ __forceinline__ void init(const AttnParams& p, int n_tiles, int groups) {
+    n_t = n_tiles;
+    if (kSK) {
+      long long a, b;
+      attn_range(static_cast<long long>(groups) * n_t, p.sk_ctas, blockIdx.x, a, b);
+      it = static_cast<int>(a);
+      it1 = static_cast<int>(b);
+    } else {
+      it = static_cast<int>(blockIdx.x) * n_t;
+      it1 = it + n_t;
+    }
+  }
+  __device__ __forceinline__ bool next(AttnSeg& sg) {
+    if (it >= it1) return false;
+    if (!kSK) {
+      sg.group = static_cast<int>(blockIdx.x);
+      sg.j0 = 0;
+      sg.j1 = n_t;
+      sg.whole = true;
+      it = it1;
+      return true;
+    }
+    sg.group = it / n_t;
+    sg.j0 = it - sg.group * n_t;
+    const int end = it1 - it + sg.j0;
+    sg.j1 = end < n_t ? end : n_t;
+    sg.whole = sg.j0 == 0 && sg.j1 == n_t;
+    it += sg.j1 - sg.j0;
+    return true;
+  }
+};
+
+// 10 warps: one SM sub-partition holds three of them, so its 16K-register slice caps the kernel at
+// 168 registers per thread.  kSK: stream-K schedule (a CTA's range of tile-steps may cut groups,
+// merged through the workspace); otherwise one whole group per CTA.
+template <bool kSK>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
@@ -85,21 +147,22 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* p_full = s_full + 2;              // [tile]      P_j^t stored, S_j^t consumed
   uint64_t* o_full = p_full + 2;              // [tile][2]   O_j^t ready
   uint64_t* o_empty = o_full + 4;             // [tile][2]   O_j^t folded
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_empty + 4);
+  uint64_t* q_empty = o_empty + 4;            // the last S MMAs of a segment read Q
+  uint64_t* ep_bar = q_empty + 1;             // the eight softmax warps meet (stream-K merge)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ep_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int q_blocks = (p.Sq + kQ - 1) / kQ;
-  const int qb = blockIdx.x % q_blocks;
-  const int bh = blockIdx.x / q_blocks;
-  const int h = bh % p.H;
-  const int b = bh / p.H;
-  const int q0 = qb * kQ;
   const int n_tiles = (p.Sk + kKV - 1) / kKV;
+  const int groups = p.B * p.H * q_blocks;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
+    mbar_init(ep_bar, 8);
     for (int s = 0; s < kKVStages; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&v_full[s], 1);
@@ -127,27 +190,51 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   griddep_launch_dependents();
   griddep_wait();  // q / k / v are written by the previous kernel
 
+  auto decode = [&](int group, int& b, int& h, int& q0) {
+    const int qb = group % q_blocks;
+    const int bh = group / q_blocks;
+    h = bh % p.H;
+    b = bh / p.H;
+    q0 = qb * kQ;
+  };
+
   if (warp == 8) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
-      mbar_arrive_expect_tx(q_full, 2 * kTileBytes);
-      tma_load_4d(sQ, &tmQ, q_full, 0, h, q0, b);
-      tma_load_4d(sQ + kTileBytes, &tmQ, q_full, 0, h, q0 + kQT, b);
       int stage = 0;
       uint32_t phase = 0;
-      for (int j = 0; j < n_tiles; ++j) {
-        if (!mbar_wait(&kv_empty[stage], phase ^ 1, abort_flag, p.status, kDevTimeoutProducer)) break;
-        mbar_arrive_expect_tx(&k_full[stage], kTileBytes);
-        tma_load_4d(sK + stage * kTileBytes, &tmK, &k_full[stage], 0, h, j * kKV, b);
-        mbar_arrive_expect_tx(&v_full[stage], kTileBytes);
-        tma_load_4d(sV + stage * kTileBytes, &tmV, &v_full[stage], 0, h, j * kKV, b);
-        if (++stage == kKVStages) {
-          stage = 0;
-          phase ^= 1;
+      int seg = 0;
+      bool ok = true;
+      AttnSegIter<kSK> si;
+      si.init(p, n_tiles, groups);
+      AttnSeg sg;
+      while (ok && si.next(sg)) {
+        int b, h, q0;
+        decode(sg.group, b, h, q0);
+        // the previous segment's last S MMAs must have read Q before it is replaced
+        if (seg > 0 && !mbar_wait(q_empty, (seg - 1) & 1, abort_flag, p.status, kDevTimeoutProducer))
+          break;
+        mbar_arrive_expect_tx(q_full, 2 * kTileBytes);
+        tma_load_4d(sQ, &tmQ, q_full, 0, h, q0, b);
+        tma_load_4d(sQ + kTileBytes, &tmQ, q_full, 0, h, q0 + kQT, b);
+        for (int j = sg.j0; j < sg.j1; ++j) {
+          if (!mbar_wait(&kv_empty[stage], phase ^ 1, abort_flag, p.status, kDevTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&k_full[stage], kTileBytes);
+          tma_load_4d(sK + stage * kTileBytes, &tmK, &k_full[stage], 0, h, j * kKV, b);
+          mbar_arrive_expect_tx(&v_full[stage], kTileBytes);
+          tma_load_4d(sV + stage * kTileBytes, &tmV, &v_full[stage], 0, h, j * kKV, b);
+          if (++stage == kKVStages) {
+            stage = 0;
+            phase ^= 1;
+          }
         }
+        ++seg;
       }
     }
   } else if (warp == 9) {
@@ -155,10 +242,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_f16_f32(kQT, kKV, false);
       constexpr uint32_t idesc_o = idesc_f16_f32(kQT, kD, true);
-      bool ok = mbar_wait(q_full, 0, abort_flag, p.status, kDevTimeoutMma);
-      auto issue_s = [&](int t, int j) -> bool {
-        const int st = j % kKVStages;
-        if (!mbar_wait(&k_full[st], (j / kKVStages) & 1, abort_flag, p.status, kDevTimeoutMma))
+      int kc = 0;   // KV tiles consumed so far (ring stage / phase)
+      int jc = 0;   // tile-steps so far (S / P / O phases)
+      int seg = 0;
+      bool ok = true;
+      auto issue_s = [&](int t, int jl) -> bool {
+        const int kk = kc + jl, st = kk % kKVStages;
+        if (!mbar_wait(&k_full[st], (kk / kKVStages) & 1, abort_flag, p.status, kDevTimeoutMma))
           return false;
         tc_fence_after();
         const uint32_t q_addr = smem_u32(sQ + t * kTileBytes);
@@ -171,42 +261,53 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         umma_commit(&s_full[t]);
         return true;
       };
-      auto issue_pv = [&](int t, int j) -> bool {
-        const int st = j % kKVStages;
-        if (!mbar_wait(&v_full[st], (j / kKVStages) & 1, abort_flag, p.status, kDevTimeoutMma))
+      auto issue_pv = [&](int t, int jl) -> bool {
+        const int kk = kc + jl, st = kk % kKVStages, jj = jc + jl;
+        if (!mbar_wait(&v_full[st], (kk / kKVStages) & 1, abort_flag, p.status, kDevTimeoutMma))
           return false;
-        if (j >= 2 && !mbar_wait(&o_empty[2 * t + (j & 1)], ((j - 2) >> 1) & 1, abort_flag,
-                                 p.status, kDevTimeoutMma))
+        if (jj >= 2 && !mbar_wait(&o_empty[2 * t + (jj & 1)], ((jj - 2) >> 1) & 1, abort_flag,
+                                  p.status, kDevTimeoutMma))
           return false;
         tc_fence_after();
         const uint32_t p_addr = smem_u32(sP + t * kPBytes);
         const uint32_t v_addr = smem_u32(sV + st * kTileBytes);
-        const uint32_t d = tbase + 256 + t * 128 + (j & 1) * kD;
+        const uint32_t d = tbase + 256 + t * 128 + (jj & 1) * kD;
 #pragma unroll
         for (int ks = 0; ks < kKV / 16; ++ks) {
           const uint64_t ad = sw128_desc(p_addr + (ks >> 2) * (kQT * 128) + (ks & 3) * 32, 16, 1024);
           const uint64_t bd = sw128_desc(v_addr + ks * 2048, 1024, 1024);
           umma_f16_ss(d, ad, bd, idesc_o, ks != 0 ? 1u : 0u);
         }
-        umma_commit(&o_full[2 * t + (j & 1)]);
+        umma_commit(&o_full[2 * t + (jj & 1)]);
         umma_commit(&kv_empty[st]);
         return true;
       };
-      if (ok) ok = issue_s(0, 0);
-      if (ok) ok = issue_s(1, 0);
-      for (int j = 0; j < n_tiles && ok; ++j) {
-        for (int t = 0; t < 2 && ok; ++t) {
-          if (!mbar_wait(&p_full[t], j & 1, abort_flag, p.status, kDevTimeoutMma)) {
-            ok = false;
-            break;
+      AttnSegIter<kSK> si;
+      si.init(p, n_tiles, groups);
+      AttnSeg sg;
+      while (ok && si.next(sg)) {
+        const int n = sg.j1 - sg.j0;
+        ok = mbar_wait(q_full, seg & 1, abort_flag, p.status, kDevTimeoutMma);
+        if (ok) ok = issue_s(0, 0);
+        if (ok) ok = issue_s(1, 0);
+        if (ok && n == 1) umma_commit(q_empty);  // Q is not read after these
+        for (int jl = 0; jl < n && ok; ++jl) {
+          for (int t = 0; t < 2 && ok; ++t) {
+            if (!mbar_wait(&p_full[t], (jc + jl) & 1, abort_flag, p.status, kDevTimeoutMma)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            if (jl + 1 < n) {
+              ok = issue_s(t, jl + 1);
+              if (ok && t == 1 && jl + 2 == n) umma_commit(q_empty);  // last S of the segment
+            }
+            if (ok) ok = issue_pv(t, jl);
           }
-          tc_fence_after();
-          if (j + 1 < n_tiles && !issue_s(t, j + 1)) {
-            ok = false;
-            break;
-          }
-          if (!issue_pv(t, j)) ok = false;
         }
+        kc += n;
+        jc += n;
+        ++seg;
       }
     }
   } else {
@@ -218,20 +319,27 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const uint32_t to = tbase + lane_off + 256 + t * 128;
     uint8_t* pbuf = sP + t * kPBytes;
     const float c = p.scale_log2;
-    float m_run = -INFINITY, l_run = 0.0f, alpha_prev = 1.0f;
     float acc[kD];
-#pragma unroll
-    for (int d = 0; d < kD; ++d) acc[d] = 0.0f;
     bool ok = true;
+    int jc = 0;
+    uint32_t ep_phase = 0;
+    // the eight softmax warps meet (bounded)
+    auto ep_meet = [&]() -> bool {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ep_bar);
+      const bool r = mbar_wait(ep_bar, ep_phase, abort_flag, p.status, kDevTimeoutSoftmax);
+      ep_phase ^= 1;
+      return r;
+    };
 
-    auto fold_o = [&](int j, float alpha) -> bool {
-      if (!mbar_wait(&o_full[2 * t + (j & 1)], (j >> 1) & 1, abort_flag, p.status,
+    auto fold_o = [&](int jj, float alpha) -> bool {
+      if (!mbar_wait(&o_full[2 * t + (jj & 1)], (jj >> 1) & 1, abort_flag, p.status,
                      kDevTimeoutSoftmax))
         return false;
       tc_fence_after();
       uint32_t r0[32], r1[32];
-      tmem_ld_32x32b_x32(to + (j & 1) * kD, r0);
-      tmem_ld_32x32b_x32(to + (j & 1) * kD + 32, r1);
+      tmem_ld_32x32b_x32(to + (jj & 1) * kD, r0);
+      tmem_ld_32x32b_x32(to + (jj & 1) * kD + 32, r1);
       tmem_ld_wait();
       const uint64_t a2 = f2_pack(alpha, alpha);
 #pragma unroll
@@ -244,108 +352,198 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         f2_unpack(v, acc[32 + q], acc[33 + q]);
       }
       tc_fence_before();
-      mbar_arrive(&o_empty[2 * t + (j & 1)]);
+      mbar_arrive(&o_empty[2 * t + (jj & 1)]);
       return true;
     };
 
-    for (int j = 0; j < n_tiles; ++j) {
-      if (!mbar_wait(&s_full[t], j & 1, abort_flag, p.status, kDevTimeoutSoftmax)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const int valid = p.Sk - j * kKV;  // keys of this tile that exist (may exceed 128)
-      const bool full_tile = valid >= kKV;
-      // pass 1: row max over 128 columns, two TMEM loads in flight, four independent chains
-      float mx0 = m_run, mx1 = m_run, mx2 = m_run, mx3 = m_run;
+    AttnSegIter<kSK> si;
+    si.init(p, n_tiles, groups);
+    AttnSeg sg;
+    while (ok && si.next(sg)) {
+      const int n = sg.j1 - sg.j0;
+      float m_run = -INFINITY, l_run = 0.0f, alpha_prev = 1.0f;
 #pragma unroll
-      for (int cc = 0; cc < 4; cc += 2) {
-        uint32_t ra[32], rb[32];
-        tmem_ld_32x32b_x32(ts + cc * 32, ra);
-        tmem_ld_32x32b_x32(ts + cc * 32 + 32, rb);
-        tmem_ld_wait();
-        if (full_tile) {
-#pragma unroll
-          for (int q = 0; q < 32; q += 4) {
-            mx0 = max3f(mx0, __uint_as_float(ra[q]), __uint_as_float(ra[q + 1]));
-            mx1 = max3f(mx1, __uint_as_float(ra[q + 2]), __uint_as_float(ra[q + 3]));
-            mx2 = max3f(mx2, __uint_as_float(rb[q]), __uint_as_float(rb[q + 1]));
-            mx3 = max3f(mx3, __uint_as_float(rb[q + 2]), __uint_as_float(rb[q + 3]));
-          }
-        } else {
-#pragma unroll
-          for (int q = 0; q < 32; ++q) {
-            if (cc * 32 + q < valid) mx0 = fmaxf(mx0, __uint_as_float(ra[q]));
-            if (cc * 32 + 32 + q < valid) mx1 = fmaxf(mx1, __uint_as_float(rb[q]));
-          }
+      for (int d = 0; d < kD; ++d) acc[d] = 0.0f;
+
+      for (int jl = 0; jl < n; ++jl) {
+        const int jj = jc + jl;
+        if (!mbar_wait(&s_full[t], jj & 1, abort_flag, p.status, kDevTimeoutSoftmax)) {
+          ok = false;
+          break;
         }
-      }
-      const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
-      const float alpha = fast_exp2((m_run - mx) * c);  // m_run = -inf on the first tile -> 0
-      const float mc = mx * c;
-      // fold O_{j-1}: also guarantees P.V of tile j-1 finished reading the P buffer
-      if (j >= 1 && !fold_o(j - 1, alpha_prev)) {
-        ok = false;
-        break;
-      }
-      // pass 2: p = exp2(s*c - m*c), fp32 row sum, fp16 P into shared memory
-      const uint64_t c2 = f2_pack(c, c), nmc2 = f2_pack(-mc, -mc);
-      uint64_t sumA = f2_pack(0.0f, 0.0f), sumB = sumA;
+        tc_fence_after();
+        const int valid = p.Sk - (sg.j0 + jl) * kKV;  // keys of this tile (may exceed 128)
+        const bool full_tile = valid >= kKV;
+        // pass 1: row max over 128 columns, two TMEM loads in flight, four independent chains
+        float mx0 = m_run, mx1 = m_run, mx2 = m_run, mx3 = m_run;
 #pragma unroll
-      for (int cc = 0; cc < 4; cc += 2) {
-        uint32_t ra[32], rb[32];
-        tmem_ld_32x32b_x32(ts + cc * 32, ra);
-        tmem_ld_32x32b_x32(ts + cc * 32 + 32, rb);
-        tmem_ld_wait();
+        for (int cc = 0; cc < 4; cc += 2) {
+          uint32_t ra[32], rb[32];
+          tmem_ld_32x32b_x32(ts + cc * 32, ra);
+          tmem_ld_32x32b_x32(ts + cc * 32 + 32, rb);
+          tmem_ld_wait();
+          if (full_tile) {
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          const uint32_t* r = half ? rb : ra;
-          const int col0 = (cc + half) * 32;
-          uint32_t hp[16];
-#pragma unroll
-          for (int q = 0; q < 32; q += 2) {
-            float x0, x1;
-            f2_unpack(f2_fma(f2_pack(__uint_as_float(r[q]), __uint_as_float(r[q + 1])), c2, nmc2),
-                      x0, x1);
-            float e0 = fast_exp2(x0);
-            float e1 = fast_exp2(x1);
-            if (!full_tile) {
-              if (col0 + q >= valid) e0 = 0.0f;
-              if (col0 + q + 1 >= valid) e1 = 0.0f;
+            for (int q = 0; q < 32; q += 4) {
+              mx0 = max3f(mx0, __uint_as_float(ra[q]), __uint_as_float(ra[q + 1]));
+              mx1 = max3f(mx1, __uint_as_float(ra[q + 2]), __uint_as_float(ra[q + 3]));
+              mx2 = max3f(mx2, __uint_as_float(rb[q]), __uint_as_float(rb[q + 1]));
+              mx3 = max3f(mx3, __uint_as_float(rb[q + 2]), __uint_as_float(rb[q + 3]));
             }
-            if (q & 2)
-              sumB = f2_add(sumB, f2_pack(e0, e1));
-            else
-              sumA = f2_add(sumA, f2_pack(e0, e1));
-            hp[q >> 1] = pack_half2(e0, e1);
+          } else {
+#pragma unroll
+            for (int q = 0; q < 32; ++q) {
+              if (cc * 32 + q < valid) mx0 = fmaxf(mx0, __uint_as_float(ra[q]));
+              if (cc * 32 + 32 + q < valid) mx1 = fmaxf(mx1, __uint_as_float(rb[q]));
+            }
           }
-          store_p_chunk(pbuf, row, cc + half, hp);
         }
+        const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+        const float alpha = fast_exp2((m_run - mx) * c);  // m_run = -inf on the first tile -> 0
+        const float mc = mx * c;
+        // fold O_{j-1}: also guarantees P.V of tile j-1 finished reading the P buffer
+        if (jl >= 1 && !fold_o(jj - 1, alpha_prev)) {
+          ok = false;
+          break;
+        }
+        // pass 2: p = exp2(s*c - m*c), fp32 row sum, fp16 P into shared memory
+        const uint64_t c2 = f2_pack(c, c), nmc2 = f2_pack(-mc, -mc);
+        uint64_t sumA = f2_pack(0.0f, 0.0f), sumB = sumA;
+#pragma unroll
+        for (int cc = 0; cc < 4; cc += 2) {
+          uint32_t ra[32], rb[32];
+          tmem_ld_32x32b_x32(ts + cc * 32, ra);
+          tmem_ld_32x32b_x32(ts + cc * 32 + 32, rb);
+          tmem_ld_wait();
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            const uint32_t* r = half ? rb : ra;
+            const int col0 = (cc + half) * 32;
+            uint32_t hp[16];
+#pragma unroll
+            for (int q = 0; q < 32; q += 2) {
+              float x0, x1;
+              f2_unpack(f2_fma(f2_pack(__uint_as_float(r[q]), __uint_as_float(r[q + 1])), c2, nmc2),
+                        x0, x1);
+              float e0 = fast_exp2(x0);
+              float e1 = fast_exp2(x1);
+              if (!full_tile) {
+                if (col0 + q >= valid) e0 = 0.0f;
+                if (col0 + q + 1 >= valid) e1 = 0.0f;
+              }
+              if (q & 2)
+                sumB = f2_add(sumB, f2_pack(e0, e1));
+              else
+                sumA = f2_add(sumA, f2_pack(e0, e1));
+              hp[q >> 1] = pack_half2(e0, e1);
+            }
+            store_p_chunk(pbuf, row, cc + half, hp);
+          }
+        }
+        float sum0, sum1, sum2, sum3;
+        f2_unpack(sumA, sum0, sum1);
+        f2_unpack(sumB, sum2, sum3);
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(&p_full[t]);
+        l_run = fmaf(l_run, alpha, (sum0 + sum1) + (sum2 + sum3));
+        m_run = mx;
+        alpha_prev = alpha;
       }
-      float sum0, sum1, sum2, sum3;
-      f2_unpack(sumA, sum0, sum1);
-      f2_unpack(sumB, sum2, sum3);
-      fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(&p_full[t]);
-      l_run = fmaf(l_run, alpha, (sum0 + sum1) + (sum2 + sum3));
-      m_run = mx;
-      alpha_prev = alpha;
-    }
-    if (ok && n_tiles > 0) ok = fold_o(n_tiles - 1, alpha_prev);
-    const int qrow = q0 + t * kQT + row;
-    if (ok && qrow < p.Sq) {
-      const float inv = 1.0f / l_run;
+      if (ok && n > 0) ok = fold_o(jc + n - 1, alpha_prev);
+      jc += n;
+      if (!ok) break;
+      int b, h, q0;
+      decode(sg.group, b, h, q0);
+      const int qrow = q0 + t * kQT + row;
       __half* dst = p.out + static_cast<size_t>(b) * p.o_sb + static_cast<size_t>(h) * p.o_sh +
                     static_cast<size_t>(qrow) * p.o_ss;
+      if (!kSK || sg.whole) {
+        if (qrow < p.Sq) {
+          const float inv = 1.0f / l_run;
 #pragma unroll
-      for (int d = 0; d < kD; d += 8) {
-        uint4 v;
-        v.x = pack_half2(acc[d] * inv, acc[d + 1] * inv);
-        v.y = pack_half2(acc[d + 2] * inv, acc[d + 3] * inv);
-        v.z = pack_half2(acc[d + 4] * inv, acc[d + 5] * inv);
-        v.w = pack_half2(acc[d + 6] * inv, acc[d + 7] * inv);
-        *reinterpret_cast<uint4*>(dst + d) = v;
+          for (int d = 0; d < kD; d += 8) {
+            uint4 v;
+            v.x = pack_half2(acc[d] * inv, acc[d + 1] * inv);
+            v.y = pack_half2(acc[d + 2] * inv, acc[d + 3] * inv);
+            v.z = pack_half2(acc[d + 4] * inv, acc[d + 5] * inv);
+            v.w = pack_half2(acc[d + 6] * inv, acc[d + 7] * inv);
+            *reinterpret_cast<uint4*>(dst + d) = v;
+          }
+        }
+        continue;
+      }
+      // ---- a group cut between CTAs: leave this piece, the last CTA to finish merges
+      const long long total = static_cast<long long>(groups) * n_tiles;
+      const int first = attn_cta_of(total, p.sk_ctas, static_cast<long long>(sg.group) * n_tiles);
+      const int last = attn_cta_of(total, p.sk_ctas, static_cast<long long>(sg.group + 1) * n_tiles - 1);
+      const int r_in = t * kQT + row;
+      {
+        const int slot = 2 * static_cast<int>(blockIdx.x) + (static_cast<int>(blockIdx.x) == first ? 1 : 0);
+        const float inv = 1.0f / l_run;
+        uint4* po = reinterpret_cast<uint4*>(p.part_o + (static_cast<size_t>(slot) * kQ + r_in) * kD);
+#pragma unroll
+        for (int d = 0; d < kD; d += 8) {
+          uint4 v;
+          v.x = pack_half2(acc[d] * inv, acc[d + 1] * inv);
+          v.y = pack_half2(acc[d + 2] * inv, acc[d + 3] * inv);
+          v.z = pack_half2(acc[d + 4] * inv, acc[d + 5] * inv);
+          v.w = pack_half2(acc[d + 6] * inv, acc[d + 7] * inv);
+          __stcg(po + d / 8, v);
+        }
+        __stcg(p.part_ml + static_cast<size_t>(slot) * kQ + r_in, make_float2(m_run, l_run));
+      }
+      __threadfence();
+      ok = ep_meet();
+      if (!ok) break;
+      if (threadIdx.x == 0) {
+        const int old = atomicAdd(p.part_cnt + sg.group, 1);
+        *last_flag = old == last - first;
+      }
+      ok = ep_meet();
+      if (!ok) break;
+      if (*last_flag) {
+        __threadfence();
+        // merge the pieces in CTA order: O = sum_s w_s O_s / sum_s w_s, w_s = l_s 2^((m_s - m) c)
+        float mmax = -INFINITY;
+        for (int cc = first; cc <= last; ++cc) {
+          const int slot = 2 * cc + (cc == first ? 1 : 0);
+          mmax = fmaxf(mmax, __ldcg(p.part_ml + static_cast<size_t>(slot) * kQ + r_in).x);
+        }
+#pragma unroll
+        for (int d = 0; d < kD; ++d) acc[d] = 0.0f;
+        float L = 0.0f;
+        for (int cc = first; cc <= last; ++cc) {
+          const int slot = 2 * cc + (cc == first ? 1 : 0);
+          const float2 ml = __ldcg(p.part_ml + static_cast<size_t>(slot) * kQ + r_in);
+          const float w = ml.y * fast_exp2((ml.x - mmax) * c);
+          L += w;
+          const uint4* po = reinterpret_cast<const uint4*>(p.part_o + (static_cast<size_t>(slot) * kQ + r_in) * kD);
+#pragma unroll
+          for (int d = 0; d < kD; d += 8) {
+            const uint4 u = __ldcg(po + d / 8);
+            const __half2* hh = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+            for (int k2 = 0; k2 < 4; ++k2) {
+              const float2 f = __half22float2(hh[k2]);
+              acc[d + 2 * k2] = fmaf(w, f.x, acc[d + 2 * k2]);
+              acc[d + 2 * k2 + 1] = fmaf(w, f.y, acc[d + 2 * k2 + 1]);
+            }
+          }
+        }
+        if (qrow < p.Sq) {
+          const float inv = 1.0f / L;
+#pragma unroll
+          for (int d = 0; d < kD; d += 8) {
+            uint4 v;
+            v.x = pack_half2(acc[d] * inv, acc[d + 1] * inv);
+            v.y = pack_half2(acc[d + 2] * inv, acc[d + 3] * inv);
+            v.z = pack_half2(acc[d + 4] * inv, acc[d + 5] * inv);
+            v.w = pack_half2(acc[d + 6] * inv, acc[d + 7] * inv);
+            *reinterpret_cast<uint4*>(dst + d) = v;
+          }
+        }
+        if (threadIdx.x == 0) p.part_cnt[sg.group] = 0;
       }
     }
   }
@@ -377,8 +575,19 @@ bool stride_ok(const AttnTensor& t) {
 
 }  // namespace
 
+size_t attn_counter_bytes(int B, int H, int Sq) {
+  const size_t groups = static_cast<size_t>(B) * H * ((Sq + kQ - 1) / kQ);
+  return ((groups * sizeof(int) + 255) / 256) * 256;
+}
+
+size_t attn_workspace_bytes(int B, int H, int Sq) {
+  const size_t slots = 2 * static_cast<size_t>(num_sms());
+  return attn_counter_bytes(B, H, Sq) + slots * kQ * sizeof(float2) + slots * kQ * kD * sizeof(__half);
+}
+
 int attn_plan(AttnOp* op, int B, int H, int Sq, int Sk, int Dh, float scale, const AttnTensor& q,
-              const AttnTensor& k, const AttnTensor& v, const AttnTensor& o) {
+              const AttnTensor& k, const AttnTensor& v, const AttnTensor& o, void* ws,
+              size_t ws_bytes) {
   DLM_REQUIRE(op != nullptr, DLM_ERR_INVALID, "attention: null op");
   DLM_REQUIRE(B > 0 && H > 0 && Sq > 0 && Sk > 0, DLM_ERR_INVALID, "attention: empty problem");
   DLM_REQUIRE(Dh == 64, DLM_ERR_UNSUPPORTED, "attention: head_dim %d (only 64 here)", Dh);
@@ -400,13 +609,34 @@ int attn_plan(AttnOp* op, int B, int H, int Sq, int Sk, int Dh, float scale, con
   p.o_sh = o.sh;
   p.o_ss = o.ss;
   p.status = device_status_ptr();
-  op->grid = B * H * ((Sq + kQ - 1) / kQ);
+  const long long groups = static_cast<long long>(B) * H * ((Sq + kQ - 1) / kQ);
+  const long long steps = groups * ((Sk + kKV - 1) / kKV);
+  DLM_REQUIRE(steps < (1ll << 31), DLM_ERR_INVALID, "attention: too many query blocks x key tiles");
+  op->grid = static_cast<int>(groups);
+  if (ws != nullptr) {
+    // stream-K: every SM takes an equal share of the groups' KV tile-steps
+    DLM_REQUIRE((reinterpret_cast<uintptr_t>(ws) & 255) == 0, DLM_ERR_INVALID,
+                "attention: workspace must be 256-byte aligned");
+    DLM_REQUIRE(ws_bytes >= attn_workspace_bytes(B, H, Sq), DLM_ERR_INVALID,
+                "attention: workspace of %zu bytes, need %zu", ws_bytes, attn_workspace_bytes(B, H, Sq));
+    const int sms = num_sms();
+    p.sk_ctas = static_cast<int>(steps < sms ? steps : sms);
+    char* base = static_cast<char*>(ws);
+    p.part_cnt = reinterpret_cast<int*>(base);
+    base += attn_counter_bytes(B, H, Sq);
+    p.part_ml = reinterpret_cast<float2*>(base);
+    base += 2 * static_cast<size_t>(sms) * kQ * sizeof(float2);
+    p.part_o = reinterpret_cast<__half*>(base);
+    op->grid = p.sk_ctas;
+  }
   return DLM_OK;
 }
 
 int attn_prepare_kernels() {
-  DLM_CHECK_CUDA(cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      kAttnSmem));
+  DLM_CHECK_CUDA(cudaFuncSetAttribute(attn_fwd_kernel<false>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem));
+  DLM_CHECK_CUDA(cudaFuncSetAttribute(attn_fwd_kernel<true>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem));
   return DLM_OK;
 }
 
@@ -415,8 +645,8 @@ int attn_launch(const AttnOp& op, cudaStream_t s) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    DLM_CHECK_CUDA(cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        kAttnSmem));
+    const int rc = attn_prepare_kernels();
+    if (rc != DLM_OK) return rc;
     attr_set[dev] = true;
   }
   cudaLaunchConfig_t cfg = {};
@@ -429,7 +659,10 @@ int attn_launch(const AttnOp& op, cudaStream_t s) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
-  DLM_CHECK_CUDA(cudaLaunchKernelEx(&cfg, attn_fwd_kernel, op.tmQ, op.tmK, op.tmV, op.p));
+  if (op.p.sk_ctas > 0)
+    DLM_CHECK_CUDA(cudaLaunchKernelEx(&cfg, attn_fwd_kernel<true>, op.tmQ, op.tmK, op.tmV, op.p));
+  else
+    DLM_CHECK_CUDA(cudaLaunchKernelEx(&cfg, attn_fwd_kernel<false>, op.tmQ, op.tmK, op.tmV, op.p));
   return DLM_OK;
 }
 
@@ -452,6 +685,29 @@ int dlm_launch_attention(const void* q, const void* k, const void* v, void* out,
   dlm::AttnOp op;
   int rc = dlm::attn_plan(&op, B, H, Sq, Sk, Dh, scale, bhsd(q, Sq), bhsd(k, Sk), bhsd(v, Sk),
                           bhsd(out, Sq));
+  if (rc != DLM_OK) return rc;
+  return dlm::attn_launch(op, static_cast<cudaStream_t>(stream));
+}
+
+size_t dlm_attention_workspace_bytes(int B, int H, int Sq) {
+  return dlm::attn_workspace_bytes(B, H, Sq);
+}
+
+int dlm_launch_attention_ws(const void* q, const void* k, const void* v, void* out, int B, int H,
+                            int Sq, int Sk, int Dh, float scale, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  if (B == 0 || H == 0 || Sq == 0 || Sk == 0) return DLM_OK;
+  auto bhsd = [&](const void* ptr, int S) {
+    dlm::AttnTensor t;
+    t.ptr = static_cast<const __half*>(ptr);
+    t.ss = Dh;
+    t.sh = static_cast<long long>(S) * Dh;
+    t.sb = static_cast<long long>(H) * S * Dh;
+    return t;
+  };
+  dlm::AttnOp op;
+  int rc = dlm::attn_plan(&op, B, H, Sq, Sk, Dh, scale, bhsd(q, Sq), bhsd(k, Sk), bhsd(v, Sk),
+                          bhsd(out, Sq), workspace, workspace_bytes);
   if (rc != DLM_OK) return rc;
   return dlm::attn_launch(op, static_cast<cudaStream_t>(stream));
 }

@@ -604,6 +604,14 @@ int UNetModel::plan_linear(const __half* A, int lda, const __half* Wt, int M, in
   return DLM_OK;
 }
 
+static bool attn_stream_k_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("DLM_ATTN_SK");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 int UNetModel::plan_attn(const __half* q, int ldq, const __half* k, int ldk, const __half* v, int ldv,
                          __half* o, int ldo, int heads, int Sq, int Sk) {
   if (dry_) return DLM_OK;
@@ -617,7 +625,7 @@ int UNetModel::plan_attn(const __half* q, int ldq, const __half* k, int ldk, con
   };
   AttnOp a;
   int rc = attn_plan(&a, B_, heads, Sq, Sk, 64, 0.125f, tok(q, ldq, Sq), tok(k, ldk, Sk),
-                     tok(v, ldv, Sk), tok(o, ldo, Sq));
+                     tok(v, ldv, Sk), tok(o, ldo, Sq), attn_ws_, attn_ws_bytes_);
   if (rc != DLM_OK) return rc;
   push_attn(a);
   return DLM_OK;
@@ -747,6 +755,15 @@ int UNetModel::build(bool dry) {
   out32_ = act(P0 * 32);
   gn_partial_cap_ = gn_partial_elems(B, H0 * W0);
   gn_partials_ = reinterpret_cast<float2*>(act(gn_partial_cap_ * 4));
+  // stream-K attention (DLM_ATTN_SK=0 keeps one CTA per 256-query block): the attention levels
+  // run one after another on the stream, so one workspace sized for the larger serves both
+  attn_ws_bytes_ = 0;
+  attn_ws_ = nullptr;
+  if (attn_stream_k_enabled()) {
+    attn_ws_bytes_ = std::max(attn_workspace_bytes(B, C1 / 64, H1 * W1),
+                              attn_workspace_bytes(B, C2 / 64, H2 * W2));
+    attn_ws_ = act((attn_ws_bytes_ + 1) / 2);
+  }
 
   // ---- embeddings
   if (!dry_) {
@@ -987,8 +1004,9 @@ int UNetModel::plan(int B, int H, int Wd) {
     release_plan();
     return rc;
   }
-  // GroupNorm's arrival counters start at zero (each launch leaves them at zero)
+  // GroupNorm's and attention's arrival counters start at zero (each launch leaves them at zero)
   DLM_CHECK_CUDA(cudaMemset(gn_partials_, 0, gn_partial_cap_ * sizeof(float2)));
+  if (attn_ws_) DLM_CHECK_CUDA(cudaMemset(attn_ws_, 0, attn_ws_bytes_));
   DLM_CHECK_CUDA(cudaDeviceSynchronize());
   return DLM_OK;
 }

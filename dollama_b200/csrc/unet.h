@@ -111,6 +111,8 @@ class UNetModel {
   float2* gn_partials_ = nullptr;
   float2* ln_stats_ = nullptr;
   size_t gn_partial_cap_ = 0;
+  void* attn_ws_ = nullptr;  // stream-K attention workspace shared by every attention launch
+  size_t attn_ws_bytes_ = 0;
 };
 
 }  // namespace dlm

@@ -63,7 +63,7 @@ def main(argv=None):
                     help="GEMM tile choice: 0 auto, 1 single CTA, 2 CTA pair, 3 stream-K "
                          "(+16 * forced N tile)")
     a = ap.parse_args(argv)
-    if a.tile_mode:
+    if a.tile_mode and a.op in ("gemm", "conv"):
         L.call("dlm_gemm_set_tile_mode", a.tile_mode)
     torch.manual_seed(0)
     dev = "cuda"
@@ -135,8 +135,14 @@ def main(argv=None):
         k = torch.randn(a.b, a.heads, a.sk, 64, device=dev).half()
         v = torch.randn_like(k)
         o = torch.empty_like(q)
-        fn = lambda: L.call("dlm_launch_attention", _p(q), _p(k), _p(v), _p(o), a.b, a.heads, a.sq, a.sk,
-                            64, 0.125, _s())
+        if a.tile_mode == 1:   # one CTA per 256-query block (no load balancing)
+            fn = lambda: L.call("dlm_launch_attention", _p(q), _p(k), _p(v), _p(o), a.b, a.heads,
+                                a.sq, a.sk, 64, 0.125, _s())
+        else:
+            nws = L.lib().dlm_attention_workspace_bytes(a.b, a.heads, a.sq)
+            ws = torch.zeros(nws, dtype=torch.uint8, device=dev)
+            fn = lambda: L.call("dlm_launch_attention_ws", _p(q), _p(k), _p(v), _p(o), a.b, a.heads,
+                                a.sq, a.sk, 64, 0.125, _p(ws), nws, _s())
         flops = 4.0 * a.b * a.heads * a.sq * a.sk * 64
         shape = {"b": a.b, "heads": a.heads, "sq": a.sq, "sk": a.sk, "dh": 64}
     ms = _time(fn, a.iters)

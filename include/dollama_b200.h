@@ -129,6 +129,16 @@ int dlm_nhwc_to_nchw(const void* in, void* out, int N, int C, int HW, void* stre
 int dlm_launch_attention(const void* q, const void* k, const void* v, void* out, int B, int H,
                          int Sq, int Sk, int Dh, float scale, void* stream);
 
+/* The same attention load-balanced over all SMs ("stream-K"): the KV tiles of all (batch, head,
+ * 256-query block) groups are split evenly over the SMs, pieces of a group split between SMs
+ * are merged by the last one to finish (fixed order).  `workspace`: at least
+ * dlm_attention_workspace_bytes(B, H, Sq) bytes, 256-byte aligned, ZEROED once before first use
+ * (every call leaves it ready); calls sharing a workspace must not overlap on the GPU. */
+size_t dlm_attention_workspace_bytes(int B, int H, int Sq);
+int dlm_launch_attention_ws(const void* q, const void* k, const void* v, void* out, int B, int H,
+                            int Sq, int Sk, int Dh, float scale, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
 /* Same op on token-major projections: q is [B*Sq, ldq] with head h in columns [h*64, h*64+64),
  * k / v are [B*Sk, ldk / ldv], out is [B*Sq, ldo].  Removes the reference's split/merge-heads
  * copies (src/infer/unet.cu:198,213). */
