@@ -1,14 +1,15 @@
 // tcgen05 GEMM for sm_100a: C[M, N] = epi(A[M, K] * B[N, K]^T), fp16 operands, fp32
 // accumulation in tensor memory.
 //
-// One persistent CTA per SM walks output tiles of 128 x BN.  Roles (192 threads):
+// One persistent CTA per SM walks output tiles of 128 x BN.  Roles (320 threads):
 //   warp 0      TMA producer: streams 128x64 A and BNx64 B tiles (128-byte swizzle) into a
 //               STAGES-deep shared-memory ring (full/empty mbarriers);
 //   warp 1      allocates TMEM; one thread issues tcgen05.mma (M=128, N=BN, K=16) into one of
 //               two TMEM accumulators (2 x BN fp32 columns) and commits to the barriers;
-//   warps 2..5  epilogue: tcgen05.ld of the accumulator (each warp owns the 32 TMEM lanes of
-//               its quadrant, warp % 4), fused bias / per-image bias / SiLU / GEGLU / residual,
-//               fp16 store; the second accumulator lets tile i's epilogue overlap tile i+1's MMAs.
+//   warps 2..9  epilogue: tcgen05.ld of the accumulator (a warp may only read the 32 TMEM lanes
+//               of its quadrant, warp % 4, so two warps share each quadrant and take alternate
+//               32-column chunks), fused bias / per-image bias / SiLU / GEGLU / residual, fp16
+//               store; the second accumulator lets tile i's epilogue overlap tile i+1's MMAs.
 //
 // The A operand is either a dense row-major matrix (2D tensor map) or an implicit-GEMM view of
 // an NHWC activation for a 3x3 / 1x1 convolution: each 64-wide k-block is one (tap, 64-channel)
@@ -128,20 +129,28 @@ struct SegIter {
 
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;
-constexpr int kGemmThreads = 192;
+constexpr int kGemmEpiWarps = 8;  // two per TMEM lane quadrant
+constexpr int kGemmThreads = 64 + 32 * kGemmEpiWarps;
 
 __host__ __device__ constexpr int gemm_stage_bytes(int BN) { return (kGemmBM + BN) * kGemmBK * 2; }
-// Epilogue staging: each of the 4 epilogue warps owns two 2 KB buffers (32 rows x 32 fp16 columns,
-// 64-byte swizzled) through which its outputs leave by TMA bulk stores.
+// Epilogue staging: each epilogue warp owns two 2 KB buffers (32 rows x 32 fp16 columns, 64-byte
+// swizzled) through which its outputs leave by TMA bulk stores; after them, the exchange slots in
+// which the second warp of a quadrant hands its row statistics to the first (32 x float4 each),
+// and per quadrant the slot's full / empty mbarriers.
 constexpr int kStageBytesPerWarp = 4096;
-constexpr int kEpiStageBytes = 4 * kStageBytesPerWarp;
+constexpr int kEpiStageBytes = kGemmEpiWarps * kStageBytesPerWarp;
+constexpr int kEpiXchgSlots = 4 * 32 * 16;
+constexpr int kEpiXchgBytes = kEpiXchgSlots + 4 * 2 * 8;
+// Shared memory outside the operand ring: staging, exchange, 1 KB alignment slack, barriers.
+constexpr int kGemmFixedSmem = kEpiStageBytes + kEpiXchgBytes + 1024 + 256;
+constexpr int kMaxDynSmem = 227 * 1024;
 __host__ __device__ constexpr int gemm_stages(int BN) {
-  return ((225 * 1024 - 2048 - kEpiStageBytes) / gemm_stage_bytes(BN)) > 8
+  return ((kMaxDynSmem - kGemmFixedSmem) / gemm_stage_bytes(BN)) > 8
              ? 8
-             : ((225 * 1024 - 2048 - kEpiStageBytes) / gemm_stage_bytes(BN));
+             : ((kMaxDynSmem - kGemmFixedSmem) / gemm_stage_bytes(BN));
 }
 __host__ __device__ constexpr int gemm_smem_bytes(int BN) {
-  return gemm_stages(BN) * gemm_stage_bytes(BN) + kEpiStageBytes + 1024 + 256;
+  return gemm_stages(BN) * gemm_stage_bytes(BN) + kGemmFixedSmem;
 }
 __host__ __device__ constexpr uint32_t gemm_tmem_cols(int BN) {
   return (2 * BN) <= 32 ? 32 : (2 * BN) <= 64 ? 64 : (2 * BN) <= 128 ? 128 : (2 * BN) <= 256 ? 256 : 512;
@@ -182,17 +191,21 @@ __device__ __forceinline__ void chan_merge(float& n_a, float& mean_a, float& m2_
 }
 
 // Epilogue of one 128 x BN accumulator held in TMEM (this warp's 32 lanes starting at t_row,
-// output rows m_base .. m_base+31): LayerNorm fold, alpha scaling, bias / per-image bias / SiLU /
-// GEGLU / residual, optional row statistics of the stored values.  Each 32-column chunk leaves
+// output rows m_base .. m_base+31, the 32-column chunks c = 32 * (half + 2 j)): LayerNorm fold,
+// alpha scaling, bias / per-image bias / SiLU / GEGLU / residual, optional row statistics of the
+// stored values (the half-1 warp hands its statistics to the half-0 warp of the same quadrant
+// through the slot `xchg` guarded by the mbarriers xbar[0] (full) / xbar[1] (empty); xphase counts
+// the hand-offs).  Returns false when a bounded wait gave up.  Each 32-column chunk leaves
 // through the warp's shared-memory staging buffer (swizzled so that row-per-thread writes and
 // the bulk copy are bank-conflict free) as one TMA bulk store of 32 rows x 32 columns (16 for
 // GEGLU); the residual chunk is read with coalesced 16-byte loads and transposed through the same
 // buffer.  Rows >= M are clipped by the store.
 template <int BN>
-__device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t t_row, int row, int n0,
+__device__ __forceinline__ bool epilogue_tile(const GemmParams& p, uint32_t t_row, int row, int n0,
                                               int m_base, uint8_t* stage, const CUtensorMap* tmC,
-                                              int& sbuf, int sk_c0 = 0, int sk_c1 = 0,
-                                              int r_in_tile = 0) {
+                                              int& sbuf, int half, float4* xchg, uint64_t* xbar,
+                                              uint32_t& xphase, volatile int* abort_flag,
+                                              int sk_c0 = 0, int sk_c1 = 0, int r_in_tile = 0) {
   const int lane = threadIdx.x & 31;
   const bool row_ok = row < p.M;
   const bool geglu = (p.flags & DLM_EPI_GEGLU) != 0;
@@ -217,7 +230,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t t_ro
   const int img = (row_ok ? row : p.M - 1) / p.rows_per_img;
   float s_cnt = 0.0f, s_mean = 0.0f, s_m2 = 0.0f;  // row statistics of this tile's outputs
 #pragma unroll 1
-  for (int c = 0; c < BN; c += 32) {
+  for (int c = 32 * half; c < BN; c += 64) {
     if (n0 + c >= p.N) break;
     uint32_t r[32];
     tmem_ld_32x32b_x32(t_row + c, r);
@@ -402,17 +415,42 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t t_ro
     }
     sbuf ^= 1;
   }
-  if ((p.flags & kEpiRowStats) && row_ok)
-    p.stats_out[static_cast<size_t>(row) * p.stats_ld + n0 / BN] = make_float2(s_mean, s_m2);
+  if (p.flags & kEpiRowStats) {
+    const uint32_t ph = xphase & 1;
+    ++xphase;
+    if (half == 1) {
+      if (!mbar_wait(&xbar[1], ph ^ 1, abort_flag, p.status, kDevTimeoutEpilogue)) return false;
+      xchg[lane] = make_float4(s_cnt, s_mean, s_m2, 0.0f);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&xbar[0]);
+    } else {
+      if (!mbar_wait(&xbar[0], ph, abort_flag, p.status, kDevTimeoutEpilogue)) return false;
+      const float4 o = xchg[lane];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&xbar[1]);
+      if (o.x > 0.0f) {
+        if (s_cnt == 0.0f) {
+          s_cnt = o.x;
+          s_mean = o.y;
+          s_m2 = o.z;
+        } else {
+          chan_merge(s_cnt, s_mean, s_m2, o.x, o.y, o.z);
+        }
+      }
+      if (row_ok) p.stats_out[static_cast<size_t>(row) * p.stats_ld + n0 / BN] = make_float2(s_mean, s_m2);
+    }
+  }
+  return true;
 }
 
 // Stream-K contributor: this CTA's fp32 partial accumulator of its 32 rows of a cut tile, to its
 // workspace slot sk_ws[blockIdx.x] (128 contiguous bytes per lane and 32-column chunk).
 template <int BN>
-__device__ __forceinline__ void epilogue_partial(const GemmParams& p, uint32_t t_row, int r_in_tile) {
+__device__ __forceinline__ void epilogue_partial(const GemmParams& p, uint32_t t_row, int r_in_tile,
+                                                 int half) {
   float* dst = p.sk_ws + (static_cast<size_t>(blockIdx.x) * kGemmBM + r_in_tile) * BN;
 #pragma unroll 1
-  for (int c = 0; c < BN; c += 32) {
+  for (int c = 32 * half; c < BN; c += 64) {
     uint32_t r[32];
     tmem_ld_32x32b_x32(t_row + c, r);
     tmem_ld_wait();
@@ -442,7 +480,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
   uint8_t* sEpi = sB + STAGES * B_BYTES;  // 1024-aligned: stage sizes are multiples of 1 KB
-  uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + kEpiStageBytes);
+  float4* sXchg = reinterpret_cast<float4*>(sEpi + kEpiStageBytes);
+  uint64_t* xbar = reinterpret_cast<uint64_t*>(sEpi + kEpiStageBytes + kEpiXchgSlots);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + kEpiStageBytes + kEpiXchgBytes);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -460,9 +500,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4);
+      mbar_init(&tempty[a], kGemmEpiWarps);
     }
-    mbar_init(sk_bar, 4);
+    mbar_init(sk_bar, kGemmEpiWarps);
+    for (int x = 0; x < 8; ++x) mbar_init(&xbar[x], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -605,16 +646,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else {
-    // ------------------------------------------------------------ epilogue (warps 2..5)
+    // ------------------------------------------------------------ epilogue (warps 2..9)
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int r_in_tile = quad * 32 + lane;
     int sbuf = 0;
     int i = 0;
-    uint32_t sk_phase = 0;
+    uint32_t sk_phase = 0, xphase = 0;
     SegIter si;
     si.init(p);
     TileSeg sg;
-    // the four epilogue warps meet (bounded) before a stream-K flag changes hands
+    // the epilogue warps meet (bounded) before a stream-K flag changes hands
     auto sk_meet = [&]() -> bool {
       __syncwarp();
       if (lane == 0) mbar_arrive(sk_bar);
@@ -635,7 +677,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                              static_cast<uint32_t>(acc * BN);
       if (p.sk_ctas > 0 && sg.kb0 > 0) {
         // contributor: hand the partial accumulator to the tile's owner
-        epilogue_partial<BN>(p, t_row, r_in_tile);
+        epilogue_partial<BN>(p, t_row, r_in_tile, half);
         __threadfence();
         ok = sk_meet();
         if (ok && warp == 2 && lane == 0) {
@@ -658,9 +700,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             ok = flag_wait_acquire(p.sk_flags + cc, 1, abort_flag, p.status, kDevTimeoutStreamK);
         }
         if (ok) {
-          epilogue_tile<BN>(p, t_row, row, n0, m0 + quad * 32, sEpi + (warp - 2) * kStageBytesPerWarp,
-                            &tmC, sbuf, c0, c1, r_in_tile);
-          if (c1 > c0) {
+          ok = epilogue_tile<BN>(p, t_row, row, n0, m0 + quad * 32,
+                                 sEpi + (warp - 2) * kStageBytesPerWarp, &tmC, sbuf, half,
+                                 sXchg + quad * 32, xbar + 2 * quad, xphase, abort_flag, c0, c1,
+                                 r_in_tile);
+          if (ok && c1 > c0) {
             // every warp has read the partials: clear the flags for the next launch
             ok = sk_meet();
             if (ok && warp == 2)
@@ -701,12 +745,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
 __host__ __device__ constexpr int gemm2_stage_bytes(int BN) { return (kGemmBM + BN / 2) * kGemmBK * 2; }
 __host__ __device__ constexpr int gemm2_stages(int BN) {
-  return ((225 * 1024 - 2048 - kEpiStageBytes) / gemm2_stage_bytes(BN)) > 8
+  return ((kMaxDynSmem - kGemmFixedSmem) / gemm2_stage_bytes(BN)) > 8
              ? 8
-             : ((225 * 1024 - 2048 - kEpiStageBytes) / gemm2_stage_bytes(BN));
+             : ((kMaxDynSmem - kGemmFixedSmem) / gemm2_stage_bytes(BN));
 }
 __host__ __device__ constexpr int gemm2_smem_bytes(int BN) {
-  return gemm2_stages(BN) * gemm2_stage_bytes(BN) + kEpiStageBytes + 1024 + 256;
+  return gemm2_stages(BN) * gemm2_stage_bytes(BN) + kGemmFixedSmem;
 }
 
 template <int BN>
@@ -728,7 +772,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
   uint8_t* sEpi = sB + STAGES * B_BYTES;  // 1024-aligned: stage sizes are multiples of 1 KB
-  uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + kEpiStageBytes);
+  float4* sXchg = reinterpret_cast<float4*>(sEpi + kEpiStageBytes);
+  uint64_t* xbar = reinterpret_cast<uint64_t*>(sEpi + kEpiStageBytes + kEpiXchgSlots);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + kEpiStageBytes + kEpiXchgBytes);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -749,8 +795,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 8);  // 4 epilogue warps in each of the two CTAs
+      mbar_init(&tempty[a], 2 * kGemmEpiWarps);  // the epilogue warps of both CTAs
     }
+    for (int x = 0; x < 8; ++x) mbar_init(&xbar[x], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -867,10 +914,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else {
-    // ------------------------------------------------------------ epilogue (warps 2..5, both CTAs)
+    // ------------------------------------------------------------ epilogue (warps 2..9, both CTAs)
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
     int sbuf = 0;
     int i = 0;
+    uint32_t xphase = 0;
     for (int t = pair; t < num_tiles; t += npairs, ++i) {
       const int acc = i & 1;
       const uint32_t acc_phase = (i >> 1) & 1;
@@ -881,8 +930,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int row = m0 + quad * 32 + lane;
       const uint32_t t_row = tbase + (static_cast<uint32_t>(quad * 32) << 16) +
                              static_cast<uint32_t>(acc * BN);
-      epilogue_tile<BN>(p, t_row, row, n0, m0 + quad * 32, sEpi + (warp - 2) * kStageBytesPerWarp,
-                        &tmC, sbuf);
+      if (!epilogue_tile<BN>(p, t_row, row, n0, m0 + quad * 32,
+                             sEpi + (warp - 2) * kStageBytesPerWarp, &tmC, sbuf, half,
+                             sXchg + quad * 32, xbar + 2 * quad, xphase, abort_flag))
+        break;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(&tempty[acc], 0);
