@@ -187,7 +187,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
-  griddep_launch_dependents();
   griddep_wait();  // q / k / v are written by the previous kernel
 
   auto decode = [&](int group, int& b, int& h, int& q0) {
@@ -309,6 +308,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         jc += n;
         ++seg;
       }
+      // the last MMA is issued: the next kernel may launch during this CTA's final softmax
+      griddep_launch_dependents();
     }
   } else {
     // ------------------------------------------------------------ softmax warps 0..7

@@ -523,7 +523,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
-  griddep_launch_dependents();
   griddep_wait();  // inputs of this GEMM are written by the previous kernel
 
   if (warp == 0) {
@@ -644,6 +643,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (ok) umma_commit(&tfull[acc]);
         ++i;
       }
+      // the last MMA is issued: the next kernel may launch during this CTA's final epilogue
+      griddep_launch_dependents();
     }
   } else {
     // ------------------------------------------------------------ epilogue (warps 2..9)
@@ -817,7 +818,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   cluster_sync_all();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
-  griddep_launch_dependents();
   griddep_wait();  // inputs of this GEMM are written by the previous kernel
   const int num_tiles = p.m_tiles * p.n_tiles;  // m tiles of 256 rows
 
@@ -912,6 +912,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         if (ok) umma2_commit_mc(&tfull[acc], 0x3);
       }
+      griddep_launch_dependents();
+    } else if (lane == 0) {
+      griddep_launch_dependents();  // the pair's trigger is the even CTA's
     }
   } else {
     // ------------------------------------------------------------ epilogue (warps 2..9, both CTAs)

@@ -68,8 +68,7 @@ __global__ void __launch_bounds__(kStatThreads, kBlocksPerSm)
   extern __shared__ float sh[];  // [PL][C] sums then [PL][C] sumsq
   __shared__ double s_fold[2][kFoldSets][kGroups];
   __shared__ int s_last;
-  griddep_launch_dependents();
-  griddep_wait();
+  griddep_wait();  // dependents launch when this grid exits
   const int C = C1 + C2;
   const int nvec = C >> 3;
   const int chunk = blockIdx.x, n = blockIdx.y, chunks = gridDim.x;
@@ -178,8 +177,7 @@ __global__ void __launch_bounds__(256, kBlocksPerSm)
                     int HW, const float2* __restrict__ mean_rstd, const __half* __restrict__ gamma,
                     const __half* __restrict__ beta, int silu, int pix_per_block,
                     __half* __restrict__ out) {
-  griddep_launch_dependents();
-  griddep_wait();
+  griddep_wait();  // dependents launch when this grid exits
   const int C = C1 + C2;
   const int n = blockIdx.y;
   const int nvec = C >> 3;
@@ -243,8 +241,7 @@ __global__ void __launch_bounds__(256)
     layer_norm_kernel(const __half* __restrict__ x, const __half* __restrict__ gamma,
                       const __half* __restrict__ beta, __half* __restrict__ out, int rows, int C,
                       float eps) {
-  griddep_launch_dependents();
-  griddep_wait();
+  griddep_wait();  // dependents launch when this grid exits
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= rows) return;
