@@ -505,30 +505,62 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (!ok) break;
       if (*last_flag) {
         __threadfence();
-        // merge the pieces in CTA order: O = sum_s w_s O_s / sum_s w_s, w_s = l_s 2^((m_s - m) c)
+        // merge the pieces in CTA order: O = sum_s w_s O_s / sum_s w_s, w_s = l_s 2^((m_s - m) c).
+        // The loads of several pieces are issued before any of them is used, so that the merge
+        // waits for about one L2 round trip per four (max, sum) pairs and per two O rows.
+        auto slot_of = [&](int cc) { return 2 * cc + (cc == first ? 1 : 0); };
         float mmax = -INFINITY;
-        for (int cc = first; cc <= last; ++cc) {
-          const int slot = 2 * cc + (cc == first ? 1 : 0);
-          mmax = fmaxf(mmax, __ldcg(p.part_ml + static_cast<size_t>(slot) * kQ + r_in).x);
+        for (int c0 = first; c0 <= last; c0 += 4) {
+          float2 m4[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            if (c0 + i <= last) m4[i] = __ldcg(p.part_ml + static_cast<size_t>(slot_of(c0 + i)) * kQ + r_in);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            if (c0 + i <= last) mmax = fmaxf(mmax, m4[i].x);
         }
 #pragma unroll
         for (int d = 0; d < kD; ++d) acc[d] = 0.0f;
         float L = 0.0f;
-        for (int cc = first; cc <= last; ++cc) {
-          const int slot = 2 * cc + (cc == first ? 1 : 0);
-          const float2 ml = __ldcg(p.part_ml + static_cast<size_t>(slot) * kQ + r_in);
-          const float w = ml.y * fast_exp2((ml.x - mmax) * c);
-          L += w;
-          const uint4* po = reinterpret_cast<const uint4*>(p.part_o + (static_cast<size_t>(slot) * kQ + r_in) * kD);
+        for (int c0 = first; c0 <= last; c0 += 2) {
+          const bool two = c0 + 1 <= last;
+          const size_t sa = static_cast<size_t>(slot_of(c0)) * kQ + r_in;
+          const size_t sb = static_cast<size_t>(slot_of(two ? c0 + 1 : c0)) * kQ + r_in;
+          const float2 mla = __ldcg(p.part_ml + sa);
+          const float2 mlb = __ldcg(p.part_ml + sb);
+          const uint4* pa = reinterpret_cast<const uint4*>(p.part_o + sa * kD);
+          const uint4* pb = reinterpret_cast<const uint4*>(p.part_o + sb * kD);
+          uint4 oa[kD / 8], ob[kD / 8];
 #pragma unroll
-          for (int d = 0; d < kD; d += 8) {
-            const uint4 u = __ldcg(po + d / 8);
-            const __half2* hh = reinterpret_cast<const __half2*>(&u);
+          for (int j = 0; j < kD / 8; ++j) oa[j] = __ldcg(pa + j);
+          if (two) {
+#pragma unroll
+            for (int j = 0; j < kD / 8; ++j) ob[j] = __ldcg(pb + j);
+          }
+          const float wa = mla.y * fast_exp2((mla.x - mmax) * c);
+          L += wa;
+#pragma unroll
+          for (int j = 0; j < kD / 8; ++j) {
+            const __half2* hh = reinterpret_cast<const __half2*>(&oa[j]);
 #pragma unroll
             for (int k2 = 0; k2 < 4; ++k2) {
               const float2 f = __half22float2(hh[k2]);
-              acc[d + 2 * k2] = fmaf(w, f.x, acc[d + 2 * k2]);
-              acc[d + 2 * k2 + 1] = fmaf(w, f.y, acc[d + 2 * k2 + 1]);
+              acc[8 * j + 2 * k2] = fmaf(wa, f.x, acc[8 * j + 2 * k2]);
+              acc[8 * j + 2 * k2 + 1] = fmaf(wa, f.y, acc[8 * j + 2 * k2 + 1]);
+            }
+          }
+          if (two) {
+            const float wb = mlb.y * fast_exp2((mlb.x - mmax) * c);
+            L += wb;
+#pragma unroll
+            for (int j = 0; j < kD / 8; ++j) {
+              const __half2* hh = reinterpret_cast<const __half2*>(&ob[j]);
+#pragma unroll
+              for (int k2 = 0; k2 < 4; ++k2) {
+                const float2 f = __half22float2(hh[k2]);
+                acc[8 * j + 2 * k2] = fmaf(wb, f.x, acc[8 * j + 2 * k2]);
+                acc[8 * j + 2 * k2 + 1] = fmaf(wb, f.y, acc[8 * j + 2 * k2 + 1]);
+              }
             }
           }
         }
