@@ -105,14 +105,31 @@ int max_pairs(int bn) {
   return cache[dev][slot];
 }
 
-// Chooses single-CTA vs CTA-pair and the N tile.
-void pick_tile(int M, int N, int force_bn, int force_mode, int* bn_out, bool* pair_out) {
+// Chooses single-CTA vs CTA-pair and the N tile.  Dense linears (conv == false) with more than
+// one row tile run on CTA pairs, whose two-k-block stages keep the issuing thread ahead of the
+// tensor pipe; the N tile minimises waves x measured clocks per k-block (B200, UNet shapes:
+// ~590 for a 256 x 160 pair tile, ~634 for 256 x 256).  Implicit-GEMM convolutions measured
+// faster on single CTAs (their 4D im2col boxes) and keep the single-CTA cost model.
+void pick_tile(int M, int N, bool conv, int force_bn, int force_mode, int* bn_out, bool* pair_out) {
   static const int single[] = {256, 192, 160, 128, 64};
   static const int paired[] = {256, 192, 160, 128};
   const int sms = num_sms();
-  const bool want_pair = force_mode == 2 || (force_mode == 0 && N >= 2560 && M <= 4096 && M > kGemmBM);
+  const bool want_pair = force_mode == 2 || (force_mode == 0 && !conv && M > kGemmBM);
   if (want_pair && M > kGemmBM) {
-    int bn = force_bn ? force_bn : 256;
+    int bn = force_bn;
+    if (bn == 0) {
+      const long mt2 = (M + 2 * kGemmBM - 1) / (2 * kGemmBM);
+      double best = 1e30;
+      for (int c : {256, 160}) {
+        const long tiles = mt2 * ((N + c - 1) / c);
+        const long pairs = max_pairs(c);
+        const double cost = static_cast<double>((tiles + pairs - 1) / pairs) * (c == 256 ? 634.0 : 590.0);
+        if (cost < best - 1e-9) {
+          best = cost;
+          bn = c;
+        }
+      }
+    }
     bool ok = false;
     for (int c : paired) ok = ok || c == bn;
     if (ok) {
@@ -292,7 +309,7 @@ int gemm_plan_dense(GemmOp* op, const __half* A, int lda, const __half* W, int M
   if (rc != DLM_OK) return rc;
   int bn = 0;
   bool pair = false;
-  pick_tile(M, N, force_bn ? force_bn : g_force_bn, g_force_mode, &bn, &pair);
+  pick_tile(M, N, false, force_bn ? force_bn : g_force_bn, g_force_mode, &bn, &pair);
   const int sk_bn = pick_stream_k((M + kGemmBM - 1) / kGemmBM, N, (K + kGemmBK - 1) / kGemmBK, bn,
                                   pair, epi, g_force_mode, force_bn ? force_bn : g_force_bn);
   if (sk_bn) {
@@ -342,7 +359,7 @@ int gemm_plan_conv(GemmOp* op, int Nb, int oH, int oW, const ConvSource* srcs, i
   const int M = Nb * oH * oW;
   int bn = 0;
   bool pair = false;
-  pick_tile(M, Cout, force_bn ? force_bn : g_force_bn, g_force_mode, &bn, &pair);
+  pick_tile(M, Cout, true, force_bn ? force_bn : g_force_bn, g_force_mode, &bn, &pair);
   long ktot_blocks = 0;
   for (int s = 0; s < nsrc; ++s) ktot_blocks += static_cast<long>(srcs[s].kind == 1 ? 1 : 9) * (srcs[s].C / 64);
   const int sk_bn = pick_stream_k(M / kGemmBM, Cout, static_cast<int>(ktot_blocks), bn, pair, epi,

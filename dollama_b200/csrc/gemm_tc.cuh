@@ -135,11 +135,11 @@ constexpr int kGemmThreads = 64 + 32 * kGemmEpiWarps;
 __host__ __device__ constexpr int gemm_stage_bytes(int BN) { return (kGemmBM + BN) * kGemmBK * 2; }
 // Epilogue staging: each epilogue warp owns two 2 KB buffers (32 rows x 32 fp16 columns, 64-byte
 // swizzled) through which its outputs leave by TMA bulk stores; after them, the exchange slots in
-// which the second warp of a quadrant hands its row statistics to the first (32 x float4 each),
+// which the second warp of a quadrant hands its row statistics to the first (32 x float2 each),
 // and per quadrant the slot's full / empty mbarriers.
 constexpr int kStageBytesPerWarp = 4096;
 constexpr int kEpiStageBytes = kGemmEpiWarps * kStageBytesPerWarp;
-constexpr int kEpiXchgSlots = 4 * 32 * 16;
+constexpr int kEpiXchgSlots = 4 * 32 * 8;
 constexpr int kEpiXchgBytes = kEpiXchgSlots + 4 * 2 * 8;
 // Shared memory outside the operand ring: staging, exchange, 1 KB alignment slack, barriers.
 constexpr int kGemmFixedSmem = kEpiStageBytes + kEpiXchgBytes + 1024 + 256;
@@ -200,13 +200,50 @@ __device__ __forceinline__ void chan_merge(float& n_a, float& mean_a, float& m2_
 // the bulk copy are bank-conflict free) as one TMA bulk store of 32 rows x 32 columns (16 for
 // GEGLU); the residual chunk is read with coalesced 16-byte loads and transposed through the same
 // buffer.  Rows >= M are clipped by the store.
+// Issued by each epilogue warp before it waits for the tile's accumulator, so that the residual
+// arrives while the tensor core still works on the tile: the fp16 residual of the warp's first two
+// chunks is copied (cp.async, coalesced 64-byte rows) into its two staging buffers in their
+// swizzled layout.  Returns whether it was (the staging buffers are then reserved for it).
+// (Prefetching the bias / LayerNorm-fold lines into L1 the same way measured slower.)
+template <int BN>
+__device__ __forceinline__ bool epilogue_prefetch(const GemmParams& p, int row, int n0, int m_base,
+                                                  int half, uint8_t* stage) {
+  const int lane = threadIdx.x & 31;
+  const bool geglu = (p.flags & DLM_EPI_GEGLU) != 0;
+  const bool resid16 = (p.flags & DLM_EPI_RESID) && !(p.flags & kEpiResidF32) && !geglu &&
+                       !(p.flags & kEpiOutF32);
+  if (!resid16 || ((p.N - n0) & 31) != 0) return false;
+  // the bulk stores of the previous tile must have finished reading the staging buffers
+  if (lane == 0) bulk_wait_read_le0();
+  __syncwarp();
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int n = n0 + 32 * half + 64 * j;
+    if (32 * half + 64 * j >= BN || n >= p.N) break;
+    uint8_t* buf = stage + j * 2048;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int rr = (lane >> 2) + 8 * i, q = lane & 3;
+      const int grow = m_base + rr;
+      const __half* src = p.resid + static_cast<size_t>(grow < p.M ? grow : 0) * p.ldr + n + q * 8;
+      cp_async16(buf + rr * 64 + ((q ^ ((rr >> 1) & 3)) * 16), src, grow < p.M ? 16u : 0u);
+    }
+  }
+  cp_async_commit();
+  return true;
+}
+
 template <int BN>
 __device__ __forceinline__ bool epilogue_tile(const GemmParams& p, uint32_t t_row, int row, int n0,
                                               int m_base, uint8_t* stage, const CUtensorMap* tmC,
-                                              int& sbuf, int half, float4* xchg, uint64_t* xbar,
+                                              int& sbuf, int half, float2* xchg, uint64_t* xbar,
                                               uint32_t& xphase, volatile int* abort_flag,
-                                              int sk_c0 = 0, int sk_c1 = 0, int r_in_tile = 0) {
+                                              bool res_pref, int sk_c0 = 0, int sk_c1 = 0,
+                                              int r_in_tile = 0) {
   const int lane = threadIdx.x & 31;
+  // with the residual prefetched, chunk j (j < 2) of this tile uses staging buffer j
+  if (res_pref) sbuf = 0;
+  int cj = 0;  // chunk index within this warp's chunks
   const bool row_ok = row < p.M;
   const bool geglu = (p.flags & DLM_EPI_GEGLU) != 0;
   float ln_mean = 0.0f, ln_rstd = 1.0f;
@@ -289,8 +326,13 @@ __device__ __forceinline__ bool epilogue_tile(const GemmParams& p, uint32_t t_ro
       for (int j = 0; j < 32; ++j) v[j] = silu_f(v[j]);
     }
     uint8_t* buf = stage + sbuf * 2048;
-    // the bulk store that last used this buffer must have finished reading it
-    if (lane == 0) bulk_wait_read_le1();
+    const bool pref = res_pref && cj < 2;
+    if (pref) {
+      if (cj == 0) cp_async_wait_all();
+    } else {
+      // the bulk store that last used this buffer must have finished reading it
+      if (lane == 0) bulk_wait_read_le1();
+    }
     __syncwarp();
     if (geglu) {
       uint32_t o[8];
@@ -320,16 +362,18 @@ __device__ __forceinline__ bool epilogue_tile(const GemmParams& p, uint32_t t_ro
           }
         }
       } else if (p.flags & DLM_EPI_RESID) {
+        if (!pref) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int rr = (lane >> 2) + 8 * i, q = lane & 3;
-          const int grow = m_base + rr;
-          uint4 u = make_uint4(0, 0, 0, 0);
-          if (grow < p.M)
-            u = *reinterpret_cast<const uint4*>(p.resid + static_cast<size_t>(grow) * p.ldr + n + q * 8);
-          *reinterpret_cast<uint4*>(buf + rr * 64 + ((q ^ ((rr >> 1) & 3)) * 16)) = u;
+          for (int i = 0; i < 4; ++i) {
+            const int rr = (lane >> 2) + 8 * i, q = lane & 3;
+            const int grow = m_base + rr;
+            uint4 u = make_uint4(0, 0, 0, 0);
+            if (grow < p.M)
+              u = *reinterpret_cast<const uint4*>(p.resid + static_cast<size_t>(grow) * p.ldr + n + q * 8);
+            *reinterpret_cast<uint4*>(buf + rr * 64 + ((q ^ ((rr >> 1) & 3)) * 16)) = u;
+          }
+          __syncwarp();
         }
-        __syncwarp();
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const uint4 u = *reinterpret_cast<const uint4*>(buf + lane * 64 + ((q ^ ((lane >> 1) & 3)) * 16));
@@ -414,27 +458,31 @@ __device__ __forceinline__ bool epilogue_tile(const GemmParams& p, uint32_t t_ro
       bulk_commit_group();
     }
     sbuf ^= 1;
+    ++cj;
   }
   if (p.flags & kEpiRowStats) {
     const uint32_t ph = xphase & 1;
     ++xphase;
     if (half == 1) {
       if (!mbar_wait(&xbar[1], ph ^ 1, abort_flag, p.status, kDevTimeoutEpilogue)) return false;
-      xchg[lane] = make_float4(s_cnt, s_mean, s_m2, 0.0f);
+      xchg[lane] = make_float2(s_mean, s_m2);
       __syncwarp();
       if (lane == 0) mbar_arrive(&xbar[0]);
     } else {
       if (!mbar_wait(&xbar[0], ph, abort_flag, p.status, kDevTimeoutEpilogue)) return false;
-      const float4 o = xchg[lane];
+      const float2 o = xchg[lane];
       __syncwarp();
       if (lane == 0) mbar_arrive(&xbar[1]);
-      if (o.x > 0.0f) {
+      // the half-1 warp stored the chunks c = 32, 96, ... below BN and N - n0 (32 values each)
+      float cnt1 = 0.0f;
+      for (int c = 32; c < BN && n0 + c < p.N; c += 64) cnt1 += 32.0f;
+      if (cnt1 > 0.0f) {
         if (s_cnt == 0.0f) {
-          s_cnt = o.x;
-          s_mean = o.y;
-          s_m2 = o.z;
+          s_cnt = cnt1;
+          s_mean = o.x;
+          s_m2 = o.y;
         } else {
-          chan_merge(s_cnt, s_mean, s_m2, o.x, o.y, o.z);
+          chan_merge(s_cnt, s_mean, s_m2, cnt1, o.x, o.y);
         }
       }
       if (row_ok) p.stats_out[static_cast<size_t>(row) * p.stats_ld + n0 / BN] = make_float2(s_mean, s_m2);
@@ -480,7 +528,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
   uint8_t* sEpi = sB + STAGES * B_BYTES;  // 1024-aligned: stage sizes are multiples of 1 KB
-  float4* sXchg = reinterpret_cast<float4*>(sEpi + kEpiStageBytes);
+  float2* sXchg = reinterpret_cast<float2*>(sEpi + kEpiStageBytes);
   uint64_t* xbar = reinterpret_cast<uint64_t*>(sEpi + kEpiStageBytes + kEpiXchgSlots);
   uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + kEpiStageBytes + kEpiXchgBytes);
   uint64_t* empty = full + STAGES;
@@ -669,11 +717,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     while (ok && si.next(p, sg)) {
       const int acc = i & 1;
       const uint32_t acc_phase = (i >> 1) & 1;
-      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status, kDevTimeoutEpilogue)) break;
-      tc_fence_after();
       const int m0 = (sg.tile / p.n_tiles) * kGemmBM;
       const int n0 = (sg.tile % p.n_tiles) * BN;
       const int row = m0 + r_in_tile;
+      uint8_t* stage_buf = sEpi + (warp - 2) * kStageBytesPerWarp;
+      const bool res_pref = !(p.sk_ctas > 0 && sg.kb0 > 0) &&
+                            epilogue_prefetch<BN>(p, row, n0, m0 + quad * 32, half, stage_buf);
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status, kDevTimeoutEpilogue)) break;
+      tc_fence_after();
       const uint32_t t_row = tbase + (static_cast<uint32_t>(quad * 32) << 16) +
                              static_cast<uint32_t>(acc * BN);
       if (p.sk_ctas > 0 && sg.kb0 > 0) {
@@ -701,10 +752,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             ok = flag_wait_acquire(p.sk_flags + cc, 1, abort_flag, p.status, kDevTimeoutStreamK);
         }
         if (ok) {
-          ok = epilogue_tile<BN>(p, t_row, row, n0, m0 + quad * 32,
-                                 sEpi + (warp - 2) * kStageBytesPerWarp, &tmC, sbuf, half,
-                                 sXchg + quad * 32, xbar + 2 * quad, xphase, abort_flag, c0, c1,
-                                 r_in_tile);
+          ok = epilogue_tile<BN>(p, t_row, row, n0, m0 + quad * 32, stage_buf, &tmC, sbuf, half,
+                                 sXchg + quad * 32, xbar + 2 * quad, xphase, abort_flag, res_pref,
+                                 c0, c1, r_in_tile);
           if (ok && c1 > c0) {
             // every warp has read the partials: clear the flags for the next launch
             ok = sk_meet();
@@ -741,10 +791,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // accumulator (two buffers of BN columns); each CTA runs the epilogue for its rows and both signal
 // the even CTA's `tempty`.  Per SM this moves half of B through L2 and shared memory compared with
 // the single-CTA kernel, which is what lets the tensor core run at full rate for BN = 256.
+// A ring stage holds two 64-wide k-blocks (kPairKsub), so the issuing thread waits, commits and
+// advances once per 8 MMAs: its per-stage bookkeeping (~450 clocks on B200, whatever N is) then
+// costs less than the tensor work of the stage for BN >= 160.  An odd k-block count leaves the
+// last stage of a tile half full.
 // Loads carry no multicast qualifier: every CTA fetches its own operands.
 // ======================================================================================
 
-__host__ __device__ constexpr int gemm2_stage_bytes(int BN) { return (kGemmBM + BN / 2) * kGemmBK * 2; }
+constexpr int kPairKsub = 2;
+__host__ __device__ constexpr int gemm2_stage_bytes(int BN) {
+  return kPairKsub * (kGemmBM + BN / 2) * kGemmBK * 2;
+}
 __host__ __device__ constexpr int gemm2_stages(int BN) {
   return ((kMaxDynSmem - kGemmFixedSmem) / gemm2_stage_bytes(BN)) > 8
              ? 8
@@ -760,8 +817,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
   constexpr int BNH = BN / 2;
-  constexpr int A_BYTES = kGemmBM * kGemmBK * 2;
-  constexpr int B_BYTES = BNH * kGemmBK * 2;
+  constexpr int A_SUB = kGemmBM * kGemmBK * 2;  // one 64-wide k-block of A (this CTA's rows)
+  constexpr int B_SUB = BNH * kGemmBK * 2;      // one k-block of this CTA's half of B
+  constexpr int A_BYTES = kPairKsub * A_SUB;    // per ring stage
+  constexpr int B_BYTES = kPairKsub * B_SUB;
   constexpr int STAGES = gemm2_stages(BN);
   constexpr uint32_t TMEM_COLS = gemm_tmem_cols(BN);
   static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "pair UMMA N");
@@ -773,7 +832,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
   uint8_t* sEpi = sB + STAGES * B_BYTES;  // 1024-aligned: stage sizes are multiples of 1 KB
-  float4* sXchg = reinterpret_cast<float4*>(sEpi + kEpiStageBytes);
+  float2* sXchg = reinterpret_cast<float2*>(sEpi + kEpiStageBytes);
   uint64_t* xbar = reinterpret_cast<uint64_t*>(sEpi + kEpiStageBytes + kEpiXchgSlots);
   uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + kEpiStageBytes + kEpiXchgBytes);
   uint64_t* empty = full + STAGES;
@@ -839,6 +898,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           ow0 = rem - oh0 * p.oW;
         }
         int kb = 0;
+        int sub = 0;  // k-block within the ring stage
         const int nseg = p.amode == 0 ? 1 : p.nseg;
         for (int s = 0; s < nseg && ok; ++s) {
           const ConvSeg sg = p.seg[s];
@@ -848,13 +908,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           for (int tap = 0; tap < ntaps && ok; ++tap) {
             const int kh = tap / 3, kw = tap - (tap / 3) * 3;
             for (int cb = 0; cb < ncb; ++cb) {
-              if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status, kDevTimeoutProducer)) {
-                ok = false;
-                break;
+              if (sub == 0) {
+                if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status, kDevTimeoutProducer)) {
+                  ok = false;
+                  break;
+                }
+                const int nsub = p.num_kb - kb >= kPairKsub ? kPairKsub : p.num_kb - kb;
+                if (leader) mbar_arrive_expect_tx(&full[stage], 2 * nsub * (A_SUB + B_SUB));
               }
-              if (leader) mbar_arrive_expect_tx(&full[stage], 2 * (A_BYTES + B_BYTES));
               const uint32_t fb = pair_leader_addr(&full[stage]);
-              uint8_t* dstA = sA + stage * A_BYTES;
+              uint8_t* dstA = sA + stage * A_BYTES + sub * A_SUB;
               if (p.amode == 0) {
                 tma2_load_2d(dstA, am, fb, cb * kGemmBK, m0);
               } else if (sg.kind == 0) {
@@ -866,11 +929,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 const int pc = (kw == 1) ? 0 : 1, dc = (kw == 0) ? -1 : 0;
                 tma2_load_5d(dstA, am, fb, cb * 64, ow0 + dc, oh0 + dr, img, pr * 2 + pc);
               }
-              tma2_load_2d(sB + stage * B_BYTES, &tmB, fb, kb * kGemmBK, nb);
+              tma2_load_2d(sB + stage * B_BYTES + sub * B_SUB, &tmB, fb, kb * kGemmBK, nb);
               ++kb;
-              if (++stage == STAGES) {
-                stage = 0;
-                phase ^= 1;
+              if (++sub == kPairKsub || kb == p.num_kb) {
+                sub = 0;
+                if (++stage == STAGES) {
+                  stage = 0;
+                  phase ^= 1;
+                }
               }
             }
           }
@@ -891,7 +957,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, p.status, kDevTimeoutMma)) break;
         tc_fence_after();
         const uint32_t d_tmem = tbase + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < p.num_kb; ++kb) {
+        for (int kb = 0; kb < p.num_kb; kb += kPairKsub) {
           if (!mbar_wait(&full[stage], phase, abort_flag, p.status, kDevTimeoutMma)) {
             ok = false;
             break;
@@ -900,9 +966,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const uint32_t a_base = smem_u32(sA + stage * A_BYTES);
           const uint32_t b_base = smem_u32(sB + stage * B_BYTES);
 #pragma unroll
-          for (int k = 0; k < kGemmBK / 16; ++k) {
-            umma2_f16_ss(d_tmem, sw128_desc(a_base + k * 32, 16, 1024),
-                         sw128_desc(b_base + k * 32, 16, 1024), idesc, (kb | k) != 0 ? 1u : 0u);
+          for (int sub = 0; sub < kPairKsub; ++sub) {
+            if (kb + sub < p.num_kb) {
+#pragma unroll
+              for (int k = 0; k < kGemmBK / 16; ++k) {
+                umma2_f16_ss(d_tmem, sw128_desc(a_base + sub * A_SUB + k * 32, 16, 1024),
+                             sw128_desc(b_base + sub * B_SUB + k * 32, 16, 1024), idesc,
+                             (kb + sub) != 0 || k != 0 ? 1u : 0u);
+              }
+            }
           }
           umma2_commit_mc(&empty[stage], 0x3);
           if (++stage == STAGES) {
@@ -926,16 +998,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int t = pair; t < num_tiles; t += npairs, ++i) {
       const int acc = i & 1;
       const uint32_t acc_phase = (i >> 1) & 1;
-      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status, kDevTimeoutEpilogue)) break;
-      tc_fence_after();
       const int m0 = (t / p.n_tiles) * (2 * kGemmBM) + static_cast<int>(rank) * kGemmBM;
       const int n0 = (t % p.n_tiles) * BN;
       const int row = m0 + quad * 32 + lane;
+      uint8_t* stage_buf = sEpi + (warp - 2) * kStageBytesPerWarp;
+      const bool res_pref = epilogue_prefetch<BN>(p, row, n0, m0 + quad * 32, half, stage_buf);
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status, kDevTimeoutEpilogue)) break;
+      tc_fence_after();
       const uint32_t t_row = tbase + (static_cast<uint32_t>(quad * 32) << 16) +
                              static_cast<uint32_t>(acc * BN);
-      if (!epilogue_tile<BN>(p, t_row, row, n0, m0 + quad * 32,
-                             sEpi + (warp - 2) * kStageBytesPerWarp, &tmC, sbuf, half,
-                             sXchg + quad * 32, xbar + 2 * quad, xphase, abort_flag))
+      if (!epilogue_tile<BN>(p, t_row, row, n0, m0 + quad * 32, stage_buf, &tmC, sbuf, half,
+                             sXchg + quad * 32, xbar + 2 * quad, xphase, abort_flag, res_pref))
         break;
       tc_fence_before();
       __syncwarp();

@@ -192,6 +192,20 @@ __device__ __forceinline__ void bulk_wait_read_le1() {
   asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
 }
 
+// Wait until no bulk group of this thread still reads shared memory.
+__device__ __forceinline__ void bulk_wait_read_le0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
+// 16-byte asynchronous global -> shared copy (L2 only); `bytes` = 0 fills the 16 bytes with zeros.
+__device__ __forceinline__ void cp_async16(void* dst_smem, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst_smem)), "l"(src),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
 // Wait until every bulk group of this thread has completed.
 __device__ __forceinline__ void bulk_wait_all() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
