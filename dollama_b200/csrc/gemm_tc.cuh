@@ -200,19 +200,50 @@ __device__ __forceinline__ void chan_merge(float& n_a, float& mean_a, float& m2_
 // the bulk copy are bank-conflict free) as one TMA bulk store of 32 rows x 32 columns (16 for
 // GEGLU); the residual chunk is read with coalesced 16-byte loads and transposed through the same
 // buffer.  Rows >= M are clipped by the store.
-// Issued by each epilogue warp before it waits for the tile's accumulator, so that the residual
-// arrives while the tensor core still works on the tile: the fp16 residual of the warp's first two
-// chunks is copied (cp.async, coalesced 64-byte rows) into its two staging buffers in their
-// swizzled layout.  Returns whether it was (the staging buffers are then reserved for it).
-// (Prefetching the bias / LayerNorm-fold lines into L1 the same way measured slower.)
+// What epilogue_prefetch fetched for a tile.
+struct EpiPre {
+  bool res = false;       // fp16 residual of chunks 0 and 1 in staging buffers 0 and 1
+  bool uv = false;        // LayerNorm-fold vectors u, v of chunks 0 and 1 in buffers 0 and 1
+  bool ln_ready = false;  // this row's LayerNorm mean / rstd below
+  float ln_mean = 0.0f, ln_rstd = 1.0f;
+};
+
+// Issued by each epilogue warp before it waits for the tile's accumulator, so that the epilogue's
+// inputs arrive while the tensor core still works on the tile: the row's LayerNorm statistics are
+// merged, and the fp16 residual (coalesced 64-byte rows, in the swizzled staging layout) or the
+// LayerNorm-fold vectors u, v (128 bytes each at the start of the buffer) of the warp's first two
+// chunks are copied with cp.async into its two staging buffers, which the chunks' outputs reuse
+// after reading them.  (Prefetching the bias lines into L1 measured slower.)
 template <int BN>
-__device__ __forceinline__ bool epilogue_prefetch(const GemmParams& p, int row, int n0, int m_base,
-                                                  int half, uint8_t* stage) {
+__device__ __forceinline__ EpiPre epilogue_prefetch(const GemmParams& p, int row, int n0, int m_base,
+                                                    int half, uint8_t* stage) {
+  EpiPre pre;
   const int lane = threadIdx.x & 31;
   const bool geglu = (p.flags & DLM_EPI_GEGLU) != 0;
+  const bool lnf = (p.flags & kEpiLnFold) != 0;
+  if (lnf) {
+    if (row < p.M) {
+      float cnt = 0.0f, mean = 0.0f, m2 = 0.0f;
+      const float2* st = p.stats_in + static_cast<size_t>(row) * p.stats_in_parts;
+      for (int i = 0; i < p.stats_in_parts; ++i) {
+        const int c = min(p.stats_in_tile, p.ln_C - i * p.stats_in_tile);
+        const float2 v = st[i];
+        if (i == 0) {
+          cnt = static_cast<float>(c);
+          mean = v.x;
+          m2 = v.y;
+        } else {
+          chan_merge(cnt, mean, m2, static_cast<float>(c), v.x, v.y);
+        }
+      }
+      pre.ln_mean = mean;
+      pre.ln_rstd = rsqrtf(fmaxf(m2 / static_cast<float>(p.ln_C), 0.0f) + p.ln_eps);
+    }
+    pre.ln_ready = true;
+  }
   const bool resid16 = (p.flags & DLM_EPI_RESID) && !(p.flags & kEpiResidF32) && !geglu &&
                        !(p.flags & kEpiOutF32);
-  if (!resid16 || ((p.N - n0) & 31) != 0) return false;
+  if ((!resid16 && !lnf) || ((p.N - n0) & 31) != 0) return pre;
   // the bulk stores of the previous tile must have finished reading the staging buffers
   if (lane == 0) bulk_wait_read_le0();
   __syncwarp();
@@ -221,16 +252,23 @@ __device__ __forceinline__ bool epilogue_prefetch(const GemmParams& p, int row, 
     const int n = n0 + 32 * half + 64 * j;
     if (32 * half + 64 * j >= BN || n >= p.N) break;
     uint8_t* buf = stage + j * 2048;
+    if (resid16) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int rr = (lane >> 2) + 8 * i, q = lane & 3;
-      const int grow = m_base + rr;
-      const __half* src = p.resid + static_cast<size_t>(grow < p.M ? grow : 0) * p.ldr + n + q * 8;
-      cp_async16(buf + rr * 64 + ((q ^ ((rr >> 1) & 3)) * 16), src, grow < p.M ? 16u : 0u);
+      for (int i = 0; i < 4; ++i) {
+        const int rr = (lane >> 2) + 8 * i, q = lane & 3;
+        const int grow = m_base + rr;
+        const __half* src = p.resid + static_cast<size_t>(grow < p.M ? grow : 0) * p.ldr + n + q * 8;
+        cp_async16(buf + rr * 64 + ((q ^ ((rr >> 1) & 3)) * 16), src, grow < p.M ? 16u : 0u);
+      }
+    } else if (lane < 16) {
+      const float* src = (lane < 8 ? p.ln_u : p.ln_v) + n + 4 * (lane & 7);
+      cp_async16(buf + 16 * lane, src, 16u);
     }
   }
   cp_async_commit();
-  return true;
+  pre.res = resid16;
+  pre.uv = !resid16;
+  return pre;
 }
 
 template <int BN>
@@ -238,16 +276,17 @@ __device__ __forceinline__ bool epilogue_tile(const GemmParams& p, uint32_t t_ro
                                               int m_base, uint8_t* stage, const CUtensorMap* tmC,
                                               int& sbuf, int half, float2* xchg, uint64_t* xbar,
                                               uint32_t& xphase, volatile int* abort_flag,
-                                              bool res_pref, int sk_c0 = 0, int sk_c1 = 0,
+                                              const EpiPre& pre, int sk_c0 = 0, int sk_c1 = 0,
                                               int r_in_tile = 0) {
   const int lane = threadIdx.x & 31;
-  // with the residual prefetched, chunk j (j < 2) of this tile uses staging buffer j
-  if (res_pref) sbuf = 0;
+  // with inputs prefetched, chunk j (j < 2) of this tile uses staging buffer j
+  const bool staged = pre.res || pre.uv;
+  if (staged) sbuf = 0;
   int cj = 0;  // chunk index within this warp's chunks
   const bool row_ok = row < p.M;
   const bool geglu = (p.flags & DLM_EPI_GEGLU) != 0;
-  float ln_mean = 0.0f, ln_rstd = 1.0f;
-  if ((p.flags & kEpiLnFold) && row_ok) {
+  float ln_mean = pre.ln_mean, ln_rstd = pre.ln_rstd;
+  if ((p.flags & kEpiLnFold) && row_ok && !pre.ln_ready) {
     float cnt = 0.0f, mean = 0.0f, m2 = 0.0f;
     const float2* st = p.stats_in + static_cast<size_t>(row) * p.stats_in_parts;
     for (int i = 0; i < p.stats_in_parts; ++i) {
@@ -288,18 +327,30 @@ __device__ __forceinline__ bool epilogue_tile(const GemmParams& p, uint32_t t_ro
         v[4 * j + 3] += t4.w;
       }
     }
+    if (p.alpha != 1.0f) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] *= p.alpha;
+      for (int j = 0; j < 32; ++j) v[j] *= p.alpha;
+    }
     const int n = n0 + c;
+    const bool pref = staged && cj < 2;
+    if (pref && cj == 0) {
+      cp_async_wait_all();
+      __syncwarp();
+    }
     if (p.flags & kEpiLnFold) {
+      // v = rstd * (v - mean * u) + w, two columns per packed f32x2 FMA (same roundings)
+      const float4* su = reinterpret_cast<const float4*>(stage + cj * 2048);
+      const uint64_t nm2 = f2_pack(-ln_mean, -ln_mean), r2 = f2_pack(ln_rstd, ln_rstd);
 #pragma unroll
       for (int j = 0; j < 32; j += 4) {
-        const float4 u4 = __ldg(reinterpret_cast<const float4*>(p.ln_u + n + j));
-        const float4 w4 = __ldg(reinterpret_cast<const float4*>(p.ln_v + n + j));
-        v[j] = fmaf(ln_rstd, v[j] - ln_mean * u4.x, w4.x);
-        v[j + 1] = fmaf(ln_rstd, v[j + 1] - ln_mean * u4.y, w4.y);
-        v[j + 2] = fmaf(ln_rstd, v[j + 2] - ln_mean * u4.z, w4.z);
-        v[j + 3] = fmaf(ln_rstd, v[j + 3] - ln_mean * u4.w, w4.w);
+        const float4 u4 = (pre.uv && cj < 2) ? su[j / 4] : __ldg(reinterpret_cast<const float4*>(p.ln_u + n + j));
+        const float4 w4 = (pre.uv && cj < 2) ? su[8 + j / 4] : __ldg(reinterpret_cast<const float4*>(p.ln_v + n + j));
+        uint64_t a0 = f2_fma(nm2, f2_pack(u4.x, u4.y), f2_pack(v[j], v[j + 1]));
+        uint64_t a1 = f2_fma(nm2, f2_pack(u4.z, u4.w), f2_pack(v[j + 2], v[j + 3]));
+        a0 = f2_fma(r2, a0, f2_pack(w4.x, w4.y));
+        a1 = f2_fma(r2, a1, f2_pack(w4.z, w4.w));
+        f2_unpack(a0, v[j], v[j + 1]);
+        f2_unpack(a1, v[j + 2], v[j + 3]);
       }
     }
     if (p.flags & DLM_EPI_BIAS) {
@@ -308,7 +359,10 @@ __device__ __forceinline__ bool epilogue_tile(const GemmParams& p, uint32_t t_ro
         float b[8];
         load_half8(p.bias + n + j, b);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) v[j + q] += b[q];
+        for (int q = 0; q < 8; q += 2) {
+          const uint64_t t = f2_add(f2_pack(v[j + q], v[j + q + 1]), f2_pack(b[q], b[q + 1]));
+          f2_unpack(t, v[j + q], v[j + q + 1]);
+        }
       }
     }
     if (p.flags & DLM_EPI_BIAS2D) {
@@ -318,7 +372,10 @@ __device__ __forceinline__ bool epilogue_tile(const GemmParams& p, uint32_t t_ro
         float b[8];
         load_half8(b2 + j, b);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) v[j + q] += b[q];
+        for (int q = 0; q < 8; q += 2) {
+          const uint64_t t = f2_add(f2_pack(v[j + q], v[j + q + 1]), f2_pack(b[q], b[q + 1]));
+          f2_unpack(t, v[j + q], v[j + q + 1]);
+        }
       }
     }
     if (p.flags & DLM_EPI_SILU) {
@@ -326,10 +383,7 @@ __device__ __forceinline__ bool epilogue_tile(const GemmParams& p, uint32_t t_ro
       for (int j = 0; j < 32; ++j) v[j] = silu_f(v[j]);
     }
     uint8_t* buf = stage + sbuf * 2048;
-    const bool pref = res_pref && cj < 2;
-    if (pref) {
-      if (cj == 0) cp_async_wait_all();
-    } else {
+    if (!pref) {
       // the bulk store that last used this buffer must have finished reading it
       if (lane == 0) bulk_wait_read_le1();
     }
@@ -362,7 +416,7 @@ __device__ __forceinline__ bool epilogue_tile(const GemmParams& p, uint32_t t_ro
           }
         }
       } else if (p.flags & DLM_EPI_RESID) {
-        if (!pref) {
+        if (!(pre.res && cj < 2)) {
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             const int rr = (lane >> 2) + 8 * i, q = lane & 3;
@@ -374,6 +428,7 @@ __device__ __forceinline__ bool epilogue_tile(const GemmParams& p, uint32_t t_ro
           }
           __syncwarp();
         }
+        const uint64_t rs2 = f2_pack(p.resid_scale, p.resid_scale);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const uint4 u = *reinterpret_cast<const uint4*>(buf + lane * 64 + ((q ^ ((lane >> 1) & 3)) * 16));
@@ -381,8 +436,8 @@ __device__ __forceinline__ bool epilogue_tile(const GemmParams& p, uint32_t t_ro
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const float2 t = __half22float2(h[k]);
-            v[q * 8 + 2 * k] += p.resid_scale * t.x;
-            v[q * 8 + 2 * k + 1] += p.resid_scale * t.y;
+            const uint64_t r = f2_fma(rs2, f2_pack(t.x, t.y), f2_pack(v[q * 8 + 2 * k], v[q * 8 + 2 * k + 1]));
+            f2_unpack(r, v[q * 8 + 2 * k], v[q * 8 + 2 * k + 1]);
           }
         }
         __syncwarp();
@@ -432,16 +487,23 @@ __device__ __forceinline__ bool epilogue_tile(const GemmParams& p, uint32_t t_ro
           f[2 * j] = t.x;
           f[2 * j + 1] = t.y;
         }
-        float sum = 0.0f;
+        // two interleaved partial sums per packed f32x2 add / FMA
+        uint64_t s2 = f2_pack(f[0], f[1]);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) sum += f[j];
-        const float cm = sum * (1.0f / 32.0f);
-        float m2 = 0.0f;
+        for (int j = 2; j < 32; j += 2) s2 = f2_add(s2, f2_pack(f[j], f[j + 1]));
+        float s_lo, s_hi;
+        f2_unpack(s2, s_lo, s_hi);
+        const float cm = (s_lo + s_hi) * (1.0f / 32.0f);
+        const uint64_t ncm = f2_pack(-cm, -cm);
+        uint64_t q2 = f2_pack(0.0f, 0.0f);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float d = f[j] - cm;
-          m2 = fmaf(d, d, m2);
+        for (int j = 0; j < 32; j += 2) {
+          const uint64_t d = f2_add(f2_pack(f[j], f[j + 1]), ncm);
+          q2 = f2_fma(d, d, q2);
         }
+        float q_lo, q_hi;
+        f2_unpack(q2, q_lo, q_hi);
+        const float m2 = q_lo + q_hi;
         if (s_cnt == 0.0f) {
           s_cnt = 32.0f;
           s_mean = cm;
@@ -721,8 +783,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int n0 = (sg.tile % p.n_tiles) * BN;
       const int row = m0 + r_in_tile;
       uint8_t* stage_buf = sEpi + (warp - 2) * kStageBytesPerWarp;
-      const bool res_pref = !(p.sk_ctas > 0 && sg.kb0 > 0) &&
-                            epilogue_prefetch<BN>(p, row, n0, m0 + quad * 32, half, stage_buf);
+      const EpiPre pre = (p.sk_ctas > 0 && sg.kb0 > 0)
+                             ? EpiPre{}
+                             : epilogue_prefetch<BN>(p, row, n0, m0 + quad * 32, half, stage_buf);
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status, kDevTimeoutEpilogue)) break;
       tc_fence_after();
       const uint32_t t_row = tbase + (static_cast<uint32_t>(quad * 32) << 16) +
@@ -753,7 +816,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         if (ok) {
           ok = epilogue_tile<BN>(p, t_row, row, n0, m0 + quad * 32, stage_buf, &tmC, sbuf, half,
-                                 sXchg + quad * 32, xbar + 2 * quad, xphase, abort_flag, res_pref,
+                                 sXchg + quad * 32, xbar + 2 * quad, xphase, abort_flag, pre,
                                  c0, c1, r_in_tile);
           if (ok && c1 > c0) {
             // every warp has read the partials: clear the flags for the next launch
@@ -1002,13 +1065,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int n0 = (t % p.n_tiles) * BN;
       const int row = m0 + quad * 32 + lane;
       uint8_t* stage_buf = sEpi + (warp - 2) * kStageBytesPerWarp;
-      const bool res_pref = epilogue_prefetch<BN>(p, row, n0, m0 + quad * 32, half, stage_buf);
+      const EpiPre pre = epilogue_prefetch<BN>(p, row, n0, m0 + quad * 32, half, stage_buf);
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status, kDevTimeoutEpilogue)) break;
       tc_fence_after();
       const uint32_t t_row = tbase + (static_cast<uint32_t>(quad * 32) << 16) +
                              static_cast<uint32_t>(acc * BN);
       if (!epilogue_tile<BN>(p, t_row, row, n0, m0 + quad * 32, stage_buf, &tmC, sbuf, half,
-                             sXchg + quad * 32, xbar + 2 * quad, xphase, abort_flag, res_pref))
+                             sXchg + quad * 32, xbar + 2 * quad, xphase, abort_flag, pre))
         break;
       tc_fence_before();
       __syncwarp();
