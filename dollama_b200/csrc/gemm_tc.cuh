@@ -392,8 +392,10 @@ __device__ __forceinline__ bool epilogue_tile(const GemmParams& p, uint32_t t_ro
       uint32_t o[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const float a0 = v[4 * j] * gelu_erf_f(v[4 * j + 1]);
-        const float a1 = v[4 * j + 2] * gelu_erf_f(v[4 * j + 3]);
+        float g0, g1;
+        gelu_erf_x2(v[4 * j + 1], v[4 * j + 3], g0, g1);
+        const float a0 = v[4 * j] * g0;
+        const float a1 = v[4 * j + 2] * g1;
         o[j] = pack_half2(a0, a1);
       }
       // 32-byte rows, 32-byte swizzle: 16-byte chunk q of row r at q ^ ((r >> 2) & 1)

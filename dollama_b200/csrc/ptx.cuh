@@ -448,6 +448,7 @@ __device__ __forceinline__ float gelu_erf_f(float x) {
   return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
 }
 
+
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
   __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
@@ -477,6 +478,30 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
+}
+
+// GELU(x) = x / 2 (1 + erf(x / sqrt 2)) of two values, with erf from Abramowitz & Stegun 7.1.26:
+// erf(z) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-z^2), t = 1 / (1 + p z), z >= 0,
+// absolute error <= 1.5e-7 (erf(-z) = -erf(z)).  The polynomial runs on packed f32x2 FMAs; the
+// reciprocal and exp2 are one MUFU instruction each per value.
+__device__ __forceinline__ void gelu_erf_x2(float x0, float x1, float& g0, float& g1) {
+  const float z0 = fabsf(x0) * 0.70710678118654752f, z1 = fabsf(x1) * 0.70710678118654752f;
+  float t0, t1;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t0) : "f"(fmaf(0.3275911f, z0, 1.0f)));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t1) : "f"(fmaf(0.3275911f, z1, 1.0f)));
+  const uint64_t t = f2_pack(t0, t1);
+  uint64_t q = f2_fma(t, f2_pack(1.061405429f, 1.061405429f), f2_pack(-1.453152027f, -1.453152027f));
+  q = f2_fma(t, q, f2_pack(1.421413741f, 1.421413741f));
+  q = f2_fma(t, q, f2_pack(-0.284496736f, -0.284496736f));
+  q = f2_fma(t, q, f2_pack(0.254829592f, 0.254829592f));
+  float q0, q1;
+  f2_unpack(q, q0, q1);
+  // exp(-z^2) = 2^(-z^2 log2 e)
+  const float e0 = fast_exp2(-1.4426950408889634f * z0 * z0);
+  const float e1 = fast_exp2(-1.4426950408889634f * z1 * z1);
+  const float erf0 = fmaf(-q0 * t0, e0, 1.0f), erf1 = fmaf(-q1 * t1, e1, 1.0f);
+  g0 = 0.5f * x0 * (1.0f + copysignf(erf0, x0));
+  g1 = 0.5f * x1 * (1.0f + copysignf(erf1, x1));
 }
 
 }  // namespace dlm
