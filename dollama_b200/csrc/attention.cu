@@ -7,19 +7,21 @@
 // One CTA = one (batch, head) and two 128-query tiles T0, T1 that share every K/V tile
 // (320 threads, one CTA per SM, all 512 TMEM columns):
 //   warps 0..3 / 4..7  softmax of T0 / T1: thread r of the warpgroup owns query row r (TMEM
-//               lane r).  Per 128-key tile j: pass 1 reads S_j (TMEM) for the row max; the
-//               previous P.V result O_{j-1} is folded into the fp32 register accumulator with
-//               the running rescale; pass 2 computes p = 2^(s*c - m*c), the fp32 row sum, and
-//               stores P_j (fp16) into a 128-byte-swizzled K-major shared tile.  The softmax is
-//               bound by instruction issue and MUFU latency with two warps per scheduler, so the
-//               scale / shift, the row sum and the O rescale run as packed f32x2 FMA / add and
-//               the row max as three-input max (half the instructions of scalar code);
+//               lane r).  Per 128-key tile j: pass 1 reads S_j (TMEM) for the row max; pass 2
+//               computes p = 2^(s*c - m*c), the fp32 row sum, and stores P_j (fp16) into a
+//               128-byte-swizzled K-major shared tile.  O accumulates in TMEM across the KV
+//               tiles (P.V with accumulate); the running max m is lazy: it only moves when a
+//               row max exceeds it by more than 8 in exp2 units (p <= 2^8 otherwise), and only
+//               then is O rescaled in place (TMEM load, scale, store), so most tiles never touch
+//               O.  The softmax is bound by instruction issue and MUFU latency with two warps
+//               per scheduler, so the scale / shift, the row sum and the O rescale run as packed
+//               f32x2 FMA / add and the row max as three-input max;
 //   warp 8      TMA producer: Q (both tiles) once, then K_j / V_j through a 3-stage ring;
 //   warp 9      TMEM owner + single-thread MMA issuer: S_j^t = Q_t K_j^T (M=128, N=128, K=64)
 //               and O_j^t = P_j^t V_j (M=128, N=64, K=128, V as an MN-major operand).
 // While one tile's softmax runs, the tensor core computes the other tile's S and P.V, so the
 // MMA latency hides behind softmax work (the two warpgroups ping-pong).
-// TMEM columns: S^0 [0,128), S^1 [128,256), O^0 [256,384) (2 x 64), O^1 [384,512) (2 x 64).
+// TMEM columns: S^0 [0,128), S^1 [128,256), O^0 [256,320), O^1 [384,448).
 //
 // Q/K/V/O are addressed through 4D tensor maps {64 (d), heads, seq, batch} with arbitrary
 // strides, so the same kernel reads the token-major [B*S, ld] projections of the UNet (head h at
@@ -145,9 +147,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* kv_empty = v_full + kKVStages;    // [stages]
   uint64_t* s_full = kv_empty + kKVStages;    // [tile]      S_j^t ready
   uint64_t* p_full = s_full + 2;              // [tile]      P_j^t stored, S_j^t consumed
-  uint64_t* o_full = p_full + 2;              // [tile][2]   O_j^t ready
-  uint64_t* o_empty = o_full + 4;             // [tile][2]   O_j^t folded
-  uint64_t* q_empty = o_empty + 4;            // the last S MMAs of a segment read Q
+  uint64_t* o_full = p_full + 2;              // [tile]      P_j^t . V_j accumulated into O^t
+  uint64_t* o_empty = o_full + 2;             // [tile]      O^t of a segment read out
+  uint64_t* q_empty = o_empty + 2;            // the last S MMAs of a segment read Q
   uint64_t* ep_bar = q_empty + 1;             // the eight softmax warps meet (stream-K merge)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ep_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -171,10 +173,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     for (int t = 0; t < 2; ++t) {
       mbar_init(&s_full[t], 1);
       mbar_init(&p_full[t], kQT);
-      mbar_init(&o_full[2 * t], 1);
-      mbar_init(&o_full[2 * t + 1], 1);
-      mbar_init(&o_empty[2 * t], kQT);
-      mbar_init(&o_empty[2 * t + 1], kQT);
+      mbar_init(&o_full[t], 1);
+      mbar_init(&o_empty[t], kQT);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -261,23 +261,25 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         return true;
       };
       auto issue_pv = [&](int t, int jl) -> bool {
-        const int kk = kc + jl, st = kk % kKVStages, jj = jc + jl;
+        const int kk = kc + jl, st = kk % kKVStages;
         if (!mbar_wait(&v_full[st], (kk / kKVStages) & 1, abort_flag, p.status, kDevTimeoutMma))
           return false;
-        if (jj >= 2 && !mbar_wait(&o_empty[2 * t + (jj & 1)], ((jj - 2) >> 1) & 1, abort_flag,
-                                  p.status, kDevTimeoutMma))
+        // O^t accumulates over the segment; its first P.V overwrites it once the softmax warps
+        // have read out the previous segment's O
+        if (jl == 0 && seg > 0 &&
+            !mbar_wait(&o_empty[t], (seg - 1) & 1, abort_flag, p.status, kDevTimeoutMma))
           return false;
         tc_fence_after();
         const uint32_t p_addr = smem_u32(sP + t * kPBytes);
         const uint32_t v_addr = smem_u32(sV + st * kTileBytes);
-        const uint32_t d = tbase + 256 + t * 128 + (jj & 1) * kD;
+        const uint32_t d = tbase + 256 + t * 128;
 #pragma unroll
         for (int ks = 0; ks < kKV / 16; ++ks) {
           const uint64_t ad = sw128_desc(p_addr + (ks >> 2) * (kQT * 128) + (ks & 3) * 32, 16, 1024);
           const uint64_t bd = sw128_desc(v_addr + ks * 2048, 1024, 1024);
-          umma_f16_ss(d, ad, bd, idesc_o, ks != 0 ? 1u : 0u);
+          umma_f16_ss(d, ad, bd, idesc_o, (jl != 0 || ks != 0) ? 1u : 0u);
         }
-        umma_commit(&o_full[2 * t + (jj & 1)]);
+        umma_commit(&o_full[t]);
         umma_commit(&kv_empty[st]);
         return true;
       };
@@ -333,28 +335,31 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       return r;
     };
 
-    auto fold_o = [&](int jj, float alpha) -> bool {
-      if (!mbar_wait(&o_full[2 * t + (jj & 1)], (jj >> 1) & 1, abort_flag, p.status,
-                     kDevTimeoutSoftmax))
-        return false;
-      tc_fence_after();
+    // bounded wait whose outcome is the same in every lane (the warp-collective TMEM accesses
+    // that follow need all 32 lanes)
+    auto wwait = [&](uint64_t* bar, uint32_t parity) -> bool {
+      return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, p.status, kDevTimeoutSoftmax));
+    };
+    // O^t *= alpha in place (this warp's 32 rows), for rows whose running max moved
+    auto rescale_o = [&](float alpha) {
       uint32_t r0[32], r1[32];
-      tmem_ld_32x32b_x32(to + (jj & 1) * kD, r0);
-      tmem_ld_32x32b_x32(to + (jj & 1) * kD + 32, r1);
+      tmem_ld_32x32b_x32(to, r0);
+      tmem_ld_32x32b_x32(to + 32, r1);
       tmem_ld_wait();
       const uint64_t a2 = f2_pack(alpha, alpha);
 #pragma unroll
       for (int q = 0; q < 32; q += 2) {
-        uint64_t v = f2_fma(f2_pack(acc[q], acc[q + 1]), a2,
-                            f2_pack(__uint_as_float(r0[q]), __uint_as_float(r0[q + 1])));
-        f2_unpack(v, acc[q], acc[q + 1]);
-        v = f2_fma(f2_pack(acc[32 + q], acc[33 + q]), a2,
-                   f2_pack(__uint_as_float(r1[q]), __uint_as_float(r1[q + 1])));
-        f2_unpack(v, acc[32 + q], acc[33 + q]);
+        float x0, x1;
+        f2_unpack(f2_fma(f2_pack(__uint_as_float(r0[q]), __uint_as_float(r0[q + 1])), a2, f2_pack(0.0f, 0.0f)), x0, x1);
+        r0[q] = __float_as_uint(x0);
+        r0[q + 1] = __float_as_uint(x1);
+        f2_unpack(f2_fma(f2_pack(__uint_as_float(r1[q]), __uint_as_float(r1[q + 1])), a2, f2_pack(0.0f, 0.0f)), x0, x1);
+        r1[q] = __float_as_uint(x0);
+        r1[q + 1] = __float_as_uint(x1);
       }
-      tc_fence_before();
-      mbar_arrive(&o_empty[2 * t + (jj & 1)]);
-      return true;
+      tmem_st_32x32b_x32(to, r0);
+      tmem_st_32x32b_x32(to + 32, r1);
+      tmem_st_wait();
     };
 
     AttnSegIter<kSK> si;
@@ -362,13 +367,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     AttnSeg sg;
     while (ok && si.next(sg)) {
       const int n = sg.j1 - sg.j0;
-      float m_run = -INFINITY, l_run = 0.0f, alpha_prev = 1.0f;
-#pragma unroll
-      for (int d = 0; d < kD; ++d) acc[d] = 0.0f;
+      float m_run = -INFINITY, l_run = 0.0f;
 
       for (int jl = 0; jl < n; ++jl) {
         const int jj = jc + jl;
-        if (!mbar_wait(&s_full[t], jj & 1, abort_flag, p.status, kDevTimeoutSoftmax)) {
+        if (!wwait(&s_full[t], jj & 1)) {
           ok = false;
           break;
         }
@@ -400,12 +403,25 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
         }
         const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
-        const float alpha = fast_exp2((m_run - mx) * c);  // m_run = -inf on the first tile -> 0
-        const float mc = mx * c;
-        // fold O_{j-1}: also guarantees P.V of tile j-1 finished reading the P buffer
-        if (jl >= 1 && !fold_o(jj - 1, alpha_prev)) {
-          ok = false;
-          break;
+        // Lazy rescale: the running max m_run only moves when a row's max exceeds it by more
+        // than 8 in exp2 units (so p = 2^(s c - m c) <= 2^8 stays exact in fp16 range); then O
+        // and the row sum are scaled by alpha = 2^((m_old - m_new) c).
+        float m_new = m_run, alpha = 1.0f;
+        if (jl == 0) {
+          m_new = mx;
+        } else if ((mx - m_run) * c > 8.0f) {
+          m_new = mx;
+          alpha = fast_exp2((m_run - mx) * c);
+        }
+        const float mc = m_new * c;
+        if (jl >= 1) {
+          // P.V of tile j-1 is complete: it has read the P buffer and added into O
+          if (!wwait(&o_full[t], (jj - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (__any_sync(0xffffffffu, alpha != 1.0f)) rescale_o(alpha);
         }
         // pass 2: p = exp2(s*c - m*c), fp32 row sum, fp16 P into shared memory
         const uint64_t c2 = f2_pack(c, c), nmc2 = f2_pack(-mc, -mc);
@@ -448,10 +464,26 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tc_fence_before();
         mbar_arrive(&p_full[t]);
         l_run = fmaf(l_run, alpha, (sum0 + sum1) + (sum2 + sum3));
-        m_run = mx;
-        alpha_prev = alpha;
+        m_run = m_new;
       }
-      if (ok && n > 0) ok = fold_o(jc + n - 1, alpha_prev);
+      if (ok && n > 0) {
+        // the segment's last P.V: read O out, then let the next segment's first P.V overwrite it
+        ok = wwait(&o_full[t], (jc + n - 1) & 1);
+        if (ok) {
+          tc_fence_after();
+          uint32_t r0[32], r1[32];
+          tmem_ld_32x32b_x32(to, r0);
+          tmem_ld_32x32b_x32(to + 32, r1);
+          tmem_ld_wait();
+#pragma unroll
+          for (int q = 0; q < 32; ++q) {
+            acc[q] = __uint_as_float(r0[q]);
+            acc[32 + q] = __uint_as_float(r1[q]);
+          }
+          tc_fence_before();
+          mbar_arrive(&o_empty[t]);
+        }
+      }
       jc += n;
       if (!ok) break;
       int b, h, q0;
@@ -505,9 +537,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (!ok) break;
       if (*last_flag) {
         __threadfence();
-        // merge the pieces in CTA order: O = sum_s w_s O_s / sum_s w_s, w_s = l_s 2^((m_s - m) c).
-        // The loads of several pieces are issued before any of them is used, so that the merge
-        // waits for about one L2 round trip per four (max, sum) pairs and per two O rows.
+        // merge the pieces in CTA order: O = sum_s w_s O_s / sum_s w_s, w_s = l_s 2^((m_s - m) c);
+        // the (max, sum) pairs of up to four pieces are requested before any is used
         auto slot_of = [&](int cc) { return 2 * cc + (cc == first ? 1 : 0); };
         float mmax = -INFINITY;
         for (int c0 = first; c0 <= last; c0 += 4) {
@@ -522,45 +553,23 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
         for (int d = 0; d < kD; ++d) acc[d] = 0.0f;
         float L = 0.0f;
-        for (int c0 = first; c0 <= last; c0 += 2) {
-          const bool two = c0 + 1 <= last;
-          const size_t sa = static_cast<size_t>(slot_of(c0)) * kQ + r_in;
-          const size_t sb = static_cast<size_t>(slot_of(two ? c0 + 1 : c0)) * kQ + r_in;
-          const float2 mla = __ldcg(p.part_ml + sa);
-          const float2 mlb = __ldcg(p.part_ml + sb);
-          const uint4* pa = reinterpret_cast<const uint4*>(p.part_o + sa * kD);
-          const uint4* pb = reinterpret_cast<const uint4*>(p.part_o + sb * kD);
-          uint4 oa[kD / 8], ob[kD / 8];
+        for (int cc = first; cc <= last; ++cc) {
+          const size_t sl = static_cast<size_t>(slot_of(cc)) * kQ + r_in;
+          const float2 ml = __ldcg(p.part_ml + sl);
+          const uint4* po = reinterpret_cast<const uint4*>(p.part_o + sl * kD);
+          uint4 ov[kD / 8];
 #pragma unroll
-          for (int j = 0; j < kD / 8; ++j) oa[j] = __ldcg(pa + j);
-          if (two) {
-#pragma unroll
-            for (int j = 0; j < kD / 8; ++j) ob[j] = __ldcg(pb + j);
-          }
-          const float wa = mla.y * fast_exp2((mla.x - mmax) * c);
-          L += wa;
+          for (int j = 0; j < kD / 8; ++j) ov[j] = __ldcg(po + j);
+          const float w = ml.y * fast_exp2((ml.x - mmax) * c);
+          L += w;
 #pragma unroll
           for (int j = 0; j < kD / 8; ++j) {
-            const __half2* hh = reinterpret_cast<const __half2*>(&oa[j]);
+            const __half2* hh = reinterpret_cast<const __half2*>(&ov[j]);
 #pragma unroll
             for (int k2 = 0; k2 < 4; ++k2) {
               const float2 f = __half22float2(hh[k2]);
-              acc[8 * j + 2 * k2] = fmaf(wa, f.x, acc[8 * j + 2 * k2]);
-              acc[8 * j + 2 * k2 + 1] = fmaf(wa, f.y, acc[8 * j + 2 * k2 + 1]);
-            }
-          }
-          if (two) {
-            const float wb = mlb.y * fast_exp2((mlb.x - mmax) * c);
-            L += wb;
-#pragma unroll
-            for (int j = 0; j < kD / 8; ++j) {
-              const __half2* hh = reinterpret_cast<const __half2*>(&ob[j]);
-#pragma unroll
-              for (int k2 = 0; k2 < 4; ++k2) {
-                const float2 f = __half22float2(hh[k2]);
-                acc[8 * j + 2 * k2] = fmaf(wb, f.x, acc[8 * j + 2 * k2]);
-                acc[8 * j + 2 * k2 + 1] = fmaf(wb, f.y, acc[8 * j + 2 * k2 + 1]);
-              }
+              acc[8 * j + 2 * k2] = fmaf(w, f.x, acc[8 * j + 2 * k2]);
+              acc[8 * j + 2 * k2 + 1] = fmaf(w, f.y, acc[8 * j + 2 * k2 + 1]);
             }
           }
         }
