@@ -8,8 +8,9 @@
 // (320 threads, one CTA per SM, all 512 TMEM columns):
 //   warps 0..3 / 4..7  softmax of T0 / T1: thread r of the warpgroup owns query row r (TMEM
 //               lane r).  Per 128-key tile j: pass 1 reads S_j (TMEM) for the row max; pass 2
-//               computes p = 2^(s*c - m*c), the fp32 row sum, and stores P_j (fp16) into a
-//               128-byte-swizzled K-major shared tile.  O accumulates in TMEM across the KV
+//               computes p = 2^(s*c - m*c), the fp32 row sum, and stores P_j as fp16 pairs
+//               into the first 64 TMEM columns of S_j (read already), from where the P.V MMA
+//               takes its A operand (no shared-memory P).  O accumulates in TMEM across the KV
 //               tiles (P.V with accumulate); the running max m is lazy: it only moves when a
 //               row max exceeds it by more than 8 in exp2 units (p <= 2^8 otherwise), and only
 //               then is O rescaled in place (TMEM load, scale, store), so most tiles never touch
@@ -18,10 +19,12 @@
 //               f32x2 FMA / add and the row max as three-input max;
 //   warp 8      TMA producer: Q (both tiles) once, then K_j / V_j through a 3-stage ring;
 //   warp 9      TMEM owner + single-thread MMA issuer: S_j^t = Q_t K_j^T (M=128, N=128, K=64)
-//               and O_j^t = P_j^t V_j (M=128, N=64, K=128, V as an MN-major operand).
+//               and O_j^t = P_j^t V_j (M=128, N=64, K=128, P from TMEM, V as an MN-major
+//               operand); P_j's P.V is issued before S_{j+1}, which overwrites P_j's columns.
 // While one tile's softmax runs, the tensor core computes the other tile's S and P.V, so the
 // MMA latency hides behind softmax work (the two warpgroups ping-pong).
-// TMEM columns: S^0 [0,128), S^1 [128,256), O^0 [256,320), O^1 [384,448).
+// TMEM columns: S^0 [0,128) (P^0 in [0,64)), S^1 [128,256) (P^1 in [128,192)), O^0 [256,320),
+// O^1 [384,448).
 //
 // Q/K/V/O are addressed through 4D tensor maps {64 (d), heads, seq, batch} with arbitrary
 // strides, so the same kernel reads the token-major [B*S, ld] projections of the UNet (head h at
@@ -43,30 +46,15 @@ constexpr int kD = 64;         // head dim
 constexpr int kKVStages = 3;
 constexpr int kAttnThreads = 320;
 constexpr int kTileBytes = kQT * kD * 2;         // 16 KB (Q, K or V tile)
-constexpr int kPBytes = kQT * kKV * 2;           // 32 KB
 constexpr uint32_t kTmemCols = 512;
 
 constexpr int kSmemQ = 0;                                   // 2 tiles
 constexpr int kSmemK = kSmemQ + 2 * kTileBytes;
 constexpr int kSmemV = kSmemK + kKVStages * kTileBytes;
-constexpr int kSmemP = kSmemV + kKVStages * kTileBytes;     // 2 tiles
-constexpr int kSmemBar = kSmemP + 2 * kPBytes;
+constexpr int kSmemBar = kSmemV + kKVStages * kTileBytes;
 constexpr int kAttnSmem = kSmemBar + 256 + 1024;
 static_assert(kAttnSmem <= 226 * 1024, "shared memory");
 
-__device__ __forceinline__ void store_p_chunk(uint8_t* pbuf, int row, int chunk32,
-                                              const uint32_t (&h)[16]) {
-  // keys [32*chunk32, +32) of `row`: four 16-byte chunks, 128B-swizzled K-major layout with
-  // two 64-key column blocks of 16 KB each.
-  const int blk = chunk32 >> 1;
-  uint8_t* base = pbuf + blk * (kQT * 128) + row * 128;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int c16 = ((chunk32 & 1) * 4 + i) ^ (row & 7);
-    *reinterpret_cast<uint4*>(base + c16 * 16) =
-        make_uint4(h[4 * i], h[4 * i + 1], h[4 * i + 2], h[4 * i + 3]);
-  }
-}
 
 // Work of one CTA: KV tiles [j0, j1) of one group (a 256-query block of one (batch, head));
 // `whole` when that is every tile of the group.
@@ -139,7 +127,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint8_t* sQ = smem + kSmemQ;
   uint8_t* sK = smem + kSmemK;
   uint8_t* sV = smem + kSmemV;
-  uint8_t* sP = smem + kSmemP;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kSmemBar);
   uint64_t* q_full = bars;                    // Q of both tiles
   uint64_t* k_full = bars + 1;                // [stages]
@@ -270,14 +257,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             !mbar_wait(&o_empty[t], (seg - 1) & 1, abort_flag, p.status, kDevTimeoutMma))
           return false;
         tc_fence_after();
-        const uint32_t p_addr = smem_u32(sP + t * kPBytes);
+        const uint32_t p_tmem = tbase + t * kKV;  // P^t: 64 columns of fp16 pairs
         const uint32_t v_addr = smem_u32(sV + st * kTileBytes);
         const uint32_t d = tbase + 256 + t * 128;
 #pragma unroll
         for (int ks = 0; ks < kKV / 16; ++ks) {
-          const uint64_t ad = sw128_desc(p_addr + (ks >> 2) * (kQT * 128) + (ks & 3) * 32, 16, 1024);
           const uint64_t bd = sw128_desc(v_addr + ks * 2048, 1024, 1024);
-          umma_f16_ss(d, ad, bd, idesc_o, (jl != 0 || ks != 0) ? 1u : 0u);
+          umma_f16_ts(d, p_tmem + ks * 8, bd, idesc_o, (jl != 0 || ks != 0) ? 1u : 0u);
         }
         umma_commit(&o_full[t]);
         umma_commit(&kv_empty[st]);
@@ -299,11 +285,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
               break;
             }
             tc_fence_after();
-            if (jl + 1 < n) {
+            // P.V reads P_j from S_j's columns before S_{j+1} overwrites them (in-order MMAs)
+            ok = issue_pv(t, jl);
+            if (ok && jl + 1 < n) {
               ok = issue_s(t, jl + 1);
               if (ok && t == 1 && jl + 2 == n) umma_commit(q_empty);  // last S of the segment
             }
-            if (ok) ok = issue_pv(t, jl);
           }
         }
         kc += n;
@@ -320,7 +307,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t ts = tbase + lane_off + t * kKV;
     const uint32_t to = tbase + lane_off + 256 + t * 128;
-    uint8_t* pbuf = sP + t * kPBytes;
     const float c = p.scale_log2;
     float acc[kD];
     bool ok = true;
@@ -423,7 +409,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           tc_fence_after();
           if (__any_sync(0xffffffffu, alpha != 1.0f)) rescale_o(alpha);
         }
-        // pass 2: p = exp2(s*c - m*c), fp32 row sum, fp16 P into shared memory
+        // pass 2: p = exp2(s*c - m*c), fp32 row sum, fp16 P (pairs of consecutive keys) into
+        // S_j's first 64 TMEM columns, which this thread's lane has read already
         const uint64_t c2 = f2_pack(c, c), nmc2 = f2_pack(-mc, -mc);
         uint64_t sumA = f2_pack(0.0f, 0.0f), sumB = sumA;
 #pragma unroll
@@ -432,11 +419,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           tmem_ld_32x32b_x32(ts + cc * 32, ra);
           tmem_ld_32x32b_x32(ts + cc * 32 + 32, rb);
           tmem_ld_wait();
+          uint32_t pp[32];
 #pragma unroll
           for (int half = 0; half < 2; ++half) {
             const uint32_t* r = half ? rb : ra;
             const int col0 = (cc + half) * 32;
-            uint32_t hp[16];
 #pragma unroll
             for (int q = 0; q < 32; q += 2) {
               float x0, x1;
@@ -452,15 +439,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 sumB = f2_add(sumB, f2_pack(e0, e1));
               else
                 sumA = f2_add(sumA, f2_pack(e0, e1));
-              hp[q >> 1] = pack_half2(e0, e1);
+              pp[half * 16 + (q >> 1)] = pack_half2(e0, e1);
             }
-            store_p_chunk(pbuf, row, cc + half, hp);
           }
+          tmem_st_32x32b_x32(ts + (cc >> 1) * 32, pp);
         }
+        tmem_st_wait();
         float sum0, sum1, sum2, sum3;
         f2_unpack(sumA, sum0, sum1);
         f2_unpack(sumB, sum2, sum3);
-        fence_proxy_async_smem();
         tc_fence_before();
         mbar_arrive(&p_full[t]);
         l_run = fmaf(l_run, alpha, (sum0 + sum1) + (sum2 + sum3));

@@ -254,6 +254,20 @@ __device__ __forceinline__ void umma_f16_ss(uint32_t d_tmem, uint64_t a_desc, ui
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem desc], kind::f16: A (M = 128 lanes x K) read from tensor memory,
+// two fp16 values of consecutive k per 32-bit column (column a_tmem + k / 2).
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "setp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n"
+      "}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive (once) on `bar` when every tcgen05.mma issued so far by this thread completes.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile(
