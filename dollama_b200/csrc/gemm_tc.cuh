@@ -1012,42 +1012,61 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // ------------------------------------------------------------ MMA issuer (even CTA)
     if (leader && lane == 0) {
       constexpr uint32_t idesc = idesc_f16_f32(2 * kGemmBM, BN, false);
-      int stage = 0;
+      // Descriptors of stage 0 as low words over one high word; the ring is walked one pass at a
+      // time with the stage index unrolled, so barrier addresses and descriptor offsets are
+      // immediates: this thread's bookkeeping per stage is what bounds short MMAs.
+      const uint64_t da0 = sw128_desc(smem_u32(sA), 16, 1024);
+      const uint32_t a_lo0 = static_cast<uint32_t>(da0);
+      const uint32_t b_lo0 = static_cast<uint32_t>(sw128_desc(smem_u32(sB), 16, 1024));
+      const uint32_t d_hi = static_cast<uint32_t>(da0 >> 32);
       uint32_t phase = 0;
       int i = 0;
+      int t = pair;
+      int kb = 0;
       bool ok = true;
-      for (int t = pair; t < num_tiles && ok; t += npairs, ++i) {
-        const int acc = i & 1;
-        const uint32_t acc_phase = (i >> 1) & 1;
-        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, p.status, kDevTimeoutMma)) break;
-        tc_fence_after();
-        const uint32_t d_tmem = tbase + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < p.num_kb; kb += kPairKsub) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, p.status, kDevTimeoutMma)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t a_base = smem_u32(sA + stage * A_BYTES);
-          const uint32_t b_base = smem_u32(sB + stage * B_BYTES);
+      bool have = t < num_tiles;
+      uint32_t d_tmem = tbase;
+      while (have && ok) {
 #pragma unroll
-          for (int sub = 0; sub < kPairKsub; ++sub) {
-            if (kb + sub < p.num_kb) {
+        for (int st = 0; st < STAGES; ++st) {
+          if (have && ok) {
+            if (kb == 0) {
+              const int acc = i & 1;
+              if (mbar_wait(&tempty[acc], ((i >> 1) & 1) ^ 1, abort_flag, p.status, kDevTimeoutMma)) {
+                tc_fence_after();
+                d_tmem = tbase + static_cast<uint32_t>(acc * BN);
+              } else {
+                ok = false;
+              }
+            }
+            if (ok && !mbar_wait(&full[st], phase, abort_flag, p.status, kDevTimeoutMma)) ok = false;
+            if (ok) {
+              tc_fence_after();
 #pragma unroll
-              for (int k = 0; k < kGemmBK / 16; ++k) {
-                umma2_f16_ss(d_tmem, sw128_desc(a_base + sub * A_SUB + k * 32, 16, 1024),
-                             sw128_desc(b_base + sub * B_SUB + k * 32, 16, 1024), idesc,
-                             (kb + sub) != 0 || k != 0 ? 1u : 0u);
+              for (int sub = 0; sub < kPairKsub; ++sub) {
+                const uint32_t a_off = static_cast<uint32_t>(st * A_BYTES + sub * A_SUB) >> 4;
+                const uint32_t b_off = static_cast<uint32_t>(st * B_BYTES + sub * B_SUB) >> 4;
+                if (sub == 0 || kb + sub < p.num_kb) {
+                  umma2_f16_ss_lo(d_tmem, a_lo0 + a_off, b_lo0 + b_off, d_hi, idesc,
+                                  (kb + sub) != 0 ? 1u : 0u);
+#pragma unroll
+                  for (int k = 1; k < kGemmBK / 16; ++k)
+                    umma2_f16_ss_lo(d_tmem, a_lo0 + a_off + 2 * k, b_lo0 + b_off + 2 * k, d_hi, idesc, 1u);
+                }
+              }
+              umma2_commit_mc(&empty[st], 0x3);
+              kb += kPairKsub;
+              if (kb >= p.num_kb) {
+                umma2_commit_mc(&tfull[i & 1], 0x3);
+                ++i;
+                kb = 0;
+                t += npairs;
+                have = t < num_tiles;
               }
             }
           }
-          umma2_commit_mc(&empty[stage], 0x3);
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1;
-          }
         }
-        if (ok) umma2_commit_mc(&tfull[acc], 0x3);
+        phase ^= 1;
       }
       griddep_launch_dependents();
     } else if (lane == 0) {

@@ -399,6 +399,24 @@ __device__ __forceinline__ void umma2_f16_ss(uint32_t d_tmem, uint64_t a_desc, u
       : "memory");
 }
 
+// Pair MMA with the descriptors given as their low words over a shared high word (the
+// 128-byte-swizzle descriptors of one kernel differ only in the start address, bits [0,14)), so
+// that the issuing thread advances them with a 32-bit add.
+__device__ __forceinline__ void umma2_f16_ss_lo(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo,
+                                                uint32_t hi, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      ".reg .b64 da, db;\n"
+      "mov.b64 da, {%1, %3};\n"
+      "mov.b64 db, {%2, %3};\n"
+      "setp.ne.b32 p, %5, 0;\n"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], da, db, %4, p;\n"
+      "}\n" ::"r"(d_tmem),
+      "r"(a_lo), "r"(b_lo), "r"(hi), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive once on the mbarrier at `bar`'s offset in every CTA of `cta_mask` when the pair MMAs
 // issued so far complete.
 __device__ __forceinline__ void umma2_commit_mc(uint64_t* bar, uint16_t cta_mask) {
