@@ -34,6 +34,25 @@ _SIGS = {
     "dlm_gemm_fp16_ex": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
                                  c_uint, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p]),
     "dlm_gemm_set_tile_mode": (c_int, [c_int]),
+    "dlm_gemm_fp16_batched": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
+                                      ctypes.c_longlong, ctypes.c_longlong, ctypes.c_longlong,
+                                      c_float, c_float, c_int, c_void_p]),
+    "dlm_gemm_f32": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_float, c_float,
+                             c_int, c_int, c_void_p]),
+    "dlm_bias_add_rowvec": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p]),
+    "dlm_bias_add_channel": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
+                                     c_void_p]),
+    "dlm_conv_bias_biasch": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
+                                     c_int, c_void_p]),
+    "dlm_conv_bias_residual": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
+                                       c_int, c_void_p]),
+    "dlm_silu": (c_int, [c_void_p, c_void_p, c_int, c_void_p]),
+    "dlm_gelu": (c_int, [c_void_p, c_void_p, c_int, c_void_p]),
+    "dlm_gelu_tanh": (c_int, [c_void_p, c_void_p, c_int, c_void_p]),
+    "dlm_add": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_void_p]),
+    "dlm_upsample_nearest2x": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p]),
+    "dlm_geglu": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p]),
+    "dlm_timestep_embedding": (c_int, [c_void_p, c_float, c_int, c_float, c_void_p]),
     "dlm_gemm_workspace_bytes": (ctypes.c_size_t, []),
     "dlm_gemm_fp16_ws": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
                                  ctypes.c_uint, c_void_p, c_void_p, c_int, c_void_p, ctypes.c_size_t,

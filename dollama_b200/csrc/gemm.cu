@@ -3,6 +3,7 @@
 #include <cstring>
 
 #include "gemm.h"
+#include "ops.h"
 
 namespace dlm {
 
@@ -534,8 +535,33 @@ int dlm_gemm_fp16_ws(const void* A, int lda, const void* W, void* C, int ldc, in
 int dlm_launch_gemm_fp16(const void* A, const void* B, void* C, int M, int N, int K, float alpha,
                          float beta, int transA, int transB, void* stream) {
   if (M == 0 || N == 0 || K == 0) return DLM_OK;
-  DLM_REQUIRE(!transA && transB, DLM_ERR_UNSUPPORTED,
-              "dlm_launch_gemm_fp16: only transA=0, transB=1 is provided");
+  DLM_REQUIRE(A && B && C, DLM_ERR_INVALID, "dlm_launch_gemm_fp16: null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // The tensor-core kernel reads A as [M, K] and B as [N, K] (both K-major); the other
+  // orientations are transposed once into stream-ordered scratch.
+  __half* at = nullptr;
+  __half* bt = nullptr;
+  const __half* a = static_cast<const __half*>(A);
+  const __half* b = static_cast<const __half*>(B);
+  if (transA) {
+    DLM_CHECK_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&at), static_cast<size_t>(M) * K * 2, s));
+    int rc = dlm::transpose_strided(a, M, at, K, M, s);  // [K, M] -> [M, K]
+    if (rc != DLM_OK) {
+      cudaFreeAsync(at, s);
+      return rc;
+    }
+    a = at;
+  }
+  if (!transB) {
+    DLM_CHECK_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&bt), static_cast<size_t>(N) * K * 2, s));
+    int rc = dlm::transpose_strided(b, N, bt, K, N, s);  // [K, N] -> [N, K]
+    if (rc != DLM_OK) {
+      if (at) cudaFreeAsync(at, s);
+      cudaFreeAsync(bt, s);
+      return rc;
+    }
+    b = bt;
+  }
   dlm::GemmEpilogue e;
   e.alpha = alpha;
   if (beta != 0.0f) {
@@ -545,11 +571,27 @@ int dlm_launch_gemm_fp16(const void* A, const void* B, void* C, int M, int N, in
     e.resid_scale = beta;
   }
   dlm::GemmOp op;
-  int rc = dlm::gemm_plan_dense(&op, static_cast<const __half*>(A), K,
-                                static_cast<const __half*>(B), M, N, K, static_cast<__half*>(C), N,
-                                e);
-  if (rc != DLM_OK) return rc;
-  return dlm::gemm_launch(op, static_cast<cudaStream_t>(stream));
+  int rc = dlm::gemm_plan_dense(&op, a, K, b, M, N, K, static_cast<__half*>(C), N, e);
+  if (rc == DLM_OK) rc = dlm::gemm_launch(op, s);
+  if (at) cudaFreeAsync(at, s);
+  if (bt) cudaFreeAsync(bt, s);
+  return rc;
+}
+
+int dlm_gemm_fp16_batched(const void* A, const void* B, void* C, int batch, int M, int N, int K,
+                          long long stride_a, long long stride_b, long long stride_c, float alpha,
+                          float beta, int trans_b, void* stream) {
+  if (batch <= 0 || M == 0 || N == 0 || K == 0) return DLM_OK;
+  DLM_REQUIRE(A && B && C && M > 0 && N > 0 && K > 0 && stride_a >= 0 && stride_b >= 0 && stride_c >= 0,
+              DLM_ERR_INVALID, "dlm_gemm_fp16_batched: bad descriptor");
+  for (int i = 0; i < batch; ++i) {
+    const int rc = dlm_launch_gemm_fp16(static_cast<const __half*>(A) + i * stride_a,
+                                        static_cast<const __half*>(B) + i * stride_b,
+                                        static_cast<__half*>(C) + i * stride_c, M, N, K, alpha, beta, 0,
+                                        trans_b, stream);
+    if (rc != DLM_OK) return rc;
+  }
+  return DLM_OK;
 }
 
 }  // extern "C"

@@ -57,12 +57,26 @@ int dlm_memcpy(void* dst, const void* src, size_t bytes, void* stream);
  *
  * Replaces launch_gemm_fp16 (reference src/kernels/gemm.cuh:44-53, gemm.cu:518):
  *   C[M,N] = alpha * op(A)[M,K] * op(B)[K,N] + beta * C, row-major fp16, fp32 accumulate.
- * Supported: transA = 0 and transB = 1 (B is [N,K], PyTorch Linear layout) — the only form
- * the reference's UNet / VAE / LM paths use.  K % 8 == 0 and N % 32 == 0.
- * transB = 0 and transA = 1 return DLM_ERR_UNSUPPORTED.
+ * transA = 0 / transB = 1 (B is [N,K], PyTorch Linear layout, the form of the reference's UNet /
+ * VAE / LM paths) runs directly; the other orientations are first transposed into
+ * stream-ordered scratch (cudaMallocAsync on `stream`).  M, N, K % 8 == 0 where transposed.
  */
 int dlm_launch_gemm_fp16(const void* A, const void* B, void* C, int M, int N, int K, float alpha,
                          float beta, int transA, int transB, void* stream);
+
+/* Replaces launch_gemm_fp16_batched (src/kernels/gemm.cuh:100-175): item i multiplies
+ * A + i*stride_a, B + i*stride_b into C + i*stride_c (strides in elements, 0 = shared operand),
+ * same alpha / beta / trans_b semantics as dlm_launch_gemm_fp16 (transA = 0). */
+int dlm_gemm_fp16_batched(const void* A, const void* B, void* C, int batch, int M, int N, int K,
+                          long long stride_a, long long stride_b, long long stride_c, float alpha,
+                          float beta, int trans_b, void* stream);
+
+/* Replaces launch_gemm_f32 (src/kernels/gemm.cuh:61-70): fp32 row-major
+ * C = alpha * op(A) op(B) + beta * C (C not read when beta == 0), fp32 FMA accumulation on the
+ * CUDA cores.  Not on any model path of this library (the VAE keeps fp32 carries through the
+ * fp16 tensor-core GEMM with a scale, see dlm_vae_create). */
+int dlm_gemm_f32(const float* A, const float* B, float* C, int M, int N, int K, float alpha, float beta,
+                 int transA, int transB, void* stream);
 
 /* Epilogue flags of dlm_gemm_fp16_ex. */
 #define DLM_EPI_BIAS 1u     /* + bias[n]                                                */
@@ -95,6 +109,36 @@ int dlm_gemm_fp16_ws(const void* A, int lda, const void* W, void* C, int ldc, in
  * mode >> 4: forced N tile width (0 = cost model; 64, 128, 160, 192, 256).  For tests and A/B
  * measurements. */
 int dlm_gemm_set_tile_mode(int mode);
+
+/* ------------------------------------------------------------------ small reference kernels
+ *
+ * The reference's broadcast / activation / layout host functions with its layouts and rounding
+ * (h = round to fp16, f = fp32): the model handles of this library fuse all of them into GEMM
+ * epilogues; these serve other callers.  Empty sizes return DLM_OK without launching. */
+/* bias_add.cuh:32   out[t, c] = h(f(in[t, c]) + f(bias[c])), [tokens, C] (in place allowed) */
+int dlm_bias_add_rowvec(const void* in, const void* bias, void* out, int tokens, int C, void* stream);
+/* bias_add.cuh:51   NCHW, out[n, c, h, w] = h(f(in) + f(bias[c])) */
+int dlm_bias_add_channel(const void* in, const void* bias, void* out, int N, int C, int H, int W,
+                         void* stream);
+/* bias_add.cuh:75   NCHW, t = h(f(conv) + f(conv_bias[c])); out = h(f(t) + f(tproj[n * Cout + c])) */
+int dlm_conv_bias_biasch(const void* conv, const void* conv_bias, const void* tproj, void* out, int B,
+                         int Cout, int H, int W, void* stream);
+/* bias_add.cuh:96   NCHW, t = h(f(conv) + f(conv_bias[c])); out = h(f(t) + f(residual)) */
+int dlm_conv_bias_residual(const void* conv, const void* conv_bias, const void* residual, void* out,
+                           int B, int Cout, int H, int W, void* stream);
+/* activation.cuh:33-41   x * sigmoid(x); 0.5 x (1 + erf(x / sqrt 2)); tanh approximation */
+int dlm_silu(const void* in, void* out, int n, void* stream);
+int dlm_gelu(const void* in, void* out, int n, void* stream);
+int dlm_gelu_tanh(const void* in, void* out, int n, void* stream);
+/* elementwise.cuh:26   out = h(f(a) + f(b)) */
+int dlm_add(const void* a, const void* b, void* out, int n, void* stream);
+/* elementwise.cuh:37   NCHW [N, C, H, W] -> [N, C, 2H, 2W], nearest */
+int dlm_upsample_nearest2x(const void* in, void* out, int N, int C, int H, int W, void* stream);
+/* geglu.cuh:42   [tokens, 2d] -> [tokens, d], out = h(x1 * gelu_erf(x2)), x1 the first half */
+int dlm_geglu(const void* in, void* out, int tokens, int d, void* stream);
+/* timeembed.cuh:44   out[i] = cos(t f_i), out[dim/2 + i] = sin(t f_i),
+ * f_i = exp(-ln(max_period) i / (dim/2)) (diffusers flip_sin_to_cos = True) */
+int dlm_timestep_embedding(void* out, float timestep, int dim, float max_period, void* stream);
 
 /* ------------------------------------------------------------------ conv2d (implicit GEMM)
  *

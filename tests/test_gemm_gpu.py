@@ -101,11 +101,12 @@ def test_device_status_clean():
     assert code.value == 0
 
 
-def test_gemm_unsupported_trans():
+def test_gemm_invalid_arguments():
+    # every orientation is provided (transposed operands go through scratch); a null operand is
+    # an invalid argument, reported without launching
     A = _rand(128, 64)
-    rc = L.lib().dlm_launch_gemm_fp16(_ptr(A), _ptr(A), _ptr(A), 128, 64, 64, 1.0, 0.0, 1, 1,
-                                      _stream())
-    assert rc == -4
+    rc = L.lib().dlm_launch_gemm_fp16(_ptr(A), None, _ptr(A), 128, 64, 64, 1.0, 0.0, 1, 1, _stream())
+    assert rc == -1
 
 
 # ---------------------------------------------------------------- stream-K
