@@ -954,6 +954,28 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int t = pair; t < num_tiles && ok; t += npairs) {
         const int m0 = (t / p.n_tiles) * (2 * kGemmBM) + static_cast<int>(rank) * kGemmBM;
         const int nb = (t % p.n_tiles) * BN + static_cast<int>(rank) * BNH;
+        if (p.amode == 0) {
+          // dense A: one wait / expect_tx per ring stage, then its k-blocks' A and B boxes (the
+          // thread's per-k-block work bounds short tiles, so this path stays minimal)
+          for (int kb = 0; kb < p.num_kb; kb += kPairKsub) {
+            if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status, kDevTimeoutProducer)) {
+              ok = false;
+              break;
+            }
+            const int nsub = p.num_kb - kb >= kPairKsub ? kPairKsub : p.num_kb - kb;
+            if (leader) mbar_arrive_expect_tx(&full[stage], 2 * nsub * (A_SUB + B_SUB));
+            const uint32_t fb = pair_leader_addr(&full[stage]);
+            for (int su = 0; su < nsub; ++su) {
+              tma2_load_2d(sA + stage * A_BYTES + su * A_SUB, &tmA0, fb, (kb + su) * kGemmBK, m0);
+              tma2_load_2d(sB + stage * B_BYTES + su * B_SUB, &tmB, fb, (kb + su) * kGemmBK, nb);
+            }
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1;
+            }
+          }
+          continue;
+        }
         int img = 0, oh0 = 0, ow0 = 0;
         if (p.amode == 1) {
           const int hw = p.oH * p.oW;
