@@ -94,6 +94,10 @@ _SIGS = {
     "dlm_unet_forward": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_float, c_void_p,
                                  c_void_p, c_void_p, c_void_p, c_void_p]),
     "dlm_unet_set_graph": (c_int, [c_void_p, c_int]),
+    "dlm_unet_apply_loras": (c_int, [c_void_p, c_void_p, c_int, c_void_p]),
+    "dlm_unet_apply_lora": (c_int, [c_void_p, c_char_p, c_void_p, c_void_p, c_int, c_int, c_int,
+                                    c_float, c_void_p]),
+    "dlm_unet_clear_loras": (c_int, [c_void_p, c_void_p]),
     "dlm_unet_weight_count": (c_int, [ctypes.POINTER(c_int), c_int]),
     "dlm_unet_weight_info": (c_int, [ctypes.POINTER(c_int), c_int, c_int, ctypes.c_char_p, c_int,
                                      ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(c_int)]),

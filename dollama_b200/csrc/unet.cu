@@ -213,6 +213,7 @@ static int64_t numel(const std::vector<int64_t>& s) {
 }
 
 UNetModel::~UNetModel() {
+  for (auto& pt : patches_) cudaFree(pt.saved);
   release_plan();
   if (wbuf_) cudaFree(wbuf_);
 }
@@ -1064,6 +1065,251 @@ int UNetModel::time_ops(cudaStream_t s, double* ms, double* flops, int* count) {
   return ops_.time(s, ms, flops, count);
 }
 
+// ================================================================== runtime LoRA
+//
+// The reference merges delta = scale * (B @ A) into its resident fp16 weight (one GEMM with fp32
+// accumulation and alpha = scale, then launch_add: W = h(W + h(delta)), src/infer/unet.cu:373-440)
+// and reverts by re-uploading the base bytes (unet.cu:442-458).  Here the resident copy is the
+// prepared one, and every preparation step is linear in W: conv repacking [o][i][tap] ->
+// [o][tap][i], the row offsets of the q|k|v, temb and cross k/v concatenations, the GEGLU row
+// interleave, the 1x1 shortcut columns after conv2's, and the LayerNorm fold W' = h(W gamma) with
+// u = sum_k W', v = sum_k beta W + bias.  So the delta is mapped through the same steps:
+// W += h(delta) (folded: W' += h(h(delta) gamma), v += sum_k beta h(delta), u re-summed).  The
+// revert restores saved copies of the touched prepared rows instead of re-deriving them.
+
+namespace {
+
+__device__ __forceinline__ int lora_row(const LoraTarget& t, int o) {
+  const int r = t.kind == 2 ? (o < t.half_rows ? 2 * o : 2 * (o - t.half_rows) + 1) : o;
+  return r + t.row_off;
+}
+
+__device__ __forceinline__ int lora_col(const LoraTarget& t, int j) {
+  if (t.kind == 1) {
+    const int i = j / t.kk, tap = j - i * t.kk;  // OIHW: j = i * KK + tap
+    return tap * t.cin_pad + i + t.col_off;
+  }
+  return j + t.col_off;
+}
+
+// delta (o, j) = h(scale * sum_r B[o, r] A[r, j]), fp32 accumulation in r order
+__device__ __forceinline__ float lora_delta(const __half* A, const __half* B, int rank, int in_flat, int o,
+                                            int j, float scale) {
+  float acc = 0.0f;
+  for (int r = 0; r < rank; ++r)
+    acc = fmaf(__half2float(B[static_cast<size_t>(o) * rank + r]),
+               __half2float(A[static_cast<size_t>(r) * in_flat + j]), acc);
+  return __half2float(__float2half_rn(scale * acc));
+}
+
+// W[row(o), col(j)] = h(W + delta) (folded: h(W' + h(delta gamma_j)))
+__global__ void lora_scatter_kernel(LoraTarget t, const __half* A, const __half* B, int rank, int in_flat,
+                                    int out, float scale) {
+  const size_t total = static_cast<size_t>(out) * in_flat;
+  for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int o = static_cast<int>(idx / in_flat), j = static_cast<int>(idx % in_flat);
+    float d = lora_delta(A, B, rank, in_flat, o, j, scale);
+    if (t.gamma) d = __half2float(__float2half_rn(d * __half2float(t.gamma[j])));
+    __half* dst = t.w + static_cast<size_t>(lora_row(t, o)) * t.ld + lora_col(t, j);
+    *dst = __float2half_rn(__half2float(*dst) + d);
+  }
+}
+
+// one warp per row o after the scatter: v[row] += sum_j beta[j] delta(o, j) and u[row] = sum_k W'[row, k]
+// of the updated row (double sums, as the fold at preparation)
+__global__ void lora_fold_rows_kernel(LoraTarget t, const __half* A, const __half* B, int rank, int in_flat,
+                                      int out, float scale) {
+  const int o = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (o >= out) return;
+  const int row = lora_row(t, o);
+  const __half* wr = t.w + static_cast<size_t>(row) * t.ld;
+  double sv = 0.0, su = 0.0;
+  for (int j = lane; j < in_flat; j += 32) {
+    sv += static_cast<double>(__half2float(t.beta[j])) *
+          static_cast<double>(lora_delta(A, B, rank, in_flat, o, j, scale));
+    su += static_cast<double>(__half2float(wr[j]));
+  }
+#pragma unroll
+  for (int k = 16; k > 0; k >>= 1) {
+    sv += __shfl_xor_sync(0xffffffffu, sv, k);
+    su += __shfl_xor_sync(0xffffffffu, su, k);
+  }
+  if (lane == 0) {
+    t.u[row] = static_cast<float>(su);
+    t.v[row] = static_cast<float>(static_cast<double>(t.v[row]) + sv);
+  }
+}
+
+}  // namespace
+
+int UNetModel::lora_target(const std::string& key, LoraTarget* t, int* out, int* in_flat) const {
+  const auto specs = unet_weight_specs(cfg_);
+  const WeightSpec* sp = nullptr;
+  for (const auto& x : specs)
+    if (x.name == key) sp = &x;
+  DLM_REQUIRE(sp != nullptr && sp->shape.size() >= 2, DLM_ERR_NOT_FOUND,
+              "unet lora: %s is not a weight matrix of this UNet", key.c_str());
+  *out = static_cast<int>(sp->shape[0]);
+  int64_t flat = 1;
+  for (size_t d = 1; d < sp->shape.size(); ++d) flat *= sp->shape[d];
+  *in_flat = static_cast<int>(flat);
+  const int o = *out, inf = *in_flat;
+  auto get = [&](const std::string& n) -> __half* {
+    auto it = w_.find(n);
+    return it == w_.end() ? nullptr : it->second;
+  };
+  auto getf = [&](const std::string& n) -> float* {
+    auto it = wf_.find(n);
+    return it == wf_.end() ? nullptr : it->second;
+  };
+  *t = LoraTarget{};
+  auto conv = [&](__half* w, int ld, int cin, int cin_pad) {
+    t->w = w;
+    t->ld = ld;
+    t->kind = 1;
+    t->kk = 9;
+    t->cin = cin;
+    t->cin_pad = cin_pad;
+  };
+  bool done = false;
+  if (key == "conv_in.weight") {
+    conv(get("conv_in.packed"), 9 * 64, 4, 64);
+    done = true;
+  } else if (key == "conv_out.weight") {
+    conv(get("conv_out.packed"), 9 * kC[0], kC[0], kC[0]);
+    done = true;
+  } else if (key.find("samplers.0.conv.weight") != std::string::npos) {
+    conv(get(key.substr(0, key.size() - 7) + ".packed"), 9 * o, o, o);
+    done = true;
+  }
+  for (size_t r = 0; !done && r < resnets_.size(); ++r) {
+    const ResnetInfo& rs = resnets_[r];
+    if (key.compare(0, rs.prefix.size(), rs.prefix) != 0) continue;
+    const std::string rest = key.substr(rs.prefix.size());
+    const int k2 = 9 * rs.cout + (rs.cin != rs.cout ? rs.cin : 0);
+    if (rest == "conv1.weight") {
+      conv(get(rs.prefix + "conv1.packed"), 9 * rs.cin, rs.cin, rs.cin);
+    } else if (rest == "conv2.weight") {
+      conv(get(rs.prefix + "conv2.packed"), k2, rs.cout, rs.cout);
+    } else if (rest == "conv_shortcut.weight") {
+      t->w = get(rs.prefix + "conv2.packed");
+      t->ld = k2;
+      t->col_off = 9 * rs.cout;
+    } else if (rest == "time_emb_proj.weight") {
+      t->w = get("temb_proj.weight");
+      t->ld = kTembDim;
+      t->row_off = rs.temb_off;
+    }
+    done = true;
+  }
+  const size_t tb = key.find("transformer_blocks.");
+  if (!done && tb != std::string::npos) {
+    const size_t dot = key.find('.', tb + 19);
+    const std::string b = key.substr(0, dot + 1);
+    const std::string rest = key.substr(dot + 1);
+    auto fold = [&](const std::string& wname, const std::string& norm) {
+      t->gamma = get(b + norm + ".weight");
+      t->beta = get(b + norm + ".bias");
+      t->u = getf(b + wname + ".u");
+      t->v = getf(b + wname + ".v");
+    };
+    if (rest == "attn1.to_q.weight" || rest == "attn1.to_k.weight" || rest == "attn1.to_v.weight") {
+      t->w = get(b + "attn1.qkv");
+      t->ld = inf;
+      t->row_off = (rest == "attn1.to_q.weight" ? 0 : rest == "attn1.to_k.weight" ? 1 : 2) * o;
+      fold("attn1.qkv", "norm1");
+    } else if (rest == "attn2.to_q.weight") {
+      t->w = get(key);
+      t->ld = inf;
+      fold("attn2.to_q.weight", "norm2");
+    } else if (rest == "attn2.to_k.weight" || rest == "attn2.to_v.weight") {
+      auto it = kv_off_.find(b);
+      DLM_REQUIRE(it != kv_off_.end(), DLM_ERR_NOT_FOUND, "unet lora: no cross k/v for %s", b.c_str());
+      t->w = kv_all_w_;
+      t->ld = kCtxDim;
+      t->row_off = it->second + (rest == "attn2.to_v.weight" ? o : 0);
+    } else if (rest == "ff.net.0.proj.weight") {
+      t->w = get(b + "ff.geglu.weight");
+      t->ld = inf;
+      t->kind = 2;
+      t->half_rows = o / 2;
+      fold("ff.geglu.weight", "norm3");
+    } else {
+      t->w = get(key);  // attn1.to_out.0 / attn2.to_out.0 / ff.net.2: copied as they are
+      t->ld = inf;
+    }
+    done = true;
+  }
+  if (!done) {
+    t->w = get(key);  // time / add embedding MLPs, proj_in / proj_out
+    t->ld = inf;
+  }
+  DLM_REQUIRE(t->w != nullptr && (t->gamma == nullptr || (t->beta && t->u && t->v)), DLM_ERR_UNSUPPORTED,
+              "unet lora: no prepared tensor for %s", key.c_str());
+  return DLM_OK;
+}
+
+int UNetModel::apply_lora(const std::string& key, const __half* A, const __half* B, int rank, int in_flat,
+                          int out, float scale, cudaStream_t s) {
+  DLM_REQUIRE(A && B && rank > 0, DLM_ERR_INVALID, "unet lora: bad A / B / rank for %s", key.c_str());
+  LoraTarget t;
+  int o = 0, inf = 0;
+  int rc = lora_target(key, &t, &o, &inf);
+  if (rc != DLM_OK) return rc;
+  DLM_REQUIRE(o == out && inf == in_flat, DLM_ERR_INVALID,
+              "unet lora: %s is [%d, %d], the delta is [%d, %d]", key.c_str(), o, inf, out, in_flat);
+  // save the touched prepared rows (the GEGLU interleave keeps the out rows contiguous too)
+  LoraPatch pt{};
+  pt.w = t.w + static_cast<size_t>(t.row_off) * t.ld;
+  pt.rows = out;
+  pt.elems = static_cast<size_t>(out) * t.ld;
+  pt.u = t.u ? t.u + t.row_off : nullptr;
+  pt.v = t.v ? t.v + t.row_off : nullptr;
+  const size_t wbytes = pt.elems * sizeof(__half);
+  DLM_CHECK_CUDA(cudaMalloc(&pt.saved, wbytes + 2 * sizeof(float) * out));
+  uint8_t* sv = static_cast<uint8_t*>(pt.saved);
+  cudaError_t e = cudaMemcpyAsync(sv, pt.w, wbytes, cudaMemcpyDeviceToDevice, s);
+  if (e == cudaSuccess && pt.u)
+    e = cudaMemcpyAsync(sv + wbytes, pt.u, sizeof(float) * out, cudaMemcpyDeviceToDevice, s);
+  if (e == cudaSuccess && pt.v)
+    e = cudaMemcpyAsync(sv + wbytes + sizeof(float) * out, pt.v, sizeof(float) * out, cudaMemcpyDeviceToDevice,
+                        s);
+  if (e != cudaSuccess) {
+    cudaFree(pt.saved);
+    DLM_CHECK_CUDA(e);
+  }
+  patches_.push_back(pt);  // tracked before the weights change, so a failed merge is still reverted
+  const size_t total = static_cast<size_t>(out) * in_flat;
+  const int blocks = static_cast<int>(std::min<size_t>((total + 255) / 256, 148 * 64));
+  lora_scatter_kernel<<<blocks, 256, 0, s>>>(t, A, B, rank, in_flat, out, scale);
+  DLM_CHECK_CUDA(cudaGetLastError());
+  if (t.gamma) {
+    lora_fold_rows_kernel<<<(out * 32 + 255) / 256, 256, 0, s>>>(t, A, B, rank, in_flat, out, scale);
+    DLM_CHECK_CUDA(cudaGetLastError());
+  }
+  return DLM_OK;
+}
+
+int UNetModel::clear_loras(cudaStream_t s) {
+  while (!patches_.empty()) {
+    LoraPatch& pt = patches_.back();
+    const size_t wbytes = pt.elems * sizeof(__half);
+    const uint8_t* sv = static_cast<const uint8_t*>(pt.saved);
+    DLM_CHECK_CUDA(cudaMemcpyAsync(pt.w, sv, wbytes, cudaMemcpyDeviceToDevice, s));
+    if (pt.u)
+      DLM_CHECK_CUDA(cudaMemcpyAsync(pt.u, sv + wbytes, sizeof(float) * pt.rows, cudaMemcpyDeviceToDevice, s));
+    if (pt.v)
+      DLM_CHECK_CUDA(cudaMemcpyAsync(pt.v, sv + wbytes + sizeof(float) * pt.rows, sizeof(float) * pt.rows,
+                                     cudaMemcpyDeviceToDevice, s));
+    DLM_CHECK_CUDA(cudaStreamSynchronize(s));  // the saved block is read before it is freed
+    cudaFree(pt.saved);
+    patches_.pop_back();
+  }
+  return DLM_OK;
+}
+
 int UNetModel::stage(const std::string& name, const __half** ptr, int* C, int* H, int* Wd) const {
   auto it = stages_.find(name);
   DLM_REQUIRE(it != stages_.end(), DLM_ERR_NOT_FOUND, "unet: no stage %s", name.c_str());
@@ -1105,6 +1351,44 @@ int dlm_unet_create(const int* depths, int mid_depth, int n, const char* const* 
 
 int dlm_unet_destroy(void* handle) {
   delete static_cast<dlm::UNetModel*>(handle);
+  return DLM_OK;
+}
+
+int dlm_unet_apply_lora(void* handle, const char* base_key, const void* A, const void* B, int rank,
+                        int in_flat, int out_dim, float scale, void* stream) {
+  DLM_REQUIRE(handle != nullptr && base_key != nullptr, DLM_ERR_INVALID, "unet_apply_lora: null argument");
+  return static_cast<dlm::UNetModel*>(handle)->apply_lora(
+      base_key, static_cast<const __half*>(A), static_cast<const __half*>(B), rank, in_flat, out_dim, scale,
+      static_cast<cudaStream_t>(stream));
+}
+
+int dlm_unet_clear_loras(void* handle, void* stream) {
+  DLM_REQUIRE(handle != nullptr, DLM_ERR_INVALID, "unet_clear_loras: null handle");
+  return static_cast<dlm::UNetModel*>(handle)->clear_loras(static_cast<cudaStream_t>(stream));
+}
+
+int dlm_unet_apply_loras(void* handle, const dlm_lora_module* mods, int n, void* stream) {
+  DLM_REQUIRE(handle != nullptr && (n == 0 || mods != nullptr), DLM_ERR_INVALID, "unet_apply_loras: null argument");
+  auto* m = static_cast<dlm::UNetModel*>(handle);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  for (int i = 0; i < n; ++i) {
+    const dlm_lora_module& md = mods[i];
+    DLM_REQUIRE(md.base_key && md.a_fp16 && md.b_fp16 && md.rank > 0 && md.in_flat > 0 && md.out_dim > 0,
+                DLM_ERR_INVALID, "unet_apply_loras: module %d is incomplete", i);
+    const size_t na = static_cast<size_t>(md.rank) * md.in_flat, nb = static_cast<size_t>(md.out_dim) * md.rank;
+    void* d = nullptr;
+    DLM_CHECK_CUDA(cudaMallocAsync(&d, 2 * (na + nb), s));
+    __half* da = static_cast<__half*>(d);
+    __half* db = da + na;
+    cudaError_t e = cudaMemcpyAsync(da, md.a_fp16, 2 * na, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(db, md.b_fp16, 2 * nb, cudaMemcpyHostToDevice, s);
+    int rc = e == cudaSuccess ? m->apply_lora(md.base_key, da, db, md.rank, md.in_flat, md.out_dim, md.scale, s)
+                              : DLM_ERR_CUDA;
+    if (e != cudaSuccess) dlm::set_error("unet_apply_loras: %s", cudaGetErrorString(e));
+    cudaFreeAsync(d, s);
+    if (rc != DLM_OK) return rc;
+  }
+  DLM_CHECK_CUDA(cudaStreamSynchronize(s));
   return DLM_OK;
 }
 

@@ -27,6 +27,22 @@ struct ResnetInfo {
   int temb_off;  // column offset of this resnet in the concatenated time-embedding projection
 };
 
+// Where a diffusers weight [out, in_flat] lives in the prepared weights (runtime LoRA / restore).
+struct LoraTarget {
+  __half* w = nullptr;  // prepared matrix
+  int ld = 0;           // its row stride (elements)
+  int row_off = 0, col_off = 0;
+  int kind = 0;         // 0 rows / columns as given, 1 conv [o][i][tap] -> [o][tap][i], 2 GEGLU rows
+  int kk = 1, cin = 0, cin_pad = 0;
+  int half_rows = 0;    // GEGLU: rows per half (row r < half -> 2r, else 2(r - half) + 1)
+  // LayerNorm fold (gamma != nullptr): the folded matrix has in_flat columns
+  const __half* gamma = nullptr;
+  const __half* beta = nullptr;
+  const __half* bias = nullptr;  // bias term of v per prepared row
+  float* u = nullptr;
+  float* v = nullptr;
+};
+
 class UNetModel {
  public:
   ~UNetModel();
@@ -44,6 +60,14 @@ class UNetModel {
     use_graph_ = on;
   }
   int stage(const std::string& name, const __half** ptr, int* C, int* H, int* W) const;
+  // Runtime LoRA: W += scale * (B A) merged into the prepared (packed / folded) copy of the
+  // diffusers weight `key` (A [rank, in_flat], B [out, rank], fp16 device).  The prepared rows it
+  // touches are saved first; clear_loras writes every saved block back, newest first, so the
+  // weights return bit for bit to their state before the first apply.
+  int apply_lora(const std::string& key, const __half* A, const __half* B, int rank, int in_flat,
+                 int out, float scale, cudaStream_t s);
+  int clear_loras(cudaStream_t s);
+  int num_lora_patches() const { return static_cast<int>(patches_.size()); }
   size_t arena_bytes() const { return arena_bytes_; }
   size_t weight_bytes() const { return woff_; }
   int num_launches() const { return ops_.num_launches(); }
@@ -55,6 +79,16 @@ class UNetModel {
   };
 
   int prepare_weights(cudaStream_t s);
+  int lora_target(const std::string& key, struct LoraTarget* t, int* out, int* in_flat) const;
+  // one saved block of prepared rows (and their LayerNorm-fold sums) per apply_lora
+  struct LoraPatch {
+    __half* w;       // first saved row of the prepared matrix
+    size_t elems;    // rows * ld
+    float* u;        // fold sums of those rows (nullptr when unfolded)
+    float* v;
+    int rows;
+    void* saved;     // device copy: elems halves, then 2 * rows floats
+  };
   const __half* src(const std::string& n) const;
   const __half* W(const std::string& n) const;
   const float* WF(const std::string& n) const;
@@ -90,6 +124,7 @@ class UNetModel {
   __half* kv_all_w_ = nullptr;                          // [kv_total_, 2048] all cross k/v weights
   int kv_total_ = 0, kv_cursor_ = 0;
   std::unordered_map<std::string, int> kv_off_;         // block prefix -> row offset in kv_all_w_
+  std::vector<LoraPatch> patches_;                      // applied LoRAs, oldest first
   int temb_total_ = 0;
   // plan
   int B_ = 0, H_ = 0, W_ = 0;

@@ -106,6 +106,25 @@ class SDXLUNet:
         torch.cuda.synchronize()
         return out.view(B, H.value, W.value, C.value).permute(0, 3, 1, 2)
 
+    def apply_loras(self, modules, stream=None) -> None:
+        """Merge LoRA modules (`dollama_b200.lora.LoraModule`, host fp16 A / B) into the resident
+        weights: W += h(scale * B @ A) per module, in order (the reference's unet_apply_loras)."""
+        from .lora import pack_modules
+        arr, keep = pack_modules(modules)
+        L.call("dlm_unet_apply_loras", self._h, arr, len(modules), _stream_ptr(stream))
+        del keep
+
+    def apply_lora(self, base_key: str, A, B, scale: float = 1.0, stream=None) -> None:
+        """One module from fp16 CUDA tensors A [rank, in_flat] and B [out, rank]."""
+        A, B = A.contiguous(), B.contiguous()
+        L.call("dlm_unet_apply_lora", self._h, base_key.encode(), ctypes.c_void_p(A.data_ptr()),
+               ctypes.c_void_p(B.data_ptr()), A.shape[0], A.shape[1], B.shape[0], float(scale),
+               _stream_ptr(stream))
+
+    def clear_loras(self, stream=None) -> None:
+        """Revert every applied LoRA, bit-exact (the reference's unet_clear_loras)."""
+        L.call("dlm_unet_clear_loras", self._h, _stream_ptr(stream))
+
     def info(self):
         a, w, n = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int()
         L.call("dlm_unet_info", self._h, ctypes.byref(a), ctypes.byref(w), ctypes.byref(n))

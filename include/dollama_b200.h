@@ -328,6 +328,33 @@ int dlm_unet_weight_info(const int* depths, int mid_depth, int index, char* name
 /* Enables (default) or disables CUDA-graph replay of the step. */
 int dlm_unet_set_graph(void* handle, int enable);
 
+/* Runtime LoRA (reference unet_apply_loras / unet_clear_loras, src/infer/unet.cuh:96-111,
+ * unet.cu:373-458; LoraModule, src/infer/lora.hpp:136-145).  One module merges
+ * W += h(scale * (B @ A)) into the resident weight named by its diffusers key (fp32
+ * accumulation over the rank, one fp16 rounding of the delta, one of the sum; the handle keeps
+ * its weights repacked, q|k|v-concatenated and LayerNorm-folded, and the delta is mapped into
+ * that layout).  The forward path and its captured graph are unchanged: only weight bytes move.
+ *   a_fp16 [rank, in_flat], b_fp16 [out_dim, rank]: HOST fp16 bits (as LoraModule holds them);
+ *   in_flat = the product of the weight's dims after the first (conv: Cin * 3 * 3).
+ * Keys must name a 2-D / 4-D weight of this UNet with matching [out_dim, in_flat], else
+ * DLM_ERR_NOT_FOUND / DLM_ERR_INVALID (the reference throws).  Modules apply in order and
+ * stack.  dlm_unet_clear_loras returns every patched weight to its bytes before the first
+ * apply (bit-exact; the reference re-uploads the base bytes) and frees the saved copies.
+ * dlm_unet_apply_lora is the same merge for one module whose A / B are DEVICE fp16 tensors. */
+typedef struct dlm_lora_module {
+  const char* base_key;
+  const uint16_t* a_fp16;
+  const uint16_t* b_fp16;
+  int rank;
+  int in_flat;
+  int out_dim;
+  float scale;
+} dlm_lora_module;
+int dlm_unet_apply_loras(void* handle, const dlm_lora_module* mods, int n, void* stream);
+int dlm_unet_apply_lora(void* handle, const char* base_key, const void* A, const void* B, int rank,
+                        int in_flat, int out_dim, float scale, void* stream);
+int dlm_unet_clear_loras(void* handle, void* stream);
+
 /* Test hook (the reference's unet_set_stage_hook, unet.cuh:53-54): device pointer and NHWC
  * geometry of a stage output of the last forward ("temb_final", "conv_in_out",
  * "down_block_{0,1,2}_out", "mid_block_out", "up_block_{0,1,2}_out"). */
