@@ -3,58 +3,12 @@
 #include <cstring>
 
 #include "gemm.h"
+#include "gemm_launch.cuh"
 #include "ops.h"
 
 namespace dlm {
 
 namespace {
-
-template <int BN>
-int launch_bn(const GemmOp& op, cudaStream_t s) {
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    DLM_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        gemm_smem_bytes(BN)));
-    attr_set[dev] = true;
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(op.grid, 1, 1);
-  cfg.blockDim = dim3(kGemmThreads, 1, 1);
-  cfg.dynamicSmemBytes = gemm_smem_bytes(BN);
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
-  DLM_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN>, op.tmA[0], op.tmA[1], op.tmA[2],
-                                    op.tmB, op.tmC, op.p));
-  return DLM_OK;
-}
-
-template <int BN>
-int launch_bn2(const GemmOp& op, cudaStream_t s) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(op.grid, 1, 1);
-  cfg.blockDim = dim3(kGemmThreads, 1, 1);
-  cfg.dynamicSmemBytes = gemm2_smem_bytes(BN);
-  cfg.stream = s;
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 2 : 1;
-  DLM_CHECK_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc2_kernel<BN>, op.tmA[0], op.tmA[1], op.tmA[2],
-                                    op.tmB, op.tmC, op.p));
-  return DLM_OK;
-}
 
 // Tile choice, calibrated on B200 sweeps of the UNet shapes (single CTA vs CTA pair, every N
 // tile).  The single-CTA kernel is bound by how fast TMA can pull operands from L2 into one SM
@@ -68,7 +22,7 @@ double tile_cost(int bn) {
   return (mma > smem ? mma : smem) + 24.0;
 }
 
-// Largest number of CTA pairs of gemm_tc2_kernel<BN> co-resident on the current device (clusters
+// Largest number of CTA pairs of gemm_tc2_kernel<BN, *> co-resident on the current device (clusters
 // are placed within a GPC, so an SM without a free partner in its GPC cannot host a pair).
 template <int BN>
 int max_pairs_bn() {
@@ -83,10 +37,10 @@ int max_pairs_bn() {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaFuncSetAttribute(gemm_tc2_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  cudaFuncSetAttribute(gemm_tc2_kernel<BN, kEpiDyn>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        gemm2_smem_bytes(BN));
   int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, gemm_tc2_kernel<BN>, &cfg) != cudaSuccess || n <= 0) {
+  if (cudaOccupancyMaxActiveClusters(&n, gemm_tc2_kernel<BN, kEpiDyn>, &cfg) != cudaSuccess || n <= 0) {
     cudaGetLastError();
     n = num_sms() / 2;
   }
@@ -430,48 +384,36 @@ int gemm_plan_conv(GemmOp* op, int Nb, int oH, int oW, const ConvSource* srcs, i
 int gemm_prepare_kernels() {
   // Sets the dynamic shared-memory limit of every tile variant up front, so that no attribute
   // call happens inside a CUDA-graph capture.
-  GemmOp dummy;
-  std::memset(&dummy, 0, sizeof(dummy));
-  (void)dummy;
-  DLM_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm_smem_bytes(256)));
-  DLM_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<192>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm_smem_bytes(192)));
-  DLM_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<160>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm_smem_bytes(160)));
-  DLM_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm_smem_bytes(128)));
-  DLM_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm_smem_bytes(64)));
-  DLM_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm2_smem_bytes(256)));
-  DLM_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<192>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm2_smem_bytes(192)));
-  DLM_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<160>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm2_smem_bytes(160)));
-  DLM_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm2_smem_bytes(128)));
-  return DLM_OK;
+  int rc = gemm_prepare_fl<kEpiDyn>();
+#define DLM_GEMM_PREPARE(F) \
+  if (rc == DLM_OK) rc = gemm_prepare_fl<F>();
+  DLM_GEMM_SPECIAL_FLAGS(DLM_GEMM_PREPARE)
+#undef DLM_GEMM_PREPARE
+  return rc;
 }
 
 int gemm_launch(const GemmOp& op, cudaStream_t s) {
-  if (op.pair) {
-    static bool attr_set[64] = {false};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-      int rc = gemm_prepare_kernels();
-      if (rc != DLM_OK) return rc;
-      attr_set[dev] = true;
-    }
-    switch (op.bn) {
-      case 256: return launch_bn2<256>(op, s);
-      case 192: return launch_bn2<192>(op, s);
-      case 160: return launch_bn2<160>(op, s);
-      case 128: return launch_bn2<128>(op, s);
-      default: set_error("gemm: op not planned"); return DLM_ERR_INVALID;
-    }
+  static bool prepared[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !prepared[dev]) {
+    const int rc = gemm_prepare_kernels();
+    if (rc != DLM_OK) return rc;
+    prepared[dev] = true;
   }
-  switch (op.bn) {
-    case 256: return launch_bn<256>(op, s);
-    case 192: return launch_bn<192>(op, s);
-    case 160: return launch_bn<160>(op, s);
-    case 128: return launch_bn<128>(op, s);
-    case 64: return launch_bn<64>(op, s);
-    default: set_error("gemm: op not planned"); return DLM_ERR_INVALID;
+  switch (op.p.flags) {
+#define DLM_GEMM_CASE(F) \
+  case F:                \
+    return gemm_launch_fl<F>(op, s);
+    DLM_GEMM_SPECIAL_FLAGS(DLM_GEMM_CASE)
+#undef DLM_GEMM_CASE
+    default:
+      return gemm_launch_fl<kEpiDyn>(op, s);
   }
 }
+
+template int gemm_launch_fl<kEpiDyn>(const GemmOp&, cudaStream_t);
+template int gemm_prepare_fl<kEpiDyn>();
 
 }  // namespace dlm
 

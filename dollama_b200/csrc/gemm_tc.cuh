@@ -83,6 +83,13 @@ constexpr unsigned kEpiRowStats = 1u << 8;
 constexpr unsigned kEpiLnFold = 1u << 9;
 constexpr unsigned kEpiOutF32 = 1u << 10;    // output stored as fp32 (p.out points to float)
 constexpr unsigned kEpiResidF32 = 1u << 11;  // residual read as fp32 (p.resid points to float)
+// Kernel template argument FL: the epilogue flags fixed at compile time, so that an instantiation
+// holds only its own epilogue path (the generic path's size costs instruction-cache misses on
+// every chunk); kEpiDyn reads p.flags at run time instead.
+constexpr unsigned kEpiDyn = 0xFFFFFFFFu;
+__host__ __device__ constexpr unsigned epi_flags(unsigned FL, unsigned runtime) {
+  return FL == kEpiDyn ? runtime : FL;
+}
 
 // Contiguous k-block iteration range [a, b) of CTA `cta` under stream-K.
 __device__ __forceinline__ void sk_range(const GemmParams& p, int cta, long long& a, long long& b) {
@@ -214,13 +221,14 @@ struct EpiPre {
 // LayerNorm-fold vectors u, v (128 bytes each at the start of the buffer) of the warp's first two
 // chunks are copied with cp.async into its two staging buffers, which the chunks' outputs reuse
 // after reading them.  (Prefetching the bias lines into L1 measured slower.)
-template <int BN>
+template <int BN, unsigned FL>
 __device__ __forceinline__ EpiPre epilogue_prefetch(const GemmParams& p, int row, int n0, int m_base,
                                                     int half, uint8_t* stage) {
+  const unsigned fl = epi_flags(FL, p.flags);
   EpiPre pre;
   const int lane = threadIdx.x & 31;
-  const bool geglu = (p.flags & DLM_EPI_GEGLU) != 0;
-  const bool lnf = (p.flags & kEpiLnFold) != 0;
+  const bool geglu = (fl & DLM_EPI_GEGLU) != 0;
+  const bool lnf = (fl & kEpiLnFold) != 0;
   if (lnf) {
     if (row < p.M) {
       float cnt = 0.0f, mean = 0.0f, m2 = 0.0f;
@@ -241,8 +249,8 @@ __device__ __forceinline__ EpiPre epilogue_prefetch(const GemmParams& p, int row
     }
     pre.ln_ready = true;
   }
-  const bool resid16 = (p.flags & DLM_EPI_RESID) && !(p.flags & kEpiResidF32) && !geglu &&
-                       !(p.flags & kEpiOutF32);
+  const bool resid16 = (fl & DLM_EPI_RESID) && !(fl & kEpiResidF32) && !geglu &&
+                       !(fl & kEpiOutF32);
   if ((!resid16 && !lnf) || ((p.N - n0) & 31) != 0) return pre;
   // the bulk stores of the previous tile must have finished reading the staging buffers
   if (lane == 0) bulk_wait_read_le0();
@@ -271,22 +279,23 @@ __device__ __forceinline__ EpiPre epilogue_prefetch(const GemmParams& p, int row
   return pre;
 }
 
-template <int BN>
+template <int BN, unsigned FL>
 __device__ __forceinline__ bool epilogue_tile(const GemmParams& p, uint32_t t_row, int row, int n0,
                                               int m_base, uint8_t* stage, const CUtensorMap* tmC,
                                               int& sbuf, int half, float2* xchg, uint64_t* xbar,
                                               uint32_t& xphase, volatile int* abort_flag,
                                               const EpiPre& pre, int sk_c0 = 0, int sk_c1 = 0,
                                               int r_in_tile = 0) {
+  const unsigned fl = epi_flags(FL, p.flags);
   const int lane = threadIdx.x & 31;
   // with inputs prefetched, chunk j (j < 2) of this tile uses staging buffer j
   const bool staged = pre.res || pre.uv;
   if (staged) sbuf = 0;
   int cj = 0;  // chunk index within this warp's chunks
   const bool row_ok = row < p.M;
-  const bool geglu = (p.flags & DLM_EPI_GEGLU) != 0;
+  const bool geglu = (fl & DLM_EPI_GEGLU) != 0;
   float ln_mean = pre.ln_mean, ln_rstd = pre.ln_rstd;
-  if ((p.flags & kEpiLnFold) && row_ok && !pre.ln_ready) {
+  if ((fl & kEpiLnFold) && row_ok && !pre.ln_ready) {
     float cnt = 0.0f, mean = 0.0f, m2 = 0.0f;
     const float2* st = p.stats_in + static_cast<size_t>(row) * p.stats_in_parts;
     for (int i = 0; i < p.stats_in_parts; ++i) {
@@ -337,7 +346,7 @@ __device__ __forceinline__ bool epilogue_tile(const GemmParams& p, uint32_t t_ro
       cp_async_wait_all();
       __syncwarp();
     }
-    if (p.flags & kEpiLnFold) {
+    if (fl & kEpiLnFold) {
       // v = rstd * (v - mean * u) + w, two columns per packed f32x2 FMA (same roundings)
       const float4* su = reinterpret_cast<const float4*>(stage + cj * 2048);
       const uint64_t nm2 = f2_pack(-ln_mean, -ln_mean), r2 = f2_pack(ln_rstd, ln_rstd);
@@ -353,7 +362,7 @@ __device__ __forceinline__ bool epilogue_tile(const GemmParams& p, uint32_t t_ro
         f2_unpack(a1, v[j + 2], v[j + 3]);
       }
     }
-    if (p.flags & DLM_EPI_BIAS) {
+    if (fl & DLM_EPI_BIAS) {
 #pragma unroll
       for (int j = 0; j < 32; j += 8) {
         float b[8];
@@ -365,7 +374,7 @@ __device__ __forceinline__ bool epilogue_tile(const GemmParams& p, uint32_t t_ro
         }
       }
     }
-    if (p.flags & DLM_EPI_BIAS2D) {
+    if (fl & DLM_EPI_BIAS2D) {
       const __half* b2 = p.bias2d + static_cast<size_t>(img) * p.ldb2 + n;
 #pragma unroll
       for (int j = 0; j < 32; j += 8) {
@@ -378,7 +387,7 @@ __device__ __forceinline__ bool epilogue_tile(const GemmParams& p, uint32_t t_ro
         }
       }
     }
-    if (p.flags & DLM_EPI_SILU) {
+    if (fl & DLM_EPI_SILU) {
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = silu_f(v[j]);
     }
@@ -405,7 +414,7 @@ __device__ __forceinline__ bool epilogue_tile(const GemmParams& p, uint32_t t_ro
       *reinterpret_cast<uint4*>(rb + ((1 ^ sw) * 16)) = make_uint4(o[4], o[5], o[6], o[7]);
     } else {
       // 64-byte rows, 64-byte swizzle: 16-byte chunk q of row r at q ^ ((r >> 1) & 3)
-      if ((p.flags & DLM_EPI_RESID) && (p.flags & kEpiResidF32)) {
+      if ((fl & DLM_EPI_RESID) && (fl & kEpiResidF32)) {
         if (row_ok) {
           const float* rs = reinterpret_cast<const float*>(p.resid) + static_cast<size_t>(row) * p.ldr + n;
 #pragma unroll
@@ -417,7 +426,7 @@ __device__ __forceinline__ bool epilogue_tile(const GemmParams& p, uint32_t t_ro
             v[j + 3] += p.resid_scale * t.w;
           }
         }
-      } else if (p.flags & DLM_EPI_RESID) {
+      } else if (fl & DLM_EPI_RESID) {
         if (!(pre.res && cj < 2)) {
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
@@ -444,7 +453,7 @@ __device__ __forceinline__ bool epilogue_tile(const GemmParams& p, uint32_t t_ro
         }
         __syncwarp();
       }
-      if (p.flags & kEpiOutF32) {
+      if (fl & kEpiOutF32) {
         // fp32 output: two halves of 16 columns, each 32 rows x 64 bytes through one staging
         // buffer and one bulk store (the second half uses the other buffer)
 #pragma unroll
@@ -480,7 +489,7 @@ __device__ __forceinline__ bool epilogue_tile(const GemmParams& p, uint32_t t_ro
       for (int q = 0; q < 4; ++q)
         *reinterpret_cast<uint4*>(rb + ((q ^ sw) * 16)) =
             make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
-      if ((p.flags & kEpiRowStats) && row_ok) {
+      if ((fl & kEpiRowStats) && row_ok) {
         // statistics of the values as stored (fp16), chunk by chunk, merged with Chan's formula
         float f[32];
 #pragma unroll
@@ -524,7 +533,7 @@ __device__ __forceinline__ bool epilogue_tile(const GemmParams& p, uint32_t t_ro
     sbuf ^= 1;
     ++cj;
   }
-  if (p.flags & kEpiRowStats) {
+  if (fl & kEpiRowStats) {
     const uint32_t ph = xphase & 1;
     ++xphase;
     if (half == 1) {
@@ -574,7 +583,7 @@ __device__ __forceinline__ void epilogue_partial(const GemmParams& p, uint32_t t
   }
 }
 
-template <int BN>
+template <int BN, unsigned FL>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
                    const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB,
@@ -787,7 +796,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint8_t* stage_buf = sEpi + (warp - 2) * kStageBytesPerWarp;
       const EpiPre pre = (p.sk_ctas > 0 && sg.kb0 > 0)
                              ? EpiPre{}
-                             : epilogue_prefetch<BN>(p, row, n0, m0 + quad * 32, half, stage_buf);
+                             : epilogue_prefetch<BN, FL>(p, row, n0, m0 + quad * 32, half, stage_buf);
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status, kDevTimeoutEpilogue)) break;
       tc_fence_after();
       const uint32_t t_row = tbase + (static_cast<uint32_t>(quad * 32) << 16) +
@@ -817,7 +826,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             ok = flag_wait_acquire(p.sk_flags + cc, 1, abort_flag, p.status, kDevTimeoutStreamK);
         }
         if (ok) {
-          ok = epilogue_tile<BN>(p, t_row, row, n0, m0 + quad * 32, stage_buf, &tmC, sbuf, half,
+          ok = epilogue_tile<BN, FL>(p, t_row, row, n0, m0 + quad * 32, stage_buf, &tmC, sbuf, half,
                                  sXchg + quad * 32, xbar + 2 * quad, xphase, abort_flag, pre,
                                  c0, c1, r_in_tile);
           if (ok && c1 > c0) {
@@ -876,7 +885,7 @@ __host__ __device__ constexpr int gemm2_smem_bytes(int BN) {
   return gemm2_stages(BN) * gemm2_stage_bytes(BN) + kGemmFixedSmem;
 }
 
-template <int BN>
+template <int BN, unsigned FL>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
                     const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB,
@@ -1108,12 +1117,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int n0 = (t % p.n_tiles) * BN;
       const int row = m0 + quad * 32 + lane;
       uint8_t* stage_buf = sEpi + (warp - 2) * kStageBytesPerWarp;
-      const EpiPre pre = epilogue_prefetch<BN>(p, row, n0, m0 + quad * 32, half, stage_buf);
+      const EpiPre pre = epilogue_prefetch<BN, FL>(p, row, n0, m0 + quad * 32, half, stage_buf);
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status, kDevTimeoutEpilogue)) break;
       tc_fence_after();
       const uint32_t t_row = tbase + (static_cast<uint32_t>(quad * 32) << 16) +
                              static_cast<uint32_t>(acc * BN);
-      if (!epilogue_tile<BN>(p, t_row, row, n0, m0 + quad * 32, stage_buf, &tmC, sbuf, half,
+      if (!epilogue_tile<BN, FL>(p, t_row, row, n0, m0 + quad * 32, stage_buf, &tmC, sbuf, half,
                              sXchg + quad * 32, xbar + 2 * quad, xphase, abort_flag, pre))
         break;
       tc_fence_before();
