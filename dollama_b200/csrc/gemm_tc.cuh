@@ -842,7 +842,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (lane == 0) mbar_arrive(&tempty[acc]);
       ++i;
     }
-    if (lane == 0) bulk_wait_all();
+    // the staging buffers must have been read before the CTA exits; the stores themselves
+    // complete with the grid (a dependent grid's griddepcontrol.wait covers them)
+    if (lane == 0) bulk_wait_read_le0();
   }
 
   __syncwarp();
@@ -1129,7 +1131,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(&tempty[acc], 0);
     }
-    if (lane == 0) bulk_wait_all();
+    // the staging buffers must have been read before the CTA exits; the stores themselves
+    // complete with the grid (a dependent grid's griddepcontrol.wait covers them)
+    if (lane == 0) bulk_wait_read_le0();
   }
 
   __syncwarp();
