@@ -308,7 +308,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const uint32_t ts = tbase + lane_off + t * kKV;
     const uint32_t to = tbase + lane_off + 256 + t * 128;
     const float c = p.scale_log2;
-    float acc[kD];
     bool ok = true;
     int jc = 0;
     uint32_t ep_phase = 0;
@@ -453,66 +452,59 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         l_run = fmaf(l_run, alpha, (sum0 + sum1) + (sum2 + sum3));
         m_run = m_new;
       }
-      if (ok && n > 0) {
-        // the segment's last P.V: read O out, then let the next segment's first P.V overwrite it
-        ok = wwait(&o_full[t], (jc + n - 1) & 1);
-        if (ok) {
-          tc_fence_after();
-          uint32_t r0[32], r1[32];
-          tmem_ld_32x32b_x32(to, r0);
-          tmem_ld_32x32b_x32(to + 32, r1);
-          tmem_ld_wait();
-#pragma unroll
-          for (int q = 0; q < 32; ++q) {
-            acc[q] = __uint_as_float(r0[q]);
-            acc[32 + q] = __uint_as_float(r1[q]);
-          }
-          tc_fence_before();
-          mbar_arrive(&o_empty[t]);
-        }
-      }
+      if (ok && n > 0) ok = wwait(&o_full[t], (jc + n - 1) & 1);  // the segment's last P.V
       jc += n;
       if (!ok) break;
+      if (n == 0) continue;
+      tc_fence_after();
       int b, h, q0;
       decode(sg.group, b, h, q0);
       const int qrow = q0 + t * kQT + row;
       __half* dst = p.out + static_cast<size_t>(b) * p.o_sb + static_cast<size_t>(h) * p.o_sh +
                     static_cast<size_t>(qrow) * p.o_ss;
-      if (!kSK || sg.whole) {
-        if (qrow < p.Sq) {
-          const float inv = 1.0f / l_run;
+      // a group cut between CTAs (stream-K): this piece goes to the workspace, normalised by its
+      // own row sum, and the last CTA to finish merges the pieces
+      const bool piece = kSK && !sg.whole;
+      const int r_in = t * kQT + row;
+      int first = 0, last = 0;
+      if (piece) {
+        const long long total = static_cast<long long>(groups) * n_tiles;
+        first = attn_cta_of(total, p.sk_ctas, static_cast<long long>(sg.group) * n_tiles);
+        last = attn_cta_of(total, p.sk_ctas, static_cast<long long>(sg.group + 1) * n_tiles - 1);
+      }
+      auto slot_of = [&](int cc) { return 2 * cc + (cc == first ? 1 : 0); };
+      const size_t my_slot = static_cast<size_t>(slot_of(static_cast<int>(blockIdx.x))) * kQ + r_in;
+      {
+        // O leaves TMEM 32 columns at a time (fp16, scaled by 1 / l), then the next segment's
+        // first P.V may overwrite it
+        const float inv = 1.0f / l_run;
+        uint4* po = reinterpret_cast<uint4*>(p.part_o + my_slot * kD);
 #pragma unroll
-          for (int d = 0; d < kD; d += 8) {
-            uint4 v;
-            v.x = pack_half2(acc[d] * inv, acc[d + 1] * inv);
-            v.y = pack_half2(acc[d + 2] * inv, acc[d + 3] * inv);
-            v.z = pack_half2(acc[d + 4] * inv, acc[d + 5] * inv);
-            v.w = pack_half2(acc[d + 6] * inv, acc[d + 7] * inv);
-            *reinterpret_cast<uint4*>(dst + d) = v;
+        for (int hf = 0; hf < 2; ++hf) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(to + hf * 32, r);
+          tmem_ld_wait();
+          uint4 v[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            v[j].x = pack_half2(__uint_as_float(r[8 * j]) * inv, __uint_as_float(r[8 * j + 1]) * inv);
+            v[j].y = pack_half2(__uint_as_float(r[8 * j + 2]) * inv, __uint_as_float(r[8 * j + 3]) * inv);
+            v[j].z = pack_half2(__uint_as_float(r[8 * j + 4]) * inv, __uint_as_float(r[8 * j + 5]) * inv);
+            v[j].w = pack_half2(__uint_as_float(r[8 * j + 6]) * inv, __uint_as_float(r[8 * j + 7]) * inv);
+          }
+          if (piece) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) __stcg(po + 4 * hf + j, v[j]);
+          } else if (qrow < p.Sq) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(dst + 32 * hf + 8 * j) = v[j];
           }
         }
-        continue;
+        tc_fence_before();
+        mbar_arrive(&o_empty[t]);
       }
-      // ---- a group cut between CTAs: leave this piece, the last CTA to finish merges
-      const long long total = static_cast<long long>(groups) * n_tiles;
-      const int first = attn_cta_of(total, p.sk_ctas, static_cast<long long>(sg.group) * n_tiles);
-      const int last = attn_cta_of(total, p.sk_ctas, static_cast<long long>(sg.group + 1) * n_tiles - 1);
-      const int r_in = t * kQT + row;
-      {
-        const int slot = 2 * static_cast<int>(blockIdx.x) + (static_cast<int>(blockIdx.x) == first ? 1 : 0);
-        const float inv = 1.0f / l_run;
-        uint4* po = reinterpret_cast<uint4*>(p.part_o + (static_cast<size_t>(slot) * kQ + r_in) * kD);
-#pragma unroll
-        for (int d = 0; d < kD; d += 8) {
-          uint4 v;
-          v.x = pack_half2(acc[d] * inv, acc[d + 1] * inv);
-          v.y = pack_half2(acc[d + 2] * inv, acc[d + 3] * inv);
-          v.z = pack_half2(acc[d + 4] * inv, acc[d + 5] * inv);
-          v.w = pack_half2(acc[d + 6] * inv, acc[d + 7] * inv);
-          __stcg(po + d / 8, v);
-        }
-        __stcg(p.part_ml + static_cast<size_t>(slot) * kQ + r_in, make_float2(m_run, l_run));
-      }
+      if (!piece) continue;
+      __stcg(p.part_ml + my_slot, make_float2(m_run, l_run));
       __threadfence();
       ok = ep_meet();
       if (!ok) break;
@@ -524,9 +516,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (!ok) break;
       if (*last_flag) {
         __threadfence();
-        // merge the pieces in CTA order: O = sum_s w_s O_s / sum_s w_s, w_s = l_s 2^((m_s - m) c);
-        // the (max, sum) pairs of up to four pieces are requested before any is used
-        auto slot_of = [&](int cc) { return 2 * cc + (cc == first ? 1 : 0); };
+        // merge the pieces in CTA order: O = sum_s w_s O_s / sum_s w_s, w_s = l_s 2^((m_s - m) c),
+        // 32 columns at a time; the (max, sum) pairs of up to four pieces are requested before
+        // any is used
         float mmax = -INFINITY;
         for (int c0 = first; c0 <= last; c0 += 4) {
           float2 m4[4];
@@ -537,39 +529,43 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           for (int i = 0; i < 4; ++i)
             if (c0 + i <= last) mmax = fmaxf(mmax, m4[i].x);
         }
+#pragma unroll 1
+        for (int hf = 0; hf < 2; ++hf) {
+          float a32[32];
 #pragma unroll
-        for (int d = 0; d < kD; ++d) acc[d] = 0.0f;
-        float L = 0.0f;
-        for (int cc = first; cc <= last; ++cc) {
-          const size_t sl = static_cast<size_t>(slot_of(cc)) * kQ + r_in;
-          const float2 ml = __ldcg(p.part_ml + sl);
-          const uint4* po = reinterpret_cast<const uint4*>(p.part_o + sl * kD);
-          uint4 ov[kD / 8];
+          for (int d = 0; d < 32; ++d) a32[d] = 0.0f;
+          float L = 0.0f;
+          for (int cc = first; cc <= last; ++cc) {
+            const size_t sl = static_cast<size_t>(slot_of(cc)) * kQ + r_in;
+            const float2 ml = __ldcg(p.part_ml + sl);
+            const uint4* po = reinterpret_cast<const uint4*>(p.part_o + sl * kD) + 4 * hf;
+            uint4 ov[4];
 #pragma unroll
-          for (int j = 0; j < kD / 8; ++j) ov[j] = __ldcg(po + j);
-          const float w = ml.y * fast_exp2((ml.x - mmax) * c);
-          L += w;
+            for (int j = 0; j < 4; ++j) ov[j] = __ldcg(po + j);
+            const float w = ml.y * fast_exp2((ml.x - mmax) * c);
+            L += w;
 #pragma unroll
-          for (int j = 0; j < kD / 8; ++j) {
-            const __half2* hh = reinterpret_cast<const __half2*>(&ov[j]);
+            for (int j = 0; j < 4; ++j) {
+              const __half2* hh = reinterpret_cast<const __half2*>(&ov[j]);
 #pragma unroll
-            for (int k2 = 0; k2 < 4; ++k2) {
-              const float2 f = __half22float2(hh[k2]);
-              acc[8 * j + 2 * k2] = fmaf(w, f.x, acc[8 * j + 2 * k2]);
-              acc[8 * j + 2 * k2 + 1] = fmaf(w, f.y, acc[8 * j + 2 * k2 + 1]);
+              for (int k2 = 0; k2 < 4; ++k2) {
+                const float2 f = __half22float2(hh[k2]);
+                a32[8 * j + 2 * k2] = fmaf(w, f.x, a32[8 * j + 2 * k2]);
+                a32[8 * j + 2 * k2 + 1] = fmaf(w, f.y, a32[8 * j + 2 * k2 + 1]);
+              }
             }
           }
-        }
-        if (qrow < p.Sq) {
-          const float inv = 1.0f / L;
+          if (qrow < p.Sq) {
+            const float inv = 1.0f / L;
 #pragma unroll
-          for (int d = 0; d < kD; d += 8) {
-            uint4 v;
-            v.x = pack_half2(acc[d] * inv, acc[d + 1] * inv);
-            v.y = pack_half2(acc[d + 2] * inv, acc[d + 3] * inv);
-            v.z = pack_half2(acc[d + 4] * inv, acc[d + 5] * inv);
-            v.w = pack_half2(acc[d + 6] * inv, acc[d + 7] * inv);
-            *reinterpret_cast<uint4*>(dst + d) = v;
+            for (int d = 0; d < 32; d += 8) {
+              uint4 v;
+              v.x = pack_half2(a32[d] * inv, a32[d + 1] * inv);
+              v.y = pack_half2(a32[d + 2] * inv, a32[d + 3] * inv);
+              v.z = pack_half2(a32[d + 4] * inv, a32[d + 5] * inv);
+              v.w = pack_half2(a32[d + 6] * inv, a32[d + 7] * inv);
+              *reinterpret_cast<uint4*>(dst + 32 * hf + d) = v;
+            }
           }
         }
         if (threadIdx.x == 0) p.part_cnt[sg.group] = 0;
