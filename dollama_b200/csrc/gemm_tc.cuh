@@ -210,6 +210,8 @@ __device__ __forceinline__ void chan_merge(float& n_a, float& mean_a, float& m2_
 // What epilogue_prefetch fetched for a tile.
 struct EpiPre {
   bool res = false;       // fp16 residual of chunks 0 and 1 in staging buffers 0 and 1
+  bool res3 = false;      // fp16 residual of the warp's third chunk in r3 (this lane's row)
+  uint4 r3[4];
   bool uv = false;        // LayerNorm-fold vectors u, v of chunks 0 and 1 in buffers 0 and 1
   bool ln_ready = false;  // this row's LayerNorm mean / rstd below
   float ln_mean = 0.0f, ln_rstd = 1.0f;
@@ -223,7 +225,7 @@ struct EpiPre {
 // after reading them.  (Prefetching the bias lines into L1 measured slower.)
 template <int BN, unsigned FL>
 __device__ __forceinline__ EpiPre epilogue_prefetch(const GemmParams& p, int row, int n0, int m_base,
-                                                    int half, uint8_t* stage) {
+                                                    int half, uint8_t* stage, bool r3_ok = false) {
   const unsigned fl = epi_flags(FL, p.flags);
   EpiPre pre;
   const int lane = threadIdx.x & 31;
@@ -272,6 +274,17 @@ __device__ __forceinline__ EpiPre epilogue_prefetch(const GemmParams& p, int row
       const float* src = (lane < 8 ? p.ln_u : p.ln_v) + n + 4 * (lane & 7);
       cp_async16(buf + 16 * lane, src, 16u);
     }
+  }
+  // the third chunk's residual row straight into registers (64 contiguous bytes per lane: whole
+  // 32-byte sectors; plain loads, since the residual may be the output itself).  Only the CTA-pair
+  // kernel asks for it: its tiles are single-wave linears whose epilogue is exposed, and the
+  // single-CTA kernel has no registers to spare.
+  if (r3_ok && resid16 && 32 * half + 128 < BN && n0 + 32 * half + 128 < p.N) {
+    const uint4* src = reinterpret_cast<const uint4*>(p.resid + static_cast<size_t>(row < p.M ? row : 0) * p.ldr +
+                                                      n0 + 32 * half + 128);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) pre.r3[q] = row < p.M ? src[q] : make_uint4(0, 0, 0, 0);
+    pre.res3 = true;
   }
   cp_async_commit();
   pre.res = resid16;
@@ -427,6 +440,19 @@ __device__ __forceinline__ bool epilogue_tile(const GemmParams& p, uint32_t t_ro
           }
         }
       } else if (fl & DLM_EPI_RESID) {
+        if (pre.res3 && cj == 2) {
+          const uint64_t rs2 = f2_pack(p.resid_scale, p.resid_scale);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const __half2* h = reinterpret_cast<const __half2*>(&pre.r3[q]);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float2 t = __half22float2(h[k]);
+              const uint64_t r = f2_fma(rs2, f2_pack(t.x, t.y), f2_pack(v[q * 8 + 2 * k], v[q * 8 + 2 * k + 1]));
+              f2_unpack(r, v[q * 8 + 2 * k], v[q * 8 + 2 * k + 1]);
+            }
+          }
+        } else {
         if (!(pre.res && cj < 2)) {
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
@@ -452,6 +478,7 @@ __device__ __forceinline__ bool epilogue_tile(const GemmParams& p, uint32_t t_ro
           }
         }
         __syncwarp();
+        }
       }
       if (fl & kEpiOutF32) {
         // fp32 output: two halves of 16 columns, each 32 rows x 64 bytes through one staging
@@ -1119,7 +1146,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int n0 = (t % p.n_tiles) * BN;
       const int row = m0 + quad * 32 + lane;
       uint8_t* stage_buf = sEpi + (warp - 2) * kStageBytesPerWarp;
-      const EpiPre pre = epilogue_prefetch<BN, FL>(p, row, n0, m0 + quad * 32, half, stage_buf);
+      const EpiPre pre = epilogue_prefetch<BN, FL>(p, row, n0, m0 + quad * 32, half, stage_buf, true);
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status, kDevTimeoutEpilogue)) break;
       tc_fence_after();
       const uint32_t t_row = tbase + (static_cast<uint32_t>(quad * 32) << 16) +
