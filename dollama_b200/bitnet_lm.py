@@ -87,6 +87,24 @@ class BitNetLM:
                _ptr(lens), _stream_ptr(stream))
         return [out[b, :lens[b]].tolist() for b in range(B)]
 
+    def generate_from_text(self, tok, text: str, max_len: int = None, stream=None):
+        """Tags for a natural-language prompt: [<bos>] + the text's greedy tag matches + [<sep>],
+        greedy decode, decoded tag strings (the reference's generate_from_text,
+        src/infer/bitnet.hpp:321-336, with the tokenizer of dollama_b200.tokenizer)."""
+        from .tokenizer import text_prompt
+        ids = self.generate(np.asarray([text_prompt(tok, text)], dtype=np.int32),
+                            max_len or self.cfg.max_seq, stream)[0]
+        return tok.decode(ids)
+
+    def generate_with_identity(self, tok, identity_tags, scene_text: str, max_len: int = None,
+                               stream=None):
+        """<bos> identity <sep> scene tags <sep> prompt, greedy decode, decoded tags
+        (generate_with_identity, src/infer/bitnet.hpp:379-385)."""
+        from .tokenizer import identity_prompt
+        ids = self.generate(np.asarray([identity_prompt(tok, identity_tags, scene_text)], dtype=np.int32),
+                            max_len or self.cfg.max_seq, stream)[0]
+        return tok.decode(ids)
+
     def generate_device(self, prompts: torch.Tensor, max_len: int, out: torch.Tensor,
                         lens: torch.Tensor, stream=None):
         """The same decode on CUDA int32 tensors (no host copies)."""

@@ -5,7 +5,9 @@
 * oracle/_ref/libref_bitnet.so      — the reference's own BitNet integer path, compiled from
   its header where it lies (src/models/bitnet.hpp under the reference tree) through
   ref_bitnet_shim.cpp, built only when the reference tree exists (it does not on GPU boxes,
-  which use the prebuilt file).  Outputs go only to oracle/_ref/ (git-ignored).
+  which use the prebuilt file).  Outputs go only to oracle/_ref/ (git-ignored);
+* oracle/_ref/libref_tokenizer.so   — the reference's tag tokenizer (src/io/tokenizer.hpp, header
+  only) through ref_tokenizer_shim.cpp, for the tokenizer golden vectors; same conditions.
 
 Usage:  python oracle/build_oracle.py
 """
@@ -51,6 +53,15 @@ def build() -> dict:
             _run(["g++", "-O2", "-fPIC", "-shared", "-std=c++17", "-ffp-contract=off",
                   "-I", str(REFERENCE / "src"), "-o", str(ref), str(shim)])
         out["ref_bitnet"] = str(ref)
+    tok_hdr = REFERENCE / "src" / "io" / "tokenizer.hpp"
+    if tok_hdr.exists():
+        REF_OUT.mkdir(exist_ok=True)
+        ref = REF_OUT / "libref_tokenizer.so"
+        shim = HERE / "ref_tokenizer_shim.cpp"
+        if _stale(ref, shim, tok_hdr):
+            _run(["g++", "-O2", "-fPIC", "-shared", "-std=c++17", "-I", str(REFERENCE / "src"),
+                  "-o", str(ref), str(shim)])
+        out["ref_tokenizer"] = str(ref)
     return out
 
 

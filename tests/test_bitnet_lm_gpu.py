@@ -103,3 +103,22 @@ def test_invalid_tokens_rejected():
     with pytest.raises(L.DlmError):
         lm.generate(np.zeros((1, 4), dtype=np.int32), max_len=SMALL["max_seq"] + 1)
     lm.close()
+
+
+def test_text_prompt_end_to_end_matches_oracle():
+    """Tokenizer -> LM -> tags (generate_from_text / generate_with_identity) at the reference's
+    vocabulary size 4999, against the oracle's greedy decode of the same prompt ids."""
+    from dollama_b200.tokenizer import Tokenizer, identity_prompt, text_prompt
+    from tests.golden.make_tokenizer_vectors import synthetic_vocab
+    tok = Tokenizer(synthetic_vocab())
+    cfg = B.lm_config(vocab=4999, d_model=128, n_layers=2, n_heads=2, ffn_dim=192, max_seq=32)
+    w = B.lm_random_weights(cfg, seed=12, kind="ternary")
+    lm = _gpu(cfg, w)
+    o = B.OracleLM(cfg, w)
+    text = "1girl with long hair and a white shirt under a blue sky"
+    got = lm.generate_from_text(tok, text, max_len=32)
+    assert got == tok.decode(o.generate(np.asarray(text_prompt(tok, text), np.int32), 32))
+    got2 = lm.generate_with_identity(tok, ["solo", "red eyes"], "open mouth, smile", max_len=32)
+    p2 = identity_prompt(tok, ["solo", "red eyes"], "open mouth, smile")
+    assert got2 == tok.decode(o.generate(np.asarray(p2, np.int32), 32))
+    lm.close()
