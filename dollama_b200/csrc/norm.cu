@@ -177,9 +177,14 @@ __global__ void __launch_bounds__(256, kBlocksPerSm)
                     int HW, const float2* __restrict__ mean_rstd, const __half* __restrict__ gamma,
                     const __half* __restrict__ beta, int silu, int pix_per_block,
                     __half* __restrict__ out) {
+  // The image's 32 (mean, rstd) pairs once per block: read per thread, every thread of the grid
+  // asks the same 256 bytes of L2 eight times and the slice holding them serialises the pass.
+  __shared__ float2 s_mr[kGroups];
   griddep_wait();  // dependents launch when this grid exits
   const int C = C1 + C2;
   const int n = blockIdx.y;
+  if (threadIdx.x < kGroups) s_mr[threadIdx.x] = __ldg(mean_rstd + n * kGroups + threadIdx.x);
+  __syncthreads();
   const int nvec = C >> 3;
   const int cpg = C / kGroups;
   const int PL = nvec >= static_cast<int>(blockDim.x) ? 1 : blockDim.x / nvec;
@@ -196,7 +201,7 @@ __global__ void __launch_bounds__(256, kBlocksPerSm)
       load8(beta + c, bt);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const float2 mr = __ldg(mean_rstd + n * kGroups + (c + i) / cpg);
+        const float2 mr = s_mr[(c + i) / cpg];
         sc[i] = mr.y * gm[i];
         sh[i] = bt[i] - mr.x * sc[i];
       }
