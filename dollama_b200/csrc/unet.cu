@@ -1293,8 +1293,9 @@ int UNetModel::apply_lora(const std::string& key, const __half* A, const __half*
 }
 
 int UNetModel::clear_loras(cudaStream_t s) {
-  while (!patches_.empty()) {
-    LoraPatch& pt = patches_.back();
+  // newest first, so rows patched twice end with the copy saved before the first patch
+  for (size_t k = patches_.size(); k-- > 0;) {
+    const LoraPatch& pt = patches_[k];
     const size_t wbytes = pt.elems * sizeof(__half);
     const uint8_t* sv = static_cast<const uint8_t*>(pt.saved);
     DLM_CHECK_CUDA(cudaMemcpyAsync(pt.w, sv, wbytes, cudaMemcpyDeviceToDevice, s));
@@ -1303,10 +1304,10 @@ int UNetModel::clear_loras(cudaStream_t s) {
     if (pt.v)
       DLM_CHECK_CUDA(cudaMemcpyAsync(pt.v, sv + wbytes + sizeof(float) * pt.rows, sizeof(float) * pt.rows,
                                      cudaMemcpyDeviceToDevice, s));
-    DLM_CHECK_CUDA(cudaStreamSynchronize(s));  // the saved block is read before it is freed
-    cudaFree(pt.saved);
-    patches_.pop_back();
   }
+  DLM_CHECK_CUDA(cudaStreamSynchronize(s));  // every saved block is read before any is freed
+  for (auto& pt : patches_) cudaFree(pt.saved);
+  patches_.clear();
   return DLM_OK;
 }
 
