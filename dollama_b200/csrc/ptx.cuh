@@ -146,15 +146,6 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, ui
       : "memory");
 }
 
-__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* tm, uint64_t* bar, int c0,
-                                            int c1, int c2) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(tm)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
-      : "memory");
-}
-
 __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* tm, uint64_t* bar, int c0,
                                             int c1, int c2, int c3) {
   asm volatile(
@@ -205,11 +196,6 @@ __device__ __forceinline__ void cp_async16(void* dst_smem, const void* src, uint
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
-
-// Wait until every bulk group of this thread has completed.
-__device__ __forceinline__ void bulk_wait_all() {
-  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
-}
 
 // Generic-proxy shared-memory writes -> visible to the async proxy (tensor core reads).
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -312,16 +298,6 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
       : "r"(taddr));
 }
 
-__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-}
-
 // ---------------------------------------------------------------- CTA pairs (cta_group::2)
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
@@ -386,22 +362,10 @@ __device__ __forceinline__ void tma2_load_5d(void* dst, const CUtensorMap* tm, u
 }
 
 // D (+)= A * B over the CTA pair: M = 256 (128 rows of A in each CTA's shared memory), B split
-// by N between the two CTAs, D rows of each CTA in its own TMEM.  Issued by the even CTA.
-__device__ __forceinline__ void umma2_f16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                             uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n"
-      ".reg .pred p;\n"
-      "setp.ne.b32 p, %4, 0;\n"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n"
-      "}\n" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// Pair MMA with the descriptors given as their low words over a shared high word (the
-// 128-byte-swizzle descriptors of one kernel differ only in the start address, bits [0,14)), so
-// that the issuing thread advances them with a 32-bit add.
+// by N between the two CTAs, D rows of each CTA in its own TMEM; issued by the even CTA.  The
+// descriptors are given as their low words over a shared high word (the 128-byte-swizzle
+// descriptors of one kernel differ only in the start address, bits [0,14)), so that the issuing
+// thread advances them with a 32-bit add.
 __device__ __forceinline__ void umma2_f16_ss_lo(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo,
                                                 uint32_t hi, uint32_t idesc, uint32_t accumulate) {
   asm volatile(
@@ -481,18 +445,7 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
-// 2^x for two fp16 values at once (ex2.approx.f16x2; -inf -> 0).
-__device__ __forceinline__ uint32_t ex2_half2(uint32_t x) {
-  uint32_t y;
-  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
-  return y;
-}
-
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
-
-__device__ __forceinline__ float gelu_erf_f(float x) {
-  return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
-}
 
 
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
