@@ -363,6 +363,90 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tc_fence_after();
         const int valid = p.Sk - (sg.j0 + jl) * kKV;  // keys of this tile (may exceed 128)
         const bool full_tile = valid >= kKV;
+        if (jl >= 1 && full_tile) {
+          // One pass over S: each 64-column half is read once, its row max checked against the
+          // running max m (the same lazy rule: m moves only when the max exceeds it by more than
+          // 8 in exp2 units, so p = 2^(s c - m c) <= 2^8), then exponentiated against m.  A move
+          // in the second half rescales the first half's P already in TMEM, the partial sums and
+          // (after the previous P.V) O.
+          float m_cur = m_run, alpha_all = 1.0f, a_second = 1.0f;
+          uint64_t sumA = f2_pack(0.0f, 0.0f), sumB = sumA;
+#pragma unroll 1
+          for (int cc = 0; cc < 4; cc += 2) {
+            uint32_t ra[32], rb[32];
+            tmem_ld_32x32b_x32(ts + cc * 32, ra);
+            tmem_ld_32x32b_x32(ts + cc * 32 + 32, rb);
+            tmem_ld_wait();
+            float h0 = m_cur, h1 = m_cur, h2 = m_cur, h3 = m_cur;
+#pragma unroll
+            for (int q = 0; q < 32; q += 4) {
+              h0 = max3f(h0, __uint_as_float(ra[q]), __uint_as_float(ra[q + 1]));
+              h1 = max3f(h1, __uint_as_float(ra[q + 2]), __uint_as_float(ra[q + 3]));
+              h2 = max3f(h2, __uint_as_float(rb[q]), __uint_as_float(rb[q + 1]));
+              h3 = max3f(h3, __uint_as_float(rb[q + 2]), __uint_as_float(rb[q + 3]));
+            }
+            const float hm = fmaxf(fmaxf(h0, h1), fmaxf(h2, h3));
+            if ((hm - m_cur) * c > 8.0f) {
+              const float a = fast_exp2((m_cur - hm) * c);
+              alpha_all *= a;
+              if (cc == 2) a_second = a;
+              const uint64_t a2 = f2_pack(a, a), z2 = f2_pack(0.0f, 0.0f);
+              sumA = f2_fma(sumA, a2, z2);
+              sumB = f2_fma(sumB, a2, z2);
+              m_cur = hm;
+            }
+            const float mcc = m_cur * c;
+            const uint64_t c2 = f2_pack(c, c), nmc2 = f2_pack(-mcc, -mcc);
+            uint32_t pp[32];
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+              const uint32_t* r = half ? rb : ra;
+#pragma unroll
+              for (int q = 0; q < 32; q += 2) {
+                float x0, x1;
+                f2_unpack(f2_fma(f2_pack(__uint_as_float(r[q]), __uint_as_float(r[q + 1])), c2, nmc2),
+                          x0, x1);
+                const float e0 = fast_exp2(x0);
+                const float e1 = fast_exp2(x1);
+                if (q & 2)
+                  sumB = f2_add(sumB, f2_pack(e0, e1));
+                else
+                  sumA = f2_add(sumA, f2_pack(e0, e1));
+                pp[half * 16 + (q >> 1)] = pack_half2(e0, e1);
+              }
+            }
+            tmem_st_32x32b_x32(ts + (cc >> 1) * 32, pp);
+          }
+          tmem_st_wait();
+          if (__any_sync(0xffffffffu, a_second != 1.0f)) {
+            // the first half's P was written against the max before the second half moved it
+            uint32_t pp[32];
+            tmem_ld_32x32b_x32(ts, pp);
+            tmem_ld_wait();
+#pragma unroll
+            for (int q = 0; q < 32; ++q) {
+              const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&pp[q]));
+              pp[q] = pack_half2(f.x * a_second, f.y * a_second);
+            }
+            tmem_st_32x32b_x32(ts, pp);
+            tmem_st_wait();
+          }
+          // P.V of tile j-1 is complete before O is rescaled and P_j released
+          if (!wwait(&o_full[t], (jj - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (__any_sync(0xffffffffu, alpha_all != 1.0f)) rescale_o(alpha_all);
+          float sum0, sum1, sum2, sum3;
+          f2_unpack(sumA, sum0, sum1);
+          f2_unpack(sumB, sum2, sum3);
+          tc_fence_before();
+          mbar_arrive(&p_full[t]);
+          l_run = fmaf(l_run, alpha_all, (sum0 + sum1) + (sum2 + sum3));
+          m_run = m_cur;
+          continue;
+        }
         // pass 1: row max over 128 columns, two TMEM loads in flight, four independent chains
         float mx0 = m_run, mx1 = m_run, mx2 = m_run, mx3 = m_run;
 #pragma unroll

@@ -111,3 +111,27 @@ def test_attention_stream_k(B, H, Sq, Sk, attn_ws):
     code = ctypes.c_int()
     L.call("dlm_get_device_status", ctypes.byref(code), 1, _s())
     assert code.value == 0
+
+
+@pytest.mark.parametrize("use_ws", [False, True])
+def test_attention_growing_scores(use_ws, attn_ws):
+    """Keys whose scale grows along the sequence, so a row's maximum keeps rising past the running
+    maximum by more than 2^8 in later key tiles and inside a tile's second half (the lazy-max
+    rescale of P already written, of the partial sums and of O)."""
+    B, H, Sq, Sk = 2, 3, 256, 1024
+    g = torch.Generator().manual_seed(77)
+    q = (2.0 * torch.randn(B, H, Sq, 64, generator=g)).half().cuda()
+    grow = (1.0 + 0.02 * torch.arange(Sk, dtype=torch.float32)).view(1, 1, Sk, 1)
+    k = (torch.randn(B, H, Sk, 64, generator=g) * grow).half().cuda()
+    v = torch.randn(B, H, Sk, 64, generator=g).half().cuda()
+    o = torch.empty_like(q)
+    if use_ws:
+        ws, nbytes = attn_ws
+        L.call("dlm_launch_attention_ws", _p(q), _p(k), _p(v), _p(o), B, H, Sq, Sk, 64, 0.125,
+               _p(ws), nbytes, _s())
+    else:
+        L.call("dlm_launch_attention", _p(q), _p(k), _p(v), _p(o), B, H, Sq, Sk, 64, 0.125, _s())
+    torch.cuda.synchronize()
+    ref = ref_attn(q, k, v)
+    assert max_rel_err(o, ref) < 2e-3
+    assert allclose_k(o, ref, Sk)
