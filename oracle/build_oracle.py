@@ -7,7 +7,9 @@
   ref_bitnet_shim.cpp, built only when the reference tree exists (it does not on GPU boxes,
   which use the prebuilt file).  Outputs go only to oracle/_ref/ (git-ignored);
 * oracle/_ref/libref_tokenizer.so   — the reference's tag tokenizer (src/io/tokenizer.hpp, header
-  only) through ref_tokenizer_shim.cpp, for the tokenizer golden vectors; same conditions.
+  only) through ref_tokenizer_shim.cpp, for the tokenizer golden vectors; same conditions;
+* oracle/_ref/libref_scheduler.so   — the reference's Euler scheduler (src/infer/scheduler.hpp,
+  header only) through ref_scheduler_shim.cpp; same conditions.
 
 Usage:  python oracle/build_oracle.py
 """
@@ -62,6 +64,15 @@ def build() -> dict:
             _run(["g++", "-O2", "-fPIC", "-shared", "-std=c++17", "-I", str(REFERENCE / "src"),
                   "-o", str(ref), str(shim)])
         out["ref_tokenizer"] = str(ref)
+    sched_hdr = REFERENCE / "src" / "infer" / "scheduler.hpp"
+    if sched_hdr.exists():
+        REF_OUT.mkdir(exist_ok=True)
+        ref = REF_OUT / "libref_scheduler.so"
+        shim = HERE / "ref_scheduler_shim.cpp"
+        if _stale(ref, shim, sched_hdr):
+            _run(["g++", "-O2", "-fPIC", "-shared", "-std=c++17", "-ffp-contract=off",
+                  "-I", str(REFERENCE / "src"), "-o", str(ref), str(shim)])
+        out["ref_scheduler"] = str(ref)
     return out
 
 

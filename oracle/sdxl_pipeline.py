@@ -25,17 +25,25 @@ def euler_schedule(steps: int):
     return sigmas, ts.astype(np.float32)
 
 
+def scale_input(x: torch.Tensor, sigma: float) -> torch.Tensor:
+    """scale_model_input (scheduler.hpp:110-119): fp32(double(x) / sqrt(sigma^2 + 1))."""
+    return (x.double() * (1.0 / np.sqrt(float(sigma) ** 2 + 1.0))).float()
+
+
+def euler_step(x: torch.Tensor, eps: torch.Tensor, sigma: float, sigma_next: float) -> torch.Tensor:
+    """Epsilon Euler step (scheduler.hpp:126-140): fp32(double(x) + double(eps) * (sigma' - sigma))."""
+    return (x.double() + eps.double() * (float(sigma_next) - float(sigma))).float()
+
+
 def denoise(sd, cfg, init_latent, ehs, te, tid, steps, guidance):
     """init_latent [1, 4, H, W] fp32; ehs [2, 77, 2048], te [2, 1280] (cond, uncond), tid [6] ->
     final latent [1, 4, H, W] fp32 (UNet in fp32)."""
     sigmas, ts = euler_schedule(steps)
-    x = init_latent.double()
+    x = init_latent.float()
     with torch.no_grad():
         for i in range(steps):
-            scale = 1.0 / np.sqrt(float(sigmas[i]) ** 2 + 1.0)
-            xin = (x * scale).float().expand(2, -1, -1, -1).contiguous()
+            xin = scale_input(x, sigmas[i]).expand(2, -1, -1, -1).contiguous()
             noise = unet_forward(sd, xin, float(ts[i]), ehs.float(), te.float(), tid.float(), cfg)
             e = noise[1] + guidance * (noise[0] - noise[1])
-            x = x + e.double() * (float(sigmas[i + 1]) - float(sigmas[i]))
-            x = x.float().double()
+            x = euler_step(x, e, sigmas[i], sigmas[i + 1])
     return x.float()
