@@ -9,7 +9,9 @@
 * oracle/_ref/libref_tokenizer.so   — the reference's tag tokenizer (src/io/tokenizer.hpp, header
   only) through ref_tokenizer_shim.cpp, for the tokenizer golden vectors; same conditions;
 * oracle/_ref/libref_scheduler.so   — the reference's Euler scheduler (src/infer/scheduler.hpp,
-  header only) through ref_scheduler_shim.cpp; same conditions.
+  header only) through ref_scheduler_shim.cpp; same conditions;
+* oracle/_ref/libref_lora.so        — the reference's kohya LoRA loader (src/infer/lora.hpp with
+  src/io/safetensors.hpp, header only) through ref_lora_shim.cpp; same conditions.
 
 Usage:  python oracle/build_oracle.py
 """
@@ -73,6 +75,15 @@ def build() -> dict:
             _run(["g++", "-O2", "-fPIC", "-shared", "-std=c++17", "-ffp-contract=off",
                   "-I", str(REFERENCE / "src"), "-o", str(ref), str(shim)])
         out["ref_scheduler"] = str(ref)
+    lora_hdr = REFERENCE / "src" / "infer" / "lora.hpp"
+    if lora_hdr.exists():
+        REF_OUT.mkdir(exist_ok=True)
+        ref = REF_OUT / "libref_lora.so"
+        shim = HERE / "ref_lora_shim.cpp"
+        if _stale(ref, shim, lora_hdr):
+            _run(["g++", "-O2", "-fPIC", "-shared", "-std=c++17", "-I", str(REFERENCE / "src"),
+                  "-o", str(ref), str(shim)])
+        out["ref_lora"] = str(ref)
     return out
 
 
