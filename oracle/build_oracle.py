@@ -11,7 +11,10 @@
 * oracle/_ref/libref_scheduler.so   — the reference's Euler scheduler (src/infer/scheduler.hpp,
   header only) through ref_scheduler_shim.cpp; same conditions;
 * oracle/_ref/libref_lora.so        — the reference's kohya LoRA loader (src/infer/lora.hpp with
-  src/io/safetensors.hpp, header only) through ref_lora_shim.cpp; same conditions.
+  src/io/safetensors.hpp, header only) through ref_lora_shim.cpp; same conditions;
+* oracle/_ref/libref_cpu_<op>.so    — the CPU reference functions of the reference's kernel tests
+  (GroupNorm, LayerNorm, GEGLU, activations, attention, timestep embedding), nvcc-compiled with the
+  test file and the reference kernels it links (ref_cpu/*.cu); same conditions.
 
 Usage:  python oracle/build_oracle.py
 """
@@ -84,6 +87,22 @@ def build() -> dict:
             _run(["g++", "-O2", "-fPIC", "-shared", "-std=c++17", "-I", str(REFERENCE / "src"),
                   "-o", str(ref), str(shim)])
         out["ref_lora"] = str(ref)
+    # the CPU references inside the reference's kernel tests (see ref_cpu/README.txt): each shim
+    # includes its test file and links the reference kernels that test calls
+    kernels = REFERENCE / "src" / "kernels"
+    ops = {"gn": ["groupnorm.cu", "activation.cu"], "ln": ["layernorm.cu"], "geglu": ["geglu.cu"],
+           "act": ["activation.cu"], "attn": ["attention.cu"], "timeembed": ["timeembed.cu"]}
+    if kernels.exists():
+        REF_OUT.mkdir(exist_ok=True)
+        for op, ks in ops.items():
+            shim = HERE / "ref_cpu" / f"{op}.cu"
+            deps = [kernels / k for k in ks]
+            ref = REF_OUT / f"libref_cpu_{op}.so"
+            if _stale(ref, shim, *deps):
+                _run(["nvcc", "-gencode", "arch=compute_100a,code=sm_100a", "-O2", "-std=c++17",
+                      "-DHAVE_CUDA", "-Xcompiler", "-fPIC", "-shared", "-I", str(REFERENCE / "src"),
+                      "-o", str(ref), str(shim)] + [str(d) for d in deps])
+            out[f"ref_cpu_{op}"] = str(ref)
     return out
 
 
