@@ -13,8 +13,10 @@
 * oracle/_ref/libref_lora.so        — the reference's kohya LoRA loader (src/infer/lora.hpp with
   src/io/safetensors.hpp, header only) through ref_lora_shim.cpp; same conditions;
 * oracle/_ref/libref_cpu_<op>.so    — the CPU reference functions of the reference's kernel tests
-  (GroupNorm, LayerNorm, GEGLU, activations, attention, timestep embedding), nvcc-compiled with the
-  test file and the reference kernels it links (ref_cpu/*.cu); same conditions.
+  (GroupNorm, LayerNorm, GEGLU, activations, attention, timestep embedding, convolution),
+  nvcc-compiled with the test file and the reference kernels it links (ref_cpu/*.cu; the
+  convolution test's kernels need cuBLAS, so its GPU entry points are left unresolved and the
+  library is opened with lazy binding); same conditions.
 
 Usage:  python oracle/build_oracle.py
 """
@@ -91,7 +93,8 @@ def build() -> dict:
     # includes its test file and links the reference kernels that test calls
     kernels = REFERENCE / "src" / "kernels"
     ops = {"gn": ["groupnorm.cu", "activation.cu"], "ln": ["layernorm.cu"], "geglu": ["geglu.cu"],
-           "act": ["activation.cu"], "attn": ["attention.cu"], "timeembed": ["timeembed.cu"]}
+           "act": ["activation.cu"], "attn": ["attention.cu"], "timeembed": ["timeembed.cu"],
+           "conv": []}  # conv: its test's GPU entry points stay unresolved (opened lazily)
     if kernels.exists():
         REF_OUT.mkdir(exist_ok=True)
         for op, ks in ops.items():

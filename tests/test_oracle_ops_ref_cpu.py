@@ -1,6 +1,7 @@
 """The UNet / VAE oracle's operations (oracle/sdxl_unet.py) against the CPU reference
 implementations inside the reference's own kernel tests (src/tests/test_groupnorm.cu,
 test_layernorm.cu, test_geglu.cu, test_activation.cu, test_attention.cu, test_timeembed.cu,
+test_conv2d.cu,
 compiled where they lie into oracle/_ref/libref_cpu_*.so by oracle/build_oracle.py).
 
 Those CPU references define what each reference kernel computes (eps placement, biased variance,
@@ -10,6 +11,8 @@ output scale (1e-4 for the GroupNorm reference's one-pass fp32 variance).  This 
 model oracle's building blocks to the reference; the whole-model goldens stay unavailable.
 """
 import ctypes
+import math
+import os
 
 import numpy as np
 import pytest
@@ -25,10 +28,11 @@ FP = ctypes.POINTER(ctypes.c_float)
 @pytest.fixture(scope="module")
 def libs():
     out = build()
-    need = ["gn", "ln", "geglu", "act", "attn", "timeembed"]
+    need = ["gn", "ln", "geglu", "act", "attn", "timeembed", "conv"]
     if any(f"ref_cpu_{k}" not in out for k in need):
         pytest.skip("reference tree absent: the kernel tests' CPU references are not built")
-    return {k: ctypes.CDLL(out[f"ref_cpu_{k}"]) for k in need}
+    # lazy binding: the convolution test's GPU entry points are never called nor linked
+    return {k: ctypes.CDLL(out[f"ref_cpu_{k}"], mode=os.RTLD_LAZY | os.RTLD_LOCAL) for k in need}
 
 
 def _p(a):
@@ -115,3 +119,20 @@ def test_timestep_embedding(libs, t):
     # both evaluate cos / sin of a float argument; the argument t * f_i may differ by an ulp of a
     # value up to ~1e3, so the bound is on that argument's rounding
     assert float(np.max(np.abs(got - out))) <= 2.0 * max(t, 1.0) * 2.0 ** -23
+
+
+@pytest.mark.parametrize("Cin,Cout,H,W,K,stride,pad", [(8, 16, 9, 7, 3, 1, 1), (8, 8, 10, 10, 3, 2, 1),
+                                                       (12, 6, 5, 6, 1, 1, 0), (4, 32, 8, 8, 3, 1, 1)])
+def test_conv2d(libs, Cin, Cout, H, W, K, stride, pad):
+    r = _rng(Cin * Cout + H)
+    N = 2
+    x = r.standard_normal((N, Cin, H, W)).astype(np.float32)
+    w = (r.standard_normal((Cout, Cin, K, K)) / math.sqrt(Cin * K * K)).astype(np.float32)
+    b = (0.1 * r.standard_normal(Cout)).astype(np.float32)
+    Ho = (H + 2 * pad - K) // stride + 1
+    Wo = (W + 2 * pad - K) // stride + 1
+    out = np.zeros((N, Cout, Ho, Wo), np.float32)
+    libs["conv"].ref_cpu_conv2d(_p(x), _p(w), _p(b), N, Cin, H, W, Cout, K, K, stride, pad, _p(out))
+    sd = {"c.weight": torch.from_numpy(w), "c.bias": torch.from_numpy(b)}
+    got = U.conv(torch.from_numpy(x), sd, "c", stride=stride, padding=pad).numpy()
+    assert _rel(got, out) <= 2e-5
