@@ -45,13 +45,18 @@ def resnet(x, sd, p):
     return x + h
 
 
+def mid_attention(q, k, v):
+    """Single-head softmax(q k^T / sqrt(C)) v over [B, S, C] (vae_decode.cu:660-691)."""
+    s = (q @ k.transpose(1, 2)) * (1.0 / math.sqrt(q.shape[-1]))
+    return torch.softmax(s, dim=-1) @ v
+
+
 def attn_block(x, sd, p):
     B, C, H, W = x.shape
     h = _gn(x, sd, p + "group_norm").permute(0, 2, 3, 1).reshape(B, H * W, C)
     lin = lambda t, n: F.linear(t, sd[p + n + ".weight"].float(), sd[p + n + ".bias"].float())
     q, k, v = lin(h, "to_q"), lin(h, "to_k"), lin(h, "to_v")
-    s = (q @ k.transpose(1, 2)) * (1.0 / math.sqrt(C))
-    o = torch.softmax(s, dim=-1) @ v
+    o = mid_attention(q, k, v)
     o = lin(o, "to_out.0").reshape(B, H, W, C).permute(0, 3, 1, 2)
     return x + o
 

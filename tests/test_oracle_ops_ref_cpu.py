@@ -20,6 +20,7 @@ import torch
 import torch.nn.functional as F
 
 from oracle import sdxl_unet as U
+from oracle import sdxl_vae as V
 from oracle.build_oracle import build
 
 FP = ctypes.POINTER(ctypes.c_float)
@@ -136,3 +137,15 @@ def test_conv2d(libs, Cin, Cout, H, W, K, stride, pad):
     sd = {"c.weight": torch.from_numpy(w), "c.bias": torch.from_numpy(b)}
     got = U.conv(torch.from_numpy(x), sd, "c", stride=stride, padding=pad).numpy()
     assert _rel(got, out) <= 2e-5
+
+
+def test_vae_mid_attention(libs):
+    """The VAE decoder's single-head mid attention (head dim 512, scale 1 / sqrt(512))."""
+    r = _rng(512)
+    B, S, C = 1, 96, 512
+    q, k, v = (r.standard_normal((B, 1, S, C)).astype(np.float32) for _ in range(3))
+    out = np.zeros_like(q)
+    libs["attn"].ref_cpu_attention(_p(q), _p(k), _p(v), B, 1, S, S, C, ctypes.c_float(1.0 / math.sqrt(C)),
+                                   _p(out))
+    got = V.mid_attention(*(torch.from_numpy(a[:, 0]) for a in (q, k, v))).numpy()
+    assert _rel(got, out[:, 0]) <= 2e-5
