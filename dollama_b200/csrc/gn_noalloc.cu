@@ -12,11 +12,16 @@
 //   * the static array holds kNoAllocPartials float2 (256 KiB); dlm_group_norm_nhwc_noalloc rejects
 //     problems whose partial sums would not fit (an error, nothing is launched);
 //   * every GPU that loads the library holds its own copy of the array until the process exits;
-//   * every call shares the array and leaves the last call's partial sums in it.  The array also
-//     holds the statistics pass's per-image arrival counters, which must be zero when a launch
-//     starts: static device memory starts zeroed and every launch leaves its counters at zero.
-//     Calls whose work overlaps on the GPU (different streams, or other threads) race on the
-//     array and give wrong results — serialise them;
+//   * on a 148-SM B200 every image size fits for batches of up to 339 images (the partial-sum
+//     count grows with the SM count and the batch, not with the image size beyond a few pixels);
+//   * every call shares the array and leaves the last call's partial sums and statistics in it.
+//     The array also holds the statistics pass's per-image arrival counters, whose position
+//     depends on the batch N (they follow the N x 32 statistics slots), so a call cannot rely on
+//     an earlier call having left them at zero: each call clears its own counters on its stream
+//     (cudaMemsetAsync, which allocates nothing) before the statistics pass.  A call that failed
+//     part-way leaves nothing behind for the next one for the same reason.  Calls whose work
+//     overlaps on the GPU (different streams, or other threads) race on the array and give wrong
+//     results — serialise them;
 //   * the array's device address is looked up (cudaGetSymbolAddress) by the first call on each
 //     device, with that device current; that first call should come before any stream capture.
 #include <mutex>
@@ -77,6 +82,10 @@ int dlm_group_norm_nhwc_noalloc(const void* x1, int C1, const void* x2, int C2, 
     return DLM_ERR_INVALID;
   }
   if (rc != DLM_OK) return rc;
+  // the counters sit after the N x 32 statistics slots, where an earlier call with another N may
+  // have left statistics: zero them for this call on its own stream
+  DLM_CHECK_CUDA(cudaMemsetAsync(op.counters, 0, dlm::gn_counter_bytes(N),
+                                 static_cast<cudaStream_t>(stream)));
   return dlm::gn_launch(op, static_cast<cudaStream_t>(stream));
 }
 

@@ -211,8 +211,10 @@ int dlm_group_norm_nhwc(const void* x1, int C1, const void* x2, int C2, int N, i
  * scratch buffer.  This entry point keeps the partial sums in a static device array of the
  * library (dlm_group_norm_nhwc_noalloc_capacity() float2 entries, 256 KiB, one copy per GPU that
  * loads the library, held until exit) and allocates nothing.  Problems needing more partial sums
- * are rejected with DLM_ERR_INVALID.  All calls share the array: calls that overlap on the GPU
- * race and must be serialised.  The first call on a device looks up the array's device address
+ * are rejected with DLM_ERR_INVALID: the count grows with the batch and the SM count, so on a
+ * 148-SM B200 any image size fits for N <= 339.  Each call zeroes its own arrival counters on its
+ * stream (a memset, no allocation), so calls with different N may follow one another.  All calls
+ * share the array: calls that overlap on the GPU race and must be serialised.  The first call on a device looks up the array's device address
  * (with that device current) and should come before any stream capture. */
 size_t dlm_group_norm_nhwc_noalloc_capacity(void);
 int dlm_group_norm_nhwc_noalloc(const void* x1, int C1, const void* x2, int C2, int N, int HW,
