@@ -11,8 +11,9 @@ Prints ONE JSON line on rank 0.  Legs of our arm:
                the launching stream, barrier + synchronize on both sides, max over ranks;
   e2e          the same steps through dlm_unet_forward_host with pinned HOST buffers: every step
                copies latent / text conditioning in and the noise prediction out;
-  roofline     the dominant kernel class (tcgen05 GEMM / implicit-GEMM conv) timed per launch
-               with CUDA events in one eager step right after the timed region;
+  roofline     the dominant kernel class (tcgen05 GEMM / implicit-GEMM conv): its launches of
+               one step replayed alone as one CUDA graph right after the timed region (CUDA
+               events), so the per-class times add up to about the step's;
   cpu_baseline the CPU fp32 oracle of the same step (oracle/sdxl_unet.py) on this host's cores
                (rank 0, N = 1 only).
 `--impl reference` times the reference's CPU path for this workload: the reference has no CPU
@@ -149,7 +150,7 @@ def job_throughput(ws: int, steps: int, ms_total: float) -> float:
     return ws * steps / (ms_total / 1000.0)
 
 
-def make_inputs(device, seed=6):
+def make_inputs(device, seed=6, pin=True):
     import torch
     g = torch.Generator(device="cpu").manual_seed(seed)
     lat = torch.randn(1, 4, LATENT, LATENT, generator=g).expand(BATCH, -1, -1, -1).contiguous()
@@ -157,7 +158,7 @@ def make_inputs(device, seed=6):
     te = torch.randn(BATCH, 1280, generator=g)
     tid = torch.tensor([1024.0, 1024.0, 0.0, 0.0, 1024.0, 1024.0])
     host = [t.half().contiguous() for t in (lat, ehs, te, tid)]
-    if torch.cuda.is_available():
+    if pin and torch.cuda.is_available():
         host = [t.pin_memory() for t in host]
     dev = [t.to(device) for t in host]
     return host, dev
@@ -178,26 +179,27 @@ def cpu_oracle_step(sd_gpu, host_inputs, timestep=999.0):
 
 
 def run_reference(args, ws, rank):
+    """The reference arm: the CPU fp32 restatement of the step on all host cores, with its
+    weights drawn on the CPU by the oracle's own initialiser.  Nothing of this library (no
+    dollama_b200 import, no CUDA) is on this path; it runs exactly --warmup untimed and --steps
+    timed steps, on rank 0 only."""
     if rank != 0:
         return 0
     import torch
-    from dollama_b200.unet import random_weights
-    from oracle.sdxl_unet import UNetConfig, unet_forward
+    from oracle.sdxl_unet import UNetConfig, init_weights, unet_forward
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    dev = "cuda" if torch.cuda.is_available() else "cpu"
-    sd = random_weights(seed=7, device=dev)
-    sdf = {k: v.float().cpu() for k, v in sd.items()}
-    del sd
-    host, _ = make_inputs("cpu")
+    sdf = {k: v.float() for k, v in init_weights(UNetConfig(), seed=7).items()}
+    host, _ = make_inputs("cpu", pin=False)
     lat, ehs, te, tid = (t.float() for t in host)
-    steps, warm = max(1, min(args.steps, 2)), max(0, min(args.warmup, 1))
+    steps, warm = max(1, args.steps), max(0, args.warmup)
+    ts = [999.0 - 50.0 * i for i in range(STEPS_PER_IMAGE)]
     with torch.no_grad():
-        for _ in range(warm):
-            unet_forward(sdf, lat, 999.0, ehs, te, tid, UNetConfig())
+        for i in range(warm):
+            unet_forward(sdf, lat, ts[i % len(ts)], ehs, te, tid, UNetConfig())
         t0 = time.perf_counter()
-        for _ in range(steps):
-            unet_forward(sdf, lat, 999.0, ehs, te, tid, UNetConfig())
+        for i in range(steps):
+            unet_forward(sdf, lat, ts[i % len(ts)], ehs, te, tid, UNetConfig())
         dt = time.perf_counter() - t0
     v = steps / dt
     sample = (f"{steps} full UNet steps (B=2, 128x128 latent, all 70 transformer blocks) after "
@@ -211,7 +213,7 @@ def run_reference(args, ws, rank):
         "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference's UNet exists only as CUDA + cuBLAS (src/infer/unet.cu); its CPU "
                 "golden path needs diffusers and pretrained weights, absent here; this arm is the "
-                "CPU fp32 restatement of the same step",
+                "CPU fp32 restatement of the same step, weights drawn on the CPU",
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -307,19 +309,12 @@ def main():
     g = ops["gemm"]
     gemm_tf = g["flops"] / (g["ms"] / 1000.0) / 1e12 if g["ms"] > 0 else 0.0
     step_flops = sum(v["flops"] for v in ops.values())
-    prof = ROOT / "profiles" / "gemm_tc_kernel_unet_step.md"
-    traffic = None
-    if prof.exists():
-        for line in prof.read_text().splitlines():
-            if line.startswith("traffic_bytes_per_launch:"):
-                try:
-                    traffic = float(line.split(":", 1)[1].strip())
-                except ValueError:
-                    traffic = None
     roofline = {
         "kernel": "gemm_tc_kernel (tcgen05 GEMM + implicit-GEMM conv), all launches of one step",
         "bound": "tensor", "achieved": gemm_tf, "peak": sustained, "unit": "TFLOP/s",
-        "frac": gemm_tf / sustained, "traffic": traffic,
+        "frac": gemm_tf / sustained, "traffic": None,
+        "traffic_note": "DRAM bytes are not measurable inside a timed run; single-launch ncu "
+                        "captures of the step's GEMM shapes are summarised under profiles/",
         "peak_source": f"{peak_src} bf16_tflops_sustained (kernel timed inside a long step)",
         "frac_of_burst_peak": gemm_tf / burst,
         "launches": g["launches"], "avg_launch_us": 1000.0 * g["ms"] / max(1, g["launches"]),
@@ -327,6 +322,10 @@ def main():
         "step": {"flops": step_flops, "achieved_tflops": step_flops / (ms_step / 1000.0) / 1e12,
                  "frac_of_sustained": step_flops / (ms_step / 1000.0) / 1e12 / sustained},
         "by_class_ms": {k: round(v["ms"], 4) for k, v in ops.items()},
+        "by_class_note": "each class's launches replayed alone as one CUDA graph (step order, "
+                         "5 replays, CUDA events); the classes' sum against ms_per_step is "
+                         "class_sum_over_step",
+        "class_sum_over_step": sum(v["ms"] for v in ops.values()) / ms_step,
     }
 
     # ---------------------------------------------------------------- whole image (txt2img)

@@ -67,8 +67,9 @@ class OpPlan {
   // The step as one CUDA graph (captured on first use), or eager when `graph` is false.
   int replay(cudaStream_t s, bool graph);
   void drop_graph();
-  // Runs the step eagerly with an event between launches; per op class: device ms, algorithmic
-  // FLOPs and launches.  DLM_OP_TABLE=<path> also writes one CSV line per launch.
+  // Per op class: device ms of the class's launches replayed alone as one CUDA graph (so the
+  // classes add up to about the step graph's time), algorithmic FLOPs and launches.
+  // DLM_OP_TABLE=<path> also writes one CSV line per launch of an eager, event-timed step.
   int time(cudaStream_t s, double* ms, double* flops, int* count);
   int num_launches() const;
   size_t size() const { return seq_.size(); }
@@ -80,6 +81,8 @@ class OpPlan {
     int idx;
   };
   int launch(const Ref& r, cudaStream_t s);
+  int op_class(const Ref& r, double* flops) const;
+  int write_table(cudaStream_t s, const char* path);
   std::vector<Ref> seq_;
   std::vector<GemmOp> gemm_;
   std::vector<double> gemm_flops_;

@@ -62,6 +62,32 @@ class UNetConfig:
 SDXL = UNetConfig()
 
 
+# ---------------------------------------------------------------------------- storage rounding
+
+_FP16_STORAGE = [False]
+
+
+class fp16_storage:
+    """Context manager: while active, the oracle rounds every activation it would hand to the
+    next layer to fp16 (then computes on in fp32), at the points where an fp16-storage
+    implementation writes its tensors: normalised inputs of a convolution / linear, each
+    convolution or linear output after its bias / residual, attention outputs, GEGLU outputs.
+    The reference stores fp16 at these points too (and at more), so the difference between this
+    variant and the plain fp32 oracle is the error that fp16 storage alone costs."""
+
+    def __enter__(self):
+        _FP16_STORAGE[0] = True
+        return self
+
+    def __exit__(self, *exc):
+        _FP16_STORAGE[0] = False
+        return False
+
+
+def _st(t: torch.Tensor) -> torch.Tensor:
+    return t.half().float() if _FP16_STORAGE[0] else t
+
+
 # ---------------------------------------------------------------------------- primitives
 
 def timestep_embedding(t: torch.Tensor, dim: int, max_period: float = 10000.0) -> torch.Tensor:
@@ -112,32 +138,32 @@ def attention(q, k, v, heads):
 
 def resnet_block(x, temb_silu, sd, prefix, cfg: UNetConfig):
     """`unet.cu:537-663`."""
-    h = F.silu(group_norm(x, sd, prefix + "norm1", cfg.groups, 1e-5))
+    h = _st(F.silu(group_norm(x, sd, prefix + "norm1", cfg.groups, 1e-5)))
     h = conv(h, sd, prefix + "conv1")
-    h = h + linear(temb_silu, sd, prefix + "time_emb_proj")[:, :, None, None]
-    h = F.silu(group_norm(h, sd, prefix + "norm2", cfg.groups, 1e-5))
+    h = _st(h + linear(temb_silu, sd, prefix + "time_emb_proj")[:, :, None, None])
+    h = _st(F.silu(group_norm(h, sd, prefix + "norm2", cfg.groups, 1e-5)))
     h = conv(h, sd, prefix + "conv2")
     if (prefix + "conv_shortcut.weight") in sd:
         x = conv(x, sd, prefix + "conv_shortcut", padding=0)
-    return x + h
+    return _st(x + h)
 
 
 def transformer_block(x, ctx, sd, p, heads):
     """`unet.cu:677-797`: x [B, S, C]."""
     n = layer_norm(x, sd, p + "norm1")
-    q = linear(n, sd, p + "attn1.to_q", bias=False)
-    k = linear(n, sd, p + "attn1.to_k", bias=False)
-    v = linear(n, sd, p + "attn1.to_v", bias=False)
-    x = x + linear(attention(q, k, v, heads), sd, p + "attn1.to_out.0")
+    q = _st(linear(n, sd, p + "attn1.to_q", bias=False))
+    k = _st(linear(n, sd, p + "attn1.to_k", bias=False))
+    v = _st(linear(n, sd, p + "attn1.to_v", bias=False))
+    x = _st(x + linear(_st(attention(q, k, v, heads)), sd, p + "attn1.to_out.0"))
     n = layer_norm(x, sd, p + "norm2")
-    q = linear(n, sd, p + "attn2.to_q", bias=False)
-    k = linear(ctx, sd, p + "attn2.to_k", bias=False)
-    v = linear(ctx, sd, p + "attn2.to_v", bias=False)
-    x = x + linear(attention(q, k, v, heads), sd, p + "attn2.to_out.0")
+    q = _st(linear(n, sd, p + "attn2.to_q", bias=False))
+    k = _st(linear(ctx, sd, p + "attn2.to_k", bias=False))
+    v = _st(linear(ctx, sd, p + "attn2.to_v", bias=False))
+    x = _st(x + linear(_st(attention(q, k, v, heads)), sd, p + "attn2.to_out.0"))
     n = layer_norm(x, sd, p + "norm3")
     h = linear(n, sd, p + "ff.net.0.proj")
     hid, gate = h.chunk(2, dim=-1)
-    x = x + linear(hid * F.gelu(gate), sd, p + "ff.net.2")
+    x = _st(x + linear(_st(hid * F.gelu(gate)), sd, p + "ff.net.2"))
     return x
 
 
@@ -145,23 +171,23 @@ def transformer2d(x, ctx, sd, prefix, layers, cfg: UNetConfig):
     """`unet.cu:810-858`: GN(eps 1e-6) -> proj_in -> blocks -> proj_out -> + residual."""
     B, C, H, W = x.shape
     heads = C // cfg.head_dim
-    h = group_norm(x, sd, prefix + "norm", cfg.groups, 1e-6)
+    h = _st(group_norm(x, sd, prefix + "norm", cfg.groups, 1e-6))
     h = h.permute(0, 2, 3, 1).reshape(B, H * W, C)
-    h = linear(h, sd, prefix + "proj_in")
+    h = _st(linear(h, sd, prefix + "proj_in"))
     for l in range(layers):
         h = transformer_block(h, ctx, sd, f"{prefix}transformer_blocks.{l}.", heads)
     h = linear(h, sd, prefix + "proj_out")
     h = h.reshape(B, H, W, C).permute(0, 3, 1, 2)
-    return x + h
+    return _st(x + h)
 
 
 def downsample(x, sd, prefix):
-    return conv(x, sd, prefix + "conv", stride=2, padding=1)
+    return _st(conv(x, sd, prefix + "conv", stride=2, padding=1))
 
 
 def upsample(x, sd, prefix):
     x = F.interpolate(x, scale_factor=2.0, mode="nearest")
-    return conv(x, sd, prefix + "conv")
+    return _st(conv(x, sd, prefix + "conv"))
 
 
 # ---------------------------------------------------------------------------- embeddings
@@ -194,7 +220,7 @@ def unet_forward(sd, latent, timestep, ehs, text_embeds, time_ids, cfg: UNetConf
     ctx = ehs.float()
     temb = tap("temb_final", time_embeddings(sd, timestep, text_embeds, time_ids, cfg))
     ts = F.silu(temb)
-    x = tap("conv_in_out", conv(latent.float(), sd, "conv_in"))
+    x = tap("conv_in_out", _st(conv(latent.float(), sd, "conv_in")))
     skips = [x]
     # down 0
     for r in range(2):
@@ -231,7 +257,7 @@ def unet_forward(sd, latent, timestep, ehs, text_embeds, time_ids, cfg: UNetConf
         if u < 2:
             x = upsample(x, sd, f"up_blocks.{u}.upsamplers.0.")
         tap(f"up_block_{u}_out", x)
-    h = F.silu(group_norm(x, sd, "conv_norm_out", cfg.groups, 1e-5))
+    h = _st(F.silu(group_norm(x, sd, "conv_norm_out", cfg.groups, 1e-5)))
     out = conv(h, sd, "conv_out")
     return tap("noise_pred", out)
 

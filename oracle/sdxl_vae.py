@@ -29,6 +29,29 @@ GROUPS = 32
 EPS = 1e-6
 
 
+_FP16_STORAGE = [False]
+
+
+class fp16_storage:
+    """Context manager: while active, the oracle rounds to fp16 every tensor that an fp16-storage
+    decoder writes — the normalised input of every convolution, the mid attention's q / k / v and
+    output, and the residual stream up to up_blocks[1] (after it the reference, and this
+    library, carry fp32, vae_decode.cu:9-20) — and computes on in fp32.  Its difference from the
+    plain fp32 oracle is the error fp16 storage alone costs."""
+
+    def __enter__(self):
+        _FP16_STORAGE[0] = True
+        return self
+
+    def __exit__(self, *exc):
+        _FP16_STORAGE[0] = False
+        return False
+
+
+def _st(t, on=True):
+    return t.half().float() if (_FP16_STORAGE[0] and on) else t
+
+
 def _conv(x, sd, name, padding=1):
     return F.conv2d(x, sd[name + ".weight"].float(), sd[name + ".bias"].float(), padding=padding)
 
@@ -37,12 +60,13 @@ def _gn(x, sd, name):
     return F.group_norm(x, GROUPS, sd[name + ".weight"].float(), sd[name + ".bias"].float(), EPS)
 
 
-def resnet(x, sd, p):
-    h = _conv(F.silu(_gn(x, sd, p + "norm1")), sd, p + "conv1")
-    h = _conv(F.silu(_gn(h, sd, p + "norm2")), sd, p + "conv2")
+def resnet(x, sd, p, carry16=False):
+    h = _conv(_st(F.silu(_gn(x, sd, p + "norm1"))), sd, p + "conv1")
+    h = _st(h, carry16)
+    h = _conv(_st(F.silu(_gn(h, sd, p + "norm2"))), sd, p + "conv2")
     if (p + "conv_shortcut.weight") in sd:
-        x = _conv(x, sd, p + "conv_shortcut", padding=0)
-    return x + h
+        x = _conv(_st(x), sd, p + "conv_shortcut", padding=0)
+    return _st(x + h, carry16)
 
 
 def mid_attention(q, k, v):
@@ -53,12 +77,12 @@ def mid_attention(q, k, v):
 
 def attn_block(x, sd, p):
     B, C, H, W = x.shape
-    h = _gn(x, sd, p + "group_norm").permute(0, 2, 3, 1).reshape(B, H * W, C)
+    h = _st(_gn(x, sd, p + "group_norm")).permute(0, 2, 3, 1).reshape(B, H * W, C)
     lin = lambda t, n: F.linear(t, sd[p + n + ".weight"].float(), sd[p + n + ".bias"].float())
-    q, k, v = lin(h, "to_q"), lin(h, "to_k"), lin(h, "to_v")
-    o = mid_attention(q, k, v)
+    q, k, v = _st(lin(h, "to_q")), _st(lin(h, "to_k")), _st(lin(h, "to_v"))
+    o = _st(mid_attention(q, k, v))
     o = lin(o, "to_out.0").reshape(B, H, W, C).permute(0, 3, 1, 2)
-    return x + o
+    return _st(x + o)
 
 
 def vae_decode(sd, latent, hook=None):
@@ -68,20 +92,21 @@ def vae_decode(sd, latent, hook=None):
             hook(n, t)
         return t
 
-    x = _conv(latent.float(), sd, "post_quant_conv", padding=0)
-    x = _conv(x, sd, "decoder.conv_in")
-    x = resnet(x, sd, "decoder.mid_block.resnets.0.")
+    x = _st(_conv(latent.float(), sd, "post_quant_conv", padding=0))
+    x = _st(_conv(x, sd, "decoder.conv_in"))
+    x = resnet(x, sd, "decoder.mid_block.resnets.0.", True)
     x = attn_block(x, sd, "decoder.mid_block.attentions.0.")
-    x = resnet(x, sd, "decoder.mid_block.resnets.1.")
+    x = resnet(x, sd, "decoder.mid_block.resnets.1.", True)
     tap("mid_block_out", x)
     for u in range(4):
         for r in range(3):
-            x = resnet(x, sd, f"decoder.up_blocks.{u}.resnets.{r}.")
+            x = resnet(x, sd, f"decoder.up_blocks.{u}.resnets.{r}.", u < 2)
         if u < 3:
             x = F.interpolate(x, scale_factor=2.0, mode="nearest")
-            x = _conv(x, sd, f"decoder.up_blocks.{u}.upsamplers.0.conv")
+            x = _conv(_st(x), sd, f"decoder.up_blocks.{u}.upsamplers.0.conv")
+            x = _st(x, u < 1)
         tap(f"up_block_{u}_out", x)
-    x = F.silu(_gn(x, sd, "decoder.conv_norm_out"))
+    x = _st(F.silu(_gn(x, sd, "decoder.conv_norm_out")))
     return tap("image", _conv(x, sd, "decoder.conv_out"))
 
 

@@ -27,3 +27,16 @@ def allclose_k(got: torch.Tensor, ref: torch.Tensor, K: int) -> bool:
     got = got.detach().float().cpu()
     ref = ref.detach().float().cpu()
     return bool(((got - ref).abs() <= atol + rtol * ref.abs()).all())
+
+
+STAGE_BAR = 2e-3        # north-star per-layer bar (max|err| / max|ref|)
+STORAGE_FACTOR = 1.5    # allowance over the fp16-storage oracle's own error at a stage
+
+
+def stage_bound(err16: float) -> float:
+    """Bound on a stage's max|err|/max|ref| against the fp32 oracle: the north-star 2e-3, or,
+    where the fp16-storage oracle (the same fp32 oracle rounding every stored activation to
+    fp16, as an fp16-storage implementation such as the reference does) is itself further than
+    that from fp32, 1.5x that storage error — an fp16-storage pipeline cannot be closer to fp32
+    than fp16 storage allows."""
+    return max(STAGE_BAR, STORAGE_FACTOR * err16)

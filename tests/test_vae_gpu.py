@@ -9,12 +9,12 @@ import pytest
 import torch
 
 from oracle.metrics import max_rel_err, ssim_uniform
-from oracle.sdxl_vae import init_weights, vae_decode
+from oracle.sdxl_vae import fp16_storage, init_weights, vae_decode
+from tests.helpers import stage_bound
 
 pytestmark = pytest.mark.gpu
 
 STAGES = ["mid_block_out", "up_block_0_out", "up_block_1_out", "up_block_2_out", "up_block_3_out"]
-STAGE_TOL = 1e-2     # per-stage max|err| / max|ref| after a chain of fp16-operand convolutions
 SSIM_BAR = 0.9999
 
 
@@ -35,23 +35,36 @@ def _decode(sd, lat, graph=True):
 
 
 def _oracle(sd, lat):
-    ref = {}
+    """fp32 oracle stages, with the fp16-storage variant's stages under key "ref16"."""
+    ref, ref16 = {}, {}
     with torch.no_grad():
         sdf = {k: v.float() for k, v in sd.items()}
         vae_decode(sdf, lat, hook=lambda n, t: ref.__setitem__(n, t))
+        with fp16_storage():
+            vae_decode(sdf, lat, hook=lambda n, t: ref16.__setitem__(n, t))
+    ref["ref16"] = ref16
     return ref
 
 
 def _check(got, ref):
-    errs = {n: max_rel_err(got[n].numpy(), ref[n].numpy()) for n in got}
-    for n, e in errs.items():
-        print(f"{n:>16s}  max_rel_err {e:.2e}")
+    """Per stage: the GPU against the fp32 oracle within the north-star 2e-3, or within 1.5x the
+    fp16-storage oracle's own distance from fp32 where that is larger; image SSIM >= 0.9999."""
+    ref16 = ref.pop("ref16")
+    errs = {}
+    for n in got:
+        e = max_rel_err(got[n].numpy(), ref[n].numpy())
+        e16 = max_rel_err(ref16[n].numpy(), ref[n].numpy())
+        eg16 = max_rel_err(got[n].numpy(), ref16[n].numpy())
+        errs[n] = e
+        print(f"{n:>16s}  gpu/fp32 {e:.2e}   fp16-storage/fp32 {e16:.2e}   gpu/fp16-storage "
+              f"{eg16:.2e}   bound {stage_bound(e16):.2e}")
     s = ssim_uniform(got["image"].numpy(), ref["image"].numpy())
     print(f"image SSIM {s:.7f}")
     assert torch.isfinite(got["image"]).all()
     assert s >= SSIM_BAR, s
-    for n, e in errs.items():
-        assert e < STAGE_TOL, (n, e)
+    for n in got:
+        e16 = max_rel_err(ref16[n].numpy(), ref[n].numpy())
+        assert errs[n] <= stage_bound(e16), (n, errs[n], e16)
     return errs, s
 
 
@@ -62,6 +75,16 @@ def test_vae_decode_parity():
     _check(got, _oracle(sd, lat))
     info = dec.info()
     assert info["launches_per_decode"] > 0 and info["arena_bytes"] > 0
+    dec.close()
+
+
+def test_vae_decode_1024_image_parity():
+    """The benchmarked configuration itself: a 128x128 latent decoded to a 1024x1024 image, so
+    the mid attention runs over 16384 tokens at head dim 512."""
+    sd = init_weights(seed=9)
+    lat = _latent(1, 128, 128, seed=8)
+    dec, got = _decode(sd, lat)
+    _check(got, _oracle(sd, lat))
     dec.close()
 
 
