@@ -178,6 +178,45 @@ def cpu_oracle_step(sd_gpu, host_inputs, timestep=999.0):
     return dt, torch.get_num_threads()
 
 
+def reference_gpu_leg(sd_gpu, dev_inputs, out, our_value, e0, e1, stream, steps=5, warmup=2):
+    """Steps/s of the reference's own CUDA UNet (launch_unet_batched, B=2, default and FAST
+    modes) recompiled for sm_100a, on the same weights and device-resident inputs, timed with
+    CUDA events over back-to-back steps on the default stream it launches on."""
+    import torch
+    try:
+        from baseline import ref_gpu
+        if not ref_gpu.available():
+            return {"unavailable": "baseline/_ref_gpu/libref_sdxl_gpu.so not built (no reference tree)"}
+        ref = ref_gpu.RefUNet({k: v.cpu() for k, v in sd_gpu.items()})
+    except Exception as exc:  # pragma: no cover - reported, not fatal
+        return {"unavailable": f"{type(exc).__name__}: {exc}"}
+    lat, ehs, te, tid = dev_inputs
+    res = {}
+    try:
+        for mode, fast in (("default", False), ("fast", True)):
+            for i in range(warmup):
+                ref.forward(lat, 999.0 - 50.0 * i, ehs, te, tid, out, attn_fast=fast, epilogue=fast)
+            torch.cuda.synchronize()
+            e0.record(stream)
+            for i in range(steps):
+                ref.forward(lat, 999.0 - 50.0 * i, ehs, te, tid, out, attn_fast=fast,
+                            epilogue=fast, sync=False)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / steps
+            res[mode] = {"ms_per_step": ms, "steps_per_s": 1000.0 / ms}
+    except Exception as exc:  # pragma: no cover
+        res["error"] = f"{type(exc).__name__}: {exc}"
+    finally:
+        ref.close()
+    best = max((v["steps_per_s"] for k, v in res.items() if isinstance(v, dict)), default=None)
+    return {"what": "the reference's own CUDA UNet (src/infer/unet.cu launch_unet_batched with its "
+                    "kernels and cuBLAS), unchanged, recompiled for sm_100a; same weights and inputs",
+            "steps": steps, "warmup": warmup, **res,
+            "ours_over_reference_fast": (our_value / res["fast"]["steps_per_s"]) if "fast" in res else None,
+            "ours_over_reference_best": (our_value / best) if best else None}
+
+
 def run_reference(args, ws, rank):
     """The reference arm: the CPU fp32 restatement of the step on all host cores, with its
     weights drawn on the CPU by the oracle's own initialiser.  Nothing of this library (no
@@ -356,6 +395,13 @@ def main():
                "image_finite": bool(torch.isfinite(img).all().item())}
     vae.close()
 
+    # ---------------------------------------------------------------- reference GPU comparator
+    # the reference's own CUDA UNet (src/infer/unet.cu + its kernels and cuBLAS), unchanged and
+    # recompiled for sm_100a, on the same weights and inputs (rank 0, N = 1 only)
+    ref_gpu_line = None
+    if keep_sd:
+        ref_gpu_line = reference_gpu_leg(sd, (lat, ehs, te, tid), out, value, e0, e1, stream)
+
     # ---------------------------------------------------------------- CPU baseline (rank 0, N=1)
     cpu = None
     if keep_sd:
@@ -381,6 +427,7 @@ def main():
                     "d2h_bytes_per_step": d2h},
             "roofline": roofline,
             "cpu_baseline": cpu,
+            "reference_gpu": ref_gpu_line,
             "clocks": clocks,
             "gpu_launches": args.steps * (info["launches_per_step"] + 1),
             "output_finite": finite,

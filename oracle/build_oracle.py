@@ -29,7 +29,8 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 BUILD = HERE / "_build"
 REF_OUT = HERE / "_ref"
-REFERENCE = Path(os.environ.get("DOLLAMA_REFERENCE", "/root/reference"))
+# the reference checkout: $DOLLAMA_REFERENCE, else a `reference` directory beside this repository
+REFERENCE = Path(os.environ.get("DOLLAMA_REFERENCE", str(HERE.parent.parent / "reference")))
 
 
 def _run(cmd):

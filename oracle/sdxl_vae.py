@@ -52,6 +52,14 @@ def _st(t, on=True):
     return t.half().float() if (_FP16_STORAGE[0] and on) else t
 
 
+def _operand(t, carry16):
+    """A GEMM operand: fp16 as stored, or, for an fp32 carry, fp16(t / 64) * 64 (how an fp32
+    carry enters an fp16 GEMM without leaving the fp16 range)."""
+    if not _FP16_STORAGE[0]:
+        return t
+    return t.half().float() if carry16 else (t / 64.0).half().float() * 64.0
+
+
 def _conv(x, sd, name, padding=1):
     return F.conv2d(x, sd[name + ".weight"].float(), sd[name + ".bias"].float(), padding=padding)
 
@@ -60,12 +68,15 @@ def _gn(x, sd, name):
     return F.group_norm(x, GROUPS, sd[name + ".weight"].float(), sd[name + ".bias"].float(), EPS)
 
 
-def resnet(x, sd, p, carry16=False):
+def resnet(x, sd, p, carry16=False, in16=None):
+    """carry16: this block's outputs are stored fp16 (else fp32 carries); in16: its input is
+    fp16 (defaults to carry16)."""
+    in16 = carry16 if in16 is None else in16
     h = _conv(_st(F.silu(_gn(x, sd, p + "norm1"))), sd, p + "conv1")
     h = _st(h, carry16)
     h = _conv(_st(F.silu(_gn(h, sd, p + "norm2"))), sd, p + "conv2")
     if (p + "conv_shortcut.weight") in sd:
-        x = _conv(_st(x), sd, p + "conv_shortcut", padding=0)
+        x = _conv(_operand(x, in16), sd, p + "conv_shortcut", padding=0)
     return _st(x + h, carry16)
 
 
@@ -100,11 +111,11 @@ def vae_decode(sd, latent, hook=None):
     tap("mid_block_out", x)
     for u in range(4):
         for r in range(3):
-            x = resnet(x, sd, f"decoder.up_blocks.{u}.resnets.{r}.", u < 2)
+            x = resnet(x, sd, f"decoder.up_blocks.{u}.resnets.{r}.", u < 2, u < 2 or (u == 2 and r == 0))
         if u < 3:
             x = F.interpolate(x, scale_factor=2.0, mode="nearest")
-            x = _conv(_st(x), sd, f"decoder.up_blocks.{u}.upsamplers.0.conv")
-            x = _st(x, u < 1)
+            x = _conv(_operand(x, u < 2), sd, f"decoder.up_blocks.{u}.upsamplers.0.conv")
+            x = _st(x, u < 2)
         tap(f"up_block_{u}_out", x)
     x = _st(F.silu(_gn(x, sd, "decoder.conv_norm_out")))
     return tap("image", _conv(x, sd, "decoder.conv_out"))
