@@ -75,6 +75,13 @@ _SIGS = {
     "dlm_group_norm_nhwc": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_void_p,
                                     c_void_p, c_float, c_int, c_int, c_void_p, c_void_p, c_size_t,
                                     c_void_p]),
+    "dlm_group_norm_nchw_scratch_bytes": (c_size_t, [c_int, c_int]),
+    "dlm_group_norm_nchw": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
+                                    c_int, c_int, c_float, c_int, c_void_p, c_size_t, c_void_p]),
+    "dlm_conv2d_direct_nchw": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int,
+                                       c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
+                                       c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p]),
+    "dlm_conv2d_uses_gemm_bias_path": (c_int, [c_int] * 13),
     "dlm_group_norm_nhwc_noalloc_capacity": (c_size_t, []),
     "dlm_group_norm_nhwc_noalloc": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int,
                                             c_void_p, c_void_p, c_float, c_int, c_int, c_void_p,

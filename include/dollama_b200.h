@@ -221,6 +221,34 @@ int dlm_group_norm_nhwc_noalloc(const void* x1, int C1, const void* x2, int C2, 
                                 const void* gamma, const void* beta, float eps, int groups,
                                 int silu, void* out, void* stream);
 
+/* GroupNorm over NCHW fp16 [N, C, H, W] (reference src/kernels/groupnorm.cuh:51-108:
+ * launch_group_norm, launch_group_norm_mb and, with silu = 1, launch_group_norm_silu, whose SiLU
+ * follows an fp16 rounding of the normalised value).  in == out allowed.  Scratch: any content,
+ * dlm_group_norm_nchw_scratch_bytes(N, groups) bytes (the call zeroes its counters on `stream`).
+ * Statistics in fp32 slices around a shift, folded in fixed order in fp64: deterministic. */
+size_t dlm_group_norm_nchw_scratch_bytes(int N, int groups);
+int dlm_group_norm_nchw(const void* in, const void* gamma, const void* beta, void* out, int N,
+                        int C, int H, int W, int groups, float eps, int silu, void* scratch,
+                        size_t scratch_bytes, void* stream);
+
+/* Direct NCHW convolution, one thread per output value, fp32 accumulation with the bias folded in
+ * and one rounding at the store (reference src/kernels/conv2d.cuh:65-69 launch_conv2d_direct;
+ * with in_f32 = out_f32 = 1 it serves launch_conv2d_f32_gemm, :79-82).  Any kernel size, stride,
+ * padding and dilation; weight [Cout, Cin, KH, KW] fp16; bias fp16 [Cout] or NULL; Hout / Wout
+ * must match the geometry. */
+int dlm_conv2d_direct_nchw(const void* in, int in_f32, const void* weight, const void* bias,
+                           void* out, int out_f32, int N, int Cin, int H, int W, int Cout, int KH,
+                           int KW, int Hout, int Wout, int stride_h, int stride_w, int pad_h,
+                           int pad_w, int dil_h, int dil_w, void* stream);
+
+/* 1 when a convolution of this shape runs on the implicit-GEMM tensor-core path (3x3 s1 / s2
+ * pad 1 or 1x1, Cin % 64 == 0, Cout % 32 == 0, 128-pixel output tiles), 0 otherwise (reference
+ * src/kernels/conv2d.cuh:54-56 conv2d_uses_gemm_bias_path: that path rounds the bias-free
+ * convolution once, so the bias may be added in a later pass). */
+int dlm_conv2d_uses_gemm_bias_path(int N, int Cin, int H, int W, int Cout, int KH, int KW,
+                                   int stride_h, int stride_w, int pad_h, int pad_w, int dil_h,
+                                   int dil_w);
+
 /* LayerNorm over the last dim of [rows, C] (reference src/kernels/layernorm.cuh:51-57);
  * gamma / beta may be NULL.  C % 8 == 0, C <= 2048. */
 int dlm_launch_layer_norm(const void* in, const void* gamma, const void* beta, void* out, int rows,
