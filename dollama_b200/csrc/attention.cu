@@ -791,6 +791,13 @@ int dlm_launch_attention(const void* q, const void* k, const void* v, void* out,
     t.sb = static_cast<long long>(H) * S * Dh;
     return t;
   };
+  if (Dh != 64) {  // wide heads (the VAE's Dh = 512)
+    dlm::AttnWideOp op;
+    int rc = dlm::attn_wide_plan(&op, B, H, Sq, Sk, Dh, scale, bhsd(q, Sq), bhsd(k, Sk),
+                                 bhsd(v, Sk), bhsd(out, Sq));
+    if (rc != DLM_OK) return rc;
+    return dlm::attn_wide_launch(op, static_cast<cudaStream_t>(stream));
+  }
   dlm::AttnOp op;
   int rc = dlm::attn_plan(&op, B, H, Sq, Sk, Dh, scale, bhsd(q, Sq), bhsd(k, Sk), bhsd(v, Sk),
                           bhsd(out, Sq));
@@ -814,6 +821,13 @@ int dlm_launch_attention_ws(const void* q, const void* k, const void* v, void* o
     t.sb = static_cast<long long>(H) * S * Dh;
     return t;
   };
+  if (Dh != 64) {  // wide heads: no stream-K, the workspace is not used
+    dlm::AttnWideOp op;
+    int rc = dlm::attn_wide_plan(&op, B, H, Sq, Sk, Dh, scale, bhsd(q, Sq), bhsd(k, Sk),
+                                 bhsd(v, Sk), bhsd(out, Sq));
+    if (rc != DLM_OK) return rc;
+    return dlm::attn_wide_launch(op, static_cast<cudaStream_t>(stream));
+  }
   dlm::AttnOp op;
   int rc = dlm::attn_plan(&op, B, H, Sq, Sk, Dh, scale, bhsd(q, Sq), bhsd(k, Sk), bhsd(v, Sk),
                           bhsd(out, Sq), workspace, workspace_bytes);
@@ -833,6 +847,13 @@ int dlm_attention_tokens(const void* q, int ldq, const void* k, int ldk, const v
     t.sb = static_cast<long long>(S) * ld;
     return t;
   };
+  if (Dh != 64) {  // wide heads
+    dlm::AttnWideOp op;
+    int rc = dlm::attn_wide_plan(&op, B, H, Sq, Sk, Dh, scale, tok(q, ldq, Sq), tok(k, ldk, Sk),
+                                 tok(v, ldv, Sk), tok(out, ldo, Sq));
+    if (rc != DLM_OK) return rc;
+    return dlm::attn_wide_launch(op, static_cast<cudaStream_t>(stream));
+  }
   dlm::AttnOp op;
   int rc = dlm::attn_plan(&op, B, H, Sq, Sk, Dh, scale, tok(q, ldq, Sq), tok(k, ldk, Sk),
                           tok(v, ldv, Sk), tok(out, ldo, Sq));

@@ -8,7 +8,7 @@
 
 namespace dlm {
 
-// Strided view of a [B, H, S, 64] tensor: element (b, h, s, d) is at ptr + b*sb + h*sh + s*ss + d.
+// Strided view of a [B, H, S, Dh] tensor: element (b, h, s, d) is at ptr + b*sb + h*sh + s*ss + d.
 struct AttnTensor {
   const __half* ptr = nullptr;
   long long sb = 0, sh = 0, ss = 0;
@@ -48,5 +48,27 @@ size_t attn_workspace_bytes(int B, int H, int Sq);
 size_t attn_counter_bytes(int B, int H, int Sq);
 int attn_launch(const AttnOp& op, cudaStream_t s);
 int attn_prepare_kernels();
+
+// Wide heads (attention_wide.cu): head_dim a multiple of 64 in [128, 512], one CTA per (batch,
+// head, 128-query tile, output slice of dv = Dh or Dh / 2 columns).
+struct AttnWideParams {
+  int B, H, Sq, Sk, Dh;
+  int dv, nsplit;      // output columns per CTA, Dh / dv
+  float scale_log2;    // softmax scale * log2(e)
+  __half* out;
+  long long o_sb, o_sh, o_ss;
+  int* status;
+};
+
+struct AttnWideOp {
+  CUtensorMap tmQ, tmK, tmV;
+  AttnWideParams p;
+  int grid = 0;
+};
+
+int attn_wide_plan(AttnWideOp* op, int B, int H, int Sq, int Sk, int Dh, float scale,
+                   const AttnTensor& q, const AttnTensor& k, const AttnTensor& v,
+                   const AttnTensor& o);
+int attn_wide_launch(const AttnWideOp& op, cudaStream_t s);
 
 }  // namespace dlm

@@ -474,11 +474,55 @@ int dlm_gemm_fp16_ws(const void* A, int lda, const void* W, void* C, int ldc, in
   return dlm::gemm_launch(op, static_cast<cudaStream_t>(stream));
 }
 
+namespace {
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// Any shape and orientation: the operands are gathered (transposed where needed) into
+// zero-padded [M, Kp] / [Np, Kp] stream-ordered scratch (Kp = K rounded up to 8, Np = N rounded
+// up to 32), the product goes to [M, Np] scratch (seeded from C when beta != 0) and its first N
+// columns are copied back.
+int gemm_fp16_padded(const __half* A, const __half* B, __half* C, int M, int N, int K, float alpha,
+                     float beta, int transA, int transB, cudaStream_t s) {
+  const int Kp = (K + 7) / 8 * 8, Np = (N + 31) / 32 * 32;
+  const size_t na = static_cast<size_t>(M) * Kp, nb = static_cast<size_t>(Np) * Kp,
+               nc = static_cast<size_t>(M) * Np;
+  __half* buf = nullptr;
+  DLM_CHECK_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&buf), (na + nb + nc) * 2 + 512, s));
+  __half* a = buf;
+  __half* b = a + (na + 127) / 128 * 128;
+  __half* c = b + (nb + 127) / 128 * 128;
+  int rc = dlm::gather_pad(A, transA ? 1 : K, transA ? M : 1, M, K, a, M, Kp, s);
+  if (rc == DLM_OK) rc = dlm::gather_pad(B, transB ? K : 1, transB ? 1 : N, N, K, b, Np, Kp, s);
+  dlm::GemmEpilogue e;
+  e.alpha = alpha;
+  if (rc == DLM_OK && beta != 0.0f) {
+    rc = dlm::gather_pad(C, N, 1, M, N, c, M, Np, s);
+    e.flags |= DLM_EPI_RESID;
+    e.resid = c;
+    e.ldr = Np;
+    e.resid_scale = beta;
+  }
+  dlm::GemmOp op;
+  if (rc == DLM_OK) rc = dlm::gemm_plan_dense(&op, a, Kp, b, M, Np, Kp, c, Np, e);
+  if (rc == DLM_OK) rc = dlm::gemm_launch(op, s);
+  if (rc == DLM_OK) rc = dlm::gather_pad(c, Np, 1, M, N, C, M, N, s);
+  cudaFreeAsync(buf, s);
+  return rc;
+}
+
+}  // namespace
+
 int dlm_launch_gemm_fp16(const void* A, const void* B, void* C, int M, int N, int K, float alpha,
                          float beta, int transA, int transB, void* stream) {
   if (M == 0 || N == 0 || K == 0) return DLM_OK;
   DLM_REQUIRE(A && B && C, DLM_ERR_INVALID, "dlm_launch_gemm_fp16: null pointer");
+  DLM_REQUIRE(M > 0 && N > 0 && K > 0, DLM_ERR_INVALID, "dlm_launch_gemm_fp16: negative size");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (K % 8 != 0 || N % 32 != 0 || !aligned16(A) || !aligned16(B) || !aligned16(C) ||
+      (transA && M % 8 != 0) || (!transB && N % 8 != 0))
+    return gemm_fp16_padded(static_cast<const __half*>(A), static_cast<const __half*>(B),
+                            static_cast<__half*>(C), M, N, K, alpha, beta, transA, transB, s);
   // The tensor-core kernel reads A as [M, K] and B as [N, K] (both K-major); the other
   // orientations are transposed once into stream-ordered scratch.
   __half* at = nullptr;

@@ -171,6 +171,19 @@ __global__ void transpose_strided_kernel(const __half* __restrict__ in, int ld, 
   }
 }
 
+// dst[r * cols_p + c] = src[r * rs + c * cs] for r < rows, c < cols; zero in the padding
+// (rows_p x cols_p); any strides, so it also transposes
+__global__ void gather_pad_kernel(const __half* __restrict__ src, long long rs, long long cs,
+                                  int rows, int cols, __half* __restrict__ dst, int rows_p,
+                                  int cols_p) {
+  const long long total = static_cast<long long>(rows_p) * cols_p;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int r = static_cast<int>(i / cols_p), c = static_cast<int>(i % cols_p);
+    dst[i] = (r < rows && c < cols) ? src[r * rs + c * cs] : __float2half(0.0f);
+  }
+}
+
 // out = fp16(in * scale), 8 elements per thread (n % 8 == 0)
 __global__ void f32_to_f16_scaled_kernel(const float4* __restrict__ in, uint4* __restrict__ out,
                                          size_t n8, float scale) {
@@ -358,6 +371,16 @@ int nhwc_to_nchw_narrow(const __half* in, int ld, __half* out, int B, int Cout, 
 int transpose_strided(const __half* in, int ld, __half* out, int S, int C, cudaStream_t s) {
   dim3 grid((S + 31) / 32, (C + 31) / 32), block(32, 8);
   transpose_strided_kernel<<<grid, block, 0, s>>>(in, ld, out, S, C);
+  DLM_CHECK_CUDA(cudaGetLastError());
+  return DLM_OK;
+}
+
+int gather_pad(const __half* src, long long rs, long long cs, int rows, int cols, __half* dst,
+               int rows_p, int cols_p, cudaStream_t s) {
+  const long long total = static_cast<long long>(rows_p) * cols_p;
+  if (total == 0) return DLM_OK;
+  gather_pad_kernel<<<grid_for(static_cast<size_t>(total), 256), 256, 0, s>>>(src, rs, cs, rows, cols,
+                                                                             dst, rows_p, cols_p);
   DLM_CHECK_CUDA(cudaGetLastError());
   return DLM_OK;
 }

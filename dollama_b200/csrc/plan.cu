@@ -21,6 +21,7 @@ void OpPlan::clear() {
   gemm_.clear();
   gemm_flops_.clear();
   attn_.clear();
+  attn_wide_.clear();
   gn_.clear();
   ln_.clear();
   custom_.clear();
@@ -35,6 +36,10 @@ void OpPlan::push_gemm(const GemmOp& g, double flops) {
 void OpPlan::push_attn(const AttnOp& a) {
   attn_.push_back(a);
   seq_.push_back({Kind::Attn, static_cast<int>(attn_.size() - 1)});
+}
+void OpPlan::push_attn_wide(const AttnWideOp& a) {
+  attn_wide_.push_back(a);
+  seq_.push_back({Kind::AttnWide, static_cast<int>(attn_wide_.size() - 1)});
 }
 void OpPlan::push_gn(const GnOp& g) {
   gn_.push_back(g);
@@ -60,6 +65,7 @@ int OpPlan::launch(const Ref& o, cudaStream_t s) {
   switch (o.kind) {
     case Kind::Gemm: return gemm_launch(gemm_[o.idx], s);
     case Kind::Attn: return attn_launch(attn_[o.idx], s);
+    case Kind::AttnWide: return attn_wide_launch(attn_wide_[o.idx], s);
     case Kind::Gn: return gn_launch(gn_[o.idx], s);
     case Kind::Ln: {
       const LnArgs& l = ln_[o.idx];
@@ -107,6 +113,11 @@ int OpPlan::op_class(const Ref& o, double* f) const {
       *f = 4.0 * p.B * p.H * static_cast<double>(p.Sq) * p.Sk * 64;
       return 1;
     }
+    case Kind::AttnWide: {
+      const AttnWideParams& p = attn_wide_[o.idx].p;
+      *f = 4.0 * p.B * p.H * static_cast<double>(p.Sq) * p.Sk * p.Dh;
+      return 1;
+    }
     case Kind::Gn: *f = 0.0; return 2;
     case Kind::Ln: *f = 0.0; return 3;
     case Kind::Custom: *f = custom_flops_[o.idx]; return 4;
@@ -143,6 +154,9 @@ int OpPlan::write_table(cudaStream_t s, const char* path) {
     } else if (o.kind == Kind::Attn) {
       const AttnParams& a = attn_[o.idx].p;
       std::fprintf(table, "attn,%d,%d,%d,%d,0,0,0,%.2f\n", a.B * a.H, a.Sq, a.Sk, 64, 1000.0 * t);
+    } else if (o.kind == Kind::AttnWide) {
+      const AttnWideParams& a = attn_wide_[o.idx].p;
+      std::fprintf(table, "attn,%d,%d,%d,%d,0,0,0,%.2f\n", a.B * a.H, a.Sq, a.Sk, a.Dh, 1000.0 * t);
     } else {
       std::fprintf(table, "%s,0,0,0,0,0,0,0,%.2f\n",
                    o.kind == Kind::Gn ? "groupnorm" : o.kind == Kind::Ln ? "layernorm" : "other",

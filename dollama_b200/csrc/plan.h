@@ -59,6 +59,7 @@ class OpPlan {
   void clear();  // drops every op and the instantiated graph
   void push_gemm(const GemmOp& g, double flops = -1.0);
   void push_attn(const AttnOp& a);
+  void push_attn_wide(const AttnWideOp& a);
   void push_gn(const GnOp& g);
   void push_ln(const LnArgs& l);
   void push_custom(std::function<int(cudaStream_t)> f, double flops = 0.0);
@@ -75,7 +76,7 @@ class OpPlan {
   size_t size() const { return seq_.size(); }
 
  private:
-  enum class Kind { Gemm, Attn, Gn, Ln, Custom };
+  enum class Kind { Gemm, Attn, AttnWide, Gn, Ln, Custom };
   struct Ref {
     Kind kind;
     int idx;
@@ -87,6 +88,7 @@ class OpPlan {
   std::vector<GemmOp> gemm_;
   std::vector<double> gemm_flops_;
   std::vector<AttnOp> attn_;
+  std::vector<AttnWideOp> attn_wide_;
   std::vector<GnOp> gn_;
   std::vector<LnArgs> ln_;
   std::vector<std::function<int(cudaStream_t)>> custom_;

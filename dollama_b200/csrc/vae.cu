@@ -18,9 +18,9 @@
 //     64 is restored exactly (a power of two) in the epilogue's alpha or in the packed shortcut
 //     weights.  fp16 operands carry the same 10-bit mantissa as the reference's default TF32
 //     GEMMs, with fp32 accumulation;
-//   * the mid-block attention (one head, Dh = 512, S = h*w tokens) runs as two tcgen05 GEMMs per
-//     image around a row softmax: scores = (Q K^T) / sqrt(512) stored fp16 [S, S], softmax in
-//     fp32 arithmetic in place, O = P V with V transposed once;
+//   * the mid-block attention (one head, Dh = 512, S = h*w tokens) is one wide-head flash
+//     attention launch over the batch (attention_wide.cu): fp32 online softmax, unnormalised fp16
+//     P, the row-sum division on the fp32 accumulator, no S x S scores in memory;
 //   * the whole decode is planned once per latent shape over one static arena and replays as one
 //     CUDA graph.
 #include <algorithm>
@@ -46,7 +46,6 @@ constexpr int kUpC[4] = {512, 512, 256, 128};
 constexpr int kOutPad = 32;   // conv_out's 3 output channels padded to one 32-column chunk
 constexpr float kEps = 1e-6f;
 constexpr float kCarryScale = 64.0f;
-constexpr int kMaxTokens = 32768;  // row softmax holds a score row in registers
 
 // w[r * ld + c] *= s for r < rows, c < cols (power-of-two scale: exact for normal fp16 values)
 __global__ void scale_block_kernel(__half* w, int rows, int cols, int ld, float s) {
@@ -376,24 +375,23 @@ int VAEModel::plan_attn(const std::string& p, const Act& x, int H, int Wd) {
     if (rc != DLM_OK) return rc;
     ops_.push_gemm(g);
   }
-  for (int b = 0; b < B_; ++b) {
-    const __half* q = qkv_ + static_cast<size_t>(b) * S * 3 * C;
-    GemmOp g;
-    GemmEpilogue e;
-    e.alpha = 1.0f / std::sqrt(static_cast<float>(C));
-    rc = gemm_plan_dense(&g, q, 3 * C, q + C, S, S, C, scores_, S, e, 0, 3 * C);
+  {
+    // one wide-head flash attention over the B images: q | k | v token-major [B*S, 3C] (one
+    // head of C = 512 columns), out [B*S, C]
+    auto tok = [&](const __half* ptr, long long ld) {
+      AttnTensor t;
+      t.ptr = ptr;
+      t.ss = ld;
+      t.sh = C;
+      t.sb = static_cast<long long>(S) * ld;
+      return t;
+    };
+    AttnWideOp a;
+    rc = attn_wide_plan(&a, B_, 1, S, S, C, 1.0f / std::sqrt(static_cast<float>(C)),
+                        tok(qkv_, 3 * C), tok(qkv_ + C, 3 * C), tok(qkv_ + 2 * C, 3 * C),
+                        tok(attn_o_, C));
     if (rc != DLM_OK) return rc;
-    ops_.push_gemm(g);
-    __half* sc = scores_;
-    ops_.push_custom([=](cudaStream_t s) { return softmax_rows_f16(sc, S, S, s); });
-    const __half* v = q + 2 * C;
-    __half* vt = vt_;
-    ops_.push_custom([=](cudaStream_t s) { return transpose_strided(v, 3 * C, vt, S, C, s); });
-    GemmOp g2;
-    rc = gemm_plan_dense(&g2, scores_, S, vt_, S, C, S, attn_o_ + static_cast<size_t>(b) * S * C, C,
-                         GemmEpilogue());
-    if (rc != DLM_OK) return rc;
-    ops_.push_gemm(g2);
+    ops_.push_attn_wide(a);
   }
   GemmOp g;
   GemmEpilogue e;
@@ -470,8 +468,6 @@ int VAEModel::build(bool dry) {
   upbuf_ = arena_.take<__half>(std::max({P[1] * kTop, P[2] * kTop, P[3] * kUpC[2]}));
   out32_ = arena_.take<__half>(P[3] * kOutPad);
   qkv_ = arena_.take<__half>(P[0] * 3 * kTop);
-  scores_ = arena_.take<__half>(static_cast<size_t>(S) * S);
-  vt_ = arena_.take<__half>(static_cast<size_t>(kTop) * S);
   attn_o_ = arena_.take<__half>(P[0] * kTop);
   gn_partial_cap_ = gn_partial_elems(B, Hs[3] * Ws[3]);
   gn_partials_ = arena_.take<float2>(gn_partial_cap_);
@@ -551,8 +547,6 @@ int VAEModel::plan(int B, int h, int w) {
   DLM_REQUIRE(tiles, DLM_ERR_INVALID,
               "vae: latent %dx%d: 128-pixel conv tiles need w %% 128 == 0, or w | 128 and (128 / w) | h",
               h, w);
-  DLM_REQUIRE(h * w <= kMaxTokens, DLM_ERR_INVALID, "vae: latent %dx%d exceeds %d attention tokens",
-              h, w, kMaxTokens);
   B_ = B;
   h_ = h;
   w_lat_ = w;

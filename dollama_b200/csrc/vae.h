@@ -78,7 +78,7 @@ class VAEModel {
   __half *lat_in_ = nullptr, *image_ = nullptr, *lat64_ = nullptr, *pqc_ = nullptr;
   __half *s_gn1_ = nullptr, *s_gn2_ = nullptr, *upbuf_ = nullptr, *out32_ = nullptr;
   void* s_c1_ = nullptr;  // conv1 output (fp16 or fp32)
-  __half *qkv_ = nullptr, *scores_ = nullptr, *vt_ = nullptr, *attn_o_ = nullptr;
+  __half *qkv_ = nullptr, *attn_o_ = nullptr;
   float2* gn_partials_ = nullptr;
   size_t gn_partial_cap_ = 0;
 };

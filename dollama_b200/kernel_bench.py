@@ -78,6 +78,7 @@ def main(argv=None):
     ap.add_argument("--heads", type=int, default=10)
     ap.add_argument("--sq", type=int, default=4096)
     ap.add_argument("--sk", type=int, default=4096)
+    ap.add_argument("--dh", type=int, default=64, help="attention head dim (64, or 128..512)")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--eager", action="store_true",
                     help="time back-to-back ABI calls instead of a captured graph of them")
@@ -153,11 +154,15 @@ def main(argv=None):
         flops = 0.0
         shape = {"n": a.n, "hw": a.h * a.w, "c": a.cin, "bytes": 3.0 * x.numel() * 2}
     else:
-        q = torch.randn(a.b, a.heads, a.sq, 64, device=dev).half()
-        k = torch.randn(a.b, a.heads, a.sk, 64, device=dev).half()
+        q = torch.randn(a.b, a.heads, a.sq, a.dh, device=dev).half()
+        k = torch.randn(a.b, a.heads, a.sk, a.dh, device=dev).half()
         v = torch.randn_like(k)
         o = torch.empty_like(q)
-        if a.tile_mode == 1:   # one CTA per 256-query block (no load balancing)
+        if a.dh != 64:         # wide heads (the VAE's Dh = 512)
+            sc = a.dh ** -0.5
+            fn = lambda: L.call("dlm_launch_attention", _p(q), _p(k), _p(v), _p(o), a.b, a.heads,
+                                a.sq, a.sk, a.dh, sc, _s())
+        elif a.tile_mode == 1:   # one CTA per 256-query block (no load balancing)
             fn = lambda: L.call("dlm_launch_attention", _p(q), _p(k), _p(v), _p(o), a.b, a.heads,
                                 a.sq, a.sk, 64, 0.125, _s())
         else:
@@ -165,8 +170,8 @@ def main(argv=None):
             ws = torch.zeros(nws, dtype=torch.uint8, device=dev)
             fn = lambda: L.call("dlm_launch_attention_ws", _p(q), _p(k), _p(v), _p(o), a.b, a.heads,
                                 a.sq, a.sk, 64, 0.125, _p(ws), nws, _s())
-        flops = 4.0 * a.b * a.heads * a.sq * a.sk * 64
-        shape = {"b": a.b, "heads": a.heads, "sq": a.sq, "sk": a.sk, "dh": 64}
+        flops = 4.0 * a.b * a.heads * a.sq * a.sk * a.dh
+        shape = {"b": a.b, "heads": a.heads, "sq": a.sq, "sk": a.sk, "dh": a.dh}
     ms = _time_graph(fn, a.iters) if a.op in ("gemm", "attn", "gn") and not a.eager else _time(fn, a.iters)
     peak = None
     pk = Path(__file__).resolve().parent.parent / "MEASURED_PEAKS.json"

@@ -168,7 +168,10 @@ int dlm_nhwc_to_nchw(const void* in, void* out, int N, int C, int HW, void* stre
  *
  * Replaces launch_attention / launch_attention_fast (reference src/kernels/attention.cuh:53-73):
  * out = softmax(q k^T * scale) v, q/k/v/out [B, H, S, Dh] contiguous fp16, fp32 online softmax.
- * Dh must be 64 (the UNet's head_dim, src/infer/unet.cu:683-684).
+ * Dh = 64 (the UNet's head_dim, src/infer/unet.cu:683-684: two 128-query tiles per CTA, stream-K
+ * with a workspace) or a multiple of 64 in [128, 512] (wide heads, e.g. the VAE mid-block's
+ * Dh = 512 that the reference passes to launch_attention, src/kernels/vae_decode.cu:682-683:
+ * one CTA per 128-query tile and 256-column output slice; the _ws workspace is not used).
  */
 int dlm_launch_attention(const void* q, const void* k, const void* v, void* out, int B, int H,
                          int Sq, int Sk, int Dh, float scale, void* stream);

@@ -135,3 +135,56 @@ def test_attention_growing_scores(use_ws, attn_ws):
     ref = ref_attn(q, k, v)
     assert max_rel_err(o, ref) < 2e-3
     assert allclose_k(o, ref, Sk)
+
+
+# ---------------------------------------------------------------- wide heads (Dh 128..512)
+# The VAE mid-block attention: one head of Dh = 512 over S = h*w tokens, which the reference runs
+# through launch_attention (src/kernels/vae_decode.cu:682-683); other multiples of 64 up to 512
+# and ragged query / key counts exercise the masking and the output split.
+
+def ref_attn_scaled(q, k, v, scale):
+    s = (q.float() @ k.float().transpose(-1, -2)) * scale
+    return torch.softmax(s, dim=-1) @ v.float()
+
+
+@pytest.mark.parametrize("B,H,Sq,Sk,Dh", [(1, 1, 256, 256, 512), (1, 1, 1024, 1024, 512),
+                                          (2, 1, 200, 300, 512), (1, 2, 384, 130, 256),
+                                          (1, 1, 128, 77, 128), (2, 2, 256, 512, 384)])
+def test_attention_wide_bhsd(B, H, Sq, Sk, Dh):
+    g = torch.Generator().manual_seed(B * 1000 + Sq + Sk + Dh)
+    q = torch.randn(B, H, Sq, Dh, generator=g).half().cuda()
+    k = torch.randn(B, H, Sk, Dh, generator=g).half().cuda()
+    v = torch.randn(B, H, Sk, Dh, generator=g).half().cuda()
+    o = torch.full_like(q, float("nan"))
+    scale = 1.0 / math.sqrt(Dh)
+    L.call("dlm_launch_attention", _p(q), _p(k), _p(v), _p(o), B, H, Sq, Sk, Dh, scale, _s())
+    torch.cuda.synchronize()
+    ref = ref_attn_scaled(q, k, v, scale)
+    assert torch.isfinite(o).all()
+    assert max_rel_err(o, ref) < 2e-3, max_rel_err(o, ref)
+    assert allclose_k(o, ref, Sk)
+    code = ctypes.c_int(-1)
+    L.call("dlm_get_device_status", ctypes.byref(code), 1, _s())
+    assert code.value == 0
+
+
+def test_attention_wide_vae_mid_block_size():
+    """The benchmarked VAE's mid attention: [16384 tokens, 512] token-major q | k | v (one head),
+    fed as the VAE feeds it (strided views of one [S, 1536] projection)."""
+    S, C = 16384, 512
+    g = torch.Generator().manual_seed(77)
+    qkv = (torch.randn(S, 3 * C, generator=g) * 0.5).half().cuda()
+    out = torch.empty(S, C, dtype=torch.float16, device="cuda")
+    scale = 1.0 / math.sqrt(C)
+    L.call("dlm_attention_tokens", _p(qkv), 3 * C, ctypes.c_void_p(qkv.data_ptr() + 2 * C), 3 * C,
+           ctypes.c_void_p(qkv.data_ptr() + 4 * C), 3 * C, _p(out), C, 1, 1, S, S, C, scale, _s())
+    torch.cuda.synchronize()
+    q, k, v = qkv[:, :C], qkv[:, C:2 * C], qkv[:, 2 * C:]
+    ref = ref_attn_scaled(q, k, v, scale)
+    assert max_rel_err(out, ref) < 2e-3, max_rel_err(out, ref)
+
+
+def test_attention_wide_rejects_unsupported_head_dim():
+    q = torch.zeros(1, 1, 128, 96, dtype=torch.float16, device="cuda")
+    rc = L.lib().dlm_launch_attention(_p(q), _p(q), _p(q), _p(q), 1, 1, 128, 128, 96, 0.1, _s())
+    assert rc == -4

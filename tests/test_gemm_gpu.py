@@ -101,6 +101,27 @@ def test_device_status_clean():
     assert code.value == 0
 
 
+@pytest.mark.parametrize("M,N,K,ta,tb,beta", [(320, 36, 4, 0, 0, 0.0),     # a LoRA delta B @ A
+                                                (37, 50, 13, 0, 1, 0.0),
+                                                (64, 96, 72, 1, 0, 0.5),
+                                                (33, 17, 40, 1, 1, -1.0),
+                                                (128, 64, 64, 0, 0, 1.0)])
+def test_gemm_any_shape_and_orientation(M, N, K, ta, tb, beta):
+    """The reference's launch_gemm_fp16 (cuBLAS) takes any M, N, K and both orientations
+    (src/kernels/gemm.cuh:44-53): sizes off the tensor-core kernel's granularity go through
+    zero-padded scratch."""
+    A = _rand(*((K, M) if ta else (M, K)), seed=3)
+    B = _rand(*((N, K) if tb else (K, N)), scale=K ** -0.5, seed=4)
+    C = _rand(M, N, seed=5)
+    C0 = C.clone()
+    L.call("dlm_launch_gemm_fp16", _ptr(A), _ptr(B), _ptr(C), M, N, K, 0.75, beta, ta, tb, _stream())
+    torch.cuda.synchronize()
+    a = A.float().t() if ta else A.float()
+    b = B.float() if tb else B.float().t()
+    ref = 0.75 * (a @ b.t()) + beta * C0.float()
+    assert max_rel_err(C, ref) < 2e-3, max_rel_err(C, ref)
+
+
 def test_gemm_invalid_arguments():
     # every orientation is provided (transposed operands go through scratch); a null operand is
     # an invalid argument, reported without launching
