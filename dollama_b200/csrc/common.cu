@@ -33,11 +33,13 @@ void set_error(const char* fmt, ...) {
 }
 
 bool pdl_enabled() {
-  // Programmatic dependent launch is opt-in (DLM_PDL=1): measured on B200 it lengthened the UNet
-  // step (early-resident dependent CTAs wait on griddepcontrol while the primary drains).
+  // Programmatic dependent launch is on by default (DLM_PDL=0 turns it off): every kernel that is
+  // launched with it waits (griddepcontrol.wait) before its first global read or write, so only
+  // its set-up (barriers, TMEM, descriptor prefetch) overlaps the previous kernel's tail.  The
+  // UNet step measured 18.6 ms with it against 19.0 ms without (B200, graph replay).
   static const bool on = [] {
     const char* e = std::getenv("DLM_PDL");
-    return e && e[0] == '1';
+    return !(e && e[0] == '0');
   }();
   return on;
 }

@@ -29,7 +29,7 @@ bool encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank, con
 bool tmap_2d_f16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
                  uint32_t box_rows, uint32_t box_cols);
 
-// Whether kernels are launched with programmatic dependent launch (opt-in: DLM_PDL=1).
+// Whether kernels are launched with programmatic dependent launch (default on; DLM_PDL=0 off).
 bool pdl_enabled();
 
 // Records the last host-side error message (thread-local), returned by dlm_last_error().
