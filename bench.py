@@ -217,6 +217,128 @@ def reference_gpu_leg(sd_gpu, dev_inputs, out, our_value, e0, e1, stream, steps=
             "ours_over_reference_best": (our_value / best) if best else None}
 
 
+LM_SEQS, LM_PROMPT, LM_NEW = 256, 64, 64   # 256 sequences, 64 + 64 tokens
+
+
+def lm_leg(dev, ws, rank, e0, e1, stream, hbm_peak, peak_src, barrier, cpu=True):
+    """BASELINE config 5, the ternary BitNet tag LM: greedy decode of LM_SEQS sequences split over
+    the ranks by sequence (each rank decodes its share; no exchange).  Whole-job generated tokens/s
+    with prompts resident on the device (CUDA events, max over ranks), the same through the host
+    API (prompts in, generated ids out), the decode step against HBM (its packed ternary weights
+    and activations per step), and — rank 0, N = 1 — the reference's own BitNet::forward
+    (src/models/bitnet.hpp:376-440, compiled from its header) timed on a slice on one host core."""
+    import numpy as np
+    import torch
+    from dollama_b200.bitnet_lm import BitNetConfig, BitNetLM, random_weights
+    cfg = BitNetConfig(max_seq=LM_PROMPT + LM_NEW)
+    lm = BitNetLM(cfg, random_weights(cfg, seed=10, device=dev))
+    B = LM_SEQS // ws + (1 if rank < LM_SEQS % ws else 0)
+    g = torch.Generator().manual_seed(11 + rank)
+    prompts_h = torch.randint(4, cfg.vocab, (B, LM_PROMPT), generator=g, dtype=torch.int32)
+    prompts = prompts_h.to(dev)
+    out = torch.zeros(B, LM_NEW, dtype=torch.int32, device=dev)
+    lens = torch.zeros(B, dtype=torch.int32, device=dev)
+    L_full = LM_PROMPT + LM_NEW
+
+    def timed(max_len, reps):
+        for _ in range(2):
+            lm.generate_device(prompts, max_len, out, lens)
+        barrier()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(reps):
+            lm.generate_device(prompts, max_len, out, lens)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        return max_over_ranks(e0.elapsed_time(e1) / reps, ws, dev)
+
+    ms_gen = timed(L_full, 5)
+    ms_prefill = timed(LM_PROMPT + 1, 5)          # prefill + the first greedy token
+    step_ms = (ms_gen - ms_prefill) / (LM_NEW - 1)
+    tokens = LM_SEQS * LM_NEW
+    # through the host API: numpy prompts in, generated ids back on the host, per call
+    ph = prompts_h.numpy()
+    lm.generate(ph, L_full)
+    barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(3):
+        lm.generate(ph, L_full)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ms_host = max_over_ranks(e0.elapsed_time(e1) / 3, ws, dev)
+    # algorithmic HBM bytes of one decode step (B tokens, one per sequence), averaged over the
+    # decode: the 2-bit ternary weights and their row scales; the BitLinears' int8 inputs and fp32
+    # outputs (the residual updates read and written); the tied fp32 embedding the lm_head reads;
+    # the fp32 K / V cache each sequence attends over (P + G / 2 positions on average)
+    D, F, NL, V = cfg.d_model, cfg.ffn_dim, cfg.n_layers, cfg.vocab
+    tern = NL * (4 * D * D + 3 * D * F)
+    w_bytes = tern / 4 + NL * 4 * (5 * D + 2 * F)
+    act_bytes = B * NL * ((3 * D + F) + 4 * (7 * D + 2 * F))
+    head_bytes = V * D * 4 + B * D * 4
+    kv_bytes = B * NL * 2 * D * 4 * (LM_PROMPT + LM_NEW / 2)
+    step_bytes = w_bytes + act_bytes + head_bytes + kv_bytes
+    res = {
+        "workload": f"BitNet tag LM (vocab {cfg.vocab}, d {D}, {NL} layers, {cfg.n_heads} heads, "
+                    f"FFN {F} SwiGLU, ternary weights): greedy decode of {LM_SEQS} sequences x "
+                    f"{LM_PROMPT} prompt + {LM_NEW} generated tokens, sequences split over {ws} rank(s)",
+        "metric": "generated tokens/s", "value": tokens / (ms_gen / 1000.0), "unit": "tokens/s",
+        "scaling": "strong", "ms_per_generate": ms_gen, "ms_prefill": ms_prefill,
+        "ms_per_decode_step": step_ms,
+        "e2e": {"value": tokens / (ms_host / 1000.0), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(ph.nbytes), "d2h_bytes_per_step": int(B * (LM_NEW + 1) * 4)},
+        "roofline": {"kernel": "one decode step (the 32 ternary BitLinear GEMMs and the context "
+                               "kernels around them, 85 launches, one CUDA graph)",
+                     "bound": "hbm", "achieved": step_bytes / (step_ms / 1000.0) / 1e9,
+                     "peak": hbm_peak, "unit": "GB/s",
+                     "frac": step_bytes / (step_ms / 1000.0) / 1e9 / hbm_peak,
+                     "traffic": None, "peak_source": f"{peak_src} hbm_gbs",
+                     "algorithmic_bytes_per_step": step_bytes,
+                     "bytes_split": {"ternary_weights": w_bytes, "activations": act_bytes,
+                                     "lm_head_embedding": head_bytes, "kv_cache": kv_bytes}},
+    }
+    lm.close()
+    if cpu and rank == 0 and ws == 1:
+        res["cpu_baseline"] = lm_reference_cpu()
+    return res
+
+
+def lm_reference_cpu(n_tokens=8):
+    """The reference's own BitNet::forward (oracle/_ref/libref_bitnet.so, compiled from
+    src/models/bitnet.hpp at the reference's own dimensions) on one host core: one forward over
+    n_tokens positions of one sequence, random ternary weights."""
+    import numpy as np
+    try:
+        from oracle import bitnet as ob
+        dims = ob.ref_dims()
+        if dims is None:
+            return {"value": None, "unit": "tokens/s", "cores": 1, "kind": "reference",
+                    "sample": "unavailable: oracle/_ref/libref_bitnet.so not built"}
+        V, D, NL, H, F, _ = dims
+        rng = np.random.default_rng(10)
+        w = {"embed": (0.02 * rng.standard_normal((V, D))).astype(np.float32),
+             "final_norm": np.ones(D, np.float32)}
+        for l in range(NL):
+            for k, shp in (("attn_norm", (D,)), ("wq", (D, D)), ("wk", (D, D)), ("wv", (D, D)),
+                           ("wo", (D, D)), ("ffn_norm", (D,)), ("w_gate", (F, D)), ("w_up", (F, D)),
+                           ("w_down", (D, F))):
+                w[f"layers.{l}.{k}"] = (np.ones(shp, np.float32) if "norm" in k
+                                        else rng.integers(-1, 2, shp).astype(np.float32))
+        toks = rng.integers(4, V, n_tokens).astype(np.int32)
+        t0 = time.perf_counter()
+        ob.ref_forward(w, toks)
+        dt = time.perf_counter() - t0
+        return {"value": n_tokens / dt, "unit": "tokens/s", "cores": 1, "kind": "reference",
+                "sample": f"the reference's BitNet::forward (compiled from src/models/bitnet.hpp, "
+                          f"its own dims vocab {V} / FFN {F}) over {n_tokens} positions of one "
+                          f"sequence, one call, one host thread: {dt:.2f} s"}
+    except Exception as exc:  # pragma: no cover - reported, not fatal
+        return {"value": None, "unit": "tokens/s", "cores": 1, "kind": "reference",
+                "sample": f"failed: {exc}"}
+
+
 def run_reference(args, ws, rank):
     """The reference arm: the CPU fp32 restatement of the step on all host cores, with its
     weights drawn on the CPU by the oracle's own initialiser.  Nothing of this library (no
@@ -395,6 +517,9 @@ def main():
                "image_finite": bool(torch.isfinite(img).all().item())}
     vae.close()
 
+    # ---------------------------------------------------------------- BitNet LM (config 5)
+    lm = lm_leg(dev, ws, rank, e0, e1, stream, hbm, peak_src, barrier, cpu=keep_sd)
+
     # ---------------------------------------------------------------- reference GPU comparator
     # the reference's own CUDA UNet (src/infer/unet.cu + its kernels and cuBLAS), unchanged and
     # recompiled for sm_100a, on the same weights and inputs (rank 0, N = 1 only)
@@ -428,6 +553,7 @@ def main():
             "roofline": roofline,
             "cpu_baseline": cpu,
             "reference_gpu": ref_gpu_line,
+            "lm": lm,
             "clocks": clocks,
             "gpu_launches": args.steps * (info["launches_per_step"] + 1),
             "output_finite": finite,
