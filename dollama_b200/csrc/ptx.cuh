@@ -240,6 +240,20 @@ __device__ __forceinline__ void umma_f16_ss(uint32_t d_tmem, uint64_t a_desc, ui
       : "memory");
 }
 
+// D[tmem] (+)= A[smem desc] * B[smem desc], kind::i8 (signed int8 operands, exact int32
+// accumulate in TMEM); K = 32 per instruction.
+__device__ __forceinline__ void umma_i8_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "setp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n"
+      "}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // D[tmem] (+)= A[tmem] * B[smem desc], kind::f16: A (M = 128 lanes x K) read from tensor memory,
 // two fp16 values of consecutive k per 32-bit column (column a_tmem + k / 2).
 __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
@@ -425,6 +439,13 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr, uint32_t lbo,
 __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N, bool b_mn_major) {
   return (1u << 4) | (static_cast<uint32_t>(b_mn_major ? 1 : 0) << 16) |
          (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// Instruction descriptor, kind::i8: D = s32 [4,6) = 2, A = s8 [7,10) = 1, B = s8 [10,13) = 1,
+// both K-major, N>>3 at [17,23), M>>4 at [24,29).
+__host__ __device__ constexpr uint32_t idesc_s8_s32(int M, int N) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
+         (static_cast<uint32_t>(M >> 4) << 24);
 }
 
 // ---------------------------------------------------------------- programmatic dependent launch

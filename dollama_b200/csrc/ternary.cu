@@ -15,7 +15,9 @@
 // tokens; the inner loop is 16-byte shared loads + dp4a.  Packed weight rows are read with
 // coalesced 16-byte loads.
 #include <cstdint>
+#include <cstdlib>
 
+#include "ptx.cuh"
 #include "ternary.h"
 
 namespace dlm {
@@ -27,6 +29,15 @@ constexpr int kTN = 64;       // outputs per CTA
 constexpr int kKC = 256;      // K chunk (elements)
 constexpr int kRow = kKC + 16;  // padded smem row (bytes)
 constexpr int kThreads = 256;
+// Token rows from which the tensor-core path is used (DLM_TERNARY_TC_ROWS overrides, for
+// measurements).
+int tc_min_rows() {
+  static const int v = [] {
+    const char* e = std::getenv("DLM_TERNARY_TC_ROWS");
+    return e ? std::atoi(e) : 1024;
+  }();
+  return v;
+}
 
 // One thread per output row: exact per-row ternary quantization, then 2-bit packing.
 __global__ void ternary_pack_kernel(const float* __restrict__ w, int N, int K,
@@ -207,6 +218,186 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
+// ---------------------------------------------------------------- tensor-core path (prefill)
+// The same exact BitLinear on the 5th-generation tensor cores: tcgen05.mma kind::i8 (signed int8
+// A and B from shared memory, int32 accumulation in TMEM — integer sums, so the result is the
+// dp4a path's bit for bit).  One CTA = 128 tokens x 128 outputs; K in 128-byte blocks through a
+// 4-stage ring:
+//   warp 0     TMA: the activation block (128 tokens x 128 int8, 128-byte swizzle);
+//   warp 1     TMEM owner + MMA issuer: 4 MMAs (K = 32) per block, M = 128, N = 128;
+//   warps 2-5  expand the weight block (128 rows x 128 two-bit codes, 4 KB packed) into int8 in
+//              the 128-byte-swizzled K-major layout the MMA reads (thread = one output row, one
+//              16-byte chunk per packed word, chunk index XOR row % 8), then, after the last block,
+//              the epilogue: TMEM -> int32 -> y = float(double(acc) * alpha[n] * xscale[m])
+//              (or y += that value), one row per thread.
+constexpr int kTcM = 128, kTcN = 128, kTcKB = 128, kTcStages = 4, kTcThreads = 192;
+constexpr int kTcStageA = kTcM * kTcKB, kTcStageB = kTcN * kTcKB;  // 16 KB each
+constexpr int kTcSmem = kTcStages * (kTcStageA + kTcStageB) + 256 + 1024;
+
+struct TernaryTcParams {
+  const uint32_t* wp;
+  const float* alpha;
+  const float* xscale;
+  float* y;
+  int M, N, K, accumulate;
+  int* status;
+};
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    ternary_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmX, const TernaryTcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + kTcStages * kTcStageA;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTcStages * (kTcStageA + kTcStageB));
+  uint64_t* a_full = bars;                 // [stages] TMA bytes
+  uint64_t* b_full = a_full + kTcStages;   // [stages] 128 expanding threads
+  uint64_t* empty = b_full + kTcStages;    // [stages] the stage's MMAs completed
+  uint64_t* acc_full = empty + kTcStages;  // the last MMA completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * kTcN, m0 = blockIdx.y * kTcM;
+  const int nkb = p.K / kTcKB;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kTcStages; ++s) {
+      mbar_init(&a_full[s], 1);
+      mbar_init(&b_full[s], 128);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTcN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmX);
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % kTcStages;
+        if (kb >= kTcStages &&
+            !mbar_wait(&empty[s], ((kb / kTcStages) - 1) & 1, abort_flag, p.status, kDevTimeoutProducer))
+          break;
+        mbar_arrive_expect_tx(&a_full[s], kTcStageA);
+        tma_load_2d(sA + s * kTcStageA, &tmX, &a_full[s], kb * kTcKB, m0);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_s8_s32(kTcM, kTcN);
+      bool ok = true;
+      for (int kb = 0; kb < nkb && ok; ++kb) {
+        const int s = kb % kTcStages;
+        const uint32_t par = (kb / kTcStages) & 1;
+        ok = mbar_wait(&a_full[s], par, abort_flag, p.status, kDevTimeoutMma) &&
+             mbar_wait(&b_full[s], par, abort_flag, p.status, kDevTimeoutMma);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(sA + s * kTcStageA), b_addr = smem_u32(sB + s * kTcStageB);
+#pragma unroll
+        for (int k = 0; k < kTcKB / 32; ++k)
+          umma_i8_ss(tbase, sw128_desc(a_addr + k * 32, 16, 1024), sw128_desc(b_addr + k * 32, 16, 1024),
+                     idesc, (kb != 0 || k != 0) ? 1u : 0u);
+        umma_commit(&empty[s]);
+      }
+      if (ok) umma_commit(acc_full);
+    }
+  } else {
+    // warps 2..5: weight expansion, then the epilogue
+    const int t = threadIdx.x - 64;          // 0..127: output row n0 + t during expansion
+    const int n = n0 + t;
+    const int wwords = p.K / 16;
+    bool ok = true;
+    for (int kb = 0; kb < nkb; ++kb) {
+      const int s = kb % kTcStages;
+      if (kb >= kTcStages &&
+          !__all_sync(0xffffffffu, mbar_wait(&empty[s], ((kb / kTcStages) - 1) & 1, abort_flag,
+                                            p.status, kDevTimeoutProducer))) {
+        ok = false;
+        break;
+      }
+      uint4 w0 = make_uint4(0, 0, 0, 0), w1 = w0;
+      if (n < p.N) {
+        const uint4* src = reinterpret_cast<const uint4*>(p.wp + static_cast<size_t>(n) * wwords + kb * 8);
+        w0 = __ldg(src);
+        w1 = __ldg(src + 1);
+      }
+      const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+      uint8_t* row = sB + s * kTcStageB + (t >> 3) * 1024 + (t & 7) * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint32_t wd = words[c];
+        uint4 v;
+        v.x = decode4(wd & 0xFFu);
+        v.y = decode4((wd >> 8) & 0xFFu);
+        v.z = decode4((wd >> 16) & 0xFFu);
+        v.w = decode4(wd >> 24);
+        *reinterpret_cast<uint4*>(row + ((c ^ (t & 7)) << 4)) = v;
+      }
+      fence_proxy_async_smem();  // the generic-proxy writes are visible to the tensor core
+      mbar_arrive(&b_full[s]);
+    }
+    // epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 = tokens m0 + 32 (w % 4) + lane; each
+    // 32-column chunk's output scales are one coalesced load per warp, broadcast by shuffles, and
+    // each 32 x 32 block of results goes through the warp's own shared-memory transpose so that
+    // every store (and the read of an accumulated output) is one coalesced 128-byte row (the
+    // ring's buffers are free after the last MMA; no barrier across warps)
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(acc_full, 0, abort_flag, p.status, kDevTimeoutEpilogue));
+    float* s_tile = reinterpret_cast<float*>(sA) + (warp - 2) * 32 * 33;  // per warp [32][33]
+    if (ok) {
+      tc_fence_after();
+      const int quad = warp & 3;
+      const int mrow0 = m0 + quad * 32;
+      const int m = mrow0 + lane;
+      const double sx = m < p.M ? static_cast<double>(p.xscale[m]) : 0.0;
+      const uint32_t taddr = tbase + (static_cast<uint32_t>(quad * 32) << 16);
+      for (int c0 = 0; c0 < kTcN; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(taddr + c0, r);
+        const int nl = n0 + c0 + lane;
+        const float a_lane = nl < p.N ? p.alpha[nl] : 0.0f;
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float aj = __shfl_sync(0xffffffffu, a_lane, j);
+          const double v = __dmul_rn(__dmul_rn(static_cast<double>(static_cast<int>(r[j])),
+                                               static_cast<double>(aj)), sx);
+          s_tile[lane * 33 + j] = __double2float_rn(v);
+        }
+        __syncwarp();
+        const int nn = n0 + c0 + lane;
+        for (int rr = 0; rr < 32; ++rr) {
+          const int mm = mrow0 + rr;
+          if (mm < p.M && nn < p.N) {
+            float* dst = p.y + static_cast<size_t>(mm) * p.N + nn;
+            const float v = s_tile[rr * 33 + lane];
+            *dst = p.accumulate ? __fadd_rn(*dst, v) : v;
+          }
+        }
+        __syncwarp();
+      }
+    }
+  }
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (*abort_flag) drain_sleep(200000);
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, kTcN);
+  }
+}
+
 }  // namespace
 
 int ternary_pack(const float* w, int N, int K, uint32_t* packed, float* alpha, cudaStream_t s) {
@@ -244,6 +435,29 @@ int ternary_gemm_i8(const uint32_t* wp, const float* alpha, const int8_t* xq, co
               "ternary_gemm_i8: K=%d must be a multiple of 64", K);
   DLM_REQUIRE((reinterpret_cast<uintptr_t>(wp) & 15) == 0 && (reinterpret_cast<uintptr_t>(xq) & 15) == 0,
               DLM_ERR_INVALID, "ternary_gemm_i8: packed weights / activations must be 16-byte aligned");
+  if (M >= tc_min_rows() && K % kTcKB == 0 && N % 32 == 0) {
+    // prefill-sized: the tensor-core path (same integer sums, same epilogue arithmetic)
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+      DLM_CHECK_CUDA(cudaFuncSetAttribute(ternary_gemm_tc_kernel,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem));
+      attr_set[dev] = true;
+    }
+    CUtensorMap tm;
+    const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(K)};
+    const uint32_t box[2] = {kTcKB, kTcM};
+    if (!encode_tmap(&tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, xq, dims, strides, box,
+                     CU_TENSOR_MAP_SWIZZLE_128B))
+      return DLM_ERR_CUDA;
+    TernaryTcParams tp{wp, alpha, xscale, y, M, N, K, accumulate ? 1 : 0, device_status_ptr()};
+    dim3 grid((N + kTcN - 1) / kTcN, (M + kTcM - 1) / kTcM);
+    ternary_gemm_tc_kernel<<<grid, kTcThreads, kTcSmem, s>>>(tm, tp);
+    DLM_CHECK_CUDA(cudaGetLastError());
+    return DLM_OK;
+  }
   dim3 grid((N + kTN - 1) / kTN, (M + kTM - 1) / kTM);
   ternary_gemm_kernel<<<grid, kThreads, 0, s>>>(wp, alpha, xq, xscale, y, M, N, K, accumulate ? 1 : 0);
   DLM_CHECK_CUDA(cudaGetLastError());

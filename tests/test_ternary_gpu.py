@@ -74,8 +74,10 @@ def test_quant_act_bit_exact(M, K):
     assert np.array_equal(xq.cpu().numpy().reshape(M, K), q_ref)
 
 
+# M >= 1024 runs the tcgen05 kind::i8 tensor-core path (prefill), smaller M the dp4a path (decode)
 @pytest.mark.parametrize("M,N,K", [(256, 512, 512), (256, 1536, 512), (256, 512, 1536),
-                                   (2048, 512, 512), (37, 70, 192), (1, 64, 64)])
+                                   (2048, 512, 512), (37, 70, 192), (1, 64, 64),
+                                   (1040, 3072, 512), (1024, 512, 1536), (1152, 96, 256)])
 def test_bitlinear_bit_exact(M, N, K):
     rng = np.random.default_rng(M + 7 * N + K)
     w = (rng.standard_normal((N, K)) * 0.05).astype(np.float32)
