@@ -18,6 +18,7 @@
 //
 // Layout: hidden state h [M, D] fp32 (M = B * S rows, row = sequence-major position); K/V cache
 // [layer][b][head][pos][64] fp32 (K after RoPE); q|k|v, gate|up are each one GEMM.
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <string>
@@ -151,31 +152,53 @@ __global__ void rope_kv_kernel(const float* __restrict__ qkv, int M, int S, int 
 
 // Causal attention (bitnet.hpp:536-569) of row r (sequence b, position pos) and one head over
 // cache positions 0..pos: double scores in index order, exp, a sequential sum, then float
-// accumulation of float(w_j * v_j) over j in order.  One block per (row, head).
+// accumulation of float(w_j * v_j) over j in order.  One block per (row, head).  For caches of up
+// to kVStageMax positions the head's V rows 0..pos are first staged in shared memory with
+// coalesced 16-byte loads (the output loop walks them in order, one dimension per thread); each
+// thread's K row is loaded into registers as 16 independent 16-byte loads before its sequential
+// dot product.
 constexpr int kAttnThreads = 128;
+constexpr int kVStageMax = 256;  // cache lengths up to which V is staged (64 KB of shared memory)
+__host__ __device__ constexpr size_t attn_smem_bytes(int Lmax) {
+  return (kHeadDim + Lmax + 40) * sizeof(double) +
+         (Lmax <= kVStageMax ? static_cast<size_t>(Lmax) * kHeadDim * 4 : 0);
+}
 __global__ void __launch_bounds__(kAttnThreads)
     attention_kernel(const float* __restrict__ q, int M, int S, int D, const int* __restrict__ pos_in,
                      const float* __restrict__ kc, const float* __restrict__ vc, int Lmax,
                      float* __restrict__ out) {
-  extern __shared__ double sh[];  // [64] q, [Lmax] scores, [32] reduction
+  extern __shared__ double sh[];  // [64] q, [Lmax] scores, [40] reduction, then [Lmax][64] V (f32)
   double* sq = sh;
   double* ss = sh + kHeadDim;
   double* red = ss + Lmax;
+  float* sv = reinterpret_cast<float*>(red + 40);
   const int H = D / kHeadDim;
   const int r = blockIdx.x / H, hd = blockIdx.x % H;
   if (r >= M) return;
   const int b = r / S, pos = (pos_in ? *pos_in : 0) + r % S;
   const int n = pos + 1;
   const float* qr = q + static_cast<size_t>(r) * D + hd * kHeadDim;
-  for (int d = threadIdx.x; d < kHeadDim; d += blockDim.x) sq[d] = static_cast<double>(qr[d]);
-  __syncthreads();
   const float* kb = kc + (static_cast<size_t>(b) * H + hd) * Lmax * kHeadDim;
   const float* vb = vc + (static_cast<size_t>(b) * H + hd) * Lmax * kHeadDim;
+  for (int d = threadIdx.x; d < kHeadDim; d += blockDim.x) sq[d] = static_cast<double>(qr[d]);
+  const bool staged = Lmax <= kVStageMax;
+  if (staged) {
+    const float4* src = reinterpret_cast<const float4*>(vb);
+    float4* dst = reinterpret_cast<float4*>(sv);
+    for (int i = threadIdx.x; i < n * (kHeadDim / 4); i += blockDim.x) dst[i] = src[i];
+  }
+  const float* vrows = staged ? sv : vb;
+  __syncthreads();
   double mx = -1e300;
   for (int j = threadIdx.x; j < n; j += blockDim.x) {
-    const float* kj = kb + static_cast<size_t>(j) * kHeadDim;
+    const float4* kj = reinterpret_cast<const float4*>(kb + static_cast<size_t>(j) * kHeadDim);
+    float4 kr[kHeadDim / 4];
+#pragma unroll
+    for (int i = 0; i < kHeadDim / 4; ++i) kr[i] = kj[i];
+    const float* kf = reinterpret_cast<const float*>(kr);
     double dot = 0.0;
-    for (int d = 0; d < kHeadDim; ++d) dot = __dadd_rn(dot, __dmul_rn(sq[d], static_cast<double>(kj[d])));
+#pragma unroll
+    for (int d = 0; d < kHeadDim; ++d) dot = __dadd_rn(dot, __dmul_rn(sq[d], static_cast<double>(kf[d])));
     dot = __dmul_rn(dot, 0.125);  // 1 / sqrt(64), exact
     ss[j] = dot;
     mx = fmax(mx, dot);
@@ -203,31 +226,30 @@ __global__ void __launch_bounds__(kAttnThreads)
     float acc = 0.0f;
     for (int j = 0; j < n; ++j) {
       const double wj = __dmul_rn(ss[j], inv);
-      acc = __fadd_rn(acc, __double2float_rn(__dmul_rn(wj, static_cast<double>(vb[static_cast<size_t>(j) * kHeadDim + d]))));
+      acc = __fadd_rn(acc, __double2float_rn(__dmul_rn(wj, static_cast<double>(vrows[j * kHeadDim + d]))));
     }
     out[static_cast<size_t>(r) * D + hd * kHeadDim + d] = acc;
   }
 }
 
 // SwiGLU (bitnet.hpp:603-610) of gate|up [M, 2F] -> float(silu(g) * u), then int8 quantization;
-// one warp per row.
-constexpr int kSwiWarps = 4;
-__global__ void __launch_bounds__(kSwiWarps * 32)
+// one block per row: every thread computes its elements into the shared row, then warp 0
+// quantizes the row (the same per-element operations in any split, so the same bits).
+constexpr int kSwiThreads = 256;
+__global__ void __launch_bounds__(kSwiThreads)
     swiglu_quant_kernel(const float* __restrict__ gu, int M, int F, int8_t* __restrict__ xq,
                         float* __restrict__ xs) {
-  extern __shared__ float srow[];  // [kSwiWarps][F]
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int r = blockIdx.x * kSwiWarps + warp;
+  extern __shared__ float srow[];  // [F]
+  const int r = blockIdx.x;
   if (r >= M) return;
-  float* row = srow + static_cast<size_t>(warp) * F;
   const float* g = gu + static_cast<size_t>(r) * 2 * F;
-  for (int f = lane; f < F; f += 32) {
+  for (int f = threadIdx.x; f < F; f += kSwiThreads) {
     const double gv = static_cast<double>(g[f]);
     const double silu = __ddiv_rn(gv, __dadd_rn(1.0, exp(-gv)));
-    row[f] = __double2float_rn(__dmul_rn(silu, static_cast<double>(g[F + f])));
+    srow[f] = __double2float_rn(__dmul_rn(silu, static_cast<double>(g[F + f])));
   }
-  __syncwarp();
-  quant_row_warp(row, F, xq + static_cast<size_t>(r) * F, xs + r);
+  __syncthreads();
+  if (threadIdx.x < 32) quant_row_warp(srow, F, xq + static_cast<size_t>(r) * F, xs + r);
 }
 
 // Tied lm_head (bitnet.hpp:414-436): logits[r, v] = float(sum_d double(x[r, d]) * double(E[v, d]))
@@ -588,8 +610,8 @@ int BitNetLM::run_layers(int S, const int* pos, cudaStream_t s) {
   const size_t kv_layer = static_cast<size_t>(B_) * H * L_ * kHeadDim;
   const int norm_blocks = (M + kNormWarps - 1) / kNormWarps;
   const size_t norm_smem = static_cast<size_t>(kNormWarps) * D * 4;
-  const size_t swi_smem = static_cast<size_t>(kSwiWarps) * F * 4;
-  const size_t attn_smem = (kHeadDim + L_ + 40) * sizeof(double);
+  const size_t swi_smem = static_cast<size_t>(F) * 4;
+  const size_t attn_smem = attn_smem_bytes(L_);
   int rc = DLM_OK;
   for (int l = 0; l < c.n_layers && rc == DLM_OK; ++l) {
     const Layer& Ly = layers_[l];
@@ -609,7 +631,7 @@ int BitNetLM::run_layers(int S, const int* pos, cudaStream_t s) {
                                                                     c.rms_eps, xq_, xs_, nullptr);
     rc = ternary_gemm_i8(Ly.wgu, Ly.agu, xq_, xs_, y_, M, 2 * F, D, s);
     if (rc != DLM_OK) break;
-    swiglu_quant_kernel<<<(M + kSwiWarps - 1) / kSwiWarps, kSwiWarps * 32, swi_smem, s>>>(y_, M, F, xq_, xs_);
+    swiglu_quant_kernel<<<M, kSwiThreads, swi_smem, s>>>(y_, M, F, xq_, xs_);
     rc = ternary_gemm_i8(Ly.wd, Ly.ad, xq_, xs_, h_, M, D, F, s, true);
   }
   if (rc == DLM_OK) DLM_CHECK_CUDA(cudaGetLastError());
@@ -632,8 +654,10 @@ int BitNetLM::run_head(int rows, int stride, int off, cudaStream_t s) {
 int BitNetLM::set_smem_attrs() {
   const BitNetCfg& c = cfg_;
   const size_t norm_smem = static_cast<size_t>(kNormWarps) * c.d_model * 4;
-  const size_t swi_smem = static_cast<size_t>(kSwiWarps) * c.ffn_dim * 4;
-  const size_t attn_smem = (kHeadDim + c.max_seq + 40) * sizeof(double);
+  const size_t swi_smem = static_cast<size_t>(c.ffn_dim) * 4;
+  // the largest a launch asks for: staged V at the longest staged length, or the scores alone
+  const size_t attn_smem = std::max(attn_smem_bytes(std::min(c.max_seq, kVStageMax)),
+                                    attn_smem_bytes(c.max_seq));
   DLM_CHECK_CUDA(cudaFuncSetAttribute(rms_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       static_cast<int>(norm_smem)));
   DLM_CHECK_CUDA(cudaFuncSetAttribute(swiglu_quant_kernel,
