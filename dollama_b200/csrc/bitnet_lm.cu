@@ -232,6 +232,85 @@ __global__ void __launch_bounds__(kAttnThreads)
   }
 }
 
+// The same causal attention for a prefill of S > 1 positions per sequence: one block per
+// (sequence, head) stages the head's K and V rows 0..base+S-1 in shared memory once, and each warp
+// takes query rows in turn (row = one position): lanes compute the double scores of keys lane,
+// lane + 32, ... (each a sequential 64-term sum in index order), the row max by shuffles, the
+// exponentials, lane 0 the sequential sum of the weights, and each lane two output dimensions,
+// accumulated in float over j in order — the reference's operation order for every value.
+constexpr int kAttnSeqWarps = 8;
+constexpr int kAttnSeqMax = 128;  // staged positions (K and V: 64 KB)
+__host__ __device__ constexpr size_t attn_seq_smem_bytes(int n) {
+  return static_cast<size_t>(n) * kHeadDim * 4 * 2 + kAttnSeqWarps * (kHeadDim + n) * sizeof(double);
+}
+__global__ void __launch_bounds__(kAttnSeqWarps * 32)
+    attention_seq_kernel(const float* __restrict__ q, int S, int D, const int* __restrict__ pos_in,
+                         const float* __restrict__ kc, const float* __restrict__ vc, int Lmax,
+                         float* __restrict__ out) {
+  extern __shared__ double shd[];
+  const int H = D / kHeadDim;
+  const int b = blockIdx.x / H, hd = blockIdx.x % H;
+  const int base = pos_in ? *pos_in : 0;
+  const int nmax = base + S;  // positions any row of this block attends to
+  float* sk = reinterpret_cast<float*>(shd);
+  float* sv = sk + static_cast<size_t>(nmax) * kHeadDim;
+  double* wbuf = reinterpret_cast<double*>(sv + static_cast<size_t>(nmax) * kHeadDim);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  double* sq = wbuf + static_cast<size_t>(warp) * (kHeadDim + nmax);
+  double* ss = sq + kHeadDim;
+  {
+    const size_t head = (static_cast<size_t>(b) * H + hd) * Lmax * kHeadDim;
+    const float4* ks = reinterpret_cast<const float4*>(kc + head);
+    const float4* vs = reinterpret_cast<const float4*>(vc + head);
+    float4* kd = reinterpret_cast<float4*>(sk);
+    float4* vd = reinterpret_cast<float4*>(sv);
+    for (int i = threadIdx.x; i < nmax * (kHeadDim / 4); i += blockDim.x) {
+      kd[i] = ks[i];
+      vd[i] = vs[i];
+    }
+  }
+  __syncthreads();
+  for (int p = warp; p < S; p += kAttnSeqWarps) {
+    const int r = b * S + p;
+    const int n = base + p + 1;
+    const float* qr = q + static_cast<size_t>(r) * D + hd * kHeadDim;
+    sq[lane] = static_cast<double>(qr[lane]);
+    sq[lane + 32] = static_cast<double>(qr[lane + 32]);
+    __syncwarp();
+    double mx = -1e300;
+    for (int j = lane; j < n; j += 32) {
+      const float* kj = sk + static_cast<size_t>(j) * kHeadDim;
+      double dot = 0.0;
+#pragma unroll 16
+      for (int d = 0; d < kHeadDim; ++d) dot = __dadd_rn(dot, __dmul_rn(sq[d], static_cast<double>(kj[d])));
+      dot = __dmul_rn(dot, 0.125);  // 1 / sqrt(64), exact
+      ss[j] = dot;
+      mx = fmax(mx, dot);
+    }
+    mx = warp_max_d(mx);
+    for (int j = lane; j < n; j += 32) ss[j] = exp(__dsub_rn(ss[j], mx));
+    __syncwarp();
+    double inv = 0.0;
+    if (lane == 0) {
+      double sum = 0.0;
+      for (int j = 0; j < n; ++j) sum = __dadd_rn(sum, ss[j]);
+      inv = __ddiv_rn(1.0, sum);
+    }
+    inv = __shfl_sync(0xffffffffu, inv, 0);
+    float acc0 = 0.0f, acc1 = 0.0f;
+    for (int j = 0; j < n; ++j) {
+      const double wj = __dmul_rn(ss[j], inv);
+      const float* vj = sv + static_cast<size_t>(j) * kHeadDim;
+      acc0 = __fadd_rn(acc0, __double2float_rn(__dmul_rn(wj, static_cast<double>(vj[lane]))));
+      acc1 = __fadd_rn(acc1, __double2float_rn(__dmul_rn(wj, static_cast<double>(vj[lane + 32]))));
+    }
+    float* orow = out + static_cast<size_t>(r) * D + hd * kHeadDim;
+    orow[lane] = acc0;
+    orow[lane + 32] = acc1;
+    __syncwarp();  // ss / sq are rewritten by this warp's next row
+  }
+}
+
 // SwiGLU (bitnet.hpp:603-610) of gate|up [M, 2F] -> float(silu(g) * u), then int8 quantization;
 // one block per row: every thread computes its elements into the shared row, then warp 0
 // quantizes the row (the same per-element operations in any split, so the same bits).
@@ -623,7 +702,11 @@ int BitNetLM::run_layers(int S, const int* pos, cudaStream_t s) {
     if (rc != DLM_OK) break;
     rope_kv_kernel<<<grid1d(static_cast<size_t>(M) * H * 32, 256), 256, 0, s>>>(
         y_, M, S, D, pos, cos_t_, sin_t_, q_, kc, vc, L_);
-    attention_kernel<<<M * H, kAttnThreads, attn_smem, s>>>(q_, M, S, D, pos, kc, vc, L_, ao_);
+    if (S > 1 && L_ <= kAttnSeqMax)  // prefill: one block per (sequence, head)
+      attention_seq_kernel<<<B_ * H, kAttnSeqWarps * 32, attn_seq_smem_bytes(L_), s>>>(
+          q_, S, D, pos, kc, vc, L_, ao_);
+    else
+      attention_kernel<<<M * H, kAttnThreads, attn_smem, s>>>(q_, M, S, D, pos, kc, vc, L_, ao_);
     rc = quantize_act_i8(ao_, M, D, xq_, xs_, s);
     if (rc == DLM_OK) rc = ternary_gemm_i8(Ly.wo, Ly.ao, xq_, xs_, h_, M, D, D, s, true);
     if (rc != DLM_OK) break;
@@ -665,6 +748,9 @@ int BitNetLM::set_smem_attrs() {
                                       static_cast<int>(swi_smem)));
   DLM_CHECK_CUDA(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       static_cast<int>(attn_smem)));
+  DLM_CHECK_CUDA(cudaFuncSetAttribute(
+      attention_seq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      static_cast<int>(attn_seq_smem_bytes(std::min(c.max_seq, kAttnSeqMax)))));
   return DLM_OK;
 }
 

@@ -30,7 +30,8 @@ def build(out: Path = OUT) -> Path | None:
     if ref is None:
         return out if out.exists() else None
     src = HERE / "shim_driver.cpp"
-    deps = [src, ROOT / "include" / "dollama_b200_shim.hpp", ROOT / "include" / "dollama_b200.h"]
+    deps = [src, ROOT / "include" / "dollama_b200_shim.hpp", ROOT / "include" / "dollama_b200.h",
+            ROOT / "include" / "dollama_b200_runner.hpp"]
     if out.exists() and all(out.stat().st_mtime >= d.stat().st_mtime for d in deps):
         return out
     out.parent.mkdir(parents=True, exist_ok=True)

@@ -9,15 +9,23 @@
 //                          and noise_clear.bin after unet_clear_loras
 //   shim_driver vae DIR    DIR/vae.safetensors + lat.bin ([1,4,128,128]) -> image.bin, through
 //                          the per-call launch_vae_decode(const SafeTensors&, ...)
+//   shim_driver runner DIR the reference's diffusion-runner plugin (IDiffusionRunner, built by
+//                          make_b200_diffusion_runner from DIR/unet.safetensors and
+//                          DIR/vae.safetensors): run_txt2img(4 steps, seed 1234, cfg 7.5) on fp32
+//                          cond / uncond embeddings from DIR -> rgb.bin (uint8 HWC) and the
+//                          initial latent it drew (lat0.bin, fp32)
 //   shim_driver ops DIR    NCHW launch_conv2d on a tensor-core shape and on a direct-path
 //                          shape, launch_group_norm_silu, launch_group_norm in place,
 //                          launch_attention; inputs / outputs as .bin files
 // Exit status 0 on success; a std::runtime_error from the shim is printed and gives 1.
 #include <cstdio>
+#include <cstring>
+#include <memory>
 #include <fstream>
 #include <string>
 #include <vector>
 
+#include "dollama_b200_runner.hpp"
 #include "dollama_b200_shim.hpp"
 
 namespace {
@@ -98,6 +106,37 @@ int run_vae(const std::string& d) {
   return 0;
 }
 
+std::vector<float> read_f32(const std::string& path) {
+  std::vector<uint16_t> raw = read_bin(path);
+  std::vector<float> v(raw.size() / 2);
+  std::memcpy(v.data(), raw.data(), v.size() * 4);
+  return v;
+}
+
+int run_runner(const std::string& d) {
+  std::unique_ptr<dollama::IDiffusionRunner> r = dollama::make_b200_diffusion_runner(
+      d + "/unet.safetensors", d + "/vae.safetensors", "", dollama::FastConfig{}, 0.13025f);
+  if (!r) throw std::runtime_error("make_b200_diffusion_runner returned nullptr");
+  const std::vector<float> ce = read_f32(d + "/cond_ehs.f32"), ct = read_f32(d + "/cond_te.f32"),
+                           ue = read_f32(d + "/uncond_ehs.f32"), ut = read_f32(d + "/uncond_te.f32"),
+                           tid = read_f32(d + "/tid.f32");
+  std::vector<uint8_t> rgb;
+  int w = 0, h = 0;
+  r->run_txt2img(4, 1234, 7.5f, ce.data(), ct.data(), ue.data(), ut.data(), tid.data(), rgb, w, h);
+  if (w != 1024 || h != 1024 || rgb.size() != static_cast<size_t>(w) * h * 3)
+    throw std::runtime_error("run_txt2img: unexpected image size");
+  write_bin(d + "/rgb.bin", rgb.data(), rgb.size());
+  float sig[5], ts[4];
+  if (dlm_sdxl_schedule(4, sig, ts) != DLM_OK) throw std::runtime_error("schedule");
+  std::vector<float> lat(4 * 128 * 128);
+  dollama::b200_initial_latent(1234, sig[0], lat.data(), lat.size());
+  write_bin(d + "/lat0.bin", lat.data(), lat.size() * 4);
+  // a factory that cannot load its weights returns nullptr (the reference's contract)
+  if (dollama::make_b200_diffusion_runner(d + "/missing.safetensors", d + "/vae.safetensors", ""))
+    throw std::runtime_error("factory did not return nullptr for missing weights");
+  return 0;
+}
+
 int run_ops(const std::string& d) {
   {  // tensor-core shape: [2,64,32,32] * [128,64,3,3] stride 1 pad 1
     Dev x(read_bin(d + "/cx.bin")), w(read_bin(d + "/cw.bin")), b(read_bin(d + "/cb.bin"));
@@ -137,7 +176,7 @@ int run_ops(const std::string& d) {
 
 int main(int argc, char** argv) {
   if (argc != 3) {
-    std::fprintf(stderr, "usage: shim_driver {unet|vae|ops} DIR\n");
+    std::fprintf(stderr, "usage: shim_driver {unet|vae|runner|ops} DIR\n");
     return 2;
   }
   const std::string cmd = argv[1], dir = argv[2];
@@ -145,6 +184,7 @@ int main(int argc, char** argv) {
     if (cmd == "unet") return run_unet(dir);
     if (cmd == "vae") return run_vae(dir);
     if (cmd == "ops") return run_ops(dir);
+    if (cmd == "runner") return run_runner(dir);
   } catch (const std::exception& e) {
     std::fprintf(stderr, "shim_driver %s: %s\n", cmd.c_str(), e.what());
     return 1;

@@ -115,3 +115,84 @@ def test_shim_kernel_entries_match_fp32_torch():
     assert max_rel_err(gni, gn6) < 2e-3
     s = torch.softmax(aq.float() @ ak.float().transpose(-1, -2) * 0.125, dim=-1)
     assert max_rel_err(att, s @ av.float()) < 2e-3
+
+
+def _seeded_normal(seed, n):
+    """The reference's initial-noise generator (src/infer/diffusion.cu:76-140), restated in
+    Python for the check: splitmix64-seeded xorshift128+ uniforms, Box-Muller pairs in double."""
+    M = (1 << 64) - 1
+
+    def mix(z):
+        z = (z + 0x9E3779B97F4A7C15) & M
+        z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & M
+        z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & M
+        return z ^ (z >> 31)
+
+    a, b = mix(seed), mix((seed + 0x9E3779B97F4A7C15) & M)
+    out, spare = [], None
+
+    def uniform():
+        nonlocal a, b
+        s1, s0 = a, b
+        a = s0
+        s1 ^= (s1 << 23) & M
+        b = s1 ^ s0 ^ (s1 >> 17) ^ (s0 >> 26)
+        return float(((b + s0) & M) >> 11) * (1.0 / 9007199254740992.0)
+
+    import math
+    while len(out) < n:
+        if spare is not None:
+            out.append(spare)
+            spare = None
+            continue
+        u1 = uniform()
+        while u1 <= 1e-12:
+            u1 = uniform()
+        u2 = uniform()
+        r = math.sqrt(-2.0 * math.log(u1))
+        out.append(r * math.cos(2.0 * math.pi * u2))
+        spare = r * math.sin(2.0 * math.pi * u2)
+    return out
+
+
+def test_shim_runner_txt2img_is_the_python_pipeline_bit_for_bit():
+    """The reference's diffusion-runner plugin (IDiffusionRunner, include/dollama_b200_runner.hpp)
+    through its own factory: the initial latent follows the reference's seeded generator, and the
+    RGB8 image equals the Python pipeline's decode of the same latent and conditioning converted
+    with the reference's rule."""
+    from baseline.ref_gpu import write_safetensors
+    from dollama_b200.pipeline import euler_schedule, generate
+    from dollama_b200.unet import SDXLUNet
+    from dollama_b200.vae import SDXLVAEDecoder
+    from oracle.sdxl_unet import init_weights
+    from oracle.sdxl_vae import init_weights as vae_init
+    sd, sdv = init_weights(seed=7), vae_init(seed=9)
+    g = torch.Generator().manual_seed(31)
+    ce, ue = torch.randn(77, 2048, generator=g), torch.randn(77, 2048, generator=g)
+    ct, ut = torch.randn(1280, generator=g), torch.randn(1280, generator=g)
+    tid = torch.tensor([1024.0, 1024.0, 0.0, 0.0, 1024.0, 1024.0])
+    with tempfile.TemporaryDirectory() as d:
+        write_safetensors(sd, str(Path(d) / "unet.safetensors"))
+        write_safetensors(sdv, str(Path(d) / "vae.safetensors"))
+        for n, t in (("cond_ehs.f32", ce), ("uncond_ehs.f32", ue), ("cond_te.f32", ct),
+                     ("uncond_te.f32", ut), ("tid.f32", tid)):
+            t.numpy().astype(np.float32).tofile(str(Path(d) / n))
+        _run("runner", d)
+        rgb = np.fromfile(str(Path(d) / "rgb.bin"), dtype=np.uint8).reshape(1024, 1024, 3)
+        lat0 = torch.from_numpy(np.fromfile(str(Path(d) / "lat0.bin"), dtype=np.float32))
+    sig, _ = euler_schedule(4)
+    want0 = torch.tensor(_seeded_normal(1234, 64), dtype=torch.float64) * sig[0]
+    assert torch.equal(lat0[:64], want0.float())
+    net = SDXLUNet({k: v.cuda() for k, v in sd.items()})
+    vae = SDXLVAEDecoder({k: v.cuda() for k, v in sdv.items()})
+    ehs = torch.stack([ce, ue]).half().cuda()
+    te = torch.stack([ct, ut]).half().cuda()
+    img = generate(net, vae, lat0.view(1, 4, 128, 128).cuda(), ehs, te, tid.half().cuda(), steps=4,
+                   guidance=7.5)
+    torch.cuda.synchronize()
+    net.close()
+    vae.close()
+    x = img[0].float().cpu().numpy() * np.float32(0.5) + np.float32(0.5)
+    q = np.floor(np.clip(x, 0.0, 1.0) * np.float32(255.0) + np.float32(0.5)).astype(np.int32)
+    want = np.clip(q, 0, 255).astype(np.uint8).transpose(1, 2, 0)
+    assert np.array_equal(rgb, want)
