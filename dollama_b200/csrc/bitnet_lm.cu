@@ -159,8 +159,11 @@ __global__ void rope_kv_kernel(const float* __restrict__ qkv, int M, int S, int 
 // dot product.
 constexpr int kAttnThreads = 128;
 constexpr int kVStageMax = 256;  // cache lengths up to which V is staged (64 KB of shared memory)
+// doubles before the staged V rows, rounded up to an even count so that V starts 16-byte aligned
+// (its rows are written with 16-byte stores) whatever the cache length
+__host__ __device__ constexpr int attn_head_doubles(int Lmax) { return (kHeadDim + Lmax + 40 + 1) & ~1; }
 __host__ __device__ constexpr size_t attn_smem_bytes(int Lmax) {
-  return (kHeadDim + Lmax + 40) * sizeof(double) +
+  return attn_head_doubles(Lmax) * sizeof(double) +
          (Lmax <= kVStageMax ? static_cast<size_t>(Lmax) * kHeadDim * 4 : 0);
 }
 __global__ void __launch_bounds__(kAttnThreads)
@@ -171,7 +174,7 @@ __global__ void __launch_bounds__(kAttnThreads)
   double* sq = sh;
   double* ss = sh + kHeadDim;
   double* red = ss + Lmax;
-  float* sv = reinterpret_cast<float*>(red + 40);
+  float* sv = reinterpret_cast<float*>(sh + attn_head_doubles(Lmax));
   const int H = D / kHeadDim;
   const int r = blockIdx.x / H, hd = blockIdx.x % H;
   if (r >= M) return;

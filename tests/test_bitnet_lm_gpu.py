@@ -94,6 +94,21 @@ def test_generate_baseline_dims_matches_oracle():
     lm.close()
 
 
+@pytest.mark.parametrize("P,max_len", [(5, 24), (6, 23), (7, 21), (9, 10), (21, 22)])
+def test_generate_odd_and_even_cache_lengths(P, max_len):
+    """Cache lengths (max_len) of both parities and prefill-only / one-step decodes: the
+    attention kernels stage K / V rows in shared memory at offsets that depend on the cache
+    length, and must stay 16-byte aligned for every length."""
+    cfg = B.lm_config(vocab=64, d_model=128, n_layers=2, n_heads=2, ffn_dim=128, max_seq=24)
+    w = B.lm_random_weights(cfg, seed=12, kind="normal")
+    prompts = np.random.default_rng(P * 100 + max_len).integers(3, cfg["vocab"], size=(4, P)).astype(np.int32)
+    lm = _gpu(cfg, w)
+    got = lm.generate(prompts, max_len=max_len)
+    o = B.OracleLM(cfg, w)
+    assert got == [o.generate(p, max_len) for p in prompts]
+    lm.close()
+
+
 def test_invalid_tokens_rejected():
     from dollama_b200 import _lib as L
     w = B.lm_random_weights(SMALL, seed=1)
