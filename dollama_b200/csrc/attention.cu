@@ -364,32 +364,36 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const int valid = p.Sk - (sg.j0 + jl) * kKV;  // keys of this tile (may exceed 128)
         const bool full_tile = valid >= kKV;
         if (jl >= 1 && full_tile) {
-          // One pass over S: each 64-column half is read once, its row max checked against the
-          // running max m (the same lazy rule: m moves only when the max exceeds it by more than
-          // 8 in exp2 units, so p = 2^(s c - m c) <= 2^8), then exponentiated against m.  A move
-          // in the second half rescales the first half's P already in TMEM, the partial sums and
+          // One pass over S, 32 columns at a time, each chunk's TMEM load issued while the
+          // previous chunk is exponentiated (so its latency hides behind that work): the chunk's
+          // row max is checked against the running max m (the same lazy rule: m moves only when
+          // the max exceeds it by more than 8 in exp2 units, so p = 2^(s c - m c) <= 2^8), then
+          // exponentiated against m and its fp16 P stored.  A move at chunk k rescales the partial
+          // sums at once and, after the pass, the P of the chunks before k already in TMEM, and
           // (after the previous P.V) O.
-          float m_cur = m_run, alpha_all = 1.0f, a_second = 1.0f;
+          float m_cur = m_run, alpha_all = 1.0f;
+          float a_after[3] = {1.0f, 1.0f, 1.0f};  // scale still owed by the P of chunk 0, 1, 2
           uint64_t sumA = f2_pack(0.0f, 0.0f), sumB = sumA;
-#pragma unroll 1
-          for (int cc = 0; cc < 4; cc += 2) {
-            uint32_t ra[32], rb[32];
-            tmem_ld_32x32b_x32(ts + cc * 32, ra);
-            tmem_ld_32x32b_x32(ts + cc * 32 + 32, rb);
-            tmem_ld_wait();
-            float h0 = m_cur, h1 = m_cur, h2 = m_cur, h3 = m_cur;
+          uint32_t buf[2][32];
+          tmem_ld_32x32b_x32(ts, buf[0]);
+          tmem_ld_wait();
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            if (k < 3) tmem_ld_32x32b_x32(ts + (k + 1) * 32, buf[(k + 1) & 1]);  // prefetch
+            const uint32_t* r = buf[k & 1];
+            float h0 = m_cur, h1 = m_cur;
 #pragma unroll
             for (int q = 0; q < 32; q += 4) {
-              h0 = max3f(h0, __uint_as_float(ra[q]), __uint_as_float(ra[q + 1]));
-              h1 = max3f(h1, __uint_as_float(ra[q + 2]), __uint_as_float(ra[q + 3]));
-              h2 = max3f(h2, __uint_as_float(rb[q]), __uint_as_float(rb[q + 1]));
-              h3 = max3f(h3, __uint_as_float(rb[q + 2]), __uint_as_float(rb[q + 3]));
+              h0 = max3f(h0, __uint_as_float(r[q]), __uint_as_float(r[q + 1]));
+              h1 = max3f(h1, __uint_as_float(r[q + 2]), __uint_as_float(r[q + 3]));
             }
-            const float hm = fmaxf(fmaxf(h0, h1), fmaxf(h2, h3));
+            const float hm = fmaxf(h0, h1);
             if ((hm - m_cur) * c > 8.0f) {
               const float a = fast_exp2((m_cur - hm) * c);
               alpha_all *= a;
-              if (cc == 2) a_second = a;
+#pragma unroll
+              for (int j = 0; j < 3; ++j)
+                if (j < k) a_after[j] *= a;
               const uint64_t a2 = f2_pack(a, a), z2 = f2_pack(0.0f, 0.0f);
               sumA = f2_fma(sumA, a2, z2);
               sumB = f2_fma(sumB, a2, z2);
@@ -397,39 +401,39 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             }
             const float mcc = m_cur * c;
             const uint64_t c2 = f2_pack(c, c), nmc2 = f2_pack(-mcc, -mcc);
-            uint32_t pp[32];
+            uint32_t pp[16];
 #pragma unroll
-            for (int half = 0; half < 2; ++half) {
-              const uint32_t* r = half ? rb : ra;
-#pragma unroll
-              for (int q = 0; q < 32; q += 2) {
-                float x0, x1;
-                f2_unpack(f2_fma(f2_pack(__uint_as_float(r[q]), __uint_as_float(r[q + 1])), c2, nmc2),
-                          x0, x1);
-                const float e0 = fast_exp2(x0);
-                const float e1 = fast_exp2(x1);
-                if (q & 2)
-                  sumB = f2_add(sumB, f2_pack(e0, e1));
-                else
-                  sumA = f2_add(sumA, f2_pack(e0, e1));
-                pp[half * 16 + (q >> 1)] = pack_half2(e0, e1);
-              }
+            for (int q = 0; q < 32; q += 2) {
+              float x0, x1;
+              f2_unpack(f2_fma(f2_pack(__uint_as_float(r[q]), __uint_as_float(r[q + 1])), c2, nmc2),
+                        x0, x1);
+              const float e0 = fast_exp2(x0);
+              const float e1 = fast_exp2(x1);
+              if (q & 2)
+                sumB = f2_add(sumB, f2_pack(e0, e1));
+              else
+                sumA = f2_add(sumA, f2_pack(e0, e1));
+              pp[q >> 1] = pack_half2(e0, e1);
             }
-            tmem_st_32x32b_x32(ts + (cc >> 1) * 32, pp);
+            tmem_st_32x32b_x16(ts + k * 16, pp);
+            if (k < 3) tmem_ld_wait();  // the prefetched chunk has arrived
           }
           tmem_st_wait();
-          if (__any_sync(0xffffffffu, a_second != 1.0f)) {
-            // the first half's P was written against the max before the second half moved it
-            uint32_t pp[32];
-            tmem_ld_32x32b_x32(ts, pp);
-            tmem_ld_wait();
 #pragma unroll
-            for (int q = 0; q < 32; ++q) {
-              const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&pp[q]));
-              pp[q] = pack_half2(f.x * a_second, f.y * a_second);
+          for (int k = 0; k < 3; ++k) {
+            if (__any_sync(0xffffffffu, a_after[k] != 1.0f)) {
+              // chunk k's P was written against a max that a later chunk moved
+              uint32_t pp[16];
+              tmem_ld_32x32b_x16(ts + k * 16, pp);
+              tmem_ld_wait();
+#pragma unroll
+              for (int q = 0; q < 16; ++q) {
+                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&pp[q]));
+                pp[q] = pack_half2(f.x * a_after[k], f.y * a_after[k]);
+              }
+              tmem_st_32x32b_x16(ts + k * 16, pp);
+              tmem_st_wait();
             }
-            tmem_st_32x32b_x32(ts, pp);
-            tmem_st_wait();
           }
           // P.V of tile j-1 is complete before O is rescaled and P_j released
           if (!wwait(&o_full[t], (jj - 1) & 1)) {

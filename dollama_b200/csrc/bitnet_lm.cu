@@ -336,8 +336,9 @@ __global__ void __launch_bounds__(kSwiThreads)
 
 // Tied lm_head (bitnet.hpp:414-436): logits[r, v] = float(sum_d double(x[r, d]) * double(E[v, d]))
 // with d in increasing order for every output (the products are exact in double, so fma equals
-// the reference's multiply-then-add).  Tile: 32 rows x 64 vocab ids, K chunks of 32.
-constexpr int kLmR = 32, kLmV = 64, kLmK = 32;
+// the reference's multiply-then-add).  Tile: 64 rows x 64 vocab ids, K chunks of 32; each thread
+// owns 4 rows x 4 ids (eight shared-memory loads per 16 fma).
+constexpr int kLmR = 64, kLmV = 64, kLmK = 32;
 __global__ void __launch_bounds__(256)
     lm_head_kernel(const float* __restrict__ x, int R, int D, const float* __restrict__ E, int V,
                    float* __restrict__ logits) {
@@ -345,9 +346,9 @@ __global__ void __launch_bounds__(256)
   __shared__ double es[kLmK][kLmV + 1];
   const int r0 = blockIdx.y * kLmR, v0 = blockIdx.x * kLmV;
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;  // v = v0 + tx + 16i, r = r0 + ty + 16j
-  double acc[2][4];
+  double acc[4][4];
 #pragma unroll
-  for (int j = 0; j < 2; ++j)
+  for (int j = 0; j < 4; ++j)
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc[j][i] = 0.0;
   for (int k0 = 0; k0 < D; k0 += kLmK) {
@@ -362,20 +363,20 @@ __global__ void __launch_bounds__(256)
     __syncthreads();
 #pragma unroll 4
     for (int kk = 0; kk < kLmK; ++kk) {
-      double xv[2], ev[4];
+      double xv[4], ev[4];
 #pragma unroll
-      for (int j = 0; j < 2; ++j) xv[j] = xs[kk][ty + 16 * j];
+      for (int j = 0; j < 4; ++j) xv[j] = xs[kk][ty + 16 * j];
 #pragma unroll
       for (int i = 0; i < 4; ++i) ev[i] = es[kk][tx + 16 * i];
 #pragma unroll
-      for (int j = 0; j < 2; ++j)
+      for (int j = 0; j < 4; ++j)
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[j][i] = __fma_rn(xv[j], ev[i], acc[j][i]);
     }
     __syncthreads();
   }
 #pragma unroll
-  for (int j = 0; j < 2; ++j) {
+  for (int j = 0; j < 4; ++j) {
     const int r = r0 + ty + 16 * j;
     if (r >= R) continue;
 #pragma unroll
