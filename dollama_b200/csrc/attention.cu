@@ -5,12 +5,14 @@
 // softmax and P rounded to fp16 for the P.V product (as attention_fast.cu:238 does).
 //
 // One CTA = one (batch, head) and two 128-query tiles T0, T1 that share every K/V tile
-// (320 threads, one CTA per SM, all 512 TMEM columns):
+// (320 or 352 threads, one CTA per SM, all 512 TMEM columns):
 //   warps 0..3 / 4..7  softmax of T0 / T1: thread r of the warpgroup owns query row r (TMEM
-//               lane r).  Per 128-key tile j: pass 1 reads S_j (TMEM) for the row max; pass 2
-//               computes p = 2^(s*c - m*c), the fp32 row sum, and stores P_j as fp16 pairs
-//               into the first 64 TMEM columns of S_j (read already), from where the P.V MMA
-//               takes its A operand (no shared-memory P).  O accumulates in TMEM across the KV
+//               lane r).  Per 128-key tile j: the row max of S_j (TMEM), p = 2^(s*c - m*c), the
+//               fp32 row sum, and P_j as fp16 pairs into the tile's own 64 TMEM columns, from
+//               where the P.V MMA takes its A operand (no shared-memory P).  As soon as all of
+//               S_j is in registers the warps release S_j's columns, so S_{j+1} = Q K_{j+1}^T is
+//               computed while P_j is still being made: both warpgroups' softmaxes run at the
+//               same time instead of taking turns.  O accumulates in TMEM across the KV
 //               tiles (P.V with accumulate); the running max m is lazy: it only moves when a
 //               row max exceeds it by more than 8 in exp2 units (p <= 2^8 otherwise), and only
 //               then is O rescaled in place (TMEM load, scale, store), so most tiles never touch
@@ -20,11 +22,14 @@
 //   warp 8      TMA producer: Q (both tiles) once, then K_j / V_j through a 3-stage ring;
 //   warp 9      TMEM owner + single-thread MMA issuer: S_j^t = Q_t K_j^T (M=128, N=128, K=64)
 //               and O_j^t = P_j^t V_j (M=128, N=64, K=128, P from TMEM, V as an MN-major
-//               operand); P_j's P.V is issued before S_{j+1}, which overwrites P_j's columns.
-// While one tile's softmax runs, the tensor core computes the other tile's S and P.V, so the
-// MMA latency hides behind softmax work (the two warpgroups ping-pong).
-// TMEM columns: S^0 [0,128) (P^0 in [0,64)), S^1 [128,256) (P^1 in [128,192)), O^0 [256,320),
-// O^1 [384,448).
+//               operand); per tile, S_{j+1} is issued as soon as the softmax has released S_j,
+//               before P_j's P.V.  With more than one key tile per query block warp 9 issues
+//               T0's MMAs and an eleventh warp T1's, each waiting only on its own tile's
+//               barriers (one issuer for both made each tile's P.V wait for the other tile's
+//               softmax: 157 -> 138 us on B2 H10 4096^2).
+// The softmax of step j+1 waits for P_j's P.V (it has read P^t) before storing P_{j+1}.
+// TMEM columns: S^0 [0,128), S^1 [128,256), O^0 [256,320), P^0 [320,384), O^1 [384,448),
+// P^1 [448,512).
 //
 // Q/K/V/O are addressed through 4D tensor maps {64 (d), heads, seq, batch} with arbitrary
 // strides, so the same kernel reads the token-major [B*S, ld] projections of the UNet (head h at
@@ -44,7 +49,8 @@ constexpr int kQ = 2 * kQT;    // queries per CTA
 constexpr int kKV = 128;       // keys per tile
 constexpr int kD = 64;         // head dim
 constexpr int kKVStages = 3;
-constexpr int kAttnThreads = 320;
+// 10 warps; 11 with a second MMA issuer (kSplit)
+constexpr int attn_threads(bool split) { return split ? 352 : 320; }
 constexpr int kTileBytes = kQT * kD * 2;         // 16 KB (Q, K or V tile)
 constexpr uint32_t kTmemCols = 512;
 
@@ -114,11 +120,13 @@ struct AttnSegIter {
   }
 };
 
-// 10 warps: one SM sub-partition holds three of them, so its 16K-register slice caps the kernel at
-// 168 registers per thread.  kSK: stream-K schedule (a CTA's range of tile-steps may cut groups,
-// merged through the workspace); otherwise one whole group per CTA.
-template <bool kSK>
-__global__ void __launch_bounds__(kAttnThreads, 1)
+// 10 or 11 warps: one SM sub-partition holds three of them, so its 16K-register slice caps the
+// kernel at 168 registers per thread.  kSK: stream-K schedule (a CTA's range of tile-steps may
+// cut groups, merged through the workspace); otherwise one whole group per CTA.  kSplit: one
+// MMA issuer per query tile (warp 9: T0, warp 10: T1) instead of one for both; worth its extra
+// warp only when a segment has more than one key tile.
+template <bool kSK, bool kSplit>
+__global__ void __launch_bounds__(attn_threads(kSplit), 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -133,10 +141,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* v_full = k_full + kKVStages;      // [stages]
   uint64_t* kv_empty = v_full + kKVStages;    // [stages]
   uint64_t* s_full = kv_empty + kKVStages;    // [tile]      S_j^t ready
-  uint64_t* p_full = s_full + 2;              // [tile]      P_j^t stored, S_j^t consumed
+  uint64_t* p_full = s_full + 2;              // [tile]      P_j^t stored
   uint64_t* o_full = p_full + 2;              // [tile]      P_j^t . V_j accumulated into O^t
   uint64_t* o_empty = o_full + 2;             // [tile]      O^t of a segment read out
-  uint64_t* q_empty = o_empty + 2;            // the last S MMAs of a segment read Q
+  uint64_t* s_free = o_empty + 2;             // [tile]      S_j^t read into registers
+  uint64_t* q_empty = s_free + 2;             // the last S MMAs of a segment read Q
   uint64_t* ep_bar = q_empty + 1;             // the eight softmax warps meet (stream-K merge)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ep_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -150,7 +159,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    mbar_init(q_empty, 1);
+    mbar_init(q_empty, kSplit ? 2 : 1);  // one commit per MMA issuer
     mbar_init(ep_bar, 8);
     for (int s = 0; s < kKVStages; ++s) {
       mbar_init(&k_full[s], 1);
@@ -162,6 +171,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(&p_full[t], kQT);
       mbar_init(&o_full[t], 1);
       mbar_init(&o_empty[t], kQT);
+      mbar_init(&s_free[t], kQT);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -223,7 +233,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         ++seg;
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == 9 || (kSplit && warp == 10)) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_f16_f32(kQT, kKV, false);
@@ -234,6 +244,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       bool ok = true;
       auto issue_s = [&](int t, int jl) -> bool {
         const int kk = kc + jl, st = kk % kKVStages;
+        const int step = jc + jl;
+        // S^t is free once the softmax warps hold the previous tile-step's S in registers
+        if (step > 0 &&
+            !mbar_wait(&s_free[t], (step - 1) & 1, abort_flag, p.status, kDevTimeoutMma))
+          return false;
         if (!mbar_wait(&k_full[st], (kk / kKVStages) & 1, abort_flag, p.status, kDevTimeoutMma))
           return false;
         tc_fence_after();
@@ -257,7 +272,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             !mbar_wait(&o_empty[t], (seg - 1) & 1, abort_flag, p.status, kDevTimeoutMma))
           return false;
         tc_fence_after();
-        const uint32_t p_tmem = tbase + t * kKV;  // P^t: 64 columns of fp16 pairs
+        const uint32_t p_tmem = tbase + 320 + t * 128;  // P^t: 64 columns of fp16 pairs
         const uint32_t v_addr = smem_u32(sV + st * kTileBytes);
         const uint32_t d = tbase + 256 + t * 128;
 #pragma unroll
@@ -269,33 +284,65 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         umma_commit(&kv_empty[st]);
         return true;
       };
-      AttnSegIter<kSK> si;
-      si.init(p, n_tiles, groups);
-      AttnSeg sg;
-      while (ok && si.next(sg)) {
-        const int n = sg.j1 - sg.j0;
-        ok = mbar_wait(q_full, seg & 1, abort_flag, p.status, kDevTimeoutMma);
-        if (ok) ok = issue_s(0, 0);
-        if (ok) ok = issue_s(1, 0);
-        if (ok && n == 1) umma_commit(q_empty);  // Q is not read after these
-        for (int jl = 0; jl < n && ok; ++jl) {
-          for (int t = 0; t < 2 && ok; ++t) {
-            if (!mbar_wait(&p_full[t], (jc + jl) & 1, abort_flag, p.status, kDevTimeoutMma)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            // P.V reads P_j from S_j's columns before S_{j+1} overwrites them (in-order MMAs)
-            ok = issue_pv(t, jl);
-            if (ok && jl + 1 < n) {
+      if constexpr (kSplit) {
+        // One issuing thread per query tile (warp 9: T0, warp 10: T1), so neither tile's MMAs
+        // wait behind the other tile's softmax: S_{j+1} once S_j is released, then P_j.V once
+        // P_j is stored.  The two issuers share the K / V ring (each commits kv_empty once per
+        // stage) and Q (each commits q_empty once per segment).
+        const int t = warp - 9;
+        AttnSegIter<kSK> si;
+        si.init(p, n_tiles, groups);
+        AttnSeg sg;
+        while (ok && si.next(sg)) {
+          const int n = sg.j1 - sg.j0;
+          ok = mbar_wait(q_full, seg & 1, abort_flag, p.status, kDevTimeoutMma);
+          if (ok) ok = issue_s(t, 0);
+          if (ok && n == 1) umma_commit(q_empty);  // Q is not read after this
+          for (int jl = 0; jl < n && ok; ++jl) {
+            if (jl + 1 < n) {
               ok = issue_s(t, jl + 1);
-              if (ok && t == 1 && jl + 2 == n) umma_commit(q_empty);  // last S of the segment
+              if (ok && jl + 2 == n) umma_commit(q_empty);  // last S of the segment
+            }
+            if (ok && !mbar_wait(&p_full[t], (jc + jl) & 1, abort_flag, p.status, kDevTimeoutMma))
+              ok = false;
+            if (!ok) break;
+            tc_fence_after();
+            ok = issue_pv(t, jl);
+          }
+          kc += n;
+          jc += n;
+          ++seg;
+        }
+      } else {
+        // one issuer for both tiles, per key tile: each tile's S_{j+1} (once S_j is released),
+        // then its P_j.V (once P_j is stored)
+        AttnSegIter<kSK> si;
+        si.init(p, n_tiles, groups);
+        AttnSeg sg;
+        while (ok && si.next(sg)) {
+          const int n = sg.j1 - sg.j0;
+          ok = mbar_wait(q_full, seg & 1, abort_flag, p.status, kDevTimeoutMma);
+          if (ok) ok = issue_s(0, 0);
+          if (ok) ok = issue_s(1, 0);
+          if (ok && n == 1) umma_commit(q_empty);  // Q is not read after these
+          for (int jl = 0; jl < n && ok; ++jl) {
+            for (int t = 0; t < 2 && ok; ++t) {
+              if (jl + 1 < n) {
+                ok = issue_s(t, jl + 1);
+                if (ok && t == 1 && jl + 2 == n) umma_commit(q_empty);  // last S of the segment
+              }
+              if (ok &&
+                  !mbar_wait(&p_full[t], (jc + jl) & 1, abort_flag, p.status, kDevTimeoutMma))
+                ok = false;
+              if (!ok) break;
+              tc_fence_after();
+              ok = issue_pv(t, jl);
             }
           }
+          kc += n;
+          jc += n;
+          ++seg;
         }
-        kc += n;
-        jc += n;
-        ++seg;
       }
       // the last MMA is issued: the next kernel may launch during this CTA's final softmax
       griddep_launch_dependents();
@@ -307,6 +354,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t ts = tbase + lane_off + t * kKV;
     const uint32_t to = tbase + lane_off + 256 + t * 128;
+    const uint32_t tp = tbase + lane_off + 320 + t * 128;
+    // S_j^t is in this thread's registers: the MMA warp may write S_{j+1}^t
+    auto release_s = [&]() {
+      tc_fence_before();
+      mbar_arrive(&s_free[t]);
+    };
     const float c = p.scale_log2;
     bool ok = true;
     int jc = 0;
@@ -375,6 +428,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           float a_after[3] = {1.0f, 1.0f, 1.0f};  // scale still owed by the P of chunk 0, 1, 2
           uint64_t sumA = f2_pack(0.0f, 0.0f), sumB = sumA;
           uint32_t buf[2][32];
+          bool waited = true;
           tmem_ld_32x32b_x32(ts, buf[0]);
           tmem_ld_wait();
 #pragma unroll
@@ -415,8 +469,22 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 sumA = f2_add(sumA, f2_pack(e0, e1));
               pp[q >> 1] = pack_half2(e0, e1);
             }
-            tmem_st_32x32b_x16(ts + k * 16, pp);
+            if (k == 0) {
+              // P_{j-1}.V is complete: it has read P^t and added into O
+              waited = wwait(&o_full[t], (jj - 1) & 1);
+              if (!waited) {
+                tmem_ld_wait();
+                break;
+              }
+              tc_fence_after();
+            }
+            tmem_st_32x32b_x16(tp + k * 16, pp);
             if (k < 3) tmem_ld_wait();  // the prefetched chunk has arrived
+            if (k == 2) release_s();    // all of S_j is in registers
+          }
+          if (!waited) {
+            ok = false;
+            break;
           }
           tmem_st_wait();
 #pragma unroll
@@ -424,23 +492,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             if (__any_sync(0xffffffffu, a_after[k] != 1.0f)) {
               // chunk k's P was written against a max that a later chunk moved
               uint32_t pp[16];
-              tmem_ld_32x32b_x16(ts + k * 16, pp);
+              tmem_ld_32x32b_x16(tp + k * 16, pp);
               tmem_ld_wait();
 #pragma unroll
               for (int q = 0; q < 16; ++q) {
                 const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&pp[q]));
                 pp[q] = pack_half2(f.x * a_after[k], f.y * a_after[k]);
               }
-              tmem_st_32x32b_x16(ts + k * 16, pp);
+              tmem_st_32x32b_x16(tp + k * 16, pp);
               tmem_st_wait();
             }
           }
-          // P.V of tile j-1 is complete before O is rescaled and P_j released
-          if (!wwait(&o_full[t], (jj - 1) & 1)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
           if (__any_sync(0xffffffffu, alpha_all != 1.0f)) rescale_o(alpha_all);
           float sum0, sum1, sum2, sum3;
           f2_unpack(sumA, sum0, sum1);
@@ -496,8 +558,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           tc_fence_after();
           if (__any_sync(0xffffffffu, alpha != 1.0f)) rescale_o(alpha);
         }
-        // pass 2: p = exp2(s*c - m*c), fp32 row sum, fp16 P (pairs of consecutive keys) into
-        // S_j's first 64 TMEM columns, which this thread's lane has read already
+        // pass 2: p = exp2(s*c - m*c), fp32 row sum, fp16 P (pairs of consecutive keys) into P^t
         const uint64_t c2 = f2_pack(c, c), nmc2 = f2_pack(-mc, -mc);
         uint64_t sumA = f2_pack(0.0f, 0.0f), sumB = sumA;
 #pragma unroll
@@ -506,6 +567,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           tmem_ld_32x32b_x32(ts + cc * 32, ra);
           tmem_ld_32x32b_x32(ts + cc * 32 + 32, rb);
           tmem_ld_wait();
+          if (cc == 2) release_s();
           uint32_t pp[32];
 #pragma unroll
           for (int half = 0; half < 2; ++half) {
@@ -529,7 +591,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
               pp[half * 16 + (q >> 1)] = pack_half2(e0, e1);
             }
           }
-          tmem_st_32x32b_x32(ts + (cc >> 1) * 32, pp);
+          tmem_st_32x32b_x32(tp + (cc >> 1) * 32, pp);
         }
         tmem_st_wait();
         float sum0, sum1, sum2, sum3;
@@ -746,10 +808,12 @@ int attn_plan(AttnOp* op, int B, int H, int Sq, int Sk, int Dh, float scale, con
 }
 
 int attn_prepare_kernels() {
-  DLM_CHECK_CUDA(cudaFuncSetAttribute(attn_fwd_kernel<false>,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem));
-  DLM_CHECK_CUDA(cudaFuncSetAttribute(attn_fwd_kernel<true>,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem));
+  const void* fns[4] = {reinterpret_cast<const void*>(attn_fwd_kernel<false, false>),
+                        reinterpret_cast<const void*>(attn_fwd_kernel<true, false>),
+                        reinterpret_cast<const void*>(attn_fwd_kernel<false, true>),
+                        reinterpret_cast<const void*>(attn_fwd_kernel<true, true>)};
+  for (const void* f : fns)
+    DLM_CHECK_CUDA(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem));
   return DLM_OK;
 }
 
@@ -764,7 +828,8 @@ int attn_launch(const AttnOp& op, cudaStream_t s) {
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(op.grid, 1, 1);
-  cfg.blockDim = dim3(kAttnThreads, 1, 1);
+  const bool split = op.p.Sk > kKV;  // more than one key tile per query block
+  cfg.blockDim = dim3(attn_threads(split), 1, 1);
   cfg.dynamicSmemBytes = kAttnSmem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -772,10 +837,15 @@ int attn_launch(const AttnOp& op, cudaStream_t s) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
-  if (op.p.sk_ctas > 0)
-    DLM_CHECK_CUDA(cudaLaunchKernelEx(&cfg, attn_fwd_kernel<true>, op.tmQ, op.tmK, op.tmV, op.p));
+  const bool sk = op.p.sk_ctas > 0;
+  if (sk && split)
+    DLM_CHECK_CUDA(cudaLaunchKernelEx(&cfg, attn_fwd_kernel<true, true>, op.tmQ, op.tmK, op.tmV, op.p));
+  else if (sk)
+    DLM_CHECK_CUDA(cudaLaunchKernelEx(&cfg, attn_fwd_kernel<true, false>, op.tmQ, op.tmK, op.tmV, op.p));
+  else if (split)
+    DLM_CHECK_CUDA(cudaLaunchKernelEx(&cfg, attn_fwd_kernel<false, true>, op.tmQ, op.tmK, op.tmV, op.p));
   else
-    DLM_CHECK_CUDA(cudaLaunchKernelEx(&cfg, attn_fwd_kernel<false>, op.tmQ, op.tmK, op.tmV, op.p));
+    DLM_CHECK_CUDA(cudaLaunchKernelEx(&cfg, attn_fwd_kernel<false, false>, op.tmQ, op.tmK, op.tmV, op.p));
   return DLM_OK;
 }
 
