@@ -41,6 +41,48 @@ __device__ __forceinline__ double warp_max_d(double v) {
   return v;
 }
 
+// p[0] + p[1] + ... + p[n-1] in index order from 0.0 (((0 + p0) + p1) + ...), by one thread: the
+// reference's sequential sums.  The loads run eight elements ahead of the additions, so the
+// dependent chain waits on the adder rather than on shared memory.
+__device__ __forceinline__ double seq_sum(const double* p, int n) {
+  double s = 0.0;
+  const int n8 = n & ~7;
+  int i = 0;
+  if (n8 > 0) {
+    double a[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) a[k] = p[k];
+    for (; i < n8; i += 8) {
+      double b[8];
+      const bool more = i + 8 < n8;
+      if (more) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) b[k] = p[i + 8 + k];
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) s = __dadd_rn(s, a[k]);
+      if (more) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) a[k] = b[k];
+      }
+    }
+  }
+  for (; i < n; ++i) s = __dadd_rn(s, p[i]);
+  return s;
+}
+
+// One element of the absmax int8 quantization (quantize_activation_int8, bitnet.hpp:123-165).
+__device__ __forceinline__ int8_t quant_one(float x, double scale, double inv) {
+  int v = 0;
+  if (scale != 0.0) {
+    double r = round(__dmul_rn(static_cast<double>(x), inv));
+    if (r > 127.0) r = 127.0;
+    if (r < -127.0) r = -127.0;
+    v = static_cast<int>(r);
+  }
+  return static_cast<int8_t>(v);
+}
+
 // Exact absmax int8 quantization of one row held in shared memory (quantize_activation_int8,
 // bitnet.hpp:123-165), by one warp.
 __device__ __forceinline__ void quant_row_warp(const float* row, int K, int8_t* q, float* scale_out) {
@@ -51,16 +93,7 @@ __device__ __forceinline__ void quant_row_warp(const float* row, int K, int8_t* 
   const double scale = __ddiv_rn(amax, 127.0);
   const double inv = scale == 0.0 ? 0.0 : __ddiv_rn(1.0, scale);
   if (lane == 0) *scale_out = static_cast<float>(scale);
-  for (int i = lane; i < K; i += 32) {
-    int v = 0;
-    if (scale != 0.0) {
-      double r = round(__dmul_rn(static_cast<double>(row[i]), inv));
-      if (r > 127.0) r = 127.0;
-      if (r < -127.0) r = -127.0;
-      v = static_cast<int>(r);
-    }
-    q[i] = static_cast<int8_t>(v);
-  }
+  for (int i = lane; i < K; i += 32) q[i] = quant_one(row[i], scale, inv);
 }
 
 // Row r of the output reads token tokens[b * ld_tok + base + p] (b = r / S, p = r % S, base =
@@ -81,30 +114,37 @@ __global__ void embed_kernel(const int* __restrict__ tokens, int ld_tok, int S,
   for (int i = threadIdx.x; i < D / 4; i += blockDim.x) dst[i] = src[i];
 }
 
-// rms_norm (bitnet.hpp:234-250), one warp per output row: the sum of squares runs in index order on
-// lane 0 (as the reference's loop), then x * inv * w per element, rounded to float.  Output row r
-// reads input row r * in_stride + in_off.  Optionally quantizes the normalised row (int8) and / or
-// stores it as float.
+// rms_norm (bitnet.hpp:234-250), one warp per output row: every lane forms the double squares of
+// its elements, lane 0 adds them in index order (as the reference's loop), then x * inv * w per
+// element, rounded to float.  Output row r reads input row r * in_stride + in_off.  Optionally
+// quantizes the normalised row (int8) and / or stores it as float.
 constexpr int kNormWarps = 4;
+// per block: the rows as float, then their squares as double
+__host__ __device__ constexpr size_t norm_smem_bytes(int D) {
+  return static_cast<size_t>(kNormWarps) * D * (4 + 8);
+}
 __global__ void __launch_bounds__(kNormWarps * 32)
     rms_norm_kernel(const float* __restrict__ h, int rows, int D, int in_stride, int in_off,
                     const float* __restrict__ w, double eps, int8_t* __restrict__ xq,
                     float* __restrict__ xs, float* __restrict__ out_f) {
-  extern __shared__ float srow[];  // [kNormWarps][D]
+  extern __shared__ float srow[];  // [kNormWarps][D] float, then [kNormWarps][D] double
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = blockIdx.x * kNormWarps + warp;
   if (r >= rows) return;
   float* row = srow + static_cast<size_t>(warp) * D;
+  // 16 * D bytes from the base: 8-byte aligned
+  double* sqr = reinterpret_cast<double*>(srow + static_cast<size_t>(kNormWarps) * D) +
+                static_cast<size_t>(warp) * D;
   const float* src = h + (static_cast<size_t>(r) * in_stride + in_off) * D;
-  for (int i = lane; i < D; i += 32) row[i] = src[i];
+  for (int i = lane; i < D; i += 32) {
+    const float v = src[i];
+    row[i] = v;
+    sqr[i] = __dmul_rn(static_cast<double>(v), static_cast<double>(v));
+  }
   __syncwarp();
   double inv = 0.0;
   if (lane == 0) {
-    double ms = 0.0;
-    for (int i = 0; i < D; ++i) {
-      const double v = static_cast<double>(row[i]);
-      ms = __dadd_rn(ms, __dmul_rn(v, v));
-    }
+    double ms = seq_sum(sqr, D);
     ms = __ddiv_rn(ms, static_cast<double>(D));
     inv = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(ms, eps)));
   }
@@ -218,19 +258,16 @@ __global__ void __launch_bounds__(kAttnThreads)
   mx = red[kAttnThreads / 32];
   for (int j = threadIdx.x; j < n; j += blockDim.x) ss[j] = exp(__dsub_rn(ss[j], mx));
   __syncthreads();
-  if (threadIdx.x == 0) {
-    double sum = 0.0;
-    for (int j = 0; j < n; ++j) sum = __dadd_rn(sum, ss[j]);
-    red[kAttnThreads / 32 + 1] = __ddiv_rn(1.0, sum);
-  }
+  if (threadIdx.x == 0) red[kAttnThreads / 32 + 1] = __ddiv_rn(1.0, seq_sum(ss, n));
   __syncthreads();
   const double inv = red[kAttnThreads / 32 + 1];
+  // the weights w_j = e_j / sum, once per key
+  for (int j = threadIdx.x; j < n; j += blockDim.x) ss[j] = __dmul_rn(ss[j], inv);
+  __syncthreads();
   for (int d = threadIdx.x; d < kHeadDim; d += blockDim.x) {
     float acc = 0.0f;
-    for (int j = 0; j < n; ++j) {
-      const double wj = __dmul_rn(ss[j], inv);
-      acc = __fadd_rn(acc, __double2float_rn(__dmul_rn(wj, static_cast<double>(vrows[j * kHeadDim + d]))));
-    }
+    for (int j = 0; j < n; ++j)
+      acc = __fadd_rn(acc, __double2float_rn(__dmul_rn(ss[j], static_cast<double>(vrows[j * kHeadDim + d]))));
     out[static_cast<size_t>(r) * D + hd * kHeadDim + d] = acc;
   }
 }
@@ -243,20 +280,28 @@ __global__ void __launch_bounds__(kAttnThreads)
 // accumulated in float over j in order — the reference's operation order for every value.
 constexpr int kAttnSeqWarps = 8;
 constexpr int kAttnSeqMax = 128;  // staged positions (K and V: 64 KB)
+// K rows are staged with a stride of 65 floats, so the 32 lanes' keys at one dimension fall in 32
+// different banks; the float count of the K block is rounded up to a multiple of four, so V
+// (written with 16-byte stores) and the doubles after it stay 16-byte aligned for any n.
+constexpr int kKStride = kHeadDim + 1;
+__host__ __device__ constexpr size_t attn_seq_k_floats(int n) {
+  return (static_cast<size_t>(n) * kKStride + 3) & ~static_cast<size_t>(3);
+}
 __host__ __device__ constexpr size_t attn_seq_smem_bytes(int n) {
-  return static_cast<size_t>(n) * kHeadDim * 4 * 2 + kAttnSeqWarps * (kHeadDim + n) * sizeof(double);
+  return (attn_seq_k_floats(n) + static_cast<size_t>(n) * kHeadDim) * 4 +
+         kAttnSeqWarps * (kHeadDim + n) * sizeof(double);
 }
 __global__ void __launch_bounds__(kAttnSeqWarps * 32)
     attention_seq_kernel(const float* __restrict__ q, int S, int D, const int* __restrict__ pos_in,
                          const float* __restrict__ kc, const float* __restrict__ vc, int Lmax,
                          float* __restrict__ out) {
-  extern __shared__ double shd[];
+  extern __shared__ __align__(16) double shd[];
   const int H = D / kHeadDim;
   const int b = blockIdx.x / H, hd = blockIdx.x % H;
   const int base = pos_in ? *pos_in : 0;
   const int nmax = base + S;  // positions any row of this block attends to
   float* sk = reinterpret_cast<float*>(shd);
-  float* sv = sk + static_cast<size_t>(nmax) * kHeadDim;
+  float* sv = sk + attn_seq_k_floats(nmax);
   double* wbuf = reinterpret_cast<double*>(sv + static_cast<size_t>(nmax) * kHeadDim);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   double* sq = wbuf + static_cast<size_t>(warp) * (kHeadDim + nmax);
@@ -265,10 +310,14 @@ __global__ void __launch_bounds__(kAttnSeqWarps * 32)
     const size_t head = (static_cast<size_t>(b) * H + hd) * Lmax * kHeadDim;
     const float4* ks = reinterpret_cast<const float4*>(kc + head);
     const float4* vs = reinterpret_cast<const float4*>(vc + head);
-    float4* kd = reinterpret_cast<float4*>(sk);
     float4* vd = reinterpret_cast<float4*>(sv);
     for (int i = threadIdx.x; i < nmax * (kHeadDim / 4); i += blockDim.x) {
-      kd[i] = ks[i];
+      const float4 kv = ks[i];
+      float* kd = sk + (i >> 4) * kKStride + (i & 15) * 4;
+      kd[0] = kv.x;
+      kd[1] = kv.y;
+      kd[2] = kv.z;
+      kd[3] = kv.w;
       vd[i] = vs[i];
     }
   }
@@ -282,7 +331,7 @@ __global__ void __launch_bounds__(kAttnSeqWarps * 32)
     __syncwarp();
     double mx = -1e300;
     for (int j = lane; j < n; j += 32) {
-      const float* kj = sk + static_cast<size_t>(j) * kHeadDim;
+      const float* kj = sk + static_cast<size_t>(j) * kKStride;
       double dot = 0.0;
 #pragma unroll 16
       for (int d = 0; d < kHeadDim; ++d) dot = __dadd_rn(dot, __dmul_rn(sq[d], static_cast<double>(kj[d])));
@@ -294,15 +343,14 @@ __global__ void __launch_bounds__(kAttnSeqWarps * 32)
     for (int j = lane; j < n; j += 32) ss[j] = exp(__dsub_rn(ss[j], mx));
     __syncwarp();
     double inv = 0.0;
-    if (lane == 0) {
-      double sum = 0.0;
-      for (int j = 0; j < n; ++j) sum = __dadd_rn(sum, ss[j]);
-      inv = __ddiv_rn(1.0, sum);
-    }
+    if (lane == 0) inv = __ddiv_rn(1.0, seq_sum(ss, n));
     inv = __shfl_sync(0xffffffffu, inv, 0);
+    // the weights w_j = e_j / sum, once per key
+    for (int j = lane; j < n; j += 32) ss[j] = __dmul_rn(ss[j], inv);
+    __syncwarp();
     float acc0 = 0.0f, acc1 = 0.0f;
     for (int j = 0; j < n; ++j) {
-      const double wj = __dmul_rn(ss[j], inv);
+      const double wj = ss[j];
       const float* vj = sv + static_cast<size_t>(j) * kHeadDim;
       acc0 = __fadd_rn(acc0, __double2float_rn(__dmul_rn(wj, static_cast<double>(vj[lane]))));
       acc1 = __fadd_rn(acc1, __double2float_rn(__dmul_rn(wj, static_cast<double>(vj[lane + 32]))));
@@ -315,23 +363,36 @@ __global__ void __launch_bounds__(kAttnSeqWarps * 32)
 }
 
 // SwiGLU (bitnet.hpp:603-610) of gate|up [M, 2F] -> float(silu(g) * u), then int8 quantization;
-// one block per row: every thread computes its elements into the shared row, then warp 0
-// quantizes the row (the same per-element operations in any split, so the same bits).
+// one block per row: every thread computes its elements and their absolute maximum, the block
+// combines the maxima, and every thread quantizes its own elements (a maximum and per-element
+// operations, so the same bits in any split).
 constexpr int kSwiThreads = 256;
 __global__ void __launch_bounds__(kSwiThreads)
     swiglu_quant_kernel(const float* __restrict__ gu, int M, int F, int8_t* __restrict__ xq,
                         float* __restrict__ xs) {
   extern __shared__ float srow[];  // [F]
+  __shared__ double s_amax[kSwiThreads / 32];
   const int r = blockIdx.x;
   if (r >= M) return;
   const float* g = gu + static_cast<size_t>(r) * 2 * F;
+  double amax = 0.0;
   for (int f = threadIdx.x; f < F; f += kSwiThreads) {
     const double gv = static_cast<double>(g[f]);
     const double silu = __ddiv_rn(gv, __dadd_rn(1.0, exp(-gv)));
-    srow[f] = __double2float_rn(__dmul_rn(silu, static_cast<double>(g[F + f])));
+    const float v = __double2float_rn(__dmul_rn(silu, static_cast<double>(g[F + f])));
+    srow[f] = v;
+    amax = fmax(amax, fabs(static_cast<double>(v)));
   }
+  amax = warp_max_d(amax);
+  if ((threadIdx.x & 31) == 0) s_amax[threadIdx.x >> 5] = amax;
   __syncthreads();
-  if (threadIdx.x < 32) quant_row_warp(srow, F, xq + static_cast<size_t>(r) * F, xs + r);
+#pragma unroll
+  for (int w = 0; w < kSwiThreads / 32; ++w) amax = fmax(amax, s_amax[w]);
+  const double scale = __ddiv_rn(amax, 127.0);
+  const double inv = scale == 0.0 ? 0.0 : __ddiv_rn(1.0, scale);
+  if (threadIdx.x == 0) xs[r] = static_cast<float>(scale);
+  int8_t* q = xq + static_cast<size_t>(r) * F;
+  for (int f = threadIdx.x; f < F; f += kSwiThreads) q[f] = quant_one(srow[f], scale, inv);
 }
 
 // Tied lm_head (bitnet.hpp:414-436): logits[r, v] = float(sum_d double(x[r, d]) * double(E[v, d]))
@@ -692,7 +753,7 @@ int BitNetLM::run_layers(int S, const int* pos, cudaStream_t s) {
   const int M = B_ * S, D = c.d_model, F = c.ffn_dim, H = D / kHeadDim;
   const size_t kv_layer = static_cast<size_t>(B_) * H * L_ * kHeadDim;
   const int norm_blocks = (M + kNormWarps - 1) / kNormWarps;
-  const size_t norm_smem = static_cast<size_t>(kNormWarps) * D * 4;
+  const size_t norm_smem = norm_smem_bytes(D);
   const size_t swi_smem = static_cast<size_t>(F) * 4;
   const size_t attn_smem = attn_smem_bytes(L_);
   int rc = DLM_OK;
@@ -729,8 +790,7 @@ int BitNetLM::run_layers(int S, const int* pos, cudaStream_t s) {
 int BitNetLM::run_head(int rows, int stride, int off, cudaStream_t s) {
   const BitNetCfg& c = cfg_;
   const int D = c.d_model;
-  rms_norm_kernel<<<(rows + kNormWarps - 1) / kNormWarps, kNormWarps * 32,
-                    static_cast<size_t>(kNormWarps) * D * 4, s>>>(h_, rows, D, stride, off, final_norm_,
+  rms_norm_kernel<<<(rows + kNormWarps - 1) / kNormWarps, kNormWarps * 32, norm_smem_bytes(D), s>>>(h_, rows, D, stride, off, final_norm_,
                                                                   c.rms_eps, nullptr, nullptr, norm_);
   dim3 grid((c.vocab + kLmV - 1) / kLmV, (rows + kLmR - 1) / kLmR);
   lm_head_kernel<<<grid, 256, 0, s>>>(norm_, rows, D, embed_, c.vocab, logits_);
@@ -740,7 +800,7 @@ int BitNetLM::run_head(int rows, int stride, int off, cudaStream_t s) {
 
 int BitNetLM::set_smem_attrs() {
   const BitNetCfg& c = cfg_;
-  const size_t norm_smem = static_cast<size_t>(kNormWarps) * c.d_model * 4;
+  const size_t norm_smem = norm_smem_bytes(c.d_model);
   const size_t swi_smem = static_cast<size_t>(c.ffn_dim) * 4;
   // the largest a launch asks for: staged V at the longest staged length, or the scores alone
   const size_t attn_smem = std::max(attn_smem_bytes(std::min(c.max_seq, kVStageMax)),
