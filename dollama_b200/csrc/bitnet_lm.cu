@@ -26,6 +26,7 @@
 #include <vector>
 
 #include "bitnet_lm.h"
+#include "ptx.cuh"
 #include "ternary.h"
 
 namespace dlm {
@@ -226,9 +227,11 @@ __global__ void __launch_bounds__(kAttnThreads)
   for (int d = threadIdx.x; d < kHeadDim; d += blockDim.x) sq[d] = static_cast<double>(qr[d]);
   const bool staged = Lmax <= kVStageMax;
   if (staged) {
-    const float4* src = reinterpret_cast<const float4*>(vb);
-    float4* dst = reinterpret_cast<float4*>(sv);
-    for (int i = threadIdx.x; i < n * (kHeadDim / 4); i += blockDim.x) dst[i] = src[i];
+    // V rows 0..n-1 into shared memory by asynchronous 16-byte copies, all in flight at once:
+    // they land while the scores are formed (16-byte aligned: attn_head_doubles is even)
+    for (int i = threadIdx.x; i < n * (kHeadDim / 4); i += blockDim.x)
+      cp_async16(sv + 4 * i, vb + 4 * i, 16);
+    cp_async_commit();
   }
   const float* vrows = staged ? sv : vb;
   __syncthreads();
@@ -263,6 +266,7 @@ __global__ void __launch_bounds__(kAttnThreads)
   const double inv = red[kAttnThreads / 32 + 1];
   // the weights w_j = e_j / sum, once per key
   for (int j = threadIdx.x; j < n; j += blockDim.x) ss[j] = __dmul_rn(ss[j], inv);
+  if (staged) cp_async_wait_all();  // this thread's V copies have landed
   __syncthreads();
   for (int d = threadIdx.x; d < kHeadDim; d += blockDim.x) {
     float acc = 0.0f;
