@@ -460,33 +460,60 @@ __global__ void __launch_bounds__(256)
     greedy_kernel(const float* __restrict__ logits, int V, const int* __restrict__ pos_io, int P,
                   int* __restrict__ tokens, int ld_tok, int* __restrict__ done,
                   int* __restrict__ out, int ld_out, int* __restrict__ out_len) {
-  __shared__ float bv[256];
-  __shared__ int bi[256];
+  __shared__ float bv[8];
+  __shared__ int bi[8];
   const int b = blockIdx.x;
   const float* row = logits + static_cast<size_t>(b) * V;
+  // the largest logit, the lowest id among equal ones (a NaN is never taken): an order-free rule,
+  // so any split of the row gives the same id.  16-byte loads, four in flight per thread.
   float best = -INFINITY;
   int idx = 0x7fffffff;
-  for (int v = threadIdx.x; v < V; v += blockDim.x) {
-    const float x = row[v];
+  auto take = [&](float x, int v) {
     if (x > best || (x == best && v < idx)) {
       best = x;
       idx = v;
     }
-  }
-  bv[threadIdx.x] = best;
-  bi[threadIdx.x] = idx;
-  __syncthreads();
-  for (int s = blockDim.x / 2; s > 0; s >>= 1) {
-    if (threadIdx.x < s) {
-      const float o = bv[threadIdx.x + s];
-      const int oi = bi[threadIdx.x + s];
-      if (o > bv[threadIdx.x] || (o == bv[threadIdx.x] && oi < bi[threadIdx.x])) {
-        bv[threadIdx.x] = o;
-        bi[threadIdx.x] = oi;
-      }
+  };
+  const int V4 = (V & 3) == 0 ? V / 4 : 0;  // rows 16-byte aligned when V % 4 == 0
+  const float4* row4 = reinterpret_cast<const float4*>(row);
+  int q = threadIdx.x;
+  for (; q + 3 * 256 < V4; q += 4 * 256) {
+    float4 c[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) c[u] = row4[q + u * 256];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int v = 4 * (q + u * 256);
+      take(c[u].x, v);
+      take(c[u].y, v + 1);
+      take(c[u].z, v + 2);
+      take(c[u].w, v + 3);
     }
-    __syncthreads();
   }
+  for (; q < V4; q += 256) {
+    const float4 c = row4[q];
+    take(c.x, 4 * q);
+    take(c.y, 4 * q + 1);
+    take(c.z, 4 * q + 2);
+    take(c.w, 4 * q + 3);
+  }
+  for (int v = 4 * V4 + threadIdx.x; v < V; v += 256) take(row[v], v);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    take(ob, oi);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    bv[threadIdx.x >> 5] = best;
+    bi[threadIdx.x >> 5] = idx;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < 8; ++w) take(bv[w], bi[w]);
+    bi[0] = idx;
+  }
+  __syncthreads();
   if (threadIdx.x != 0) return;
   const int pos = *pos_io;
   const int step = pos - (P - 1);

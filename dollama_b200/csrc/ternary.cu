@@ -10,7 +10,8 @@
 //
 // The GEMM keeps the reference's exact arithmetic: int32 accumulation (|acc| <= 127 * K fits for
 // K < 2^24) and y = float(double(acc) * double(alpha_n) * double(scale_m)).  Each CTA computes a
-// 32-token x 64-output tile: the weight chunk is expanded to int8 once in shared memory (rows padded
+// 32-token x 64-output tile (32 outputs when 64-wide tiles would leave most SMs idle: the decode's
+// 512-output projections): the weight chunk is expanded to int8 once in shared memory (rows padded
 // by 16 bytes, so 16-byte reads of consecutive rows hit distinct banks) and amortised over the 32
 // tokens; the inner loop is 16-byte shared loads + dp4a.  Packed weight rows are read with
 // coalesced 16-byte loads.
@@ -25,7 +26,7 @@ namespace dlm {
 namespace {
 
 constexpr int kTM = 32;       // tokens per CTA
-constexpr int kTN = 64;       // outputs per CTA
+constexpr int kTN = 64;       // outputs per CTA (or 32, see ternary_gemm_i8)
 constexpr int kKC = 256;      // K chunk (elements)
 constexpr int kRow = kKC + 16;  // padded smem row (bytes)
 constexpr int kThreads = 256;
@@ -137,26 +138,28 @@ __device__ __forceinline__ uint32_t decode4(uint32_t b) {
   return lo | (hi * 0xFEu);
 }
 
+template <int TN>
 __global__ void __launch_bounds__(kThreads)
     ternary_gemm_kernel(const uint32_t* __restrict__ wp, const float* __restrict__ alpha,
                         const int8_t* __restrict__ xq, const float* __restrict__ xscale,
                         float* __restrict__ y, int M, int N, int K, int accumulate) {
-  __shared__ __align__(16) int8_t sw[kTN * kRow];
+  constexpr int NI = TN / 16;  // outputs per thread
+  __shared__ __align__(16) int8_t sw[TN * kRow];
   __shared__ __align__(16) int8_t sx[kTM * kRow];
-  const int n0 = blockIdx.x * kTN, m0 = blockIdx.y * kTM;
+  const int n0 = blockIdx.x * TN, m0 = blockIdx.y * kTM;
   const int tid = threadIdx.x;
   const int tx = tid & 15, ty = tid >> 4;  // outputs n0 + tx + 16i, tokens m0 + ty + 16j
-  int acc[2][4];
+  int acc[2][NI];
 #pragma unroll
   for (int j = 0; j < 2; ++j)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) acc[j][i] = 0;
+    for (int i = 0; i < NI; ++i) acc[j][i] = 0;
   const int wwords = K / 16;
   for (int k0 = 0; k0 < K; k0 += kKC) {
     const int kc = min(kKC, K - k0);  // multiple of 16
-    // expand the weight chunk: 64 rows x kc/16 words, four words (64 codes) per 16-byte load
+    // expand the weight chunk: TN rows x kc/16 words, four words (64 codes) per 16-byte load
     const int wq = kc / 64;           // uint4 per row (kc multiple of 64 on this path)
-    for (int idx = tid; idx < kTN * wq; idx += kThreads) {
+    for (int idx = tid; idx < TN * wq; idx += kThreads) {
       const int r = idx / wq, c = idx - r * wq;
       uint4 v = make_uint4(0, 0, 0, 0);
       if (n0 + r < N)
@@ -182,15 +185,15 @@ __global__ void __launch_bounds__(kThreads)
     }
     __syncthreads();
     for (int k = 0; k < kc; k += 16) {
-      uint4 xv4[2], wv4[4];
+      uint4 xv4[2], wv4[NI];
 #pragma unroll
       for (int j = 0; j < 2; ++j) xv4[j] = *reinterpret_cast<const uint4*>(sx + (ty + 16 * j) * kRow + k);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) wv4[i] = *reinterpret_cast<const uint4*>(sw + (tx + 16 * i) * kRow + k);
+      for (int i = 0; i < NI; ++i) wv4[i] = *reinterpret_cast<const uint4*>(sw + (tx + 16 * i) * kRow + k);
 #pragma unroll
       for (int j = 0; j < 2; ++j)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int i = 0; i < NI; ++i) {
           int a = acc[j][i];
           a = __dp4a(static_cast<int>(xv4[j].x), static_cast<int>(wv4[i].x), a);
           a = __dp4a(static_cast<int>(xv4[j].y), static_cast<int>(wv4[i].y), a);
@@ -207,7 +210,7 @@ __global__ void __launch_bounds__(kThreads)
     if (m >= M) continue;
     const double s = static_cast<double>(xscale[m]);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < NI; ++i) {
       const int n = n0 + tx + 16 * i;
       if (n >= N) continue;
       const double v = __dmul_rn(__dmul_rn(static_cast<double>(acc[j][i]), static_cast<double>(alpha[n])), s);
@@ -458,8 +461,15 @@ int ternary_gemm_i8(const uint32_t* wp, const float* alpha, const int8_t* xq, co
     DLM_CHECK_CUDA(cudaGetLastError());
     return DLM_OK;
   }
-  dim3 grid((N + kTN - 1) / kTN, (M + kTM - 1) / kTM);
-  ternary_gemm_kernel<<<grid, kThreads, 0, s>>>(wp, alpha, xq, xscale, y, M, N, K, accumulate ? 1 : 0);
+  // 64-output tiles unless they leave more than half of the SMs idle (decode-sized projections)
+  const long tiles64 = static_cast<long>((N + kTN - 1) / kTN) * ((M + kTM - 1) / kTM);
+  if (2 * tiles64 < num_sms()) {
+    dim3 grid((N + 31) / 32, (M + kTM - 1) / kTM);
+    ternary_gemm_kernel<32><<<grid, kThreads, 0, s>>>(wp, alpha, xq, xscale, y, M, N, K, accumulate ? 1 : 0);
+  } else {
+    dim3 grid((N + kTN - 1) / kTN, (M + kTM - 1) / kTM);
+    ternary_gemm_kernel<kTN><<<grid, kThreads, 0, s>>>(wp, alpha, xq, xscale, y, M, N, K, accumulate ? 1 : 0);
+  }
   DLM_CHECK_CUDA(cudaGetLastError());
   return DLM_OK;
 }
