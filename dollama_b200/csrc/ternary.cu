@@ -204,6 +204,16 @@ __global__ void __launch_bounds__(kThreads)
     }
     __syncthreads();
   }
+  // accumulate: the residual update h += bitlinear(x) as one float add (bitnet.hpp:579-583); the
+  // accumulated outputs are all requested before any is written
+  float old[2][NI];
+#pragma unroll
+  for (int j = 0; j < 2; ++j)
+#pragma unroll
+    for (int i = 0; i < NI; ++i) {
+      const int m = m0 + ty + 16 * j, n = n0 + tx + 16 * i;
+      old[j][i] = (accumulate && m < M && n < N) ? y[static_cast<size_t>(m) * N + n] : 0.0f;
+    }
 #pragma unroll
   for (int j = 0; j < 2; ++j) {
     const int m = m0 + ty + 16 * j;
@@ -215,8 +225,7 @@ __global__ void __launch_bounds__(kThreads)
       if (n >= N) continue;
       const double v = __dmul_rn(__dmul_rn(static_cast<double>(acc[j][i]), static_cast<double>(alpha[n])), s);
       float* dst = y + static_cast<size_t>(m) * N + n;
-      // accumulate: the residual update h += bitlinear(x) as one float add (bitnet.hpp:579-583)
-      *dst = accumulate ? __fadd_rn(*dst, __double2float_rn(v)) : __double2float_rn(v);
+      *dst = accumulate ? __fadd_rn(old[j][i], __double2float_rn(v)) : __double2float_rn(v);
     }
   }
 }
@@ -379,12 +388,28 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         __syncwarp();
         const int nn = n0 + c0 + lane;
-        for (int rr = 0; rr < 32; ++rr) {
-          const int mm = mrow0 + rr;
-          if (mm < p.M && nn < p.N) {
-            float* dst = p.y + static_cast<size_t>(mm) * p.N + nn;
-            const float v = s_tile[rr * 33 + lane];
-            *dst = p.accumulate ? __fadd_rn(*dst, v) : v;
+        if (p.accumulate) {
+          // the accumulated outputs are all requested before any is written (one round trip per
+          // 16 rows instead of one per row)
+#pragma unroll
+          for (int r0 = 0; r0 < 32; r0 += 16) {
+            float old[16];
+#pragma unroll
+            for (int rr = 0; rr < 16; ++rr) {
+              const int mm = mrow0 + r0 + rr;
+              old[rr] = (mm < p.M && nn < p.N) ? p.y[static_cast<size_t>(mm) * p.N + nn] : 0.0f;
+            }
+#pragma unroll
+            for (int rr = 0; rr < 16; ++rr) {
+              const int mm = mrow0 + r0 + rr;
+              if (mm < p.M && nn < p.N)
+                p.y[static_cast<size_t>(mm) * p.N + nn] = __fadd_rn(old[rr], s_tile[(r0 + rr) * 33 + lane]);
+            }
+          }
+        } else {
+          for (int rr = 0; rr < 32; ++rr) {
+            const int mm = mrow0 + rr;
+            if (mm < p.M && nn < p.N) p.y[static_cast<size_t>(mm) * p.N + nn] = s_tile[rr * 33 + lane];
           }
         }
         __syncwarp();
