@@ -402,13 +402,22 @@ __global__ void __launch_bounds__(kSwiThreads)
 // Tied lm_head (bitnet.hpp:414-436): logits[r, v] = float(sum_d double(x[r, d]) * double(E[v, d]))
 // with d in increasing order for every output (the products are exact in double, so fma equals
 // the reference's multiply-then-add).  Tile: 64 rows x 64 vocab ids, K chunks of 32; each thread
-// owns 4 rows x 4 ids (eight shared-memory loads per 16 fma).
+// owns 4 rows x 4 ids (eight shared-memory loads per 16 fma).  The next chunk's raw floats arrive
+// by asynchronous copies while the current chunk is multiplied, then all threads convert them
+// into the transposed double tiles between two barriers.
 constexpr int kLmR = 64, kLmV = 64, kLmK = 32;
+// dynamic shared memory: raw float rows [64][32] of x and of E, then the double tiles
+constexpr size_t kLmRawBytes = static_cast<size_t>(kLmR + kLmV) * kLmK * 4;
+constexpr size_t kLmSmem = kLmRawBytes + static_cast<size_t>(kLmK) * ((kLmR + 1) + (kLmV + 1)) * 8;
 __global__ void __launch_bounds__(256)
     lm_head_kernel(const float* __restrict__ x, int R, int D, const float* __restrict__ E, int V,
                    float* __restrict__ logits) {
-  __shared__ double xs[kLmK][kLmR + 1];
-  __shared__ double es[kLmK][kLmV + 1];
+  extern __shared__ __align__(16) uint8_t lm_smem[];
+  float* xf = reinterpret_cast<float*>(lm_smem);  // [kLmR][kLmK]
+  float* ef = xf + kLmR * kLmK;                   // [kLmV][kLmK]
+  double(*xs)[kLmR + 1] = reinterpret_cast<double(*)[kLmR + 1]>(lm_smem + kLmRawBytes);
+  double(*es)[kLmV + 1] = reinterpret_cast<double(*)[kLmV + 1]>(
+      lm_smem + kLmRawBytes + static_cast<size_t>(kLmK) * (kLmR + 1) * 8);
   const int r0 = blockIdx.y * kLmR, v0 = blockIdx.x * kLmV;
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;  // v = v0 + tx + 16i, r = r0 + ty + 16j
   double acc[4][4];
@@ -416,16 +425,40 @@ __global__ void __launch_bounds__(256)
   for (int j = 0; j < 4; ++j)
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc[j][i] = 0.0;
-  for (int k0 = 0; k0 < D; k0 += kLmK) {
+  // raw chunk k0 (rows beyond R / V read as zeros): 8 16-byte copies per 32-float row
+  auto fetch = [&](int k0) {
+#pragma unroll
+    for (int t = threadIdx.x; t < (kLmR + kLmV) * (kLmK / 4); t += 256) {
+      const int row = t / (kLmK / 4), q = t % (kLmK / 4);
+      if (row < kLmR) {
+        const bool in = r0 + row < R;
+        const float* src = in ? x + static_cast<size_t>(r0 + row) * D + k0 + 4 * q : x;
+        cp_async16(xf + row * kLmK + 4 * q, src, in ? 16u : 0u);
+      } else {
+        const int vv = row - kLmR;
+        const bool in = v0 + vv < V;
+        const float* src = in ? E + static_cast<size_t>(v0 + vv) * D + k0 + 4 * q : E;
+        cp_async16(ef + vv * kLmK + 4 * q, src, in ? 16u : 0u);
+      }
+    }
+    cp_async_commit();
+  };
+  // landed raw chunk -> transposed double tiles
+  auto convert = [&]() {
+#pragma unroll
     for (int t = threadIdx.x; t < kLmR * kLmK; t += 256) {
       const int rr = t / kLmK, kk = t % kLmK;
-      xs[kk][rr] = (r0 + rr < R) ? static_cast<double>(x[static_cast<size_t>(r0 + rr) * D + k0 + kk]) : 0.0;
+      xs[kk][rr] = static_cast<double>(xf[rr * kLmK + kk]);
+      es[kk][rr] = static_cast<double>(ef[rr * kLmK + kk]);
     }
-    for (int t = threadIdx.x; t < kLmV * kLmK; t += 256) {
-      const int vv = t / kLmK, kk = t % kLmK;
-      es[kk][vv] = (v0 + vv < V) ? static_cast<double>(E[static_cast<size_t>(v0 + vv) * D + k0 + kk]) : 0.0;
-    }
-    __syncthreads();
+  };
+  fetch(0);
+  for (int k0 = 0; k0 < D; k0 += kLmK) {
+    cp_async_wait_all();
+    __syncthreads();  // chunk k0 landed for every thread; the previous chunk's tiles are free
+    convert();
+    __syncthreads();  // tiles ready; the raw buffer is free
+    if (k0 + kLmK < D) fetch(k0 + kLmK);
 #pragma unroll 4
     for (int kk = 0; kk < kLmK; ++kk) {
       double xv[4], ev[4];
@@ -438,7 +471,6 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[j][i] = __fma_rn(xv[j], ev[i], acc[j][i]);
     }
-    __syncthreads();
   }
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
@@ -821,10 +853,11 @@ int BitNetLM::run_layers(int S, const int* pos, cudaStream_t s) {
 int BitNetLM::run_head(int rows, int stride, int off, cudaStream_t s) {
   const BitNetCfg& c = cfg_;
   const int D = c.d_model;
+  DLM_REQUIRE(D % kLmK == 0, DLM_ERR_INVALID, "bitnet: d_model %d must be a multiple of %d", D, kLmK);
   rms_norm_kernel<<<(rows + kNormWarps - 1) / kNormWarps, kNormWarps * 32, norm_smem_bytes(D), s>>>(h_, rows, D, stride, off, final_norm_,
                                                                   c.rms_eps, nullptr, nullptr, norm_);
   dim3 grid((c.vocab + kLmV - 1) / kLmV, (rows + kLmR - 1) / kLmR);
-  lm_head_kernel<<<grid, 256, 0, s>>>(norm_, rows, D, embed_, c.vocab, logits_);
+  lm_head_kernel<<<grid, 256, kLmSmem, s>>>(norm_, rows, D, embed_, c.vocab, logits_);
   DLM_CHECK_CUDA(cudaGetLastError());
   return DLM_OK;
 }
@@ -836,6 +869,8 @@ int BitNetLM::set_smem_attrs() {
   // the largest a launch asks for: staged V at the longest staged length, or the scores alone
   const size_t attn_smem = std::max(attn_smem_bytes(std::min(c.max_seq, kVStageMax)),
                                     attn_smem_bytes(c.max_seq));
+  DLM_CHECK_CUDA(cudaFuncSetAttribute(lm_head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(kLmSmem)));
   DLM_CHECK_CUDA(cudaFuncSetAttribute(rms_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       static_cast<int>(norm_smem)));
   DLM_CHECK_CUDA(cudaFuncSetAttribute(swiglu_quant_kernel,
