@@ -102,6 +102,7 @@ __device__ __forceinline__ void quant_row_warp(const float* row, int K, int8_t* 
 __global__ void embed_kernel(const int* __restrict__ tokens, int ld_tok, int S,
                              const int* __restrict__ pos_in, const float* __restrict__ embed, int V,
                              int D, float* __restrict__ h, int M, int* __restrict__ bad) {
+  griddep_wait();  // inputs come from the previous kernel (programmatic dependent launch)
   const int r = blockIdx.x;
   if (r >= M) return;
   const int base = pos_in ? *pos_in : 0;
@@ -128,6 +129,7 @@ __global__ void __launch_bounds__(kNormWarps * 32)
     rms_norm_kernel(const float* __restrict__ h, int rows, int D, int in_stride, int in_off,
                     const float* __restrict__ w, double eps, int8_t* __restrict__ xq,
                     float* __restrict__ xs, float* __restrict__ out_f) {
+  griddep_wait();  // inputs come from the previous kernel (programmatic dependent launch)
   extern __shared__ float srow[];  // [kNormWarps][D] float, then [kNormWarps][D] double
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = blockIdx.x * kNormWarps + warp;
@@ -165,6 +167,7 @@ __global__ void rope_kv_kernel(const float* __restrict__ qkv, int M, int S, int 
                                const int* __restrict__ pos_in, const double* __restrict__ cos_t,
                                const double* __restrict__ sin_t, float* __restrict__ q,
                                float* __restrict__ kc, float* __restrict__ vc, int Lmax) {
+  griddep_wait();  // inputs come from the previous kernel (programmatic dependent launch)
   const int half = kHeadDim / 2;
   const int H = D / kHeadDim;
   const size_t total = static_cast<size_t>(M) * H * half;
@@ -211,6 +214,7 @@ __global__ void __launch_bounds__(kAttnThreads)
     attention_kernel(const float* __restrict__ q, int M, int S, int D, const int* __restrict__ pos_in,
                      const float* __restrict__ kc, const float* __restrict__ vc, int Lmax,
                      float* __restrict__ out) {
+  griddep_wait();  // inputs come from the previous kernel (programmatic dependent launch)
   extern __shared__ double sh[];  // [64] q, [Lmax] scores, [40] reduction, then [Lmax][64] V (f32)
   double* sq = sh;
   double* ss = sh + kHeadDim;
@@ -299,6 +303,7 @@ __global__ void __launch_bounds__(kAttnSeqWarps * 32)
     attention_seq_kernel(const float* __restrict__ q, int S, int D, const int* __restrict__ pos_in,
                          const float* __restrict__ kc, const float* __restrict__ vc, int Lmax,
                          float* __restrict__ out) {
+  griddep_wait();  // inputs come from the previous kernel (programmatic dependent launch)
   extern __shared__ __align__(16) double shd[];
   const int H = D / kHeadDim;
   const int b = blockIdx.x / H, hd = blockIdx.x % H;
@@ -374,6 +379,7 @@ constexpr int kSwiThreads = 256;
 __global__ void __launch_bounds__(kSwiThreads)
     swiglu_quant_kernel(const float* __restrict__ gu, int M, int F, int8_t* __restrict__ xq,
                         float* __restrict__ xs) {
+  griddep_wait();  // inputs come from the previous kernel (programmatic dependent launch)
   extern __shared__ float srow[];  // [F]
   __shared__ double s_amax[kSwiThreads / 32];
   const int r = blockIdx.x;
@@ -412,6 +418,7 @@ constexpr size_t kLmSmem = kLmRawBytes + static_cast<size_t>(kLmK) * ((kLmR + 1)
 __global__ void __launch_bounds__(256)
     lm_head_kernel(const float* __restrict__ x, int R, int D, const float* __restrict__ E, int V,
                    float* __restrict__ logits) {
+  griddep_wait();  // inputs come from the previous kernel (programmatic dependent launch)
   extern __shared__ __align__(16) uint8_t lm_smem[];
   float* xf = reinterpret_cast<float*>(lm_smem);  // [kLmR][kLmK]
   float* ef = xf + kLmR * kLmK;                   // [kLmV][kLmK]
@@ -492,6 +499,7 @@ __global__ void __launch_bounds__(256)
     greedy_kernel(const float* __restrict__ logits, int V, const int* __restrict__ pos_io, int P,
                   int* __restrict__ tokens, int ld_tok, int* __restrict__ done,
                   int* __restrict__ out, int ld_out, int* __restrict__ out_len) {
+  griddep_wait();  // inputs come from the previous kernel (programmatic dependent launch)
   __shared__ float bv[8];
   __shared__ int bi[8];
   const int b = blockIdx.x;
@@ -563,8 +571,14 @@ __global__ void __launch_bounds__(256)
   if (pos + 1 < ld_tok) tokens[static_cast<size_t>(b) * ld_tok + pos + 1] = next;
 }
 
-__global__ void set_int_kernel(int* p, int v) { *p = v; }
-__global__ void inc_int_kernel(int* p) { *p += 1; }
+__global__ void set_int_kernel(int* p, int v) {
+  griddep_wait();
+  *p = v;
+}
+__global__ void inc_int_kernel(int* p) {
+  griddep_wait();
+  *p += 1;
+}
 
 int grid1d(size_t n, int t) {
   size_t g = (n + t - 1) / t;
@@ -824,25 +838,27 @@ int BitNetLM::run_layers(int S, const int* pos, cudaStream_t s) {
     const Layer& Ly = layers_[l];
     float* kc = kc_ + l * kv_layer;
     float* vc = vc_ + l * kv_layer;
-    rms_norm_kernel<<<norm_blocks, kNormWarps * 32, norm_smem, s>>>(h_, M, D, 1, 0, Ly.attn_norm,
-                                                                    c.rms_eps, xq_, xs_, nullptr);
+    DLM_CHECK_CUDA(launch_pdl(rms_norm_kernel, dim3(norm_blocks), dim3(kNormWarps * 32), norm_smem,
+        s, h_, M, D, 1, 0, Ly.attn_norm, c.rms_eps, xq_, xs_, nullptr));
     rc = ternary_gemm_i8(Ly.wqkv, Ly.aqkv, xq_, xs_, y_, M, 3 * D, D, s);
     if (rc != DLM_OK) break;
-    rope_kv_kernel<<<grid1d(static_cast<size_t>(M) * H * 32, 256), 256, 0, s>>>(
-        y_, M, S, D, pos, cos_t_, sin_t_, q_, kc, vc, L_);
+    DLM_CHECK_CUDA(launch_pdl(rope_kv_kernel, dim3(grid1d(static_cast<size_t>(M) * H * 32, 256)),
+        dim3(256), 0, s, y_, M, S, D, pos, cos_t_, sin_t_, q_, kc, vc, L_));
     if (S > 1 && L_ <= kAttnSeqMax)  // prefill: one block per (sequence, head)
-      attention_seq_kernel<<<B_ * H, kAttnSeqWarps * 32, attn_seq_smem_bytes(L_), s>>>(
-          q_, S, D, pos, kc, vc, L_, ao_);
+      DLM_CHECK_CUDA(launch_pdl(attention_seq_kernel, dim3(B_ * H), dim3(kAttnSeqWarps * 32),
+          attn_seq_smem_bytes(L_), s, q_, S, D, pos, kc, vc, L_, ao_));
     else
-      attention_kernel<<<M * H, kAttnThreads, attn_smem, s>>>(q_, M, S, D, pos, kc, vc, L_, ao_);
+      DLM_CHECK_CUDA(launch_pdl(attention_kernel, dim3(M * H), dim3(kAttnThreads), attn_smem, s, q_,
+          M, S, D, pos, kc, vc, L_, ao_));
     rc = quantize_act_i8(ao_, M, D, xq_, xs_, s);
     if (rc == DLM_OK) rc = ternary_gemm_i8(Ly.wo, Ly.ao, xq_, xs_, h_, M, D, D, s, true);
     if (rc != DLM_OK) break;
-    rms_norm_kernel<<<norm_blocks, kNormWarps * 32, norm_smem, s>>>(h_, M, D, 1, 0, Ly.ffn_norm,
-                                                                    c.rms_eps, xq_, xs_, nullptr);
+    DLM_CHECK_CUDA(launch_pdl(rms_norm_kernel, dim3(norm_blocks), dim3(kNormWarps * 32), norm_smem,
+        s, h_, M, D, 1, 0, Ly.ffn_norm, c.rms_eps, xq_, xs_, nullptr));
     rc = ternary_gemm_i8(Ly.wgu, Ly.agu, xq_, xs_, y_, M, 2 * F, D, s);
     if (rc != DLM_OK) break;
-    swiglu_quant_kernel<<<M, kSwiThreads, swi_smem, s>>>(y_, M, F, xq_, xs_);
+    DLM_CHECK_CUDA(launch_pdl(swiglu_quant_kernel, dim3(M), dim3(kSwiThreads), swi_smem, s, y_, M,
+        F, xq_, xs_));
     rc = ternary_gemm_i8(Ly.wd, Ly.ad, xq_, xs_, h_, M, D, F, s, true);
   }
   if (rc == DLM_OK) DLM_CHECK_CUDA(cudaGetLastError());
@@ -854,10 +870,12 @@ int BitNetLM::run_head(int rows, int stride, int off, cudaStream_t s) {
   const BitNetCfg& c = cfg_;
   const int D = c.d_model;
   DLM_REQUIRE(D % kLmK == 0, DLM_ERR_INVALID, "bitnet: d_model %d must be a multiple of %d", D, kLmK);
-  rms_norm_kernel<<<(rows + kNormWarps - 1) / kNormWarps, kNormWarps * 32, norm_smem_bytes(D), s>>>(h_, rows, D, stride, off, final_norm_,
-                                                                  c.rms_eps, nullptr, nullptr, norm_);
+  DLM_CHECK_CUDA(launch_pdl(rms_norm_kernel, dim3((rows + kNormWarps - 1) / kNormWarps),
+      dim3(kNormWarps * 32), norm_smem_bytes(D), s, h_, rows, D, stride, off, final_norm_,
+      c.rms_eps, nullptr, nullptr, norm_));
   dim3 grid((c.vocab + kLmV - 1) / kLmV, (rows + kLmR - 1) / kLmR);
-  lm_head_kernel<<<grid, 256, kLmSmem, s>>>(norm_, rows, D, embed_, c.vocab, logits_);
+  DLM_CHECK_CUDA(launch_pdl(lm_head_kernel, dim3(grid), dim3(256), kLmSmem, s, norm_, rows, D,
+      embed_, c.vocab, logits_));
   DLM_CHECK_CUDA(cudaGetLastError());
   return DLM_OK;
 }
@@ -899,8 +917,8 @@ int BitNetLM::forward(const int* tokens, int B, int S, float* logits, cudaStream
   if ((rc = set_smem_attrs()) != DLM_OK) return rc;
   DLM_CHECK_CUDA(cudaMemcpyAsync(tokens_, tokens, static_cast<size_t>(B) * S * 4, cudaMemcpyDefault, s));
   DLM_CHECK_CUDA(cudaMemsetAsync(state_, 0, 8, s));
-  embed_kernel<<<B * S, 128, 0, s>>>(tokens_, S, S, nullptr, embed_, cfg_.vocab, cfg_.d_model, h_,
-                                     B * S, state_ + 1);
+  DLM_CHECK_CUDA(launch_pdl(embed_kernel, dim3(B * S), dim3(128), 0, s, tokens_, S, S, nullptr,
+      embed_, cfg_.vocab, cfg_.d_model, h_, B * S, state_ + 1));
   if ((rc = run_layers(S, nullptr, s)) != DLM_OK) return rc;
   if ((rc = run_head(B * S, 1, 0, s)) != DLM_OK) return rc;
   DLM_CHECK_CUDA(cudaMemcpyAsync(logits, logits_, static_cast<size_t>(B) * S * cfg_.vocab * 4,
@@ -912,14 +930,14 @@ int BitNetLM::forward(const int* tokens, int B, int S, float* logits, cudaStream
 // greedy step, advance *pos.
 int BitNetLM::decode_step(cudaStream_t s) {
   int* pos = state_;
-  embed_kernel<<<B_, 128, 0, s>>>(tokens_, L_, 1, pos, embed_, cfg_.vocab, cfg_.d_model, h_, B_,
-                                  state_ + 1);
+  DLM_CHECK_CUDA(launch_pdl(embed_kernel, dim3(B_), dim3(128), 0, s, tokens_, L_, 1, pos, embed_,
+      cfg_.vocab, cfg_.d_model, h_, B_, state_ + 1));
   int rc = run_layers(1, pos, s);
   if (rc == DLM_OK) rc = run_head(B_, 1, 0, s);
   if (rc != DLM_OK) return rc;
-  greedy_kernel<<<B_, 256, 0, s>>>(logits_, cfg_.vocab, pos, P_, tokens_, L_, done_, out_, L_ - P_,
-                                   out_len_);
-  inc_int_kernel<<<1, 1, 0, s>>>(pos);
+  DLM_CHECK_CUDA(launch_pdl(greedy_kernel, dim3(B_), dim3(256), 0, s, logits_, cfg_.vocab, pos, P_,
+      tokens_, L_, done_, out_, L_ - P_, out_len_));
+  DLM_CHECK_CUDA(launch_pdl(inc_int_kernel, dim3(1), dim3(1), 0, s, pos));
   DLM_CHECK_CUDA(cudaGetLastError());
   return DLM_OK;
 }
@@ -939,13 +957,14 @@ int BitNetLM::generate(const int* prompts, int B, int P, int max_len, int* out, 
   DLM_CHECK_CUDA(cudaMemsetAsync(out_len_, 0, static_cast<size_t>(B) * 4, s));
   if (G > 0) {
     // prefill: all prompt positions, logits of the last one, first greedy step
-    embed_kernel<<<B * P, 128, 0, s>>>(tokens_, L_, P, nullptr, embed_, cfg_.vocab, cfg_.d_model,
-                                       h_, B * P, state_ + 1);
+    DLM_CHECK_CUDA(launch_pdl(embed_kernel, dim3(B * P), dim3(128), 0, s, tokens_, L_, P, nullptr,
+        embed_, cfg_.vocab, cfg_.d_model, h_, B * P, state_ + 1));
     if ((rc = run_layers(P, nullptr, s)) != DLM_OK) return rc;
     if ((rc = run_head(B, P, P - 1, s)) != DLM_OK) return rc;
-    set_int_kernel<<<1, 1, 0, s>>>(state_, P - 1);
-    greedy_kernel<<<B, 256, 0, s>>>(logits_, cfg_.vocab, state_, P, tokens_, L_, done_, out_, G, out_len_);
-    inc_int_kernel<<<1, 1, 0, s>>>(state_);
+    DLM_CHECK_CUDA(launch_pdl(set_int_kernel, dim3(1), dim3(1), 0, s, state_, P - 1));
+    DLM_CHECK_CUDA(launch_pdl(greedy_kernel, dim3(B), dim3(256), 0, s, logits_, cfg_.vocab, state_,
+        P, tokens_, L_, done_, out_, G, out_len_));
+    DLM_CHECK_CUDA(launch_pdl(inc_int_kernel, dim3(1), dim3(1), 0, s, state_));
     DLM_CHECK_CUDA(cudaGetLastError());
     // decode passes (the last greedy step needs no pass after it), replayed as one CUDA graph
     if (G > 1) {

@@ -32,6 +32,25 @@ bool tmap_2d_f16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t col
 // Whether kernels are launched with programmatic dependent launch (default on; DLM_PDL=0 off).
 bool pdl_enabled();
 
+// Launches `kernel` with programmatic dependent launch when it is enabled: the kernel may start
+// while the previous kernel in the stream finishes, so it must execute griddepcontrol.wait before
+// its first global memory access.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // Records the last host-side error message (thread-local), returned by dlm_last_error().
 void set_error(const char* fmt, ...);
 

@@ -106,6 +106,7 @@ __global__ void ternary_pack_alpha_kernel(const float* __restrict__ w, int N, in
 // One warp per token: exact absmax int8 quantization.
 __global__ void quant_act_kernel(const float* __restrict__ x, int M, int K, int8_t* __restrict__ xq,
                                  float* __restrict__ xscale) {
+  griddep_wait();  // inputs come from the previous kernel (programmatic dependent launch)
   const int m = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (m >= M) return;
@@ -143,6 +144,7 @@ __global__ void __launch_bounds__(kThreads)
     ternary_gemm_kernel(const uint32_t* __restrict__ wp, const float* __restrict__ alpha,
                         const int8_t* __restrict__ xq, const float* __restrict__ xscale,
                         float* __restrict__ y, int M, int N, int K, int accumulate) {
+  griddep_wait();  // inputs come from the previous kernel (programmatic dependent launch)
   constexpr int NI = TN / 16;  // outputs per thread
   __shared__ __align__(16) int8_t sw[TN * kRow];
   __shared__ __align__(16) int8_t sx[kTM * kRow];
@@ -291,6 +293,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
+  griddep_wait();  // the activations come from the previous kernel (programmatic dependent launch)
 
   if (warp == 0) {
     if (lane == 0) {
@@ -451,7 +454,8 @@ int quantize_act_i8(const float* x, int M, int K, int8_t* xq, float* xscale, cud
   DLM_REQUIRE(x && xq && xscale, DLM_ERR_INVALID, "quantize_act_i8: null pointer");
   DLM_REQUIRE(M > 0 && K > 0, DLM_ERR_INVALID, "quantize_act_i8: empty");
   const int warps = 8;
-  quant_act_kernel<<<(M + warps - 1) / warps, warps * 32, 0, s>>>(x, M, K, xq, xscale);
+  DLM_CHECK_CUDA(launch_pdl(quant_act_kernel, dim3((M + warps - 1) / warps), dim3(warps * 32), 0, s,
+      x, M, K, xq, xscale));
   DLM_CHECK_CUDA(cudaGetLastError());
   return DLM_OK;
 }
@@ -482,7 +486,8 @@ int ternary_gemm_i8(const uint32_t* wp, const float* alpha, const int8_t* xq, co
       return DLM_ERR_CUDA;
     TernaryTcParams tp{wp, alpha, xscale, y, M, N, K, accumulate ? 1 : 0, device_status_ptr()};
     dim3 grid((N + kTcN - 1) / kTcN, (M + kTcM - 1) / kTcM);
-    ternary_gemm_tc_kernel<<<grid, kTcThreads, kTcSmem, s>>>(tm, tp);
+    DLM_CHECK_CUDA(launch_pdl(ternary_gemm_tc_kernel, dim3(grid), dim3(kTcThreads), kTcSmem, s, tm,
+        tp));
     DLM_CHECK_CUDA(cudaGetLastError());
     return DLM_OK;
   }
@@ -490,10 +495,12 @@ int ternary_gemm_i8(const uint32_t* wp, const float* alpha, const int8_t* xq, co
   const long tiles64 = static_cast<long>((N + kTN - 1) / kTN) * ((M + kTM - 1) / kTM);
   if (2 * tiles64 < num_sms()) {
     dim3 grid((N + 31) / 32, (M + kTM - 1) / kTM);
-    ternary_gemm_kernel<32><<<grid, kThreads, 0, s>>>(wp, alpha, xq, xscale, y, M, N, K, accumulate ? 1 : 0);
+    DLM_CHECK_CUDA(launch_pdl(ternary_gemm_kernel<32>, dim3(grid), dim3(kThreads), 0, s, wp, alpha,
+        xq, xscale, y, M, N, K, accumulate ? 1 : 0));
   } else {
     dim3 grid((N + kTN - 1) / kTN, (M + kTM - 1) / kTM);
-    ternary_gemm_kernel<kTN><<<grid, kThreads, 0, s>>>(wp, alpha, xq, xscale, y, M, N, K, accumulate ? 1 : 0);
+    DLM_CHECK_CUDA(launch_pdl(ternary_gemm_kernel<kTN>, dim3(grid), dim3(kThreads), 0, s, wp, alpha,
+        xq, xscale, y, M, N, K, accumulate ? 1 : 0));
   }
   DLM_CHECK_CUDA(cudaGetLastError());
   return DLM_OK;
