@@ -94,6 +94,22 @@ def test_generate_baseline_dims_matches_oracle():
     lm.close()
 
 
+def test_generate_sequence_shards_match_full_batch():
+    """The multi-GPU LM split: every rank generates its own shard of the sequences.  At the
+    config-5 dims, each shard of 128, 64 or 32 of 256 sequences (the per-rank batches of 2, 4 and
+    8 GPUs) generated alone gives the full batch's tokens for those sequences — the decode tile
+    choices, which depend on the batch, change no bit."""
+    cfg = B.lm_config()
+    w = B.lm_random_weights(cfg, seed=10, kind="ternary")
+    prompts = np.random.default_rng(13).integers(3, cfg["vocab"], size=(256, 64)).astype(np.int32)
+    lm = _gpu(cfg, w)
+    full = lm.generate(prompts, max_len=128)
+    for b in (128, 64, 32):
+        for r0 in (0, 256 - b):
+            assert lm.generate(prompts[r0:r0 + b], max_len=128) == full[r0:r0 + b], (b, r0)
+    lm.close()
+
+
 @pytest.mark.parametrize("P,max_len", [(5, 24), (6, 23), (7, 21), (9, 10), (21, 22)])
 def test_generate_odd_and_even_cache_lengths(P, max_len):
     """Cache lengths (max_len) of both parities and prefill-only / one-step decodes: the
