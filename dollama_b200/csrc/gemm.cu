@@ -48,14 +48,15 @@ int max_pairs_bn() {
 }
 
 int max_pairs(int bn) {
-  static int cache[64][4] = {{0}};
+  static int cache[64][5] = {{0}};
   int dev = 0;
   cudaGetDevice(&dev);
-  const int slot = bn == 256 ? 0 : bn == 192 ? 1 : bn == 160 ? 2 : 3;
+  const int slot = bn == 256 ? 0 : bn == 192 ? 1 : bn == 160 ? 2 : bn == 224 ? 4 : 3;
   if (dev < 0 || dev >= 64) return num_sms() / 2;
   if (cache[dev][slot] == 0) {
-    cache[dev][slot] = bn == 256 ? max_pairs_bn<256>() : bn == 192 ? max_pairs_bn<192>()
-                     : bn == 160 ? max_pairs_bn<160>() : max_pairs_bn<128>();
+    cache[dev][slot] = bn == 256 ? max_pairs_bn<256>() : bn == 224 ? max_pairs_bn<224>()
+                     : bn == 192 ? max_pairs_bn<192>() : bn == 160 ? max_pairs_bn<160>()
+                     : max_pairs_bn<128>();
   }
   return cache[dev][slot];
 }
@@ -63,11 +64,13 @@ int max_pairs(int bn) {
 // Chooses single-CTA vs CTA-pair and the N tile.  Dense linears (conv == false) with more than
 // one row tile run on CTA pairs, whose two-k-block stages keep the issuing thread ahead of the
 // tensor pipe; the N tile minimises waves x measured clocks per k-block (B200, UNet shapes:
-// ~590 for a 256 x 160 pair tile, ~634 for 256 x 256).  Implicit-GEMM convolutions measured
+// ~590 for a 256 x 160 pair tile, ~600 for 256 x 224, ~634 for 256 x 256; 224 wins where it
+// rounds the tile count under a whole number of waves that 256 exceeds, e.g. the 32^2 level's
+// q|k|v 2048 x 3840 x 1280: 19.0 -> 17.5 us).  Implicit-GEMM convolutions measured
 // faster on single CTAs (their 4D im2col boxes) and keep the single-CTA cost model.
 void pick_tile(int M, int N, bool conv, int force_bn, int force_mode, int* bn_out, bool* pair_out) {
   static const int single[] = {256, 192, 160, 128, 64};
-  static const int paired[] = {256, 192, 160, 128};
+  static const int paired[] = {256, 224, 192, 160, 128};
   const int sms = num_sms();
   const bool want_pair = force_mode == 2 || (force_mode == 0 && !conv && M > kGemmBM);
   if (want_pair && M > kGemmBM) {
@@ -75,10 +78,11 @@ void pick_tile(int M, int N, bool conv, int force_bn, int force_mode, int* bn_ou
     if (bn == 0) {
       const long mt2 = (M + 2 * kGemmBM - 1) / (2 * kGemmBM);
       double best = 1e30;
-      for (int c : {256, 160}) {
+      for (int c : {256, 224, 160}) {
         const long tiles = mt2 * ((N + c - 1) / c);
         const long pairs = max_pairs(c);
-        const double cost = static_cast<double>((tiles + pairs - 1) / pairs) * (c == 256 ? 634.0 : 590.0);
+        const double clk = c == 256 ? 634.0 : c == 224 ? 600.0 : 590.0;
+        const double cost = static_cast<double>((tiles + pairs - 1) / pairs) * clk;
         if (cost < best - 1e-9) {
           best = cost;
           bn = c;
@@ -143,7 +147,7 @@ int pick_stream_k(long m_tiles, int N, int num_kb, int bn, bool pair, const Gemm
 }
 
 bool bn_supported(int bn, bool pair) {
-  if (pair) return bn == 256 || bn == 192 || bn == 160 || bn == 128;
+  if (pair) return bn == 256 || bn == 224 || bn == 192 || bn == 160 || bn == 128;
   return bn == 256 || bn == 192 || bn == 160 || bn == 128 || bn == 64;
 }
 
@@ -423,7 +427,7 @@ int dlm_gemm_set_tile_mode(int mode) {
   const int kernel = mode & 15, bn = mode >> 4;
   DLM_REQUIRE(kernel >= 0 && kernel <= 3, DLM_ERR_INVALID,
               "gemm_set_tile_mode: low bits 0 auto, 1 single, 2 pair, 3 stream-K");
-  DLM_REQUIRE(bn == 0 || bn == 64 || bn == 128 || bn == 160 || bn == 192 || bn == 256,
+  DLM_REQUIRE(bn == 0 || bn == 64 || bn == 128 || bn == 160 || bn == 192 || bn == 224 || bn == 256,
               DLM_ERR_INVALID, "gemm_set_tile_mode: forced tile width %d", bn);
   dlm::g_force_mode = kernel;
   dlm::g_force_bn = bn;

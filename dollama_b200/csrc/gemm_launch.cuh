@@ -57,6 +57,7 @@ int gemm_prepare_fl() {
   DLM_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<128, FL>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm_smem_bytes(128)));
   DLM_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<64, FL>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm_smem_bytes(64)));
   DLM_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<256, FL>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm2_smem_bytes(256)));
+  DLM_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<224, FL>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm2_smem_bytes(224)));
   DLM_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<192, FL>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm2_smem_bytes(192)));
   DLM_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<160, FL>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm2_smem_bytes(160)));
   DLM_CHECK_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<128, FL>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm2_smem_bytes(128)));
@@ -68,6 +69,7 @@ int gemm_launch_fl(const GemmOp& op, cudaStream_t s) {
   if (op.pair) {
     switch (op.bn) {
       case 256: return launch_bn2<256, FL>(op, s);
+      case 224: return launch_bn2<224, FL>(op, s);
       case 192: return launch_bn2<192, FL>(op, s);
       case 160: return launch_bn2<160, FL>(op, s);
       case 128: return launch_bn2<128, FL>(op, s);
