@@ -11,10 +11,10 @@
 // The GEMM keeps the reference's exact arithmetic: int32 accumulation (|acc| <= 127 * K fits for
 // K < 2^24) and y = float(double(acc) * double(alpha_n) * double(scale_m)).  Each CTA computes a
 // 32-token x 64-output tile (32 outputs when 64-wide tiles would leave most SMs idle: the decode's
-// 512-output projections): the weight chunk is expanded to int8 once in shared memory (rows padded
-// by 16 bytes, so 16-byte reads of consecutive rows hit distinct banks) and amortised over the 32
-// tokens; the inner loop is 16-byte shared loads + dp4a.  Packed weight rows are read with
-// coalesced 16-byte loads.
+// 512-output projections): K runs in chunks of 256 whose packed weights and activations arrive by
+// asynchronous copies while the previous chunk is multiplied; the weight chunk is expanded to int8
+// once in shared memory (rows padded by 16 bytes, so 16-byte reads of consecutive rows hit distinct
+// banks) and amortised over the 32 tokens; the inner loop is 16-byte shared loads + dp4a.
 #include <cstdint>
 #include <cstdlib>
 
@@ -146,8 +146,9 @@ __global__ void __launch_bounds__(kThreads)
                         float* __restrict__ y, int M, int N, int K, int accumulate) {
   griddep_wait();  // inputs come from the previous kernel (programmatic dependent launch)
   constexpr int NI = TN / 16;  // outputs per thread
-  __shared__ __align__(16) int8_t sw[TN * kRow];
-  __shared__ __align__(16) int8_t sx[kTM * kRow];
+  __shared__ __align__(16) int8_t sw[TN * kRow];              // expanded int8 weight chunk
+  __shared__ __align__(16) int8_t sx[2][kTM * kRow];          // activation chunks (double buffer)
+  __shared__ __align__(16) uint32_t sp[2][TN * (kKC / 16)];   // packed weight chunks (double buffer)
   const int n0 = blockIdx.x * TN, m0 = blockIdx.y * kTM;
   const int tid = threadIdx.x;
   const int tx = tid & 15, ty = tid >> 4;  // outputs n0 + tx + 16i, tokens m0 + ty + 16j
@@ -157,15 +158,38 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
     for (int i = 0; i < NI; ++i) acc[j][i] = 0;
   const int wwords = K / 16;
-  for (int k0 = 0; k0 < K; k0 += kKC) {
-    const int kc = min(kKC, K - k0);  // multiple of 16
-    // expand the weight chunk: TN rows x kc/16 words, four words (64 codes) per 16-byte load
-    const int wq = kc / 64;           // uint4 per row (kc multiple of 64 on this path)
+  // chunk [k0, k0 + kc) of the packed weights and activations into buffer `buf` by 16-byte
+  // asynchronous copies (rows beyond N / M arrive as zeros); K % 64 == 0 keeps every source
+  // 16-byte aligned
+  auto fetch = [&](int k0, int buf) {
+    const int kc = min(kKC, K - k0);
+    const int wq = kc / 64;  // 16-byte pieces per packed row
     for (int idx = tid; idx < TN * wq; idx += kThreads) {
       const int r = idx / wq, c = idx - r * wq;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (n0 + r < N)
-        v = __ldg(reinterpret_cast<const uint4*>(wp + static_cast<size_t>(n0 + r) * wwords + k0 / 16) + c);
+      const bool in = n0 + r < N;
+      const uint32_t* src = in ? wp + static_cast<size_t>(n0 + r) * wwords + k0 / 16 + 4 * c : wp;
+      cp_async16(&sp[buf][r * (kKC / 16) + 4 * c], src, in ? 16u : 0u);
+    }
+    const int xv = kc / 16;
+    for (int idx = tid; idx < kTM * xv; idx += kThreads) {
+      const int r = idx / xv, c = idx - r * xv;
+      const bool in = m0 + r < M;
+      const int8_t* src = in ? xq + static_cast<size_t>(m0 + r) * K + k0 + 16 * c : xq;
+      cp_async16(sx[buf] + r * kRow + 16 * c, src, in ? 16u : 0u);
+    }
+    cp_async_commit();
+  };
+  fetch(0, 0);
+  int buf = 0;
+  for (int k0 = 0; k0 < K; k0 += kKC, buf ^= 1) {
+    const int kc = min(kKC, K - k0);  // multiple of 64
+    cp_async_wait_all();
+    __syncthreads();  // chunk k0 landed for every thread; the previous chunk's reads are done
+    // expand the packed chunk: TN rows x kc/16 words, four words (64 codes) per 16-byte piece
+    const int wq = kc / 64;
+    for (int idx = tid; idx < TN * wq; idx += kThreads) {
+      const int r = idx / wq, c = idx - r * wq;
+      const uint4 v = *reinterpret_cast<const uint4*>(&sp[buf][r * (kKC / 16) + 4 * c]);
       const uint32_t words[4] = {v.x, v.y, v.z, v.w};
       uint32_t* dst = reinterpret_cast<uint32_t*>(sw + r * kRow + c * 64);
 #pragma unroll
@@ -177,19 +201,13 @@ __global__ void __launch_bounds__(kThreads)
         dst[4 * q + 3] = decode4(wd >> 24);
       }
     }
-    // activations: 32 rows x kc bytes, 16-byte loads
-    const int xv = kc / 16;
-    for (int idx = tid; idx < kTM * xv; idx += kThreads) {
-      const int r = idx / xv, c = idx - r * xv;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (m0 + r < M) v = __ldg(reinterpret_cast<const uint4*>(xq + static_cast<size_t>(m0 + r) * K + k0) + c);
-      *reinterpret_cast<uint4*>(sx + r * kRow + c * 16) = v;
-    }
-    __syncthreads();
+    __syncthreads();  // expanded weights ready; packed buffer `buf` free
+    if (k0 + kKC < K) fetch(k0 + kKC, buf ^ 1);  // lands while this chunk is multiplied
+    const int8_t* sxb = sx[buf];
     for (int k = 0; k < kc; k += 16) {
       uint4 xv4[2], wv4[NI];
 #pragma unroll
-      for (int j = 0; j < 2; ++j) xv4[j] = *reinterpret_cast<const uint4*>(sx + (ty + 16 * j) * kRow + k);
+      for (int j = 0; j < 2; ++j) xv4[j] = *reinterpret_cast<const uint4*>(sxb + (ty + 16 * j) * kRow + k);
 #pragma unroll
       for (int i = 0; i < NI; ++i) wv4[i] = *reinterpret_cast<const uint4*>(sw + (tx + 16 * i) * kRow + k);
 #pragma unroll
@@ -204,7 +222,6 @@ __global__ void __launch_bounds__(kThreads)
           acc[j][i] = a;
         }
     }
-    __syncthreads();
   }
   // accumulate: the residual update h += bitlinear(x) as one float add (bitnet.hpp:579-583); the
   // accumulated outputs are all requested before any is written
