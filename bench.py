@@ -217,11 +217,11 @@ def reference_gpu_leg(sd_gpu, dev_inputs, out, our_value, e0, e1, stream, steps=
             "ours_over_reference_best": (our_value / best) if best else None}
 
 
-LM_SEQS, LM_PROMPT, LM_NEW = 256, 64, 64   # 256 sequences, 64 + 64 tokens
+LM_SEQS, LM_PROMPT, LM_NEW = 256, 64, 64   # the LM benchmark: 256 sequences, 64 + 64 tokens
 
 
 def lm_leg(dev, ws, rank, e0, e1, stream, hbm_peak, peak_src, barrier, cpu=True):
-    """BASELINE config 5, the ternary BitNet tag LM: greedy decode of LM_SEQS sequences split over
+    """The LM benchmark, the ternary BitNet tag LM: greedy decode of LM_SEQS sequences split over
     the ranks by sequence (each rank decodes its share; no exchange).  Whole-job generated tokens/s
     with prompts resident on the device (CUDA events, max over ranks), the same through the host
     API (prompts in, generated ids out), the decode step against HBM (its packed ternary weights
@@ -517,7 +517,7 @@ def main():
                "image_finite": bool(torch.isfinite(img).all().item())}
     vae.close()
 
-    # ---------------------------------------------------------------- BitNet LM (config 5)
+    # ---------------------------------------------------------------- BitNet tag LM
     lm = lm_leg(dev, ws, rank, e0, e1, stream, hbm, peak_src, barrier, cpu=keep_sd)
 
     # ---------------------------------------------------------------- reference GPU comparator

@@ -17,7 +17,8 @@ from . import _lib as L
 
 
 class BitNetConfig(ctypes.Structure):
-    """dlm_bitnet_config (BASELINE config 5 by default; head_dim = d_model / n_heads = 64)."""
+    """dlm_bitnet_config (by default the benchmarked tag LM: vocab 16000, d 512, 8 layers, FFN 1536;
+    head_dim = d_model / n_heads = 64)."""
     _fields_ = [("vocab", ctypes.c_int), ("d_model", ctypes.c_int), ("n_layers", ctypes.c_int),
                 ("n_heads", ctypes.c_int), ("ffn_dim", ctypes.c_int), ("max_seq", ctypes.c_int),
                 ("rope_base", ctypes.c_double), ("rms_eps", ctypes.c_double),
@@ -140,7 +141,7 @@ def weight_spec(cfg: BitNetConfig) -> dict:
 
 
 def random_weights(cfg: BitNetConfig, seed: int = 10, device="cuda") -> dict:
-    """Synthetic weights of BASELINE config 5 on `device`: BitLinear weights uniform over
+    """Synthetic weights of the benchmarked tag LM on `device`: BitLinear weights uniform over
     {-1, 0, +1}, embed ~ N(0, 0.02), norms ~ N(1, 0.01) (fp32)."""
     g = torch.Generator(device=device).manual_seed(seed)
     out = {}

@@ -165,7 +165,7 @@ TOK_EOS = 2   # src/io/tokenizer.hpp:44
 
 def lm_config(vocab=16000, d_model=512, n_layers=8, n_heads=8, ffn_dim=1536, max_seq=128,
               rope_base=10000.0, rms_eps=1e-5, per_tensor_scale=0) -> dict:
-    """Model dimensions (BASELINE config 5 by default; the reference's compiled-in ones are
+    """Model dimensions (the benchmarked tag LM's by default; the reference's compiled-in ones are
     vocab 4999, FFN 1792, max_seq 64, src/models/bitnet_config.hpp:41-58)."""
     return dict(vocab=vocab, d_model=d_model, n_layers=n_layers, n_heads=n_heads, ffn_dim=ffn_dim,
                 max_seq=max_seq, rope_base=rope_base, rms_eps=rms_eps,
@@ -188,7 +188,7 @@ def lm_shapes(cfg) -> dict:
 def lm_random_weights(cfg, seed=10, kind="ternary") -> dict:
     """Seeded fp32 weights.  embed ~ N(0, 0.02) and norms ~ N(1, 0.01) as the reference's
     init_random (src/models/bitnet.hpp:300-331); BitLinear weights either uniform over {-1, 0, +1}
-    (kind="ternary") or N(0, 0.02) (kind="normal", the reference's init)."""
+    (kind="ternary", the benchmarked tag LM) or N(0, 0.02) (kind="normal", the reference's init)."""
     rng = np.random.default_rng(seed)
     out = {}
     for name, shape in lm_shapes(cfg).items():

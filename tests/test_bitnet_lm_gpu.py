@@ -81,7 +81,7 @@ def test_generate_matches_oracle_with_eos_stops():
 
 
 def test_generate_baseline_dims_matches_oracle():
-    """BASELINE config 5 dims (vocab 16000, d 512, 8 layers, FFN 1536), 64 prompt + 64 greedy
+    """The benchmarked tag LM's dims (vocab 16000, d 512, 8 layers, FFN 1536), 64 prompt + 64 greedy
     tokens, ternary weights; 8 sequences on the GPU, two of them re-derived by the oracle."""
     cfg = B.lm_config()
     w = B.lm_random_weights(cfg, seed=10, kind="ternary")
@@ -96,7 +96,7 @@ def test_generate_baseline_dims_matches_oracle():
 
 def test_generate_sequence_shards_match_full_batch():
     """The multi-GPU LM split: every rank generates its own shard of the sequences.  At the
-    config-5 dims, each shard of 128, 64 or 32 of 256 sequences (the per-rank batches of 2, 4 and
+    benchmarked dims, each shard of 128, 64 or 32 of 256 sequences (the per-rank batches of 2, 4 and
     8 GPUs) generated alone gives the full batch's tokens for those sequences — the decode tile
     choices, which depend on the batch, change no bit."""
     cfg = B.lm_config()
