@@ -253,9 +253,9 @@ __global__ void __launch_bounds__(kThreads)
 // The same exact BitLinear on the 5th-generation tensor cores: tcgen05.mma kind::i8 (signed int8
 // A and B from shared memory, int32 accumulation in TMEM — integer sums, so the result is the
 // dp4a path's bit for bit).  One CTA = 128 tokens x 128 outputs; K in 128-byte blocks through a
-// 3-stage ring, two CTAs per SM (97 KB of shared memory, 128 TMEM columns and <= 168 registers
-// each), so one CTA's epilogue runs beside the other's mainloop (one CTA per SM with 4 stages:
-// 212 -> 151 us for the 16384 x 3072 x 512 gate|up projection):
+// 2-stage ring, three CTAs per SM (66 KB of shared memory, 128 TMEM columns and <= 112 registers
+// each), so the CTAs' epilogues run beside each other's mainloops (16384 x 3072 x 512 gate|up
+// projection: one CTA per SM with 4 stages 212 us, two with 3 stages 151 us, three 114 us):
 //   warp 0     TMA: the activation block (128 tokens x 128 int8, 128-byte swizzle);
 //   warp 1     TMEM owner + MMA issuer: 4 MMAs (K = 32) per block, M = 128, N = 128;
 //   warps 2-5  expand the weight block (128 rows x 128 two-bit codes, 4 KB packed) into int8 in
@@ -263,7 +263,7 @@ __global__ void __launch_bounds__(kThreads)
 //              16-byte chunk per packed word, chunk index XOR row % 8), then, after the last block,
 //              the epilogue: TMEM -> int32 -> y = float(double(acc) * alpha[n] * xscale[m])
 //              (or y += that value), one row per thread.
-constexpr int kTcM = 128, kTcN = 128, kTcKB = 128, kTcStages = 3, kTcThreads = 192;
+constexpr int kTcM = 128, kTcN = 128, kTcKB = 128, kTcStages = 2, kTcThreads = 192;
 constexpr int kTcStageA = kTcM * kTcKB, kTcStageB = kTcN * kTcKB;  // 16 KB each
 constexpr int kTcSmem = kTcStages * (kTcStageA + kTcStageB) + 256 + 1024;
 
@@ -276,7 +276,7 @@ struct TernaryTcParams {
   int* status;
 };
 
-__global__ void __launch_bounds__(kTcThreads, 2)
+__global__ void __launch_bounds__(kTcThreads, 3)
     ternary_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmX, const TernaryTcParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
