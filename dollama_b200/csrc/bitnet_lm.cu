@@ -845,8 +845,10 @@ int BitNetLM::run_layers(int S, const int* pos, cudaStream_t s) {
     DLM_CHECK_CUDA(launch_pdl(rope_kv_kernel, dim3(grid1d(static_cast<size_t>(M) * H * 32, 256)),
         dim3(256), 0, s, y_, M, S, D, pos, cos_t_, sin_t_, q_, kc, vc, L_));
     if (S > 1 && L_ <= kAttnSeqMax)  // prefill: one block per (sequence, head)
+      // a block stages base + S positions: S when the pass starts at position 0 (no device
+      // position), which leaves room for more blocks per SM than the cache length would
       DLM_CHECK_CUDA(launch_pdl(attention_seq_kernel, dim3(B_ * H), dim3(kAttnSeqWarps * 32),
-          attn_seq_smem_bytes(L_), s, q_, S, D, pos, kc, vc, L_, ao_));
+          attn_seq_smem_bytes(pos ? L_ : S), s, q_, S, D, pos, kc, vc, L_, ao_));
     else
       DLM_CHECK_CUDA(launch_pdl(attention_kernel, dim3(M * H), dim3(kAttnThreads), attn_smem, s, q_,
           M, S, D, pos, kc, vc, L_, ao_));
