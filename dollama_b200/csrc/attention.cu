@@ -614,7 +614,8 @@ __global__ void __launch_bounds__(attn_threads(kSplit), 1)
                     static_cast<size_t>(qrow) * p.o_ss;
       // a group cut between CTAs (stream-K): this piece goes to the workspace, normalised by its
       // own row sum, and the last CTA to finish merges the pieces
-      const bool piece = kSK && !sg.whole;
+      // a cut query block (stream-K); with one key tile per block (not kSplit) none is ever cut
+      const bool piece = kSK && kSplit && !sg.whole;
       const int r_in = t * kQT + row;
       int first = 0, last = 0;
       if (piece) {
@@ -624,6 +625,80 @@ __global__ void __launch_bounds__(attn_threads(kSplit), 1)
       }
       auto slot_of = [&](int cc) { return 2 * cc + (cc == first ? 1 : 0); };
       const size_t my_slot = static_cast<size_t>(slot_of(static_cast<int>(blockIdx.x))) * kQ + r_in;
+      if (piece) {
+        // The last piece of a cut query block, when every other piece is already in the workspace
+        // (their CTAs have counted them): merge straight from this CTA's O in TMEM, without
+        // writing and re-reading its own piece.  This CTA does not count itself, so no other can
+        // also find itself last; otherwise the counted path below runs as before.
+        ok = ep_meet();
+        if (!ok) break;
+        if (threadIdx.x == 0) {
+          int cnt;
+          asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(cnt) : "l"(p.part_cnt + sg.group) : "memory");
+          *last_flag = cnt == last - first;
+        }
+        ok = ep_meet();
+        if (!ok) break;
+        if (*last_flag) {
+          const int me = static_cast<int>(blockIdx.x);
+          float mmax = m_run;
+          for (int cc = first; cc <= last; ++cc)
+            if (cc != me) mmax = fmaxf(mmax, __ldcg(p.part_ml + static_cast<size_t>(slot_of(cc)) * kQ + r_in).x);
+          // own O is unnormalised (sum of 2^((s - m) c) v): its weight l 2^((m - M) c) over l
+          const float so = fast_exp2((m_run - mmax) * c);
+          float L = l_run * so;
+          for (int cc = first; cc <= last; ++cc) {
+            if (cc == me) continue;
+            const float2 ml = __ldcg(p.part_ml + static_cast<size_t>(slot_of(cc)) * kQ + r_in);
+            L += ml.y * fast_exp2((ml.x - mmax) * c);
+          }
+          const float inv = 1.0f / L;
+#pragma unroll 1
+          for (int qd = 0; qd < 4; ++qd) {  // 16 columns at a time
+            uint32_t r[16];
+            tmem_ld_32x32b_x16(to + qd * 16, r);
+            tmem_ld_wait();
+            float a16[16];
+#pragma unroll
+            for (int d = 0; d < 16; ++d) a16[d] = __uint_as_float(r[d]) * so;
+            for (int cc = first; cc <= last; ++cc) {
+              if (cc == me) continue;
+              const size_t sl = static_cast<size_t>(slot_of(cc)) * kQ + r_in;
+              const float2 ml = __ldcg(p.part_ml + sl);
+              const uint4* po = reinterpret_cast<const uint4*>(p.part_o + sl * kD) + 2 * qd;
+              const uint4 o0 = __ldcg(po), o1 = __ldcg(po + 1);
+              const float w = ml.y * fast_exp2((ml.x - mmax) * c);
+              const __half2* h0 = reinterpret_cast<const __half2*>(&o0);
+              const __half2* h1 = reinterpret_cast<const __half2*>(&o1);
+#pragma unroll
+              for (int k2 = 0; k2 < 4; ++k2) {
+                const float2 f0 = __half22float2(h0[k2]), f1 = __half22float2(h1[k2]);
+                a16[2 * k2] = fmaf(w, f0.x, a16[2 * k2]);
+                a16[2 * k2 + 1] = fmaf(w, f0.y, a16[2 * k2 + 1]);
+                a16[8 + 2 * k2] = fmaf(w, f1.x, a16[8 + 2 * k2]);
+                a16[8 + 2 * k2 + 1] = fmaf(w, f1.y, a16[8 + 2 * k2 + 1]);
+              }
+            }
+            if (qrow < p.Sq) {
+              uint4 v0, v1;
+              v0.x = pack_half2(a16[0] * inv, a16[1] * inv);
+              v0.y = pack_half2(a16[2] * inv, a16[3] * inv);
+              v0.z = pack_half2(a16[4] * inv, a16[5] * inv);
+              v0.w = pack_half2(a16[6] * inv, a16[7] * inv);
+              v1.x = pack_half2(a16[8] * inv, a16[9] * inv);
+              v1.y = pack_half2(a16[10] * inv, a16[11] * inv);
+              v1.z = pack_half2(a16[12] * inv, a16[13] * inv);
+              v1.w = pack_half2(a16[14] * inv, a16[15] * inv);
+              *reinterpret_cast<uint4*>(dst + 16 * qd) = v0;
+              *reinterpret_cast<uint4*>(dst + 16 * qd + 8) = v1;
+            }
+          }
+          tc_fence_before();
+          mbar_arrive(&o_empty[t]);
+          if (threadIdx.x == 0) p.part_cnt[sg.group] = 0;
+          continue;
+        }
+      }
       {
         // O leaves TMEM 32 columns at a time (fp16, scaled by 1 / l), then the next segment's
         // first P.V may overwrite it
