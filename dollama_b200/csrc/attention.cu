@@ -625,11 +625,13 @@ __global__ void __launch_bounds__(attn_threads(kSplit), 1)
       }
       auto slot_of = [&](int cc) { return 2 * cc + (cc == first ? 1 : 0); };
       const size_t my_slot = static_cast<size_t>(slot_of(static_cast<int>(blockIdx.x))) * kQ + r_in;
-      if (piece) {
+      if (piece && sg.j0 == 0) {
         // The last piece of a cut query block, when every other piece is already in the workspace
         // (their CTAs have counted them): merge straight from this CTA's O in TMEM, without
         // writing and re-reading its own piece.  This CTA does not count itself, so no other can
-        // also find itself last; otherwise the counted path below runs as before.
+        // also find itself last; otherwise the counted path below runs as before.  Only a block's
+        // head piece checks: it ends its CTA's range, while the tail pieces, which begin theirs,
+        // finish early and are almost never last.
         ok = ep_meet();
         if (!ok) break;
         if (threadIdx.x == 0) {
