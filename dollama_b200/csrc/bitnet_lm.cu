@@ -840,10 +840,17 @@ int BitNetLM::run_layers(int S, const int* pos, cudaStream_t s) {
     float* vc = vc_ + l * kv_layer;
     DLM_CHECK_CUDA(launch_pdl(rms_norm_kernel, dim3(norm_blocks), dim3(kNormWarps * 32), norm_smem,
         s, h_, M, D, 1, 0, Ly.attn_norm, c.rms_eps, xq_, xs_, nullptr));
-    rc = ternary_gemm_i8(Ly.wqkv, Ly.aqkv, xq_, xs_, y_, M, 3 * D, D, s);
-    if (rc != DLM_OK) break;
-    DLM_CHECK_CUDA(launch_pdl(rope_kv_kernel, dim3(grid1d(static_cast<size_t>(M) * H * 32, 256)),
-        dim3(256), 0, s, y_, M, S, D, pos, cos_t_, sin_t_, q_, kc, vc, L_));
+    if (S == 1 && pos != nullptr && M < ternary_tc_min_rows()) {
+      // decode: RoPE and the K / V append in the q|k|v projection's epilogue
+      const RopeQkv rq{pos, cos_t_, sin_t_, q_, kc, vc, D, L_};
+      rc = ternary_gemm_qkv_rope(Ly.wqkv, Ly.aqkv, xq_, xs_, M, D, rq, s);
+      if (rc != DLM_OK) break;
+    } else {
+      rc = ternary_gemm_i8(Ly.wqkv, Ly.aqkv, xq_, xs_, y_, M, 3 * D, D, s);
+      if (rc != DLM_OK) break;
+      DLM_CHECK_CUDA(launch_pdl(rope_kv_kernel, dim3(grid1d(static_cast<size_t>(M) * H * 32, 256)),
+          dim3(256), 0, s, y_, M, S, D, pos, cos_t_, sin_t_, q_, kc, vc, L_));
+    }
     if (S > 1 && L_ <= kAttnSeqMax)  // prefill: one block per (sequence, head)
       // a block stages base + S positions: S when the pass starts at position 0 (no device
       // position), which leaves room for more blocks per SM than the cache length would

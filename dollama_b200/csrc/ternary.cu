@@ -139,11 +139,11 @@ __device__ __forceinline__ uint32_t decode4(uint32_t b) {
   return lo | (hi * 0xFEu);
 }
 
-template <int TN>
+template <int TN, bool kRope>
 __global__ void __launch_bounds__(kThreads)
     ternary_gemm_kernel(const uint32_t* __restrict__ wp, const float* __restrict__ alpha,
                         const int8_t* __restrict__ xq, const float* __restrict__ xscale,
-                        float* __restrict__ y, int M, int N, int K, int accumulate) {
+                        float* __restrict__ y, int M, int N, int K, int accumulate, RopeQkv rp) {
   griddep_wait();  // inputs come from the previous kernel (programmatic dependent launch)
   constexpr int NI = TN / 16;  // outputs per thread
   __shared__ __align__(16) int8_t sw[TN * kRow];              // expanded int8 weight chunk
@@ -222,6 +222,43 @@ __global__ void __launch_bounds__(kThreads)
           acc[j][i] = a;
         }
     }
+  }
+  if constexpr (kRope) {
+    // q|k|v of one position per sequence: a 64-output tile is one head of q, k or v; this thread's
+    // outputs tx, tx + 16, tx + 32, tx + 48 of it are the RoPE pairs (tx, tx + 32) and
+    // (tx + 16, tx + 48) (bitnet.hpp:472-488), rotated in double from the float outputs
+    static_assert(TN == 64, "one head per tile");
+    const int base = *rp.pos;
+    const int part = n0 / rp.D, hd = (n0 % rp.D) / kTN, H = rp.D / kTN;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int m = m0 + ty + 16 * j;
+      if (m >= M) continue;
+      const double sc = static_cast<double>(xscale[m]);
+      float v[NI];
+#pragma unroll
+      for (int i = 0; i < NI; ++i)
+        v[i] = __double2float_rn(__dmul_rn(
+            __dmul_rn(static_cast<double>(acc[j][i]), static_cast<double>(alpha[n0 + tx + 16 * i])), sc));
+      const size_t cache = ((static_cast<size_t>(m) * H + hd) * rp.Lmax + base) * kTN;
+      if (part == 2) {
+#pragma unroll
+        for (int i = 0; i < NI; ++i) rp.vc[cache + tx + 16 * i] = v[i];
+        continue;
+      }
+#pragma unroll
+      for (int pr = 0; pr < 2; ++pr) {
+        const int ih = tx + 16 * pr;
+        const double cs = rp.cos_t[base * (kTN / 2) + ih], sn = rp.sin_t[base * (kTN / 2) + ih];
+        const double a = static_cast<double>(v[pr]), bb = static_cast<double>(v[pr + 2]);
+        const float o0 = __double2float_rn(__dsub_rn(__dmul_rn(a, cs), __dmul_rn(bb, sn)));
+        const float o1 = __double2float_rn(__dadd_rn(__dmul_rn(a, sn), __dmul_rn(bb, cs)));
+        float* dst = part == 0 ? rp.q + static_cast<size_t>(m) * rp.D + hd * kTN : rp.kc + cache;
+        dst[ih] = o0;
+        dst[ih + kTN / 2] = o1;
+      }
+    }
+    return;
   }
   // accumulate: the residual update h += bitlinear(x) as one float add (bitnet.hpp:579-583); the
   // accumulated outputs are all requested before any is written
@@ -514,14 +551,31 @@ int ternary_gemm_i8(const uint32_t* wp, const float* alpha, const int8_t* xq, co
   const long tiles64 = static_cast<long>((N + kTN - 1) / kTN) * ((M + kTM - 1) / kTM);
   if (2 * tiles64 < num_sms()) {
     dim3 grid((N + 31) / 32, (M + kTM - 1) / kTM);
-    DLM_CHECK_CUDA(launch_pdl(ternary_gemm_kernel<32>, dim3(grid), dim3(kThreads), 0, s, wp, alpha,
-        xq, xscale, y, M, N, K, accumulate ? 1 : 0));
+    DLM_CHECK_CUDA(launch_pdl(ternary_gemm_kernel<32, false>, dim3(grid), dim3(kThreads), 0, s, wp, alpha,
+        xq, xscale, y, M, N, K, accumulate ? 1 : 0, RopeQkv{}));
   } else {
     dim3 grid((N + kTN - 1) / kTN, (M + kTM - 1) / kTM);
-    DLM_CHECK_CUDA(launch_pdl(ternary_gemm_kernel<kTN>, dim3(grid), dim3(kThreads), 0, s, wp, alpha,
-        xq, xscale, y, M, N, K, accumulate ? 1 : 0));
+    DLM_CHECK_CUDA(launch_pdl(ternary_gemm_kernel<kTN, false>, dim3(grid), dim3(kThreads), 0, s, wp, alpha,
+        xq, xscale, y, M, N, K, accumulate ? 1 : 0, RopeQkv{}));
   }
   DLM_CHECK_CUDA(cudaGetLastError());
+  return DLM_OK;
+}
+
+int ternary_tc_min_rows() { return tc_min_rows(); }
+
+int ternary_gemm_qkv_rope(const uint32_t* wp, const float* alpha, const int8_t* xq,
+                          const float* xscale, int M, int K, const RopeQkv& r, cudaStream_t s) {
+  DLM_REQUIRE(wp && alpha && xq && xscale && r.pos && r.cos_t && r.sin_t && r.q && r.kc && r.vc,
+              DLM_ERR_INVALID, "ternary_gemm_qkv_rope: null pointer");
+  DLM_REQUIRE(K % 64 == 0 && r.D % kTN == 0 && r.Lmax > 0, DLM_ERR_INVALID,
+              "ternary_gemm_qkv_rope: K=%d, D=%d", K, r.D);
+  DLM_REQUIRE((reinterpret_cast<uintptr_t>(wp) & 15) == 0 && (reinterpret_cast<uintptr_t>(xq) & 15) == 0,
+              DLM_ERR_INVALID, "ternary_gemm_qkv_rope: packed weights / activations must be 16-byte aligned");
+  const int N = 3 * r.D;
+  dim3 grid(N / kTN, (M + kTM - 1) / kTM);
+  DLM_CHECK_CUDA(launch_pdl(ternary_gemm_kernel<kTN, true>, dim3(grid), dim3(kThreads), 0, s, wp,
+      alpha, xq, xscale, static_cast<float*>(nullptr), M, N, K, 0, r));
   return DLM_OK;
 }
 

@@ -19,4 +19,24 @@ int quantize_act_i8(const float* x, int M, int K, int8_t* xq, float* xscale, cud
 int ternary_gemm_i8(const uint32_t* wp, const float* alpha, const int8_t* xq, const float* xscale,
                     float* y, int M, int N, int K, cudaStream_t s, bool accumulate = false);
 
+// Token rows from which ternary_gemm_i8 uses the tensor cores.
+int ternary_tc_min_rows();
+
+// The LM's decode q|k|v projection (one position per sequence, N = 3 D) with RoPE and the K / V
+// cache append in its epilogue: row m is sequence m at position *pos; output columns [0, D) are q
+// (rotated, to q[m][D]), [D, 2D) k (rotated, into kc), [2D, 3D) v (into vc); caches
+// [M][D / 64][Lmax][64]; cos_t / sin_t [position][32].  Same operations, in the same order, as
+// the projection followed by the separate RoPE kernel.
+struct RopeQkv {
+  const int* pos;
+  const double* cos_t;
+  const double* sin_t;
+  float* q;
+  float* kc;
+  float* vc;
+  int D, Lmax;
+};
+int ternary_gemm_qkv_rope(const uint32_t* wp, const float* alpha, const int8_t* xq,
+                          const float* xscale, int M, int K, const RopeQkv& r, cudaStream_t s);
+
 }  // namespace dlm
