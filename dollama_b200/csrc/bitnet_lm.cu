@@ -203,12 +203,17 @@ __global__ void rope_kv_kernel(const float* __restrict__ qkv, int M, int S, int 
 // dot product.
 constexpr int kAttnThreads = 128;
 constexpr int kVStageMax = 256;  // cache lengths up to which V is staged (64 KB of shared memory)
+// cache lengths up to which K is staged as well, in rows of 68 floats (272 bytes: 16-byte aligned,
+// and the 16-byte reads of eight consecutive rows fall in distinct banks)
+constexpr int kKStageMax = 128;
+constexpr int kKRow = kHeadDim + 4;
 // doubles before the staged V rows, rounded up to an even count so that V starts 16-byte aligned
 // (its rows are written with 16-byte stores) whatever the cache length
 __host__ __device__ constexpr int attn_head_doubles(int Lmax) { return (kHeadDim + Lmax + 40 + 1) & ~1; }
 __host__ __device__ constexpr size_t attn_smem_bytes(int Lmax) {
   return attn_head_doubles(Lmax) * sizeof(double) +
-         (Lmax <= kVStageMax ? static_cast<size_t>(Lmax) * kHeadDim * 4 : 0);
+         (Lmax <= kVStageMax ? static_cast<size_t>(Lmax) * kHeadDim * 4 : 0) +
+         (Lmax <= kKStageMax ? static_cast<size_t>(Lmax) * kKRow * 4 : 0);
 }
 __global__ void __launch_bounds__(kAttnThreads)
     attention_kernel(const float* __restrict__ q, int M, int S, int D, const int* __restrict__ pos_in,
@@ -230,6 +235,15 @@ __global__ void __launch_bounds__(kAttnThreads)
   const float* vb = vc + (static_cast<size_t>(b) * H + hd) * Lmax * kHeadDim;
   for (int d = threadIdx.x; d < kHeadDim; d += blockDim.x) sq[d] = static_cast<double>(qr[d]);
   const bool staged = Lmax <= kVStageMax;
+  const bool kstaged = Lmax <= kKStageMax;
+  float* skk = sv + static_cast<size_t>(Lmax) * kHeadDim;  // K rows (kstaged), after V
+  if (kstaged) {
+    // K rows 0..n-1 by coalesced asynchronous 16-byte copies (read per thread from the global
+    // cache instead, each 16-byte load of a warp touches 32 rows): one group, awaited first
+    for (int i = threadIdx.x; i < n * (kHeadDim / 4); i += blockDim.x)
+      cp_async16(skk + (i >> 4) * kKRow + 4 * (i & 15), kb + 4 * i, 16);
+    cp_async_commit();
+  }
   if (staged) {
     // V rows 0..n-1 into shared memory by asynchronous 16-byte copies, all in flight at once:
     // they land while the scores are formed (16-byte aligned: attn_head_doubles is even)
@@ -238,10 +252,17 @@ __global__ void __launch_bounds__(kAttnThreads)
     cp_async_commit();
   }
   const float* vrows = staged ? sv : vb;
+  if (kstaged) {
+    if (staged)
+      asm volatile("cp.async.wait_group 1;" ::: "memory");  // K landed; V may still be in flight
+    else
+      cp_async_wait_all();
+  }
   __syncthreads();
   double mx = -1e300;
   for (int j = threadIdx.x; j < n; j += blockDim.x) {
-    const float4* kj = reinterpret_cast<const float4*>(kb + static_cast<size_t>(j) * kHeadDim);
+    const float4* kj = kstaged ? reinterpret_cast<const float4*>(skk + static_cast<size_t>(j) * kKRow)
+                               : reinterpret_cast<const float4*>(kb + static_cast<size_t>(j) * kHeadDim);
     float4 kr[kHeadDim / 4];
 #pragma unroll
     for (int i = 0; i < kHeadDim / 4; ++i) kr[i] = kj[i];
