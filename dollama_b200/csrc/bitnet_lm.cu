@@ -204,7 +204,8 @@ __global__ void rope_kv_kernel(const float* __restrict__ qkv, int M, int S, int 
 constexpr int kAttnThreads = 128;
 constexpr int kVStageMax = 256;  // cache lengths up to which V is staged (64 KB of shared memory)
 // cache lengths up to which K is staged as well, in rows of 68 floats (272 bytes: 16-byte aligned,
-// and the 16-byte reads of eight consecutive rows fall in distinct banks)
+// and the 16-byte reads of eight consecutive rows fall in distinct banks); V then arrives in the
+// same buffer once the scores are formed, so a block needs no more shared memory than for V alone
 constexpr int kKStageMax = 128;
 constexpr int kKRow = kHeadDim + 4;
 // doubles before the staged V rows, rounded up to an even count so that V starts 16-byte aligned
@@ -212,15 +213,15 @@ constexpr int kKRow = kHeadDim + 4;
 __host__ __device__ constexpr int attn_head_doubles(int Lmax) { return (kHeadDim + Lmax + 40 + 1) & ~1; }
 __host__ __device__ constexpr size_t attn_smem_bytes(int Lmax) {
   return attn_head_doubles(Lmax) * sizeof(double) +
-         (Lmax <= kVStageMax ? static_cast<size_t>(Lmax) * kHeadDim * 4 : 0) +
-         (Lmax <= kKStageMax ? static_cast<size_t>(Lmax) * kKRow * 4 : 0);
+         (Lmax <= kKStageMax ? static_cast<size_t>(Lmax) * kKRow * 4
+          : Lmax <= kVStageMax ? static_cast<size_t>(Lmax) * kHeadDim * 4 : 0);
 }
 __global__ void __launch_bounds__(kAttnThreads)
     attention_kernel(const float* __restrict__ q, int M, int S, int D, const int* __restrict__ pos_in,
                      const float* __restrict__ kc, const float* __restrict__ vc, int Lmax,
                      float* __restrict__ out) {
   griddep_wait();  // inputs come from the previous kernel (programmatic dependent launch)
-  extern __shared__ double sh[];  // [64] q, [Lmax] scores, [40] reduction, then [Lmax][64] V (f32)
+  extern __shared__ double sh[];  // [64] q, [Lmax] scores, [40] reduction, then K rows / V rows (f32)
   double* sq = sh;
   double* ss = sh + kHeadDim;
   double* red = ss + Lmax;
@@ -236,28 +237,23 @@ __global__ void __launch_bounds__(kAttnThreads)
   for (int d = threadIdx.x; d < kHeadDim; d += blockDim.x) sq[d] = static_cast<double>(qr[d]);
   const bool staged = Lmax <= kVStageMax;
   const bool kstaged = Lmax <= kKStageMax;
-  float* skk = sv + static_cast<size_t>(Lmax) * kHeadDim;  // K rows (kstaged), after V
+  float* skk = sv;  // K rows (kstaged), then V in the same buffer
   if (kstaged) {
     // K rows 0..n-1 by coalesced asynchronous 16-byte copies (read per thread from the global
-    // cache instead, each 16-byte load of a warp touches 32 rows): one group, awaited first
+    // cache instead, each 16-byte load of a warp touches 32 rows); 16-byte aligned:
+    // attn_head_doubles is even
     for (int i = threadIdx.x; i < n * (kHeadDim / 4); i += blockDim.x)
       cp_async16(skk + (i >> 4) * kKRow + 4 * (i & 15), kb + 4 * i, 16);
     cp_async_commit();
-  }
-  if (staged) {
+    cp_async_wait_all();
+  } else if (staged) {
     // V rows 0..n-1 into shared memory by asynchronous 16-byte copies, all in flight at once:
-    // they land while the scores are formed (16-byte aligned: attn_head_doubles is even)
+    // they land while the scores are formed
     for (int i = threadIdx.x; i < n * (kHeadDim / 4); i += blockDim.x)
       cp_async16(sv + 4 * i, vb + 4 * i, 16);
     cp_async_commit();
   }
   const float* vrows = staged ? sv : vb;
-  if (kstaged) {
-    if (staged)
-      asm volatile("cp.async.wait_group 1;" ::: "memory");  // K landed; V may still be in flight
-    else
-      cp_async_wait_all();
-  }
   __syncthreads();
   double mx = -1e300;
   for (int j = threadIdx.x; j < n; j += blockDim.x) {
@@ -277,6 +273,13 @@ __global__ void __launch_bounds__(kAttnThreads)
   mx = warp_max_d(mx);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
   __syncthreads();
+  if (kstaged) {
+    // every thread has its score: V rows 0..n-1 into the K buffer, landing during the
+    // exponentials and the sequential sum
+    for (int i = threadIdx.x; i < n * (kHeadDim / 4); i += blockDim.x)
+      cp_async16(sv + 4 * i, vb + 4 * i, 16);
+    cp_async_commit();
+  }
   if (threadIdx.x == 0) {
     double m = red[0];
     for (int w = 1; w < kAttnThreads / 32; ++w) m = fmax(m, red[w]);
