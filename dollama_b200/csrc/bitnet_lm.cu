@@ -119,7 +119,8 @@ __global__ void embed_kernel(const int* __restrict__ tokens, int ld_tok, int S,
 // rms_norm (bitnet.hpp:234-250), one warp per output row: every lane forms the double squares of
 // its elements, lane 0 adds them in index order (as the reference's loop), then x * inv * w per
 // element, rounded to float.  Output row r reads input row r * in_stride + in_off.  Optionally
-// quantizes the normalised row (int8) and / or stores it as float.
+// quantizes the normalised row (int8) and / or stores it transposed in double (out_t[d * ldt + r],
+// the lm_head's operand layout; each thread writes the block's four rows of one element).
 constexpr int kNormWarps = 4;
 // per block: the rows as float, then their squares as double
 __host__ __device__ constexpr size_t norm_smem_bytes(int D) {
@@ -128,37 +129,46 @@ __host__ __device__ constexpr size_t norm_smem_bytes(int D) {
 __global__ void __launch_bounds__(kNormWarps * 32)
     rms_norm_kernel(const float* __restrict__ h, int rows, int D, int in_stride, int in_off,
                     const float* __restrict__ w, double eps, int8_t* __restrict__ xq,
-                    float* __restrict__ xs, float* __restrict__ out_f) {
+                    float* __restrict__ xs, double* __restrict__ out_t, int ldt) {
   griddep_wait();  // inputs come from the previous kernel (programmatic dependent launch)
   extern __shared__ float srow[];  // [kNormWarps][D] float, then [kNormWarps][D] double
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int r = blockIdx.x * kNormWarps + warp;
-  if (r >= rows) return;
+  const int r0 = blockIdx.x * kNormWarps;
+  const int r = r0 + warp;
+  if (r >= rows && !out_t) return;  // (with out_t every warp reaches the block barrier below)
   float* row = srow + static_cast<size_t>(warp) * D;
-  // 16 * D bytes from the base: 8-byte aligned
-  double* sqr = reinterpret_cast<double*>(srow + static_cast<size_t>(kNormWarps) * D) +
-                static_cast<size_t>(warp) * D;
-  const float* src = h + (static_cast<size_t>(r) * in_stride + in_off) * D;
-  for (int i = lane; i < D; i += 32) {
-    const float v = src[i];
-    row[i] = v;
-    sqr[i] = __dmul_rn(static_cast<double>(v), static_cast<double>(v));
+  if (r < rows) {
+    // 16 * D bytes from the base: 8-byte aligned
+    double* sqr = reinterpret_cast<double*>(srow + static_cast<size_t>(kNormWarps) * D) +
+                  static_cast<size_t>(warp) * D;
+    const float* src = h + (static_cast<size_t>(r) * in_stride + in_off) * D;
+    for (int i = lane; i < D; i += 32) {
+      const float v = src[i];
+      row[i] = v;
+      sqr[i] = __dmul_rn(static_cast<double>(v), static_cast<double>(v));
+    }
+    __syncwarp();
+    double inv = 0.0;
+    if (lane == 0) {
+      double ms = seq_sum(sqr, D);
+      ms = __ddiv_rn(ms, static_cast<double>(D));
+      inv = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(ms, eps)));
+    }
+    inv = __shfl_sync(0xffffffffu, inv, 0);
+    for (int i = lane; i < D; i += 32)
+      row[i] = __double2float_rn(
+          __dmul_rn(__dmul_rn(static_cast<double>(row[i]), inv), static_cast<double>(w[i])));
+    __syncwarp();
+    if (xq) quant_row_warp(row, D, xq + static_cast<size_t>(r) * D, xs + r);
   }
-  __syncwarp();
-  double inv = 0.0;
-  if (lane == 0) {
-    double ms = seq_sum(sqr, D);
-    ms = __ddiv_rn(ms, static_cast<double>(D));
-    inv = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(ms, eps)));
+  if (out_t) {
+    __syncthreads();  // the block's normalised rows are in shared memory
+    const int nr = min(kNormWarps, rows - r0);
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+      double* dst = out_t + static_cast<size_t>(d) * ldt + r0;
+      for (int k = 0; k < nr; ++k) dst[k] = static_cast<double>(srow[static_cast<size_t>(k) * D + d]);
+    }
   }
-  inv = __shfl_sync(0xffffffffu, inv, 0);
-  for (int i = lane; i < D; i += 32)
-    row[i] = __double2float_rn(
-        __dmul_rn(__dmul_rn(static_cast<double>(row[i]), inv), static_cast<double>(w[i])));
-  __syncwarp();
-  if (out_f)
-    for (int i = lane; i < D; i += 32) out_f[static_cast<size_t>(r) * D + i] = row[i];
-  if (xq) quant_row_warp(row, D, xq + static_cast<size_t>(r) * D, xs + r);
 }
 
 // RoPE (bitnet.hpp:472-488) on q and k of every head and append k, v to the cache.  Row r is
@@ -431,87 +441,96 @@ __global__ void __launch_bounds__(kSwiThreads)
 
 // Tied lm_head (bitnet.hpp:414-436): logits[r, v] = float(sum_d double(x[r, d]) * double(E[v, d]))
 // with d in increasing order for every output (the products are exact in double, so fma equals
-// the reference's multiply-then-add).  Tile: 64 rows x 64 vocab ids, K chunks of 32; each thread
-// owns 4 rows x 4 ids (eight shared-memory loads per 16 fma).  The next chunk's raw floats arrive
-// by asynchronous copies while the current chunk is multiplied, then all threads convert them
-// into the transposed double tiles between two barriers.
-constexpr int kLmR = 64, kLmV = 64, kLmK = 32;
-// dynamic shared memory: raw float rows [64][32] of x and of E, then the double tiles
-constexpr size_t kLmRawBytes = static_cast<size_t>(kLmR + kLmV) * kLmK * 4;
-constexpr size_t kLmSmem = kLmRawBytes + static_cast<size_t>(kLmK) * ((kLmR + 1) + (kLmV + 1)) * 8;
+// the reference's multiply-then-add).  Both operands are read already in double and transposed —
+// xT [D][ldx] (written by the final rms_norm) and ET [D][ldv] (the embedding, transposed once when
+// the model is created, zero beyond V) — so K chunks of 16 arrive by asynchronous 16-byte copies
+// straight into the tiles the loop reads, double-buffered (converting fp32 chunks in every block
+// instead repeated each x element's conversion for all 250 vocabulary tiles).  Tile: 64 rows x 64
+// vocab ids; each thread owns 4 rows (two adjacent pairs, each read by one 16-byte load that the
+// warp's 16 threads of a row pair share) x 4 ids: six shared-memory wavefronts per 16 fma per
+// warp, which leaves the fp64 pipe the bound.  ldx and ldv are multiples of 64, so every copy is
+// in bounds (rows r >= R are computed and not stored).
+constexpr int kLmR = 64, kLmV = 64, kLmK = 16;
 __global__ void __launch_bounds__(256)
-    lm_head_kernel(const float* __restrict__ x, int R, int D, const float* __restrict__ E, int V,
-                   float* __restrict__ logits) {
+    lm_head_kernel(const double* __restrict__ xT, int ldx, int R, int D,
+                   const double* __restrict__ ET, int ldv, int V, float* __restrict__ logits) {
   griddep_wait();  // inputs come from the previous kernel (programmatic dependent launch)
-  extern __shared__ __align__(16) uint8_t lm_smem[];
-  float* xf = reinterpret_cast<float*>(lm_smem);  // [kLmR][kLmK]
-  float* ef = xf + kLmR * kLmK;                   // [kLmV][kLmK]
-  double(*xs)[kLmR + 1] = reinterpret_cast<double(*)[kLmR + 1]>(lm_smem + kLmRawBytes);
-  double(*es)[kLmV + 1] = reinterpret_cast<double(*)[kLmV + 1]>(
-      lm_smem + kLmRawBytes + static_cast<size_t>(kLmK) * (kLmR + 1) * 8);
+  __shared__ __align__(16) double xs[2][kLmK][kLmR];
+  __shared__ __align__(16) double es[2][kLmK][kLmV];
   const int r0 = blockIdx.y * kLmR, v0 = blockIdx.x * kLmV;
-  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;  // v = v0 + tx + 16i, r = r0 + ty + 16j
+  // v = v0 + tx + 16 i;  r = r0 + 2 ty + 32 (j >> 1) + (j & 1)
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
   double acc[4][4];
 #pragma unroll
   for (int j = 0; j < 4; ++j)
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc[j][i] = 0.0;
-  // raw chunk k0 (rows beyond R / V read as zeros): 8 16-byte copies per 32-float row
-  auto fetch = [&](int k0) {
+  // chunk k0 into buffer b: per tile row kk, 32 copies of two doubles (x then E)
+  auto fetch = [&](int k0, int b) {
 #pragma unroll
-    for (int t = threadIdx.x; t < (kLmR + kLmV) * (kLmK / 4); t += 256) {
-      const int row = t / (kLmK / 4), q = t % (kLmK / 4);
-      if (row < kLmR) {
-        const bool in = r0 + row < R;
-        const float* src = in ? x + static_cast<size_t>(r0 + row) * D + k0 + 4 * q : x;
-        cp_async16(xf + row * kLmK + 4 * q, src, in ? 16u : 0u);
-      } else {
-        const int vv = row - kLmR;
-        const bool in = v0 + vv < V;
-        const float* src = in ? E + static_cast<size_t>(v0 + vv) * D + k0 + 4 * q : E;
-        cp_async16(ef + vv * kLmK + 4 * q, src, in ? 16u : 0u);
-      }
+    for (int t = threadIdx.x; t < kLmK * (kLmR + kLmV) / 2; t += 256) {
+      const int kk = t / ((kLmR + kLmV) / 2), q = t % ((kLmR + kLmV) / 2);
+      if (q < kLmR / 2)
+        cp_async16(&xs[b][kk][2 * q], xT + static_cast<size_t>(k0 + kk) * ldx + r0 + 2 * q, 16);
+      else
+        cp_async16(&es[b][kk][2 * (q - kLmR / 2)],
+                   ET + static_cast<size_t>(k0 + kk) * ldv + v0 + 2 * (q - kLmR / 2), 16);
     }
     cp_async_commit();
   };
-  // landed raw chunk -> transposed double tiles
-  auto convert = [&]() {
-#pragma unroll
-    for (int t = threadIdx.x; t < kLmR * kLmK; t += 256) {
-      const int rr = t / kLmK, kk = t % kLmK;
-      xs[kk][rr] = static_cast<double>(xf[rr * kLmK + kk]);
-      es[kk][rr] = static_cast<double>(ef[rr * kLmK + kk]);
+  fetch(0, 0);
+  int b = 0;
+  for (int k0 = 0; k0 < D; k0 += kLmK, b ^= 1) {
+    if (k0 + kLmK < D) {
+      fetch(k0 + kLmK, b ^ 1);  // its buffer was last read before the previous closing barrier
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      cp_async_wait_all();
     }
-  };
-  fetch(0);
-  for (int k0 = 0; k0 < D; k0 += kLmK) {
-    cp_async_wait_all();
-    __syncthreads();  // chunk k0 landed for every thread; the previous chunk's tiles are free
-    convert();
-    __syncthreads();  // tiles ready; the raw buffer is free
-    if (k0 + kLmK < D) fetch(k0 + kLmK);
+    __syncthreads();  // chunk k0 landed for every thread
 #pragma unroll 4
     for (int kk = 0; kk < kLmK; ++kk) {
       double xv[4], ev[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) xv[j] = xs[kk][ty + 16 * j];
+      for (int jj = 0; jj < 2; ++jj) {
+        const double2 p = *reinterpret_cast<const double2*>(&xs[b][kk][2 * ty + 32 * jj]);
+        xv[2 * jj] = p.x;
+        xv[2 * jj + 1] = p.y;
+      }
 #pragma unroll
-      for (int i = 0; i < 4; ++i) ev[i] = es[kk][tx + 16 * i];
+      for (int i = 0; i < 4; ++i) ev[i] = es[b][kk][tx + 16 * i];
 #pragma unroll
       for (int j = 0; j < 4; ++j)
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[j][i] = __fma_rn(xv[j], ev[i], acc[j][i]);
     }
+    __syncthreads();  // every thread is done with buffer b
   }
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    const int r = r0 + ty + 16 * j;
+    const int r = r0 + 2 * ty + 32 * (j >> 1) + (j & 1);
     if (r >= R) continue;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int v = v0 + tx + 16 * i;
       if (v < V) logits[static_cast<size_t>(r) * V + v] = __double2float_rn(acc[j][i]);
     }
+  }
+}
+
+// Embedding E [V][D] (fp32) -> ET [D][ldv] (double), zero for v in [V, ldv): the lm_head's operand.
+__global__ void embed_transpose_kernel(const float* __restrict__ E, int V, int D, int ldv,
+                                       double* __restrict__ ET) {
+  __shared__ float tile[32][33];
+  const int v0 = blockIdx.x * 32, d0 = blockIdx.y * 32;
+  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
+    const int v = v0 + k, d = d0 + threadIdx.x;
+    tile[k][threadIdx.x] = (v < V && d < D) ? E[static_cast<size_t>(v) * D + d] : 0.0f;
+  }
+  __syncthreads();
+  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
+    const int d = d0 + k, v = v0 + threadIdx.x;
+    if (d < D && v < ldv) ET[static_cast<size_t>(d) * ldv + v] = static_cast<double>(tile[threadIdx.x][k]);
   }
 }
 
@@ -730,6 +749,15 @@ int BitNetLM::create(const BitNetCfg& cfg, int n, const char* const* names, cons
   embed_ = copy(src["embed"], static_cast<size_t>(V) * D);
   final_norm_ = copy(src["final_norm"], D);
   DLM_REQUIRE(embed_ && final_norm_, DLM_ERR_NOMEM, "bitnet_create: out of device memory");
+  DLM_REQUIRE(D % kLmK == 0, DLM_ERR_INVALID, "bitnet_create: d_model %d must be a multiple of %d", D,
+              kLmK);
+  // the lm_head's operand: the embedding transposed to [D][ldv] in double
+  ldv_ = (V + kLmV - 1) / kLmV * kLmV;
+  embT_ = walloc<double>(static_cast<size_t>(D) * ldv_);
+  DLM_REQUIRE(embT_, DLM_ERR_NOMEM, "bitnet_create: out of device memory");
+  embed_transpose_kernel<<<dim3((ldv_ + 31) / 32, (D + 31) / 32), dim3(32, 8), 0, s>>>(embed_, V, D,
+                                                                                    ldv_, embT_);
+  DLM_CHECK_CUDA(cudaGetLastError());
   double* scratch = walloc<double>(1);
   DLM_REQUIRE(scratch, DLM_ERR_NOMEM, "bitnet_create: out of device memory");
   // pack rows [row0, row0 + N) of a concatenated linear from one source tensor
@@ -812,7 +840,8 @@ int BitNetLM::plan(int B, int P, int Lmax, bool all_logits) {
   const size_t o_k = take(kv);
   const size_t o_v = take(kv);
   const size_t rows_lm = all_logits ? M : static_cast<size_t>(B);  // forward(): every position
-  const size_t o_norm = take(rows_lm * D * 4);
+  const size_t ldx = (rows_lm + kLmR - 1) / kLmR * kLmR;  // the final norm's transposed rows
+  const size_t o_norm = take(ldx * D * 8);
   const size_t o_logits = take(rows_lm * V * 4);
   const size_t o_state = take(64);
   const size_t o_done = take(static_cast<size_t>(B) * 4);
@@ -834,7 +863,8 @@ int BitNetLM::plan(int B, int P, int Lmax, bool all_logits) {
   ao_ = reinterpret_cast<float*>(base + o_ao);
   kc_ = reinterpret_cast<float*>(base + o_k);
   vc_ = reinterpret_cast<float*>(base + o_v);
-  norm_ = reinterpret_cast<float*>(base + o_norm);
+  normT_ = reinterpret_cast<double*>(base + o_norm);
+  ldx_ = static_cast<int>(ldx);
   logits_ = reinterpret_cast<float*>(base + o_logits);
   state_ = reinterpret_cast<int*>(base + o_state);  // [0] position, [1] bad-token flag
   done_ = reinterpret_cast<int*>(base + o_done);
@@ -863,7 +893,7 @@ int BitNetLM::run_layers(int S, const int* pos, cudaStream_t s) {
     float* kc = kc_ + l * kv_layer;
     float* vc = vc_ + l * kv_layer;
     DLM_CHECK_CUDA(launch_pdl(rms_norm_kernel, dim3(norm_blocks), dim3(kNormWarps * 32), norm_smem,
-        s, h_, M, D, 1, 0, Ly.attn_norm, c.rms_eps, xq_, xs_, nullptr));
+        s, h_, M, D, 1, 0, Ly.attn_norm, c.rms_eps, xq_, xs_, nullptr, 0));
     if (S == 1 && pos != nullptr && M < ternary_tc_min_rows()) {
       // decode: RoPE and the K / V append in the q|k|v projection's epilogue
       const RopeQkv rq{pos, cos_t_, sin_t_, q_, kc, vc, D, L_};
@@ -887,7 +917,7 @@ int BitNetLM::run_layers(int S, const int* pos, cudaStream_t s) {
     if (rc == DLM_OK) rc = ternary_gemm_i8(Ly.wo, Ly.ao, xq_, xs_, h_, M, D, D, s, true);
     if (rc != DLM_OK) break;
     DLM_CHECK_CUDA(launch_pdl(rms_norm_kernel, dim3(norm_blocks), dim3(kNormWarps * 32), norm_smem,
-        s, h_, M, D, 1, 0, Ly.ffn_norm, c.rms_eps, xq_, xs_, nullptr));
+        s, h_, M, D, 1, 0, Ly.ffn_norm, c.rms_eps, xq_, xs_, nullptr, 0));
     rc = ternary_gemm_i8(Ly.wgu, Ly.agu, xq_, xs_, y_, M, 2 * F, D, s);
     if (rc != DLM_OK) break;
     DLM_CHECK_CUDA(launch_pdl(swiglu_quant_kernel, dim3(M), dim3(kSwiThreads), swi_smem, s, y_, M,
@@ -902,13 +932,14 @@ int BitNetLM::run_layers(int S, const int* pos, cudaStream_t s) {
 int BitNetLM::run_head(int rows, int stride, int off, cudaStream_t s) {
   const BitNetCfg& c = cfg_;
   const int D = c.d_model;
-  DLM_REQUIRE(D % kLmK == 0, DLM_ERR_INVALID, "bitnet: d_model %d must be a multiple of %d", D, kLmK);
+  DLM_REQUIRE(D % kLmK == 0 && rows <= ldx_, DLM_ERR_INVALID, "bitnet: d_model %d / head rows %d", D,
+              rows);
   DLM_CHECK_CUDA(launch_pdl(rms_norm_kernel, dim3((rows + kNormWarps - 1) / kNormWarps),
       dim3(kNormWarps * 32), norm_smem_bytes(D), s, h_, rows, D, stride, off, final_norm_,
-      c.rms_eps, nullptr, nullptr, norm_));
+      c.rms_eps, nullptr, nullptr, normT_, ldx_));
   dim3 grid((c.vocab + kLmV - 1) / kLmV, (rows + kLmR - 1) / kLmR);
-  DLM_CHECK_CUDA(launch_pdl(lm_head_kernel, dim3(grid), dim3(256), kLmSmem, s, norm_, rows, D,
-      embed_, c.vocab, logits_));
+  DLM_CHECK_CUDA(launch_pdl(lm_head_kernel, dim3(grid), dim3(256), 0, s, normT_, ldx_, rows, D,
+      embT_, ldv_, c.vocab, logits_));
   DLM_CHECK_CUDA(cudaGetLastError());
   return DLM_OK;
 }
@@ -920,8 +951,6 @@ int BitNetLM::set_smem_attrs() {
   // the largest a launch asks for: staged V at the longest staged length, or the scores alone
   const size_t attn_smem = std::max(attn_smem_bytes(std::min(c.max_seq, kVStageMax)),
                                     attn_smem_bytes(c.max_seq));
-  DLM_CHECK_CUDA(cudaFuncSetAttribute(lm_head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(kLmSmem)));
   DLM_CHECK_CUDA(cudaFuncSetAttribute(rms_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       static_cast<int>(norm_smem)));
   DLM_CHECK_CUDA(cudaFuncSetAttribute(swiglu_quant_kernel,

@@ -53,6 +53,8 @@ class BitNetLM {
   BitNetCfg cfg_;
   std::vector<void*> wallocs_;
   float *embed_ = nullptr, *final_norm_ = nullptr;
+  double* embT_ = nullptr;  // the embedding transposed, [d_model][ldv_], double (lm_head operand)
+  int ldv_ = 0;
   double *cos_t_ = nullptr, *sin_t_ = nullptr;
   std::vector<Layer> layers_;
   // plan
@@ -63,7 +65,9 @@ class BitNetLM {
   int* tokens_ = nullptr;
   float *h_ = nullptr, *xs_ = nullptr, *y_ = nullptr, *q_ = nullptr, *ao_ = nullptr;
   int8_t* xq_ = nullptr;
-  float *kc_ = nullptr, *vc_ = nullptr, *norm_ = nullptr, *logits_ = nullptr;
+  float *kc_ = nullptr, *vc_ = nullptr, *logits_ = nullptr;
+  double* normT_ = nullptr;  // the final norm's rows transposed, [d_model][ldx_], double
+  int ldx_ = 0;
   int *state_ = nullptr, *done_ = nullptr, *out_ = nullptr, *out_len_ = nullptr;
   cudaGraphExec_t step_graph_ = nullptr;
   cudaStream_t cap_stream_ = nullptr;
