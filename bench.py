@@ -271,8 +271,10 @@ def lm_leg(dev, ws, rank, e0, e1, stream, hbm_peak, peak_src, barrier, cpu=True)
     ms_host = max_over_ranks(e0.elapsed_time(e1) / 3, ws, dev)
     # algorithmic HBM bytes of one decode step (B tokens, one per sequence), averaged over the
     # decode: the 2-bit ternary weights and their row scales; the BitLinears' int8 inputs and fp32
-    # outputs (the residual updates read and written); the tied fp32 embedding the lm_head reads;
-    # the fp32 K / V cache each sequence attends over (P + G / 2 positions on average)
+    # outputs (the residual updates read and written); the tied embedding at its fp32 size (the
+    # lm_head reads a transposed double copy of it, twice these bytes; the fp32 size is the
+    # algorithmic minimum); the fp32 K / V cache each sequence attends over (P + G / 2 positions on
+    # average)
     D, F, NL, V = cfg.d_model, cfg.ffn_dim, cfg.n_layers, cfg.vocab
     tern = NL * (4 * D * D + 3 * D * F)
     w_bytes = tern / 4 + NL * 4 * (5 * D + 2 * F)
@@ -290,7 +292,7 @@ def lm_leg(dev, ws, rank, e0, e1, stream, hbm_peak, peak_src, barrier, cpu=True)
         "e2e": {"value": tokens / (ms_host / 1000.0), "unit": "tokens/s",
                 "h2d_bytes_per_step": int(ph.nbytes), "d2h_bytes_per_step": int(B * (LM_NEW + 1) * 4)},
         "roofline": {"kernel": "one decode step (the 32 ternary BitLinear GEMMs and the context "
-                               "kernels around them, 85 launches, one CUDA graph)",
+                               "kernels around them, 77 launches, one CUDA graph)",
                      "bound": "hbm", "achieved": step_bytes / (step_ms / 1000.0) / 1e9,
                      "peak": hbm_peak, "unit": "GB/s",
                      "frac": step_bytes / (step_ms / 1000.0) / 1e9 / hbm_peak,
