@@ -900,7 +900,7 @@ int BitNetLM::run_layers(int S, const int* pos, cudaStream_t s) {
       rc = ternary_gemm_qkv_rope(Ly.wqkv, Ly.aqkv, xq_, xs_, M, D, rq, s);
       if (rc != DLM_OK) break;
     } else {
-      rc = ternary_gemm_i8(Ly.wqkv, Ly.aqkv, xq_, xs_, y_, M, 3 * D, D, s);
+      rc = ternary_gemm_i8(Ly.wqkv, Ly.aqkv, xq_, xs_, y_, M, 3 * D, D, s, false, true);
       if (rc != DLM_OK) break;
       DLM_CHECK_CUDA(launch_pdl(rope_kv_kernel, dim3(grid1d(static_cast<size_t>(M) * H * 32, 256)),
           dim3(256), 0, s, y_, M, S, D, pos, cos_t_, sin_t_, q_, kc, vc, L_));
@@ -914,15 +914,15 @@ int BitNetLM::run_layers(int S, const int* pos, cudaStream_t s) {
       DLM_CHECK_CUDA(launch_pdl(attention_kernel, dim3(M * H), dim3(kAttnThreads), attn_smem, s, q_,
           M, S, D, pos, kc, vc, L_, ao_));
     rc = quantize_act_i8(ao_, M, D, xq_, xs_, s);
-    if (rc == DLM_OK) rc = ternary_gemm_i8(Ly.wo, Ly.ao, xq_, xs_, h_, M, D, D, s, true);
+    if (rc == DLM_OK) rc = ternary_gemm_i8(Ly.wo, Ly.ao, xq_, xs_, h_, M, D, D, s, true, true);
     if (rc != DLM_OK) break;
     DLM_CHECK_CUDA(launch_pdl(rms_norm_kernel, dim3(norm_blocks), dim3(kNormWarps * 32), norm_smem,
         s, h_, M, D, 1, 0, Ly.ffn_norm, c.rms_eps, xq_, xs_, nullptr, 0));
-    rc = ternary_gemm_i8(Ly.wgu, Ly.agu, xq_, xs_, y_, M, 2 * F, D, s);
+    rc = ternary_gemm_i8(Ly.wgu, Ly.agu, xq_, xs_, y_, M, 2 * F, D, s, false, true);
     if (rc != DLM_OK) break;
     DLM_CHECK_CUDA(launch_pdl(swiglu_quant_kernel, dim3(M), dim3(kSwiThreads), swi_smem, s, y_, M,
         F, xq_, xs_));
-    rc = ternary_gemm_i8(Ly.wd, Ly.ad, xq_, xs_, h_, M, D, F, s, true);
+    rc = ternary_gemm_i8(Ly.wd, Ly.ad, xq_, xs_, h_, M, D, F, s, true, true);
   }
   if (rc == DLM_OK) DLM_CHECK_CUDA(cudaGetLastError());
   return rc;

@@ -32,6 +32,15 @@ constexpr int kRow = kKC + 16;  // padded smem row (bytes)
 constexpr int kThreads = 256;
 // Token rows from which the tensor-core path is used (DLM_TERNARY_TC_ROWS overrides, for
 // measurements).
+// The decode tensor-core path (DLM_TERNARY_TCD=0 keeps dp4a for every decode-sized call).
+bool tcd_enabled() {
+  static const bool v = [] {
+    const char* e = std::getenv("DLM_TERNARY_TCD");
+    return !(e && e[0] == '0');
+  }();
+  return v;
+}
+
 int tc_min_rows() {
   static const int v = [] {
     const char* e = std::getenv("DLM_TERNARY_TC_ROWS");
@@ -311,6 +320,7 @@ struct TernaryTcParams {
   float* y;
   int M, N, K, accumulate;
   int* status;
+  int weights_early;  // decode path: no kernel still in the stream writes wp / alpha
 };
 
 __global__ void __launch_bounds__(kTcThreads, 3)
@@ -485,6 +495,186 @@ __global__ void __launch_bounds__(kTcThreads, 3)
   }
 }
 
+// ---------------------------------------------------------------- tensor-core path (decode)
+// The same exact BitLinear for decode-sized inputs (fewer than tc_min_rows tokens, K <= 512): one
+// CTA = 128 tokens x TN outputs (TN = 32 or 64, so a decode projection spreads over 32-192 CTAs
+// where 128-output tiles gave 8-48) with every k-block resident at once, so no step of the
+// pipeline waits for a buffer to come free.  The 128 expanding threads fetch the CTA's packed
+// weights and row scales, expand them into the 128-byte-swizzled K-major int8 layout and arrive
+// on b_full — before waiting for the previous kernel when the caller states that no kernel still
+// in the stream writes the weights (the LM's, packed when the model is created); after it, warp 0 TMA-loads every activation block at once, warp 1
+// issues the K / 32 MMAs (M = 128, N = TN) into a TN-column TMEM accumulator, and the epilogue
+// warps fetch the token scales and, for h +=, the accumulated outputs while the MMAs run.  The
+// epilogue's operations are the prefill kernel's: y = float(double(acc) * alpha[n] * xscale[m]).
+constexpr int kTdKB = 128;   // k-block: 128 int8 = one 128-byte swizzled row
+constexpr int kTdMaxKB = 4;  // K <= 512
+constexpr int kTdThreads = 192;
+constexpr int kTdStageA = kTcM * kTdKB;  // 16 KB
+__host__ __device__ constexpr int td_smem_bytes(int TN) {
+  return kTdMaxKB * kTdStageA + kTdMaxKB * TN * kTdKB + TN * (kTdMaxKB * kTdKB / 4) + TN * 4 +
+         256 + 1024;
+}
+
+template <int TN>
+__global__ void __launch_bounds__(kTdThreads, 2)
+    ternary_gemm_tcd_kernel(const __grid_constant__ CUtensorMap tmX, const TernaryTcParams p) {
+  static_assert(TN == 32 || TN == 64, "decode tile width");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;                                  // [kTdMaxKB][128 x 128] int8, swizzled
+  uint8_t* sB = sA + kTdMaxKB * kTdStageA;             // [kTdMaxKB][TN x 128] int8, swizzled
+  uint8_t* sRaw = sB + kTdMaxKB * TN * kTdKB;          // [TN][K / 4] packed codes
+  float* sAlpha = reinterpret_cast<float*>(sRaw + TN * (kTdMaxKB * kTdKB / 4));  // [TN]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sAlpha + TN);
+  uint64_t* a_full = bars;        // TMA bytes of every activation block
+  uint64_t* b_full = bars + 1;    // the 128 expanding threads
+  uint64_t* acc_full = bars + 2;  // the last MMA completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  constexpr uint32_t kCols = TN;  // a power of two >= 32
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * TN, m0 = blockIdx.y * kTcM;
+  const int nkb = p.K / kTdKB;
+  if (threadIdx.x == 0) {
+    mbar_init(a_full, 1);
+    mbar_init(b_full, 128);
+    mbar_init(acc_full, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmX);
+      griddep_wait();  // the activations come from the previous kernel
+      mbar_arrive_expect_tx(a_full, nkb * kTdStageA);
+      for (int kb = 0; kb < nkb; ++kb) tma_load_2d(sA + kb * kTdStageA, &tmX, a_full, kb * kTdKB, m0);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_s8_s32(kTcM, TN);
+      const bool ok = mbar_wait(b_full, 0, abort_flag, p.status, kDevTimeoutMma) &&
+                      mbar_wait(a_full, 0, abort_flag, p.status, kDevTimeoutMma);
+      if (ok) {
+        tc_fence_after();
+        for (int kb = 0; kb < nkb; ++kb) {
+          const uint32_t a_addr = smem_u32(sA + kb * kTdStageA), b_addr = smem_u32(sB + kb * TN * kTdKB);
+#pragma unroll
+          for (int k = 0; k < kTdKB / 32; ++k)
+            umma_i8_ss(tbase, sw128_desc(a_addr + k * 32, 16, 1024), sw128_desc(b_addr + k * 32, 16, 1024),
+                       idesc, (kb != 0 || k != 0) ? 1u : 0u);
+        }
+        umma_commit(acc_full);
+      }
+    }
+  } else {
+    // warps 2..5: the weights (before the previous kernel has finished), then the epilogue
+    const int t = threadIdx.x - 64;  // 0..127
+    const int rowb = p.K / 4;        // packed bytes per output row
+    if (!p.weights_early) griddep_wait();
+    for (int q = t; q < TN * (rowb / 16); q += 128) {
+      const int r = q / (rowb / 16), c = q - r * (rowb / 16);
+      const bool in = n0 + r < p.N;
+      const uint8_t* src = in ? reinterpret_cast<const uint8_t*>(p.wp) + static_cast<size_t>(n0 + r) * rowb + 16 * c
+                              : reinterpret_cast<const uint8_t*>(p.wp);
+      cp_async16(sRaw + r * rowb + 16 * c, src, in ? 16u : 0u);
+    }
+    cp_async_commit();
+    if (t < TN) sAlpha[t] = n0 + t < p.N ? p.alpha[n0 + t] : 0.0f;
+    cp_async_wait_all();
+    asm volatile("bar.sync 1, 128;" ::: "memory");  // every packed row of the CTA has landed
+    for (int q = t; q < TN * nkb; q += 128) {
+      const int r = q % TN, kb = q / TN;
+      const uint4* src = reinterpret_cast<const uint4*>(sRaw + r * rowb + kb * 32);
+      const uint4 w0 = src[0], w1 = src[1];
+      const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+      uint8_t* row = sB + kb * TN * kTdKB + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint32_t wd = words[c];
+        uint4 v;
+        v.x = decode4(wd & 0xFFu);
+        v.y = decode4((wd >> 8) & 0xFFu);
+        v.z = decode4((wd >> 16) & 0xFFu);
+        v.w = decode4(wd >> 24);
+        *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) << 4)) = v;
+      }
+    }
+    fence_proxy_async_smem();  // the generic-proxy writes are visible to the tensor core
+    mbar_arrive(b_full);
+    if (p.weights_early) griddep_wait();  // the token scales and accumulated outputs are earlier kernels'
+    // epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 = tokens m0 + 32 (w % 4) + lane, and
+    // writes each 32 x 32 block through its own shared-memory transpose (coalesced rows)
+    const int quad = warp & 3;
+    const int mrow0 = m0 + quad * 32;
+    const int m = mrow0 + lane;
+    const double sx = m < p.M ? static_cast<double>(p.xscale[m]) : 0.0;
+    constexpr int NC = TN / 32;
+    float old[NC][32];
+    if (p.accumulate) {
+      // the accumulated outputs, lane = column, requested while the MMAs run
+#pragma unroll
+      for (int c = 0; c < NC; ++c) {
+        const int nn = n0 + c * 32 + lane;
+#pragma unroll
+        for (int rr = 0; rr < 32; ++rr) {
+          const int mm = mrow0 + rr;
+          old[c][rr] = (mm < p.M && nn < p.N) ? p.y[static_cast<size_t>(mm) * p.N + nn] : 0.0f;
+        }
+      }
+    }
+    bool ok = __all_sync(0xffffffffu, mbar_wait(acc_full, 0, abort_flag, p.status, kDevTimeoutEpilogue));
+    float* s_tile = reinterpret_cast<float*>(sA) + (warp - 2) * 32 * 33;  // per warp [32][33]
+    if (ok) {
+      tc_fence_after();
+      const uint32_t taddr = tbase + (static_cast<uint32_t>(quad * 32) << 16);
+#pragma unroll
+      for (int c = 0; c < NC; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(taddr + c * 32, r);
+        const float a_lane = sAlpha[c * 32 + lane];
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float aj = __shfl_sync(0xffffffffu, a_lane, j);
+          const double v = __dmul_rn(__dmul_rn(static_cast<double>(static_cast<int>(r[j])),
+                                               static_cast<double>(aj)), sx);
+          s_tile[lane * 33 + j] = __double2float_rn(v);
+        }
+        __syncwarp();
+        const int nn = n0 + c * 32 + lane;
+#pragma unroll
+        for (int rr = 0; rr < 32; ++rr) {
+          const int mm = mrow0 + rr;
+          if (mm < p.M && nn < p.N) {
+            const float v = s_tile[rr * 33 + lane];
+            p.y[static_cast<size_t>(mm) * p.N + nn] = p.accumulate ? __fadd_rn(old[c][rr], v) : v;
+          }
+        }
+        __syncwarp();
+      }
+    }
+  }
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (*abort_flag) drain_sleep(200000);
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, kCols);
+  }
+}
+
 }  // namespace
 
 int ternary_pack(const float* w, int N, int K, uint32_t* packed, float* alpha, cudaStream_t s) {
@@ -517,7 +707,8 @@ int quantize_act_i8(const float* x, int M, int K, int8_t* xq, float* xscale, cud
 }
 
 int ternary_gemm_i8(const uint32_t* wp, const float* alpha, const int8_t* xq, const float* xscale,
-                    float* y, int M, int N, int K, cudaStream_t s, bool accumulate) {
+                    float* y, int M, int N, int K, cudaStream_t s, bool accumulate,
+                    bool weights_resident) {
   DLM_REQUIRE(wp && alpha && xq && xscale && y, DLM_ERR_INVALID, "ternary_gemm_i8: null pointer");
   DLM_REQUIRE(K % 64 == 0 && K < (1 << 24), DLM_ERR_INVALID,
               "ternary_gemm_i8: K=%d must be a multiple of 64", K);
@@ -544,6 +735,39 @@ int ternary_gemm_i8(const uint32_t* wp, const float* alpha, const int8_t* xq, co
     dim3 grid((N + kTcN - 1) / kTcN, (M + kTcM - 1) / kTcM);
     DLM_CHECK_CUDA(launch_pdl(ternary_gemm_tc_kernel, dim3(grid), dim3(kTcThreads), kTcSmem, s, tm,
         tp));
+    DLM_CHECK_CUDA(cudaGetLastError());
+    return DLM_OK;
+  }
+  if (tcd_enabled() && K % kTdKB == 0 && K <= kTdMaxKB * kTdKB && N % 32 == 0) {
+    // decode-sized: the tensor-core path with narrow tiles and every k-block resident (same
+    // integer sums, same epilogue arithmetic); 64-output tiles only where 32-output ones would
+    // need more than two CTAs per SM
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+      DLM_CHECK_CUDA(cudaFuncSetAttribute(ternary_gemm_tcd_kernel<32>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, td_smem_bytes(32)));
+      DLM_CHECK_CUDA(cudaFuncSetAttribute(ternary_gemm_tcd_kernel<64>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, td_smem_bytes(64)));
+      attr_set[dev] = true;
+    }
+    CUtensorMap tm;
+    const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(K)};
+    const uint32_t box[2] = {kTdKB, kTcM};
+    if (!encode_tmap(&tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, xq, dims, strides, box,
+                     CU_TENSOR_MAP_SWIZZLE_128B))
+      return DLM_ERR_CUDA;
+    TernaryTcParams tp{wp, alpha, xscale, y, M, N, K, accumulate ? 1 : 0, device_status_ptr(),
+                       weights_resident ? 1 : 0};
+    const int mt = (M + kTcM - 1) / kTcM;
+    if (N % 64 != 0 || static_cast<long>(N / 32) * mt <= 2L * num_sms())
+      DLM_CHECK_CUDA(launch_pdl(ternary_gemm_tcd_kernel<32>, dim3(N / 32, mt), dim3(kTdThreads),
+          td_smem_bytes(32), s, tm, tp));
+    else
+      DLM_CHECK_CUDA(launch_pdl(ternary_gemm_tcd_kernel<64>, dim3(N / 64, mt), dim3(kTdThreads),
+          td_smem_bytes(64), s, tm, tp));
     DLM_CHECK_CUDA(cudaGetLastError());
     return DLM_OK;
   }

@@ -15,9 +15,11 @@ int ternary_pack_per_tensor(const float* w, int N, int K, uint32_t* packed, floa
 // Per-token absmax int8 quantization of x [M, K].
 int quantize_act_i8(const float* x, int M, int K, int8_t* xq, float* xscale, cudaStream_t s);
 // y [M, N] = float(double(int32 sum) * alpha[n] * xscale[m]); with `accumulate`, y += that
-// value (one float add) instead.
+// value (one float add) instead.  `weights_resident`: no kernel still queued or running in the
+// stream writes wp / alpha, so a decode-sized call may read them before the previous kernel ends.
 int ternary_gemm_i8(const uint32_t* wp, const float* alpha, const int8_t* xq, const float* xscale,
-                    float* y, int M, int N, int K, cudaStream_t s, bool accumulate = false);
+                    float* y, int M, int N, int K, cudaStream_t s, bool accumulate = false,
+                    bool weights_resident = false);
 
 // Token rows from which ternary_gemm_i8 uses the tensor cores.
 int ternary_tc_min_rows();

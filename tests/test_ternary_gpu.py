@@ -74,10 +74,14 @@ def test_quant_act_bit_exact(M, K):
     assert np.array_equal(xq.cpu().numpy().reshape(M, K), q_ref)
 
 
-# M >= 1024 runs the tcgen05 kind::i8 tensor-core path (prefill), smaller M the dp4a path (decode)
+# M >= 1024 runs the tcgen05 kind::i8 tensor-core path (prefill); smaller M runs the decode
+# tensor-core path (32-output tiles, 64-output ones when 32 would need more than two CTAs per SM)
+# where K is a multiple of 128 up to 512 and N a multiple of 32, else dp4a
 @pytest.mark.parametrize("M,N,K", [(256, 512, 512), (256, 1536, 512), (256, 512, 1536),
                                    (2048, 512, 512), (37, 70, 192), (1, 64, 64),
-                                   (1040, 3072, 512), (1024, 512, 1536), (1152, 96, 256)])
+                                   (1040, 3072, 512), (1024, 512, 1536), (1152, 96, 256),
+                                   (256, 3072, 512), (512, 3072, 512), (100, 96, 256),
+                                   (1, 32, 128), (300, 640, 384)])
 def test_bitlinear_bit_exact(M, N, K):
     rng = np.random.default_rng(M + 7 * N + K)
     w = (rng.standard_normal((N, K)) * 0.05).astype(np.float32)
