@@ -897,7 +897,7 @@ int BitNetLM::run_layers(int S, const int* pos, cudaStream_t s) {
     if (S == 1 && pos != nullptr && M < ternary_tc_min_rows()) {
       // decode: RoPE and the K / V append in the q|k|v projection's epilogue
       const RopeQkv rq{pos, cos_t_, sin_t_, q_, kc, vc, D, L_};
-      rc = ternary_gemm_qkv_rope(Ly.wqkv, Ly.aqkv, xq_, xs_, M, D, rq, s);
+      rc = ternary_gemm_qkv_rope(Ly.wqkv, Ly.aqkv, xq_, xs_, M, D, rq, s, true);
       if (rc != DLM_OK) break;
     } else {
       rc = ternary_gemm_i8(Ly.wqkv, Ly.aqkv, xq_, xs_, y_, M, 3 * D, D, s, false, true);

@@ -496,49 +496,59 @@ __global__ void __launch_bounds__(kTcThreads, 3)
 }
 
 // ---------------------------------------------------------------- tensor-core path (decode)
-// The same exact BitLinear for decode-sized inputs (fewer than tc_min_rows tokens, K <= 512): one
+// The same exact BitLinear for decode-sized inputs (fewer than tc_min_rows tokens, K <= 2048): one
 // CTA = 128 tokens x TN outputs (TN = 32 or 64, so a decode projection spreads over 32-192 CTAs
-// where 128-output tiles gave 8-48) with every k-block resident at once, so no step of the
-// pipeline waits for a buffer to come free.  The 128 expanding threads fetch the CTA's packed
-// weights and row scales, expand them into the 128-byte-swizzled K-major int8 layout and arrive
-// on b_full — before waiting for the previous kernel when the caller states that no kernel still
-// in the stream writes the weights (the LM's, packed when the model is created); after it, warp 0 TMA-loads every activation block at once, warp 1
-// issues the K / 32 MMAs (M = 128, N = TN) into a TN-column TMEM accumulator, and the epilogue
-// warps fetch the token scales and, for h +=, the accumulated outputs while the MMAs run.  The
-// epilogue's operations are the prefill kernel's: y = float(double(acc) * alpha[n] * xscale[m]).
-constexpr int kTdKB = 128;   // k-block: 128 int8 = one 128-byte swizzled row
-constexpr int kTdMaxKB = 4;  // K <= 512
+// where 128-output tiles gave 8-48) with the CTA's whole expanded weight slice resident, so the
+// only ring is the activations' (four 16 KB blocks: K <= 512 is resident at once).  The 128
+// expanding threads fetch the CTA's packed weights and row scales, expand them into the
+// 128-byte-swizzled K-major int8 layout and arrive on b_full — before waiting for the previous
+// kernel when the caller states that no kernel still in the stream writes the weights (the LM's,
+// packed when the model is created); warp 0 TMA-loads the activation blocks, warp 1 issues the
+// K / 32 MMAs (M = 128, N = TN) into a TN-column TMEM accumulator, and the epilogue warps fetch
+// the token scales and, for h +=, the accumulated outputs while the MMAs run.  The epilogue's
+// operations are the prefill kernel's: y = float(double(acc) * alpha[n] * xscale[m]).  kRope (TN
+// = 64: one head of q, k or v per tile): the q|k|v projection of one position per sequence, each
+// thread rotating its token's RoPE pairs (c, c + 32) in double from the float outputs and
+// writing q or the K / V cache row, as ternary_gemm_kernel<64, true> does.
+constexpr int kTdKB = 128;     // k-block: 128 int8 = one 128-byte swizzled row
+constexpr int kTdStages = 4;   // activation ring
+constexpr int kTdMaxK = 2048;
 constexpr int kTdThreads = 192;
 constexpr int kTdStageA = kTcM * kTdKB;  // 16 KB
-__host__ __device__ constexpr int td_smem_bytes(int TN) {
-  return kTdMaxKB * kTdStageA + kTdMaxKB * TN * kTdKB + TN * (kTdMaxKB * kTdKB / 4) + TN * 4 +
-         256 + 1024;
+__host__ __device__ constexpr int td_smem_bytes(int TN, int K) {
+  return kTdStages * kTdStageA + TN * K + TN * (K / 4) + TN * 4 + 256 + 1024;
 }
 
-template <int TN>
+template <int TN, bool kRope>
 __global__ void __launch_bounds__(kTdThreads, 2)
-    ternary_gemm_tcd_kernel(const __grid_constant__ CUtensorMap tmX, const TernaryTcParams p) {
+    ternary_gemm_tcd_kernel(const __grid_constant__ CUtensorMap tmX, const TernaryTcParams p,
+                            const RopeQkv rp) {
   static_assert(TN == 32 || TN == 64, "decode tile width");
+  static_assert(!kRope || TN == 64, "a RoPE tile is one head");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint8_t* sA = smem;                                  // [kTdMaxKB][128 x 128] int8, swizzled
-  uint8_t* sB = sA + kTdMaxKB * kTdStageA;             // [kTdMaxKB][TN x 128] int8, swizzled
-  uint8_t* sRaw = sB + kTdMaxKB * TN * kTdKB;          // [TN][K / 4] packed codes
-  float* sAlpha = reinterpret_cast<float*>(sRaw + TN * (kTdMaxKB * kTdKB / 4));  // [TN]
+  const int nkb = p.K / kTdKB;
+  uint8_t* sA = smem;                                    // [kTdStages][128 x 128] int8, swizzled
+  uint8_t* sB = sA + kTdStages * kTdStageA;              // [K / 128][TN x 128] int8, swizzled
+  uint8_t* sRaw = sB + static_cast<size_t>(TN) * p.K;    // [TN][K / 4] packed codes
+  float* sAlpha = reinterpret_cast<float*>(sRaw + TN * (p.K / 4));  // [TN]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sAlpha + TN);
-  uint64_t* a_full = bars;        // TMA bytes of every activation block
-  uint64_t* b_full = bars + 1;    // the 128 expanding threads
-  uint64_t* acc_full = bars + 2;  // the last MMA completed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3);
+  uint64_t* a_full = bars;                  // [kTdStages] TMA bytes
+  uint64_t* empty = bars + kTdStages;       // [kTdStages] the block's MMAs completed
+  uint64_t* b_full = bars + 2 * kTdStages;  // the 128 expanding threads
+  uint64_t* acc_full = b_full + 1;          // the last MMA completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   constexpr uint32_t kCols = TN;  // a power of two >= 32
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * TN, m0 = blockIdx.y * kTcM;
-  const int nkb = p.K / kTdKB;
   if (threadIdx.x == 0) {
-    mbar_init(a_full, 1);
+    for (int st = 0; st < kTdStages; ++st) {
+      mbar_init(&a_full[st], 1);
+      mbar_init(&empty[st], 1);
+    }
     mbar_init(b_full, 128);
     mbar_init(acc_full, 1);
     *abort_flag = 0;
@@ -557,28 +567,36 @@ __global__ void __launch_bounds__(kTdThreads, 2)
     if (lane == 0) {
       tma_prefetch_desc(&tmX);
       griddep_wait();  // the activations come from the previous kernel
-      mbar_arrive_expect_tx(a_full, nkb * kTdStageA);
-      for (int kb = 0; kb < nkb; ++kb) tma_load_2d(sA + kb * kTdStageA, &tmX, a_full, kb * kTdKB, m0);
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int st = kb % kTdStages;
+        if (kb >= kTdStages &&
+            !mbar_wait(&empty[st], ((kb / kTdStages) - 1) & 1, abort_flag, p.status, kDevTimeoutProducer))
+          break;
+        mbar_arrive_expect_tx(&a_full[st], kTdStageA);
+        tma_load_2d(sA + st * kTdStageA, &tmX, &a_full[st], kb * kTdKB, m0);
+      }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_s8_s32(kTcM, TN);
-      const bool ok = mbar_wait(b_full, 0, abort_flag, p.status, kDevTimeoutMma) &&
-                      mbar_wait(a_full, 0, abort_flag, p.status, kDevTimeoutMma);
-      if (ok) {
+      bool ok = mbar_wait(b_full, 0, abort_flag, p.status, kDevTimeoutMma);
+      for (int kb = 0; kb < nkb && ok; ++kb) {
+        const int st = kb % kTdStages;
+        ok = mbar_wait(&a_full[st], (kb / kTdStages) & 1, abort_flag, p.status, kDevTimeoutMma);
+        if (!ok) break;
         tc_fence_after();
-        for (int kb = 0; kb < nkb; ++kb) {
-          const uint32_t a_addr = smem_u32(sA + kb * kTdStageA), b_addr = smem_u32(sB + kb * TN * kTdKB);
+        const uint32_t a_addr = smem_u32(sA + st * kTdStageA);
+        const uint32_t b_addr = smem_u32(sB + static_cast<size_t>(kb) * TN * kTdKB);
 #pragma unroll
-          for (int k = 0; k < kTdKB / 32; ++k)
-            umma_i8_ss(tbase, sw128_desc(a_addr + k * 32, 16, 1024), sw128_desc(b_addr + k * 32, 16, 1024),
-                       idesc, (kb != 0 || k != 0) ? 1u : 0u);
-        }
-        umma_commit(acc_full);
+        for (int k = 0; k < kTdKB / 32; ++k)
+          umma_i8_ss(tbase, sw128_desc(a_addr + k * 32, 16, 1024), sw128_desc(b_addr + k * 32, 16, 1024),
+                     idesc, (kb != 0 || k != 0) ? 1u : 0u);
+        umma_commit(&empty[st]);
       }
+      if (ok) umma_commit(acc_full);
     }
   } else {
-    // warps 2..5: the weights (before the previous kernel has finished), then the epilogue
+    // warps 2..5: the weights, then the epilogue
     const int t = threadIdx.x - 64;  // 0..127
     const int rowb = p.K / 4;        // packed bytes per output row
     if (!p.weights_early) griddep_wait();
@@ -598,7 +616,7 @@ __global__ void __launch_bounds__(kTdThreads, 2)
       const uint4* src = reinterpret_cast<const uint4*>(sRaw + r * rowb + kb * 32);
       const uint4 w0 = src[0], w1 = src[1];
       const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-      uint8_t* row = sB + kb * TN * kTdKB + (r >> 3) * 1024 + (r & 7) * 128;
+      uint8_t* row = sB + static_cast<size_t>(kb) * TN * kTdKB + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         const uint32_t wd = words[c];
@@ -613,55 +631,94 @@ __global__ void __launch_bounds__(kTdThreads, 2)
     fence_proxy_async_smem();  // the generic-proxy writes are visible to the tensor core
     mbar_arrive(b_full);
     if (p.weights_early) griddep_wait();  // the token scales and accumulated outputs are earlier kernels'
-    // epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 = tokens m0 + 32 (w % 4) + lane, and
-    // writes each 32 x 32 block through its own shared-memory transpose (coalesced rows)
+    // epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 = tokens m0 + 32 (w % 4) + lane
     const int quad = warp & 3;
     const int mrow0 = m0 + quad * 32;
     const int m = mrow0 + lane;
     const double sx = m < p.M ? static_cast<double>(p.xscale[m]) : 0.0;
-    constexpr int NC = TN / 32;
-    float old[NC][32];
-    if (p.accumulate) {
-      // the accumulated outputs, lane = column, requested while the MMAs run
+    const uint32_t taddr = tbase + (static_cast<uint32_t>(quad * 32) << 16);
+    if constexpr (kRope) {
+      const int base = *rp.pos;
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(acc_full, 0, abort_flag, p.status, kDevTimeoutEpilogue));
+      if (ok) {
+        tc_fence_after();
+        uint32_t r0[32], r1[32];
+        tmem_ld_32x32b_x32(taddr, r0);
+        tmem_ld_32x32b_x32(taddr + 32, r1);
+        tmem_ld_wait();
+        if (m < p.M) {
+          float v[64];
 #pragma unroll
-      for (int c = 0; c < NC; ++c) {
-        const int nn = n0 + c * 32 + lane;
+          for (int j = 0; j < 32; ++j) {
+            v[j] = __double2float_rn(__dmul_rn(
+                __dmul_rn(static_cast<double>(static_cast<int>(r0[j])), static_cast<double>(sAlpha[j])), sx));
+            v[32 + j] = __double2float_rn(__dmul_rn(
+                __dmul_rn(static_cast<double>(static_cast<int>(r1[j])), static_cast<double>(sAlpha[32 + j])), sx));
+          }
+          const int part = n0 / rp.D, hd = (n0 % rp.D) / 64, H = rp.D / 64;
+          const size_t cache = ((static_cast<size_t>(m) * H + hd) * rp.Lmax + base) * 64;
+          float* dst = part == 0 ? rp.q + static_cast<size_t>(m) * rp.D + hd * 64
+                                 : (part == 1 ? rp.kc : rp.vc) + cache;
+          if (part != 2) {
+            // RoPE (bitnet.hpp:472-488) of the pairs (ih, ih + 32), in double from the floats
 #pragma unroll
-        for (int rr = 0; rr < 32; ++rr) {
-          const int mm = mrow0 + rr;
-          old[c][rr] = (mm < p.M && nn < p.N) ? p.y[static_cast<size_t>(mm) * p.N + nn] : 0.0f;
+            for (int ih = 0; ih < 32; ++ih) {
+              const double cs = rp.cos_t[base * 32 + ih], sn = rp.sin_t[base * 32 + ih];
+              const double a = static_cast<double>(v[ih]), bb = static_cast<double>(v[ih + 32]);
+              v[ih] = __double2float_rn(__dsub_rn(__dmul_rn(a, cs), __dmul_rn(bb, sn)));
+              v[ih + 32] = __double2float_rn(__dadd_rn(__dmul_rn(a, sn), __dmul_rn(bb, cs)));
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            reinterpret_cast<float4*>(dst)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
         }
       }
-    }
-    bool ok = __all_sync(0xffffffffu, mbar_wait(acc_full, 0, abort_flag, p.status, kDevTimeoutEpilogue));
-    float* s_tile = reinterpret_cast<float*>(sA) + (warp - 2) * 32 * 33;  // per warp [32][33]
-    if (ok) {
-      tc_fence_after();
-      const uint32_t taddr = tbase + (static_cast<uint32_t>(quad * 32) << 16);
+    } else {
+      // each 32 x 32 block leaves through the warp's own shared-memory transpose (coalesced rows)
+      constexpr int NC = TN / 32;
+      float old[NC][32];
+      if (p.accumulate) {
+        // the accumulated outputs, lane = column, requested while the MMAs run
 #pragma unroll
-      for (int c = 0; c < NC; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(taddr + c * 32, r);
-        const float a_lane = sAlpha[c * 32 + lane];
-        tmem_ld_wait();
+        for (int c = 0; c < NC; ++c) {
+          const int nn = n0 + c * 32 + lane;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float aj = __shfl_sync(0xffffffffu, a_lane, j);
-          const double v = __dmul_rn(__dmul_rn(static_cast<double>(static_cast<int>(r[j])),
-                                               static_cast<double>(aj)), sx);
-          s_tile[lane * 33 + j] = __double2float_rn(v);
-        }
-        __syncwarp();
-        const int nn = n0 + c * 32 + lane;
-#pragma unroll
-        for (int rr = 0; rr < 32; ++rr) {
-          const int mm = mrow0 + rr;
-          if (mm < p.M && nn < p.N) {
-            const float v = s_tile[rr * 33 + lane];
-            p.y[static_cast<size_t>(mm) * p.N + nn] = p.accumulate ? __fadd_rn(old[c][rr], v) : v;
+          for (int rr = 0; rr < 32; ++rr) {
+            const int mm = mrow0 + rr;
+            old[c][rr] = (mm < p.M && nn < p.N) ? p.y[static_cast<size_t>(mm) * p.N + nn] : 0.0f;
           }
         }
-        __syncwarp();
+      }
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(acc_full, 0, abort_flag, p.status, kDevTimeoutEpilogue));
+      float* s_tile = reinterpret_cast<float*>(sA) + (warp - 2) * 32 * 33;  // per warp [32][33]
+      if (ok) {
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(taddr + c * 32, r);
+          const float a_lane = sAlpha[c * 32 + lane];
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float aj = __shfl_sync(0xffffffffu, a_lane, j);
+            const double v = __dmul_rn(__dmul_rn(static_cast<double>(static_cast<int>(r[j])),
+                                                 static_cast<double>(aj)), sx);
+            s_tile[lane * 33 + j] = __double2float_rn(v);
+          }
+          __syncwarp();
+          const int nn = n0 + c * 32 + lane;
+#pragma unroll
+          for (int rr = 0; rr < 32; ++rr) {
+            const int mm = mrow0 + rr;
+            if (mm < p.M && nn < p.N) {
+              const float v = s_tile[rr * 33 + lane];
+              p.y[static_cast<size_t>(mm) * p.N + nn] = p.accumulate ? __fadd_rn(old[c][rr], v) : v;
+            }
+          }
+          __syncwarp();
+        }
       }
     }
   }
@@ -673,6 +730,32 @@ __global__ void __launch_bounds__(kTdThreads, 2)
     tc_fence_after();
     tmem_dealloc(tbase, kCols);
   }
+}
+
+// Launches the decode kernel on xq [M][K] (int8): the tensor map, the shared-memory limits once
+// per device, and the grid (N / TN, M / 128).
+template <int TN, bool kRope>
+int launch_tcd(const TernaryTcParams& tp, const int8_t* xq, const RopeQkv& rp, cudaStream_t s) {
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    DLM_CHECK_CUDA(cudaFuncSetAttribute(ternary_gemm_tcd_kernel<TN, kRope>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        td_smem_bytes(TN, kTdMaxK)));
+    attr_set[dev] = true;
+  }
+  CUtensorMap tm;
+  const uint64_t dims[2] = {static_cast<uint64_t>(tp.K), static_cast<uint64_t>(tp.M)};
+  const uint64_t strides[1] = {static_cast<uint64_t>(tp.K)};
+  const uint32_t box[2] = {kTdKB, kTcM};
+  if (!encode_tmap(&tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, xq, dims, strides, box,
+                   CU_TENSOR_MAP_SWIZZLE_128B))
+    return DLM_ERR_CUDA;
+  DLM_CHECK_CUDA(launch_pdl(ternary_gemm_tcd_kernel<TN, kRope>, dim3(tp.N / TN, (tp.M + kTcM - 1) / kTcM),
+      dim3(kTdThreads), td_smem_bytes(TN, tp.K), s, tm, tp, rp));
+  DLM_CHECK_CUDA(cudaGetLastError());
+  return DLM_OK;
 }
 
 }  // namespace
@@ -738,38 +821,15 @@ int ternary_gemm_i8(const uint32_t* wp, const float* alpha, const int8_t* xq, co
     DLM_CHECK_CUDA(cudaGetLastError());
     return DLM_OK;
   }
-  if (tcd_enabled() && K % kTdKB == 0 && K <= kTdMaxKB * kTdKB && N % 32 == 0) {
-    // decode-sized: the tensor-core path with narrow tiles and every k-block resident (same
-    // integer sums, same epilogue arithmetic); 64-output tiles only where 32-output ones would
-    // need more than two CTAs per SM
-    static bool attr_set[64] = {false};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-      DLM_CHECK_CUDA(cudaFuncSetAttribute(ternary_gemm_tcd_kernel<32>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, td_smem_bytes(32)));
-      DLM_CHECK_CUDA(cudaFuncSetAttribute(ternary_gemm_tcd_kernel<64>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, td_smem_bytes(64)));
-      attr_set[dev] = true;
-    }
-    CUtensorMap tm;
-    const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
-    const uint64_t strides[1] = {static_cast<uint64_t>(K)};
-    const uint32_t box[2] = {kTdKB, kTcM};
-    if (!encode_tmap(&tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, xq, dims, strides, box,
-                     CU_TENSOR_MAP_SWIZZLE_128B))
-      return DLM_ERR_CUDA;
-    TernaryTcParams tp{wp, alpha, xscale, y, M, N, K, accumulate ? 1 : 0, device_status_ptr(),
-                       weights_resident ? 1 : 0};
-    const int mt = (M + kTcM - 1) / kTcM;
+  if (tcd_enabled() && K % kTdKB == 0 && K <= kTdMaxK && N % 32 == 0) {
+    // decode-sized: the tensor-core path with narrow tiles (same integer sums, same epilogue
+    // arithmetic); 64-output tiles only where 32-output ones would need more than two CTAs per SM
+    const TernaryTcParams tp{wp, alpha, xscale, y, M, N, K, accumulate ? 1 : 0, device_status_ptr(),
+                             weights_resident ? 1 : 0};
+    const long mt = (M + kTcM - 1) / kTcM;
     if (N % 64 != 0 || static_cast<long>(N / 32) * mt <= 2L * num_sms())
-      DLM_CHECK_CUDA(launch_pdl(ternary_gemm_tcd_kernel<32>, dim3(N / 32, mt), dim3(kTdThreads),
-          td_smem_bytes(32), s, tm, tp));
-    else
-      DLM_CHECK_CUDA(launch_pdl(ternary_gemm_tcd_kernel<64>, dim3(N / 64, mt), dim3(kTdThreads),
-          td_smem_bytes(64), s, tm, tp));
-    DLM_CHECK_CUDA(cudaGetLastError());
-    return DLM_OK;
+      return launch_tcd<32, false>(tp, xq, RopeQkv{}, s);
+    return launch_tcd<64, false>(tp, xq, RopeQkv{}, s);
   }
   // 64-output tiles unless they leave more than half of the SMs idle (decode-sized projections)
   const long tiles64 = static_cast<long>((N + kTN - 1) / kTN) * ((M + kTM - 1) / kTM);
@@ -789,7 +849,8 @@ int ternary_gemm_i8(const uint32_t* wp, const float* alpha, const int8_t* xq, co
 int ternary_tc_min_rows() { return tc_min_rows(); }
 
 int ternary_gemm_qkv_rope(const uint32_t* wp, const float* alpha, const int8_t* xq,
-                          const float* xscale, int M, int K, const RopeQkv& r, cudaStream_t s) {
+                          const float* xscale, int M, int K, const RopeQkv& r, cudaStream_t s,
+                          bool weights_resident) {
   DLM_REQUIRE(wp && alpha && xq && xscale && r.pos && r.cos_t && r.sin_t && r.q && r.kc && r.vc,
               DLM_ERR_INVALID, "ternary_gemm_qkv_rope: null pointer");
   DLM_REQUIRE(K % 64 == 0 && r.D % kTN == 0 && r.Lmax > 0, DLM_ERR_INVALID,
@@ -797,6 +858,12 @@ int ternary_gemm_qkv_rope(const uint32_t* wp, const float* alpha, const int8_t* 
   DLM_REQUIRE((reinterpret_cast<uintptr_t>(wp) & 15) == 0 && (reinterpret_cast<uintptr_t>(xq) & 15) == 0,
               DLM_ERR_INVALID, "ternary_gemm_qkv_rope: packed weights / activations must be 16-byte aligned");
   const int N = 3 * r.D;
+  if (tcd_enabled() && K % kTdKB == 0 && K <= kTdMaxK) {
+    // the decode tensor-core path, one head per 64-output tile
+    const TernaryTcParams tp{wp, alpha, xscale, nullptr, M, N, K, 0, device_status_ptr(),
+                             weights_resident ? 1 : 0};
+    return launch_tcd<64, true>(tp, xq, r, s);
+  }
   dim3 grid(N / kTN, (M + kTM - 1) / kTM);
   DLM_CHECK_CUDA(launch_pdl(ternary_gemm_kernel<kTN, true>, dim3(grid), dim3(kThreads), 0, s, wp,
       alpha, xq, xscale, static_cast<float*>(nullptr), M, N, K, 0, r));

@@ -39,6 +39,7 @@ struct RopeQkv {
   int D, Lmax;
 };
 int ternary_gemm_qkv_rope(const uint32_t* wp, const float* alpha, const int8_t* xq,
-                          const float* xscale, int M, int K, const RopeQkv& r, cudaStream_t s);
+                          const float* xscale, int M, int K, const RopeQkv& r, cudaStream_t s,
+                          bool weights_resident = false);
 
 }  // namespace dlm

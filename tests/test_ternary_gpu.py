@@ -75,13 +75,15 @@ def test_quant_act_bit_exact(M, K):
 
 
 # M >= 1024 runs the tcgen05 kind::i8 tensor-core path (prefill); smaller M runs the decode
-# tensor-core path (32-output tiles, 64-output ones when 32 would need more than two CTAs per SM)
-# where K is a multiple of 128 up to 512 and N a multiple of 32, else dp4a
+# tensor-core path (32-output tiles, 64-output ones when 32 would need more than two CTAs per SM;
+# a four-block activation ring beyond K = 512) where K is a multiple of 128 up to 2048 and N a
+# multiple of 32, else dp4a
 @pytest.mark.parametrize("M,N,K", [(256, 512, 512), (256, 1536, 512), (256, 512, 1536),
                                    (2048, 512, 512), (37, 70, 192), (1, 64, 64),
                                    (1040, 3072, 512), (1024, 512, 1536), (1152, 96, 256),
                                    (256, 3072, 512), (512, 3072, 512), (100, 96, 256),
-                                   (1, 32, 128), (300, 640, 384)])
+                                   (1, 32, 128), (300, 640, 384), (200, 96, 1024),
+                                   (256, 64, 2048)])
 def test_bitlinear_bit_exact(M, N, K):
     rng = np.random.default_rng(M + 7 * N + K)
     w = (rng.standard_normal((N, K)) * 0.05).astype(np.float32)
