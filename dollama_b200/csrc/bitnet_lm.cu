@@ -116,41 +116,61 @@ __global__ void embed_kernel(const int* __restrict__ tokens, int ld_tok, int S,
   for (int i = threadIdx.x; i < D / 4; i += blockDim.x) dst[i] = src[i];
 }
 
-// rms_norm (bitnet.hpp:234-250), one warp per output row: every lane forms the double squares of
-// its elements, lane 0 adds them in index order (as the reference's loop), then x * inv * w per
-// element, rounded to float.  Output row r reads input row r * in_stride + in_off.  Optionally
+// rms_norm (bitnet.hpp:234-250), one warp per output row: lane 0 adds the double squares of the
+// row's elements in index order (as the reference's loop) — as fma(x, x, s), equal to
+// s + x * x because the square of a float is exact in double — reading the row from shared
+// memory 16 bytes at a time, eight elements ahead of the adds; then x * inv * w per element,
+// rounded to float.  Output row r reads input row r * in_stride + in_off.  Optionally
 // quantizes the normalised row (int8) and / or stores it transposed in double (out_t[d * ldt + r],
 // the lm_head's operand layout; each thread writes the block's four rows of one element).
 constexpr int kNormWarps = 4;
-// per block: the rows as float, then their squares as double
+// per block: the rows as float
 __host__ __device__ constexpr size_t norm_smem_bytes(int D) {
-  return static_cast<size_t>(kNormWarps) * D * (4 + 8);
+  return static_cast<size_t>(kNormWarps) * D * 4;
 }
 __global__ void __launch_bounds__(kNormWarps * 32)
     rms_norm_kernel(const float* __restrict__ h, int rows, int D, int in_stride, int in_off,
                     const float* __restrict__ w, double eps, int8_t* __restrict__ xq,
                     float* __restrict__ xs, double* __restrict__ out_t, int ldt) {
   griddep_wait();  // inputs come from the previous kernel (programmatic dependent launch)
-  extern __shared__ float srow[];  // [kNormWarps][D] float, then [kNormWarps][D] double
+  extern __shared__ __align__(16) float srow[];  // [kNormWarps][D]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r0 = blockIdx.x * kNormWarps;
   const int r = r0 + warp;
   if (r >= rows && !out_t) return;  // (with out_t every warp reaches the block barrier below)
   float* row = srow + static_cast<size_t>(warp) * D;
   if (r < rows) {
-    // 16 * D bytes from the base: 8-byte aligned
-    double* sqr = reinterpret_cast<double*>(srow + static_cast<size_t>(kNormWarps) * D) +
-                  static_cast<size_t>(warp) * D;
     const float* src = h + (static_cast<size_t>(r) * in_stride + in_off) * D;
-    for (int i = lane; i < D; i += 32) {
-      const float v = src[i];
-      row[i] = v;
-      sqr[i] = __dmul_rn(static_cast<double>(v), static_cast<double>(v));
-    }
+    for (int i = lane; i < D; i += 32) row[i] = src[i];
     __syncwarp();
     double inv = 0.0;
     if (lane == 0) {
-      double ms = seq_sum(sqr, D);
+      double ms = 0.0;
+      int i = 0;
+      if ((D & 7) == 0) {
+        // rows of D floats start 16-byte aligned (D % 8 == 0, D * 4 bytes per row)
+        const float4* p4 = reinterpret_cast<const float4*>(row);
+        float4 a0 = p4[0], a1 = p4[1];
+        for (; i < D; i += 8) {
+          float4 b0 = a0, b1 = a1;
+          if (i + 8 < D) {
+            b0 = p4[(i >> 2) + 2];
+            b1 = p4[(i >> 2) + 3];
+          }
+          const float e[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const double x = static_cast<double>(e[k]);
+            ms = __fma_rn(x, x, ms);
+          }
+          a0 = b0;
+          a1 = b1;
+        }
+      }
+      for (; i < D; ++i) {
+        const double x = static_cast<double>(row[i]);
+        ms = __fma_rn(x, x, ms);
+      }
       ms = __ddiv_rn(ms, static_cast<double>(D));
       inv = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(ms, eps)));
     }
