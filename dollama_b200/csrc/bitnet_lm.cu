@@ -429,7 +429,8 @@ __global__ void __launch_bounds__(kAttnSeqWarps * 32)
 // one block per row: every thread computes its elements and their absolute maximum, the block
 // combines the maxima, and every thread quantizes its own elements (a maximum and per-element
 // operations, so the same bits in any split).
-constexpr int kSwiThreads = 256;
+constexpr int kSwiThreads = 512;  // three of F = 1536 elements per thread: fewer dependent
+                                  // double exp / divide chains in a row than with 256
 __global__ void __launch_bounds__(kSwiThreads)
     swiglu_quant_kernel(const float* __restrict__ gu, int M, int F, int8_t* __restrict__ xq,
                         float* __restrict__ xs) {
@@ -467,8 +468,8 @@ __global__ void __launch_bounds__(kSwiThreads)
 // straight into the tiles the loop reads, double-buffered (converting fp32 chunks in every block
 // instead repeated each x element's conversion for all 250 vocabulary tiles).  Tile: 64 rows x 64
 // vocab ids; each thread owns 4 rows (two adjacent pairs, each read by one 16-byte load that the
-// warp's 16 threads of a row pair share) x 4 ids: six shared-memory wavefronts per 16 fma per
-// warp, which leaves the fp64 pipe the bound.  ldx and ldv are multiples of 64, so every copy is
+// warp's 16 threads of a row pair share) x 4 ids (the L1 data pipe bounds it: 84 % of its
+// wavefronts against 54 % of the fp64 pipe, measured on one launch).  ldx and ldv are multiples of 64, so every copy is
 // in bounds (rows r >= R are computed and not stored).
 constexpr int kLmR = 64, kLmV = 64, kLmK = 16;
 __global__ void __launch_bounds__(256)
