@@ -267,6 +267,9 @@ int dlm_launch_layer_norm(const void* in, const void* gamma, const void* beta, v
  * xq = clamp(round(x/scale), -127, 127) per token (quantize_activation_int8, bitnet.hpp:123-165).
  * Packed weights: [N, K/16] uint32, 16 two-bit codes per word (00 = 0, 01 = +1, 11 = -1,
  * code j at bits 2j); K % 64 == 0; packed weights and activations 16-byte aligned.
+ * M >= 1024 runs on the tensor cores in 128 x 128 tiles; smaller M on the tensor cores in
+ * 128 x 32 (or 64) tiles when K % 128 == 0, K <= 2048 and N % 32 == 0; other shapes on dp4a.
+ * Every path gives the same bits.
  */
 int dlm_ternary_pack(const float* w, int N, int K, void* w_packed2b, float* row_scale, void* stream);
 int dlm_quantize_act_i8(const float* x, int M, int K, int8_t* xq, float* x_scale, void* stream);
