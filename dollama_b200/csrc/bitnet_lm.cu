@@ -84,6 +84,19 @@ __device__ __forceinline__ int8_t quant_one(float x, double scale, double inv) {
   return static_cast<int8_t>(v);
 }
 
+// Exact absmax int8 quantization of one row held in shared memory (quantize_activation_int8,
+// bitnet.hpp:123-165), by one warp.
+__device__ __forceinline__ void quant_row_warp(const float* row, int K, int8_t* q, float* scale_out) {
+  const int lane = threadIdx.x & 31;
+  double amax = 0.0;
+  for (int i = lane; i < K; i += 32) amax = fmax(amax, fabs(static_cast<double>(row[i])));
+  amax = warp_max_d(amax);
+  const double scale = __ddiv_rn(amax, 127.0);
+  const double inv = scale == 0.0 ? 0.0 : __ddiv_rn(1.0, scale);
+  if (lane == 0) *scale_out = static_cast<float>(scale);
+  for (int i = lane; i < K; i += 32) q[i] = quant_one(row[i], scale, inv);
+}
+
 // Row r of the output reads token tokens[b * ld_tok + base + p] (b = r / S, p = r % S, base =
 // *pos_in or 0) and copies its embedding row.  Ids outside [0, vocab) use id 0 and raise *bad.
 __global__ void embed_kernel(const int* __restrict__ tokens, int ld_tok, int S,
@@ -103,84 +116,79 @@ __global__ void embed_kernel(const int* __restrict__ tokens, int ld_tok, int S,
   for (int i = threadIdx.x; i < D / 4; i += blockDim.x) dst[i] = src[i];
 }
 
-// rms_norm (bitnet.hpp:234-250), one block of 128 threads per output row: thread 0 adds the
-// double squares of the row's elements in index order (as the reference's loop) — as
-// fma(x, x, s), equal to s + x * x because the square of a float is exact in double — reading the
-// row from shared memory 16 bytes at a time, eight elements ahead of the adds; then every thread
-// forms x * inv * w for its elements, rounded to float.  Output row r reads input row
-// r * in_stride + in_off.  Optionally quantizes the normalised row (int8: the block's absolute
-// maximum, then every thread's own elements) and / or stores it transposed in double
-// (out_t[d * ldt + r], the lm_head's operand layout).  With one warp per row, 256 rows reached
-// 64 SMs and each lane normalised and quantized 16 elements after the sum.
-constexpr int kNormThreads = 128;
-// per block: the row as float
-__host__ __device__ constexpr size_t norm_smem_bytes(int D) { return static_cast<size_t>(D) * 4; }
-__global__ void __launch_bounds__(kNormThreads)
+// rms_norm (bitnet.hpp:234-250), one warp per output row: lane 0 adds the double squares of the
+// row's elements in index order (as the reference's loop) — as fma(x, x, s), equal to
+// s + x * x because the square of a float is exact in double — reading the row from shared
+// memory 16 bytes at a time, eight elements ahead of the adds; then x * inv * w per element,
+// rounded to float.  Output row r reads input row r * in_stride + in_off.  Optionally
+// quantizes the normalised row (int8) and / or stores it transposed in double (out_t[d * ldt + r],
+// the lm_head's operand layout; each thread writes the block's four rows of one element).
+constexpr int kNormWarps = 4;
+// per block: the rows as float
+__host__ __device__ constexpr size_t norm_smem_bytes(int D) {
+  return static_cast<size_t>(kNormWarps) * D * 4;
+}
+__global__ void __launch_bounds__(kNormWarps * 32)
     rms_norm_kernel(const float* __restrict__ h, int rows, int D, int in_stride, int in_off,
                     const float* __restrict__ w, double eps, int8_t* __restrict__ xq,
                     float* __restrict__ xs, double* __restrict__ out_t, int ldt) {
   griddep_wait();  // inputs come from the previous kernel (programmatic dependent launch)
-  extern __shared__ __align__(16) float srow[];  // [D]
-  __shared__ double s_red[kNormThreads / 32 + 1];
-  const int r = blockIdx.x;
-  if (r >= rows) return;
-  const int tid = threadIdx.x;
-  const float* src = h + (static_cast<size_t>(r) * in_stride + in_off) * D;
-  for (int i = tid; i < D; i += kNormThreads) srow[i] = src[i];
-  __syncthreads();
-  if (tid == 0) {
-    double ms = 0.0;
-    int i = 0;
-    if ((D & 7) == 0) {
-      const float4* p4 = reinterpret_cast<const float4*>(srow);
-      float4 a0 = p4[0], a1 = p4[1];
-      for (; i < D; i += 8) {
-        float4 b0 = a0, b1 = a1;
-        if (i + 8 < D) {
-          b0 = p4[(i >> 2) + 2];
-          b1 = p4[(i >> 2) + 3];
-        }
-        const float e[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+  extern __shared__ __align__(16) float srow[];  // [kNormWarps][D]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r0 = blockIdx.x * kNormWarps;
+  const int r = r0 + warp;
+  if (r >= rows && !out_t) return;  // (with out_t every warp reaches the block barrier below)
+  float* row = srow + static_cast<size_t>(warp) * D;
+  if (r < rows) {
+    const float* src = h + (static_cast<size_t>(r) * in_stride + in_off) * D;
+    for (int i = lane; i < D; i += 32) row[i] = src[i];
+    __syncwarp();
+    double inv = 0.0;
+    if (lane == 0) {
+      double ms = 0.0;
+      int i = 0;
+      if ((D & 7) == 0) {
+        // rows of D floats start 16-byte aligned (D % 8 == 0, D * 4 bytes per row)
+        const float4* p4 = reinterpret_cast<const float4*>(row);
+        float4 a0 = p4[0], a1 = p4[1];
+        for (; i < D; i += 8) {
+          float4 b0 = a0, b1 = a1;
+          if (i + 8 < D) {
+            b0 = p4[(i >> 2) + 2];
+            b1 = p4[(i >> 2) + 3];
+          }
+          const float e[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const double x = static_cast<double>(e[k]);
-          ms = __fma_rn(x, x, ms);
+          for (int k = 0; k < 8; ++k) {
+            const double x = static_cast<double>(e[k]);
+            ms = __fma_rn(x, x, ms);
+          }
+          a0 = b0;
+          a1 = b1;
         }
-        a0 = b0;
-        a1 = b1;
       }
+      for (; i < D; ++i) {
+        const double x = static_cast<double>(row[i]);
+        ms = __fma_rn(x, x, ms);
+      }
+      ms = __ddiv_rn(ms, static_cast<double>(D));
+      inv = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(ms, eps)));
     }
-    for (; i < D; ++i) {
-      const double x = static_cast<double>(srow[i]);
-      ms = __fma_rn(x, x, ms);
+    inv = __shfl_sync(0xffffffffu, inv, 0);
+    for (int i = lane; i < D; i += 32)
+      row[i] = __double2float_rn(
+          __dmul_rn(__dmul_rn(static_cast<double>(row[i]), inv), static_cast<double>(w[i])));
+    __syncwarp();
+    if (xq) quant_row_warp(row, D, xq + static_cast<size_t>(r) * D, xs + r);
+  }
+  if (out_t) {
+    __syncthreads();  // the block's normalised rows are in shared memory
+    const int nr = min(kNormWarps, rows - r0);
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+      double* dst = out_t + static_cast<size_t>(d) * ldt + r0;
+      for (int k = 0; k < nr; ++k) dst[k] = static_cast<double>(srow[static_cast<size_t>(k) * D + d]);
     }
-    ms = __ddiv_rn(ms, static_cast<double>(D));
-    s_red[kNormThreads / 32] = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(ms, eps)));
   }
-  __syncthreads();
-  const double inv = s_red[kNormThreads / 32];
-  double amax = 0.0;
-  for (int i = tid; i < D; i += kNormThreads) {
-    const float v = __double2float_rn(
-        __dmul_rn(__dmul_rn(static_cast<double>(srow[i]), inv), static_cast<double>(w[i])));
-    srow[i] = v;
-    amax = fmax(amax, fabs(static_cast<double>(v)));
-  }
-  if (out_t)
-    for (int i = tid; i < D; i += kNormThreads)
-      out_t[static_cast<size_t>(i) * ldt + r] = static_cast<double>(srow[i]);
-  if (!xq) return;
-  // quantize_activation_int8 (bitnet.hpp:123-165): the row's absolute maximum, then per element
-  amax = warp_max_d(amax);
-  if ((tid & 31) == 0) s_red[tid >> 5] = amax;
-  __syncthreads();
-#pragma unroll
-  for (int k = 0; k < kNormThreads / 32; ++k) amax = fmax(amax, s_red[k]);
-  const double scale = __ddiv_rn(amax, 127.0);
-  const double qinv = scale == 0.0 ? 0.0 : __ddiv_rn(1.0, scale);
-  if (tid == 0) xs[r] = static_cast<float>(scale);
-  int8_t* q = xq + static_cast<size_t>(r) * D;
-  for (int i = tid; i < D; i += kNormThreads) q[i] = quant_one(srow[i], scale, qinv);
 }
 
 // RoPE (bitnet.hpp:472-488) on q and k of every head and append k, v to the cache.  Row r is
@@ -287,7 +295,8 @@ __global__ void __launch_bounds__(kAttnThreads)
     const float* kf = reinterpret_cast<const float*>(kr);
     double dot = 0.0;
 #pragma unroll
-    for (int d = 0; d < kHeadDim; ++d) dot = __dadd_rn(dot, __dmul_rn(sq[d], static_cast<double>(kf[d])));
+    // fma equals the multiply-then-add: q and k are floats, whose product is exact in double
+    for (int d = 0; d < kHeadDim; ++d) dot = __fma_rn(sq[d], static_cast<double>(kf[d]), dot);
     dot = __dmul_rn(dot, 0.125);  // 1 / sqrt(64), exact
     ss[j] = dot;
     mx = fmax(mx, dot);
@@ -389,7 +398,8 @@ __global__ void __launch_bounds__(kAttnSeqWarps * 32)
       const float* kj = sk + static_cast<size_t>(j) * kKStride;
       double dot = 0.0;
 #pragma unroll 16
-      for (int d = 0; d < kHeadDim; ++d) dot = __dadd_rn(dot, __dmul_rn(sq[d], static_cast<double>(kj[d])));
+      // fma equals the multiply-then-add: q and k are floats, whose product is exact in double
+      for (int d = 0; d < kHeadDim; ++d) dot = __fma_rn(sq[d], static_cast<double>(kj[d]), dot);
       dot = __dmul_rn(dot, 0.125);  // 1 / sqrt(64), exact
       ss[j] = dot;
       mx = fmax(mx, dot);
@@ -420,9 +430,12 @@ __global__ void __launch_bounds__(kAttnSeqWarps * 32)
 // SwiGLU (bitnet.hpp:603-610) of gate|up [M, 2F] -> float(silu(g) * u), then int8 quantization;
 // one block per row: every thread computes its elements and their absolute maximum, the block
 // combines the maxima, and every thread quantizes its own elements (a maximum and per-element
-// operations, so the same bits in any split).
-constexpr int kSwiThreads = 512;  // three of F = 1536 elements per thread: fewer dependent
-                                  // double exp / divide chains in a row than with 256
+// operations, so the same bits in any split).  kSwiThreads = 512 for decode-sized inputs (three
+// of F = 1536 elements per thread: fewer dependent double exp / divide chains per thread, 9.7 ->
+// 7.7 µs for 256 rows) and 256 for prefill-sized ones (16384 rows: 1247 µs against 1717 µs with
+// 512, where the blocks already fill the SMs).
+constexpr int kSwiRowsWide = 1024;  // rows below which a row gets 512 threads
+template <int kSwiThreads>
 __global__ void __launch_bounds__(kSwiThreads)
     swiglu_quant_kernel(const float* __restrict__ gu, int M, int F, int8_t* __restrict__ xq,
                         float* __restrict__ xs) {
@@ -461,8 +474,8 @@ __global__ void __launch_bounds__(kSwiThreads)
 // instead repeated each x element's conversion for all 250 vocabulary tiles).  Tile: 64 rows x 64
 // vocab ids; each thread owns 4 rows (two adjacent pairs, each read by one 16-byte load that the
 // warp's 16 threads of a row pair share) x 4 ids (the L1 data pipe bounds it: 84 % of its
-// wavefronts against 54 % of the fp64 pipe, measured on one launch).  ldx and ldv are multiples of 64, so every copy is
-// in bounds (rows r >= R are computed and not stored).
+// wavefronts against 54 % of the fp64 pipe, measured on one launch).  ldx and ldv are multiples
+// of 64, so every copy is in bounds (rows r >= R are computed and not stored).
 constexpr int kLmR = 64, kLmV = 64, kLmK = 16;
 __global__ void __launch_bounds__(256)
     lm_head_kernel(const double* __restrict__ xT, int ldx, int R, int D,
@@ -896,7 +909,7 @@ int BitNetLM::run_layers(int S, const int* pos, cudaStream_t s) {
   const BitNetCfg& c = cfg_;
   const int M = B_ * S, D = c.d_model, F = c.ffn_dim, H = D / kHeadDim;
   const size_t kv_layer = static_cast<size_t>(B_) * H * L_ * kHeadDim;
-  const int norm_blocks = M;
+  const int norm_blocks = (M + kNormWarps - 1) / kNormWarps;
   const size_t norm_smem = norm_smem_bytes(D);
   const size_t swi_smem = static_cast<size_t>(F) * 4;
   const size_t attn_smem = attn_smem_bytes(L_);
@@ -905,7 +918,7 @@ int BitNetLM::run_layers(int S, const int* pos, cudaStream_t s) {
     const Layer& Ly = layers_[l];
     float* kc = kc_ + l * kv_layer;
     float* vc = vc_ + l * kv_layer;
-    DLM_CHECK_CUDA(launch_pdl(rms_norm_kernel, dim3(norm_blocks), dim3(kNormThreads), norm_smem,
+    DLM_CHECK_CUDA(launch_pdl(rms_norm_kernel, dim3(norm_blocks), dim3(kNormWarps * 32), norm_smem,
         s, h_, M, D, 1, 0, Ly.attn_norm, c.rms_eps, xq_, xs_, nullptr, 0));
     if (S == 1 && pos != nullptr && M < ternary_tc_min_rows()) {
       // decode: RoPE and the K / V append in the q|k|v projection's epilogue
@@ -929,12 +942,16 @@ int BitNetLM::run_layers(int S, const int* pos, cudaStream_t s) {
     rc = quantize_act_i8(ao_, M, D, xq_, xs_, s);
     if (rc == DLM_OK) rc = ternary_gemm_i8(Ly.wo, Ly.ao, xq_, xs_, h_, M, D, D, s, true, true);
     if (rc != DLM_OK) break;
-    DLM_CHECK_CUDA(launch_pdl(rms_norm_kernel, dim3(norm_blocks), dim3(kNormThreads), norm_smem,
+    DLM_CHECK_CUDA(launch_pdl(rms_norm_kernel, dim3(norm_blocks), dim3(kNormWarps * 32), norm_smem,
         s, h_, M, D, 1, 0, Ly.ffn_norm, c.rms_eps, xq_, xs_, nullptr, 0));
     rc = ternary_gemm_i8(Ly.wgu, Ly.agu, xq_, xs_, y_, M, 2 * F, D, s, false, true);
     if (rc != DLM_OK) break;
-    DLM_CHECK_CUDA(launch_pdl(swiglu_quant_kernel, dim3(M), dim3(kSwiThreads), swi_smem, s, y_, M,
-        F, xq_, xs_));
+    if (M < kSwiRowsWide)
+      DLM_CHECK_CUDA(launch_pdl(swiglu_quant_kernel<512>, dim3(M), dim3(512), swi_smem, s, y_, M, F,
+          xq_, xs_));
+    else
+      DLM_CHECK_CUDA(launch_pdl(swiglu_quant_kernel<256>, dim3(M), dim3(256), swi_smem, s, y_, M, F,
+          xq_, xs_));
     rc = ternary_gemm_i8(Ly.wd, Ly.ad, xq_, xs_, h_, M, D, F, s, true, true);
   }
   if (rc == DLM_OK) DLM_CHECK_CUDA(cudaGetLastError());
@@ -947,8 +964,8 @@ int BitNetLM::run_head(int rows, int stride, int off, cudaStream_t s) {
   const int D = c.d_model;
   DLM_REQUIRE(D % kLmK == 0 && rows <= ldx_, DLM_ERR_INVALID, "bitnet: d_model %d / head rows %d", D,
               rows);
-  DLM_CHECK_CUDA(launch_pdl(rms_norm_kernel, dim3(rows), dim3(kNormThreads), norm_smem_bytes(D), s,
-      h_, rows, D, stride, off, final_norm_,
+  DLM_CHECK_CUDA(launch_pdl(rms_norm_kernel, dim3((rows + kNormWarps - 1) / kNormWarps),
+      dim3(kNormWarps * 32), norm_smem_bytes(D), s, h_, rows, D, stride, off, final_norm_,
       c.rms_eps, nullptr, nullptr, normT_, ldx_));
   dim3 grid((c.vocab + kLmV - 1) / kLmV, (rows + kLmR - 1) / kLmR);
   DLM_CHECK_CUDA(launch_pdl(lm_head_kernel, dim3(grid), dim3(256), 0, s, normT_, ldx_, rows, D,
@@ -966,7 +983,10 @@ int BitNetLM::set_smem_attrs() {
                                     attn_smem_bytes(c.max_seq));
   DLM_CHECK_CUDA(cudaFuncSetAttribute(rms_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       static_cast<int>(norm_smem)));
-  DLM_CHECK_CUDA(cudaFuncSetAttribute(swiglu_quant_kernel,
+  DLM_CHECK_CUDA(cudaFuncSetAttribute(swiglu_quant_kernel<512>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(swi_smem)));
+  DLM_CHECK_CUDA(cudaFuncSetAttribute(swiglu_quant_kernel<256>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       static_cast<int>(swi_smem)));
   DLM_CHECK_CUDA(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
