@@ -9,12 +9,15 @@
 // same order as the reference, so codes and scales are identical.
 //
 // The GEMM keeps the reference's exact arithmetic: int32 accumulation (|acc| <= 127 * K fits for
-// K < 2^24) and y = float(double(acc) * double(alpha_n) * double(scale_m)).  Each CTA computes a
-// 32-token x 64-output tile (32 outputs when 64-wide tiles would leave most SMs idle: the decode's
-// 512-output projections): K runs in chunks of 256 whose packed weights and activations arrive by
-// asynchronous copies while the previous chunk is multiplied; the weight chunk is expanded to int8
-// once in shared memory (rows padded by 16 bytes, so 16-byte reads of consecutive rows hit distinct
-// banks) and amortised over the 32 tokens; the inner loop is 16-byte shared loads + dp4a.
+// K < 2^24) and y = float(double(acc) * double(alpha_n) * double(scale_m)), on three paths that
+// give the same bits: the tensor cores (tcgen05.mma kind::i8) in 128 x 128 tiles for prefill-sized
+// inputs (ternary_gemm_tc_kernel), in 128 x 32 / 64 tiles for decode-sized ones
+// (ternary_gemm_tcd_kernel), and dp4a for the remaining shapes (ternary_gemm_kernel: a 32-token x
+// 64-output tile per CTA, 32 outputs when 64-wide tiles would leave most SMs idle; K runs in
+// chunks of 256 whose packed weights and activations arrive by asynchronous copies while the
+// previous chunk is multiplied; the weight chunk is expanded to int8 once in shared memory, rows
+// padded by 16 bytes so 16-byte reads of consecutive rows hit distinct banks, and amortised over
+// the 32 tokens; the inner loop is 16-byte shared loads + dp4a).
 #include <cstdint>
 #include <cstdlib>
 
