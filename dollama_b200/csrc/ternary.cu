@@ -522,6 +522,11 @@ __host__ __device__ constexpr int td_smem_bytes(int TN, int K) {
   return kTdStages * kTdStageA + TN * K + TN * (K / 4) + TN * 4 + 256 + 1024;
 }
 
+static_assert(td_smem_bytes(64, kTdMaxK) <= 227 * 1024 && td_smem_bytes(32, kTdMaxK) <= 227 * 1024,
+              "decode tile's shared memory at the largest K");
+static_assert(td_smem_bytes(32, 4 * kTdKB) * 2 <= 228 * 1024 - 2 * 1024,
+              "two 32-output CTAs per SM at K = 512");
+
 template <int TN, bool kRope>
 __global__ void __launch_bounds__(kTdThreads, 2)
     ternary_gemm_tcd_kernel(const __grid_constant__ CUtensorMap tmX, const TernaryTcParams p,
